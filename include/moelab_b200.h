@@ -1,0 +1,110 @@
+/*
+ * moelab_b200 - C ABI of the B200-native (sm_100a) quantized MoE-layer forward.
+ *
+ * Drop-in boundary for moe-lab's hot path. moe-lab (Tigerly1/moe-lab) has no native library: its boundary is
+ * the Python variant contract `prepare / run(state, x, idx, wts[, act]) / dequant` driven by
+ * moelab/torch_backend.py:103-126 and moelab/worker.py:33-43, plus the layer composition of
+ * moelab/e2e.py:51-69 (router -> run -> shared experts). Each entry point below names the reference interface
+ * it replaces. All pointers are device pointers unless stated; every call is asynchronous on `stream`,
+ * allocates nothing and returns MOEB_OK (0) or an error code with a message from moeb_last_error().
+ *
+ * Weight layout (B200 layout, produced by moeb_quantize_* or moeb_*_from_mlx from the mlx layout):
+ *   int4 affine g64: q  uint32 [E][N][K/8]  (word j = elements 8j..8j+7; nibble p = element 8j+2p and
+ *                                             nibble p+4 = element 8j+2p+1, p = 0..3)
+ *                    sb uint32 [E][N][K/64] (bf16 scale in bits 0-15, bf16 bias in bits 16-31)
+ *   MXFP4:           q  uint32 [E][N][K/8]  (same nibble order, E2M1 codes), sc uint8 [E][N][K/32] (E8M0)
+ *   gate/up: N = f, K = d; down: N = d, K = f. Activations x, y, residual: bf16 [T][d].
+ */
+#ifndef MOELAB_B200_H
+#define MOELAB_B200_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#ifndef __CUDA_RUNTIME_H__
+typedef struct CUstream_st *cudaStream_t;
+#endif
+
+#define MOEB_VERSION 1
+
+/* status codes */
+#define MOEB_OK 0
+#define MOEB_EINVAL 1   /* bad shape or argument */
+#define MOEB_ELAUNCH 2  /* CUDA launch / runtime error */
+#define MOEB_ETIMEOUT 3 /* a bounded device wait gave up */
+#define MOEB_EUNSUP 4   /* unsupported format / configuration */
+
+/* dispatcher policies (reference: custom_wins / load_max, moelab/variants/mlx/metal_q4_moe.py:42-46,
+ * metal_mxfp4_moe.py:468-471) */
+#define MOEB_POLICY_AUTO 0    /* choose by load = T*k/E */
+#define MOEB_POLICY_SLOTS 1   /* one tile per slot, no routing step (decode) */
+#define MOEB_POLICY_TILES8 2  /* slots grouped by expert, tiles of <= 8 slots */
+#define MOEB_POLICY_TILES16 3 /* tiles of <= 16 slots */
+
+/* device error bits readable with moeb_read_error */
+#define MOEB_DEVERR_EXPERT_ID 1u /* an expert id outside [0, E) was given; that slot contributed nothing */
+#define MOEB_DEVERR_TIMEOUT 2u
+
+int moeb_version(void);
+const char *moeb_last_error(void); /* thread-local message of the last failing call */
+
+/* Scratch for one layer call of up to T tokens (h, per-slot partials, routing tables, counters). The buffer
+ * must be zeroed once with moeb_workspace_init before its first use; calls leave the counters zero again.
+ * One workspace serves one stream at a time. (Reference: the variant caches its scratch per shape in
+ * `state`, moelab/variants/mlx/metal_q4_tiles_v2.py:432-448; here the caller owns it.) */
+size_t moeb_workspace_bytes(int T, int d, int f, int E, int k);
+int moeb_workspace_init(void *ws, size_t ws_bytes, cudaStream_t stream);
+/* Copies the sticky device error word to *out (host) and clears it. Synchronises `stream`. */
+int moeb_read_error(void *ws, unsigned *out, cudaStream_t stream);
+/* Policy the dispatcher picks for AUTO (host-only, no device work). */
+int moeb_policy(int T, int E, int k);
+
+/* --- quantizers: w bf16 [rows][K] -> B200 layout. Replace mx.quantize(w, group_size=64, bits=4) and
+ * mx.quantize(w, mode="mxfp4") in prepare() (metal_q4_moe.py:32-35, metal_mxfp4_moe.py:448-451). */
+int moeb_quantize_q4(const void *w, long rows, long K, void *q, void *sb, cudaStream_t stream);
+int moeb_quantize_mxfp4(const void *w, long rows, long K, void *q, void *sc, cudaStream_t stream);
+/* --- fp32 dequantisation in natural element order (the weights the kernels multiply). Replace
+ * mx.dequantize in dequant() (metal_q4_moe.py:38-39, metal_mxfp4_moe.py:454-455). */
+int moeb_dequant_q4(const void *q, const void *sb, long rows, long K, float *out, cudaStream_t stream);
+int moeb_dequant_mxfp4(const void *q, const void *sc, long rows, long K, float *out, cudaStream_t stream);
+/* --- mlx state (weight uint32 natural nibble order, bf16 scales / biases or uint8 scales) -> B200 layout.
+ * Replaces the state construction from mlx-lm modules (e2e.py:48-49, metal_mxfp4_gptoss.py:100-107). */
+int moeb_q4_from_mlx(const void *wq, const void *scales, const void *biases, long rows, long K, void *q,
+                     void *sb, cudaStream_t stream);
+int moeb_mxfp4_from_mlx(const void *wq, const void *scales, long rows, long K, void *q, void *sc,
+                        cudaStream_t stream);
+
+/* --- router: logits = x . gate_w^T (+ gate_b), fp32, fixed summation order; top-k (ties -> lowest id,
+ * NaN -> -inf); norm=1: softmax over the top-k, norm=0: full-softmax probabilities; times `scale`.
+ * Replaces moelab/router.py:71-80 topk_norm and the stock sequence of e2e.py:56-63 / :171-176 / :136-140.
+ * idx int32 [T][k], wts fp32 [T][k], logits fp32 [T][E] (may be NULL). ws: a workspace from
+ * moeb_workspace_bytes(T, d, 64, E, k) used by this router alone. */
+int moeb_router(const void *x, const void *gate_w, const void *gate_b, int T, int d, int E, int k, int norm,
+                float scale, int *idx, float *wts, float *logits, void *ws, size_t ws_bytes, cudaStream_t stream);
+
+/* --- expert forward with given routing: y = sum_j wts[t,j] * (Wd act(Wg x + bg, Wu x + bu) + bd) (+ residual).
+ * Replaces the variant run(state, x, idx, wts, act) (metal_q4_moe.py:54-64 dispatcher; contract
+ * problem.py:3-10). act: 0 SwiGLU, 1 tanh-GELU GLU, 2 gpt-oss clamped SwiGLU (alpha 1.702, limit 7, up+1).
+ * Biases (fp32, NULL = none): bg, bu [E][f], bd [E][d]. residual bf16 [T][d] or NULL. */
+int moeb_experts_q4(const void *x, const void *qg, const void *sbg, const void *qu, const void *sbu,
+                    const void *qd, const void *sbd, const float *bg, const float *bu, const float *bd,
+                    const int *idx, const float *wts, int T, int d, int f, int E, int k, int act, int policy,
+                    const void *residual, void *y, void *ws, size_t ws_bytes, cudaStream_t stream);
+
+/* --- full layer call (x, gate weights, packed expert weights + scales + biases, k) -> y: router, routing
+ * step, grouped experts and the weighted combine in one stream-ordered sequence (3-4 launches).
+ * Replaces the patched MoE block call of moelab/e2e.py:51-69 (router + mod.run). idx_out / wts_out may be
+ * NULL (then they live in the workspace). */
+int moeb_layer_q4(const void *x, const void *gate_w, const void *gate_b, int norm, float rscale, const void *qg,
+                  const void *sbg, const void *qu, const void *sbu, const void *qd, const void *sbd,
+                  const float *bg, const float *bu, const float *bd, int T, int d, int f, int E, int k, int act,
+                  int policy, const void *residual, void *y, int *idx_out, float *wts_out, void *ws,
+                  size_t ws_bytes, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOELAB_B200_H */

@@ -1,0 +1,405 @@
+// C ABI of libmoelab_b200 (declared in include/moelab_b200.h). Plain pointers and sizes, int status,
+// no allocation, no host synchronisation except moeb_read_error.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <mutex>
+#include <unordered_map>
+
+#include "../../include/moelab_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace moeb;
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char *fmt, const char *detail = "") {
+    snprintf(g_err, sizeof g_err, fmt, detail);
+    return code;
+}
+
+int check_launch(const char *what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        snprintf(g_err, sizeof g_err, "%s: %s", what, cudaGetErrorString(e));
+        return MOEB_ELAUNCH;
+    }
+    return MOEB_OK;
+}
+
+int sm_count() {
+    static std::mutex mu;
+    static std::unordered_map<int, int> cache;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(dev);
+    if (it != cache.end()) return it->second;
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n;
+    return n;
+}
+
+int occupancy(const void *fn, int threads, size_t smem) {
+    static std::mutex mu;
+    static std::unordered_map<const void *, int> cache;
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(fn);
+    if (it != cache.end()) return it->second;
+    int n = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads, smem);
+    if (n < 1) n = 1;
+    cache[fn] = n;
+    return n;
+}
+
+// Launch with programmatic dependent launch so the kernel's prologue overlaps the previous kernel's tail;
+// every kernel calls griddepcontrol.wait before touching data produced upstream.
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// Workspace layout for up to Tc tokens. The first region holds counters that must be zero before the first
+// call (moeb_workspace_init); every kernel leaves them zero again.
+struct Layout {
+    size_t err, cnt_all, rcnt, ycnt, zero_end;
+    size_t logits, idx, wts, xsum, ntiles, tiles, sorted, h, hsum, yp, total;
+};
+
+Layout layout(long Tc, int d, int f, int E, int k) {
+    Layout L;
+    const long TK = Tc * k;
+    size_t o = 0;
+    L.err = o; o += 256;
+    L.cnt_all = o; o += 256;
+    L.rcnt = o; o = align256(o + 4 * (size_t)((Tc + 7) / 8));
+    L.ycnt = o; o = align256(o + 4 * (size_t)Tc * (d / 16));
+    L.zero_end = o;
+    L.logits = o; o = align256(o + 4 * (size_t)Tc * E);
+    L.idx = o; o = align256(o + 4 * (size_t)TK);
+    L.wts = o; o = align256(o + 4 * (size_t)TK);
+    L.xsum = o; o = align256(o + 4 * (size_t)Tc * (d / 64));
+    L.ntiles = o; o += 256;
+    L.tiles = o; o = align256(o + 16 * (size_t)(TK + E + 1));
+    L.sorted = o; o = align256(o + 4 * (size_t)TK);
+    L.h = o; o = align256(o + 2 * (size_t)TK * f);
+    L.hsum = o; o = align256(o + 4 * (size_t)TK * (f / 16));
+    L.yp = o; o = align256(o + 4 * (size_t)TK * d);
+    L.total = o;
+    return L;
+}
+
+// Largest token capacity whose layout fits in `bytes` (layout size is monotone in T).
+long capacity(size_t bytes, int d, int f, int E, int k) {
+    long lo = 0, hi = 1;
+    while (layout(hi, d, f, E, k).total <= bytes && hi < (1L << 24)) hi *= 2;
+    while (lo < hi) {
+        long mid = (lo + hi + 1) / 2;
+        if (layout(mid, d, f, E, k).total <= bytes) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+template <typename T>
+T *at(void *ws, size_t off) { return reinterpret_cast<T *>(static_cast<char *>(ws) + off); }
+
+int check_shape(int T, int d, int f, int E, int k) {
+    if (T < 0 || d <= 0 || f <= 0 || E <= 0 || k <= 0) return fail(MOEB_EINVAL, "non-positive dimension%s");
+    if (d % 64 || f % 64) return fail(MOEB_EINVAL, "d and f must be multiples of 64%s");
+    if (k > 32 || k > E) return fail(MOEB_EINVAL, "k must be <= min(E, 32)%s");
+    if (E > 1024) return fail(MOEB_EINVAL, "E must be <= 1024%s");
+    return MOEB_OK;
+}
+
+// ------------------------------------------------------------------ dispatcher
+// Load = T*k/E (average slots per expert; the reference's policy variable, metal_q4_moe.py:42-46).
+// Few slots: one tile per slot (no routing step). Otherwise group slots by expert into tiles of 8 or 16.
+int choose_policy(int T, int E, int k) {
+    const long TK = (long)T * k;
+    const double load = (double)TK / E;
+    if (TK <= 64 || load < 1.0) return MOEB_POLICY_SLOTS;
+    return load <= 6.0 ? MOEB_POLICY_TILES8 : MOEB_POLICY_TILES16;
+}
+
+int nt_of(int policy) { return policy == MOEB_POLICY_TILES16 ? 16 : 8; }
+
+struct ExpLaunch {
+    void (*gu)(ExpArgs);
+    void (*dn)(ExpArgs);
+    int threads;
+};
+
+ExpLaunch pick_kernels(int fmt, int policy) {
+    const bool wide = policy == MOEB_POLICY_TILES16;
+    if (fmt == FMT_Q4) {
+        if (wide) return {k_gate_up<FMT_Q4, 2, 4>, k_down<FMT_Q4, 2, 4>, 128};
+        return {k_gate_up<FMT_Q4, 1, 4>, k_down<FMT_Q4, 1, 4>, 128};
+    }
+    return {nullptr, nullptr, 0};
+}
+
+int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaStream_t st) {
+    const long TK = (long)a.T * a.k;
+    const int nt = nt_of(policy);
+    const long max_tiles = a.tile_mode ? std::min<long>(TK, (long)a.E + TK / nt) : TK;
+    ExpLaunch K = pick_kernels(fmt, policy);
+    if (!K.gu) return fail(MOEB_EUNSUP, "format not supported%s");
+    const int nsm = sm_count();
+    {
+        const long units = max_tiles * (a.f / 16);
+        const long cap = (long)occupancy((const void *)K.gu, K.threads, 0) * nsm;
+        const int grid = (int)std::max<long>(1, std::min(units, cap));
+        if (launch(K.gu, dim3(grid), dim3(K.threads), 0, st, a) != cudaSuccess) return check_launch("gate_up");
+    }
+    {
+        const long units = max_tiles * (a.d / 16);
+        const long cap = (long)occupancy((const void *)K.dn, K.threads, 0) * nsm;
+        const int grid = (int)std::max<long>(1, std::min(units, cap));
+        if (launch(K.dn, dim3(grid), dim3(K.threads), 0, st, a) != cudaSuccess) return check_launch("down");
+    }
+    (void)L;
+    (void)ws;
+    return MOEB_OK;
+}
+
+template <int TPB>
+void (*router_kernel(int E))(RouterArgs) {
+    const int J = (E + 31) / 32;
+    if (J <= 1) return k_router<TPB, 1>;
+    if (J <= 2) return k_router<TPB, 2>;
+    if (J <= 4) return k_router<TPB, 4>;
+    if (J <= 8) return k_router<TPB, 8>;
+    if (J <= 16) return k_router<TPB, 16>;
+    return k_router<TPB, 32>;
+}
+
+int launch_router(const void *x, const void *wg, const void *bias, int T, int d, int E, int k, int norm,
+                  float scale, int *idx, float *wts, float *logits, bool want_xsum, int policy, const Layout &L,
+                  void *ws, cudaStream_t st) {
+    RouterArgs r = {};
+    r.x = static_cast<const uint16_t *>(x);
+    r.wg = static_cast<const uint16_t *>(wg);
+    r.bias = static_cast<const uint16_t *>(bias);
+    r.T = T; r.d = d; r.E = E; r.k = k; r.norm = norm; r.scale = scale;
+    r.logits = logits ? logits : at<float>(ws, L.logits);
+    r.idx = idx;
+    r.wts = wts;
+    r.xsum = want_xsum ? at<float>(ws, L.xsum) : nullptr;
+    r.cnt = at<unsigned>(ws, L.rcnt);
+    r.cnt_all = at<unsigned>(ws, L.cnt_all);
+    r.err = at<unsigned>(ws, L.err);
+    const bool tiles = policy == MOEB_POLICY_TILES8 || policy == MOEB_POLICY_TILES16;
+    r.NT = nt_of(policy);
+    r.tiles = tiles ? at<int4>(ws, L.tiles) : nullptr;
+    r.ntiles = at<int>(ws, L.ntiles);
+    r.sorted = at<int>(ws, L.sorted);
+    const size_t smem = tiles ? 12 * (size_t)E : 0;
+    if (launch(router_kernel<8>(E), dim3((E + 3) / 4, (T + 7) / 8), dim3(128), smem, st, r) != cudaSuccess)
+        return check_launch("router");
+    return MOEB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int moeb_version(void) { return MOEB_VERSION; }
+
+const char *moeb_last_error(void) { return g_err; }
+
+size_t moeb_workspace_bytes(int T, int d, int f, int E, int k) {
+    if (T < 1) T = 1;
+    return layout(T, d, f, E, k).total;
+}
+
+int moeb_workspace_init(void *ws, size_t ws_bytes, cudaStream_t st) {
+    if (!ws) return fail(MOEB_EINVAL, "null workspace%s");
+    if (cudaMemsetAsync(ws, 0, ws_bytes, st) != cudaSuccess) return check_launch("workspace_init");
+    return MOEB_OK;
+}
+
+int moeb_read_error(void *ws, unsigned *out, cudaStream_t st) {
+    unsigned v = 0;
+    if (cudaMemcpyAsync(&v, ws, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess) return check_launch("read_error");
+    if (cudaStreamSynchronize(st) != cudaSuccess) return check_launch("read_error sync");
+    if (cudaMemsetAsync(ws, 0, 4, st) != cudaSuccess) return check_launch("read_error clear");
+    *out = v;
+    return MOEB_OK;
+}
+
+int moeb_policy(int T, int E, int k) { return choose_policy(T, E, k); }
+
+// ------------------------------------------------------------------ quantizers
+int moeb_quantize_q4(const void *w, long rows, long K, void *qw, void *sb, cudaStream_t st) {
+    if (K % 64 || rows < 0) return fail(MOEB_EINVAL, "K must be a multiple of 64%s");
+    const long n = rows * (K / 64);
+    if (n == 0) return MOEB_OK;
+    k_q4_quantize<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(static_cast<const uint16_t *>(w), rows, K,
+                                                             static_cast<uint32_t *>(qw), static_cast<uint32_t *>(sb));
+    return check_launch("quantize_q4");
+}
+
+int moeb_dequant_q4(const void *qw, const void *sb, long rows, long K, float *out, cudaStream_t st) {
+    if (K % 64 || rows < 0) return fail(MOEB_EINVAL, "K must be a multiple of 64%s");
+    const long n = rows * (K / 8);
+    if (n == 0) return MOEB_OK;
+    k_q4_dequant<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(static_cast<const uint32_t *>(qw),
+                                                            static_cast<const uint32_t *>(sb), rows, K, out);
+    return check_launch("dequant_q4");
+}
+
+int moeb_q4_from_mlx(const void *wq, const void *scales, const void *biases, long rows, long K, void *qw, void *sb,
+                     cudaStream_t st) {
+    if (K % 64 || rows < 0) return fail(MOEB_EINVAL, "K must be a multiple of 64%s");
+    const long n = rows * (K / 8);
+    if (n == 0) return MOEB_OK;
+    k_q4_from_mlx<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
+        static_cast<const uint32_t *>(wq), static_cast<const uint16_t *>(scales), static_cast<const uint16_t *>(biases),
+        rows, K, static_cast<uint32_t *>(qw), static_cast<uint32_t *>(sb));
+    return check_launch("q4_from_mlx");
+}
+
+int moeb_quantize_mxfp4(const void *w, long rows, long K, void *qw, void *sc, cudaStream_t st) {
+    if (K % 64 || rows < 0) return fail(MOEB_EINVAL, "K must be a multiple of 64%s");
+    const long n = rows * (K / 32);
+    if (n == 0) return MOEB_OK;
+    k_fp4_quantize<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(static_cast<const uint16_t *>(w), rows, K,
+                                                              static_cast<uint32_t *>(qw), static_cast<uint8_t *>(sc));
+    return check_launch("quantize_mxfp4");
+}
+
+int moeb_dequant_mxfp4(const void *qw, const void *sc, long rows, long K, float *out, cudaStream_t st) {
+    if (K % 64 || rows < 0) return fail(MOEB_EINVAL, "K must be a multiple of 64%s");
+    const long n = rows * (K / 8);
+    if (n == 0) return MOEB_OK;
+    k_fp4_dequant<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(static_cast<const uint32_t *>(qw),
+                                                             static_cast<const uint8_t *>(sc), rows, K, out);
+    return check_launch("dequant_mxfp4");
+}
+
+int moeb_mxfp4_from_mlx(const void *wq, const void *scales, long rows, long K, void *qw, void *sc, cudaStream_t st) {
+    if (K % 64 || rows < 0) return fail(MOEB_EINVAL, "K must be a multiple of 64%s");
+    const long n = rows * (K / 8);
+    if (n == 0) return MOEB_OK;
+    k_fp4_from_mlx<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(static_cast<const uint32_t *>(wq),
+                                                              static_cast<const uint8_t *>(scales), rows, K,
+                                                              static_cast<uint32_t *>(qw), static_cast<uint8_t *>(sc));
+    return check_launch("mxfp4_from_mlx");
+}
+
+// ------------------------------------------------------------------ router
+int moeb_router(const void *x, const void *wg, const void *bias, int T, int d, int E, int k, int norm, float scale,
+                int *idx, float *wts, float *logits, void *ws, size_t ws_bytes, cudaStream_t st) {
+    if (d <= 0 || d % 8) return fail(MOEB_EINVAL, "d must be a positive multiple of 8%s");
+    if (E <= 0 || E > 1024 || k <= 0 || k > 32 || k > E) return fail(MOEB_EINVAL, "need 0 < k <= min(E, 32), E <= 1024%s");
+    if (T == 0) return MOEB_OK;
+    const long cap = capacity(ws_bytes, d, 64, E, k);
+    if (cap < T) return fail(MOEB_EINVAL, "workspace too small%s");
+    const Layout L = layout(cap, d, 64, E, k);
+    return launch_router(x, wg, bias, T, d, E, k, norm, scale, idx, wts, logits, false, MOEB_POLICY_SLOTS, L, ws, st);
+}
+
+// ------------------------------------------------------------------ experts (ids given) and full layer
+static int experts_common(int fmt, const void *x, const void *qg, const void *sbg, const void *qu, const void *sbu,
+                          const void *qd, const void *sbd, const float *bg, const float *bu, const float *bd,
+                          const int *idx, const float *wts, int T, int d, int f, int E, int k, int act, int policy,
+                          const void *residual, void *y, void *ws, size_t ws_bytes, cudaStream_t st,
+                          const void *gate_w, const void *gate_b, int norm, float rscale, int *idx_out,
+                          float *wts_out) {
+    int rc = check_shape(T, d, f, E, k);
+    if (rc) return rc;
+    if (act < 0 || act > 2) return fail(MOEB_EINVAL, "act must be 0, 1 or 2%s");
+    if (T == 0) return MOEB_OK;
+    const long cap = capacity(ws_bytes, d, f, E, k);
+    if (cap < T) return fail(MOEB_EINVAL, "workspace too small for T tokens%s");
+    const Layout L = layout(cap, d, f, E, k);
+    if (policy == MOEB_POLICY_AUTO) policy = choose_policy(T, E, k);
+    if (policy != MOEB_POLICY_SLOTS && policy != MOEB_POLICY_TILES8 && policy != MOEB_POLICY_TILES16)
+        return fail(MOEB_EINVAL, "unknown policy%s");
+    const bool tiles = policy != MOEB_POLICY_SLOTS;
+    if (gate_w) {  // layer call: router produces ids, weights, x group sums and (tile mode) the tiles
+        int *ri = idx_out ? idx_out : at<int>(ws, L.idx);
+        float *rw = wts_out ? wts_out : at<float>(ws, L.wts);
+        rc = launch_router(x, gate_w, gate_b, T, d, E, k, norm, rscale, ri, rw, nullptr, true, policy, L, ws, st);
+        if (rc) return rc;
+        idx = ri;
+        wts = rw;
+    } else {
+        PrepArgs p = {};
+        p.x = static_cast<const uint16_t *>(x);
+        p.idx = idx;
+        p.T = T; p.d = d; p.E = E; p.k = k;
+        p.xsum = at<float>(ws, L.xsum);
+        p.cnt_all = at<unsigned>(ws, L.cnt_all);
+        p.NT = nt_of(policy);
+        p.tiles = tiles ? at<int4>(ws, L.tiles) : nullptr;
+        p.ntiles = at<int>(ws, L.ntiles);
+        p.sorted = at<int>(ws, L.sorted);
+        p.err = at<unsigned>(ws, L.err);
+        const size_t smem = tiles ? 12 * (size_t)E : 0;
+        if (launch(k_prep, dim3((T + 7) / 8), dim3(256), smem, st, p) != cudaSuccess) return check_launch("prep");
+    }
+    ExpArgs a = {};
+    a.x = static_cast<const uint16_t *>(x);
+    a.xsum = at<float>(ws, L.xsum);
+    a.g = {static_cast<const uint32_t *>(qg), static_cast<const uint32_t *>(sbg)};
+    a.u = {static_cast<const uint32_t *>(qu), static_cast<const uint32_t *>(sbu)};
+    a.dn = {static_cast<const uint32_t *>(qd), static_cast<const uint32_t *>(sbd)};
+    a.bg = bg; a.bu = bu; a.bd = bd;
+    if ((bg == nullptr) != (bu == nullptr)) return fail(MOEB_EINVAL, "gate and up biases go together%s");
+    a.idx = idx;
+    a.wts = wts;
+    a.tiles = at<int4>(ws, L.tiles);
+    a.ntiles = at<int>(ws, L.ntiles);
+    a.sorted = at<int>(ws, L.sorted);
+    a.h = at<uint16_t>(ws, L.h);
+    a.hsum = at<float>(ws, L.hsum);
+    a.yp = at<float>(ws, L.yp);
+    a.ycnt = at<unsigned>(ws, L.ycnt);
+    a.residual = static_cast<const uint16_t *>(residual);
+    a.y = static_cast<uint16_t *>(y);
+    a.err = at<unsigned>(ws, L.err);
+    a.T = T; a.d = d; a.f = f; a.E = E; a.k = k; a.act = act; a.tile_mode = tiles ? 1 : 0;
+    return run_experts(fmt, a, policy, L, ws, st);
+}
+
+int moeb_experts_q4(const void *x, const void *qg, const void *sbg, const void *qu, const void *sbu, const void *qd,
+                    const void *sbd, const float *bg, const float *bu, const float *bd, const int *idx,
+                    const float *wts, int T, int d, int f, int E, int k, int act, int policy, const void *residual,
+                    void *y, void *ws, size_t ws_bytes, cudaStream_t st) {
+    if (!idx || !wts) return fail(MOEB_EINVAL, "idx and wts are required%s");
+    return experts_common(FMT_Q4, x, qg, sbg, qu, sbu, qd, sbd, bg, bu, bd, idx, wts, T, d, f, E, k, act, policy,
+                          residual, y, ws, ws_bytes, st, nullptr, nullptr, 0, 1.f, nullptr, nullptr);
+}
+
+int moeb_layer_q4(const void *x, const void *gate_w, const void *gate_b, int norm, float rscale, const void *qg,
+                  const void *sbg, const void *qu, const void *sbu, const void *qd, const void *sbd, const float *bg,
+                  const float *bu, const float *bd, int T, int d, int f, int E, int k, int act, int policy,
+                  const void *residual, void *y, int *idx_out, float *wts_out, void *ws, size_t ws_bytes,
+                  cudaStream_t st) {
+    if (!gate_w) return fail(MOEB_EINVAL, "gate weights are required%s");
+    return experts_common(FMT_Q4, x, qg, sbg, qu, sbu, qd, sbd, bg, bu, bd, nullptr, nullptr, T, d, f, E, k, act,
+                          policy, residual, y, ws, ws_bytes, st, gate_w, gate_b, norm, rscale, idx_out, wts_out);
+}
+
+}  // extern "C"

@@ -1,0 +1,83 @@
+// Shared device helpers for the moelab_b200 kernels (sm_100a).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define MOEB_DEV __device__ __forceinline__
+
+namespace moeb {
+
+// Error bits written to the workspace error word by device code (read back with moeb_read_error).
+enum : uint32_t {
+    ERR_EXPERT_ID = 1u,  // an expert id outside [0, E): the slot contributes nothing
+    ERR_TIMEOUT = 2u,    // a bounded wait gave up
+};
+
+MOEB_DEV float bf16lo(uint32_t v) { return __uint_as_float(v << 16); }
+MOEB_DEV float bf16hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+MOEB_DEV float bf2f(uint16_t h) { return __uint_as_float(((uint32_t)h) << 16); }
+MOEB_DEV uint16_t f2bf(float f) {
+    __nv_bfloat16 b = __float2bfloat16_rn(f);
+    return *reinterpret_cast<uint16_t *>(&b);
+}
+MOEB_DEV uint32_t pack_bf2(float lo, float hi) {
+    return (uint32_t)f2bf(lo) | ((uint32_t)f2bf(hi) << 16);
+}
+
+// Programmatic dependent launch: wait for the preceding grid's results / let the next grid launch early.
+MOEB_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+MOEB_DEV void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// Streaming loads of expert weights (read once per call): keep them out of L1.
+MOEB_DEV uint2 ld_stream_u2(const void *p) {
+    uint2 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+    return r;
+}
+MOEB_DEV uint32_t ld_stream_u32(const void *p) {
+    uint32_t r;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+    return r;
+}
+MOEB_DEV uint4 ld_stream_u4(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+
+// Warp-level bf16 tensor-core MMA, fp32 accumulate: D = A(16x16) * B(16x8) + C.
+MOEB_DEV void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// bf16x2 (128 + q_lo, 128 + q_hi) from the nibble pair (p, p + 4) of a packed int4 word: q | 0x4300 read as
+// bf16 is exactly 128 + q, so one lop3 turns two codes into two exact MMA operands.
+MOEB_DEV uint32_t q4pair(uint32_t w, int p) {
+    uint32_t t = w >> (4 * p), r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(r) : "r"(t), "r"(0x000F000Fu), "r"(0x43004300u));
+    return r;
+}
+
+MOEB_DEV float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+MOEB_DEV float act_glu(int act, float g, float u) {
+    if (act == 1) return 0.5f * g * (1.f + tanhf(0.7978845608028654f * (g + 0.044715f * g * g * g))) * u;
+    if (act == 2) {
+        g = fminf(g, 7.0f);
+        u = fminf(fmaxf(u, -7.0f), 7.0f);
+        return g / (1.f + expf(-1.702f * g)) * (u + 1.f);
+    }
+    return g / (1.f + expf(-g)) * u;
+}
+
+}  // namespace moeb

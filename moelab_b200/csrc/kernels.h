@@ -1,0 +1,87 @@
+// Internal kernel argument blocks and declarations (not part of the C ABI).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace moeb {
+
+struct RouterArgs {
+    const uint16_t *x;     // [T][d] bf16
+    const uint16_t *wg;    // [E][d] bf16 gate
+    const uint16_t *bias;  // [E] bf16 or null
+    int T, d, E, k, norm;
+    float scale;
+    float *logits;  // [T][E] fp32 (workspace or caller buffer)
+    int *idx;       // [T][k]
+    float *wts;     // [T][k]
+    float *xsum;    // [T][d/64] or null
+    unsigned *cnt;      // [ceil(T/TPB)] zero-initialised, self-resetting
+    unsigned *cnt_all;  // [1] zero-initialised, self-resetting
+    // tile mode (null tiles = slot mode)
+    int NT;
+    int4 *tiles;
+    int *ntiles;
+    int *sorted;
+    unsigned *err;
+};
+
+struct PrepArgs {
+    const uint16_t *x;
+    const int *idx;
+    int T, d, E, k;
+    float *xsum;
+    unsigned *cnt_all;
+    int NT;
+    int4 *tiles;
+    int *ntiles;
+    int *sorted;
+    unsigned *err;
+};
+
+// Expert weights of one projection in the B200 layout.
+struct QProj {
+    const uint32_t *q;   // packed codes [E][N][K/8]
+    const uint32_t *sb;  // int4: scale|bias [E][N][K/64]; mxfp4: e8m0 bytes [E][N][K/32]
+};
+
+struct ExpArgs {
+    const uint16_t *x;  // [T][d] bf16
+    const float *xsum;  // [T][d/64]
+    QProj g, u, dn;
+    const float *bg, *bu, *bd;  // optional expert biases [E][f], [E][f], [E][d]
+    const int *idx;             // [T*k]
+    const float *wts;           // [T*k]
+    const int4 *tiles;          // tile mode: (expert, start, n, 0)
+    const int *ntiles;
+    const int *sorted;
+    uint16_t *h;           // [TK][f] bf16
+    float *hsum;           // [TK][f/16] fp32 (sums of 16 consecutive bf16 h values)
+    float *yp;             // [TK][d] fp32 weighted per-slot outputs
+    unsigned *ycnt;        // [T][d/16] zero-initialised, self-resetting
+    const uint16_t *residual;  // optional [T][d]
+    uint16_t *y;               // [T][d] bf16
+    unsigned *err;
+    int T, d, f, E, k, act, tile_mode;
+};
+
+template <int TPB, int JMAX>
+__global__ void k_router(RouterArgs a);
+__global__ void k_prep(PrepArgs a);
+
+__global__ void k_q4_quantize(const uint16_t *w, long rows, long K, uint32_t *qw, uint32_t *sb);
+__global__ void k_q4_dequant(const uint32_t *qw, const uint32_t *sb, long rows, long K, float *out);
+__global__ void k_q4_from_mlx(const uint32_t *wq, const uint16_t *scales, const uint16_t *biases, long rows, long K,
+                              uint32_t *qw, uint32_t *sb);
+__global__ void k_fp4_quantize(const uint16_t *w, long rows, long K, uint32_t *qw, uint8_t *sc);
+__global__ void k_fp4_dequant(const uint32_t *qw, const uint8_t *sc, long rows, long K, float *out);
+__global__ void k_fp4_from_mlx(const uint32_t *wq, const uint8_t *scales, long rows, long K, uint32_t *qw,
+                               uint8_t *sc);
+
+template <int FMT, int NT8, int KS>
+__global__ void k_gate_up(ExpArgs a);
+template <int FMT, int NT8, int KS>
+__global__ void k_down(ExpArgs a);
+
+enum { FMT_Q4 = 0, FMT_FP4 = 1 };
+
+}  // namespace moeb

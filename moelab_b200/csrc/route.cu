@@ -1,0 +1,271 @@
+// Router and routing kernels.
+//
+// k_router: the fused router of the layer call (moelab/e2e.py:51-65 composes gate -> top-k -> experts; the
+// reference's fused tail is moelab/router.py:15-80). One launch does
+//   1. logits[t][e] = x[t] . Wg[e] (+ bias[e]) in fp32, summation order fixed (lane l of a warp takes the
+//      8-element chunks l, l+32, ... with fmaf, then a xor butterfly) so the CPU oracle reproduces the
+//      logits - and hence the expert ids - bit for bit;
+//   2. in the last CTA of each token block (last-arriver counter, no spin): top-k with router.py's rules
+//      (NaN = -inf, ties to the lowest id, fewer than k finite -> lowest unused ids with weight 0), softmax
+//      over the top-k (norm) or full-softmax probabilities (!norm), times the routed scaling factor; plus the
+//      per-64-group sums of x used by the expert kernels' scale/bias promotion;
+//   3. in the last of those (tile mode only): the routing step - per-expert histogram, prefix sum and the
+//      slot permutation grouped by expert, cut into tiles of <= NT slots (replaces the O(TK^2) map kernels
+//      metal_q4_tiles_v2.py:362-373 / metal_mxfp4_moe.py:143-153).
+// k_prep: the same steps 2b-3 for the harness contract run(state, x, idx, wts), where ids come from outside.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace moeb {
+
+// ------------------------------------------------------------------ tile builder (one CTA)
+// Counting sort of the TK slots by expert. Slot order inside an expert follows atomic arrival; this does not
+// change any result (every slot is its own MMA column and the combine sums slots in fixed j order).
+__device__ void build_tiles(const int *__restrict__ idx, int TK, int E, int NT, int4 *__restrict__ tiles,
+                            int *__restrict__ ntiles, int *__restrict__ sorted, unsigned *__restrict__ err) {
+    extern __shared__ int smem[];
+    int *cnt = smem;           // [E]
+    int *off = smem + E;       // [E]
+    int *toff = smem + 2 * E;  // [E]
+    __shared__ int part[1024];
+    const int tid = threadIdx.x, nth = blockDim.x;
+    for (int e = tid; e < E; e += nth) cnt[e] = 0;
+    __syncthreads();
+    bool bad = false;
+    for (int s = tid; s < TK; s += nth) {
+        int e = __ldcg(idx + s);
+        if (e < 0 || e >= E) { bad = true; e = 0; }
+        atomicAdd(&cnt[e], 1);
+    }
+    if (bad) atomicOr(err, ERR_EXPERT_ID);
+    __syncthreads();
+    // exclusive scans of slot counts and tile counts (thread-chunked, then a serial pass over the partials)
+    const int per = (E + nth - 1) / nth;
+    const int e0 = tid * per, e1 = min(E, e0 + per);
+    int sc = 0, st = 0;
+    for (int e = e0; e < e1; ++e) {
+        sc += cnt[e];
+        st += (cnt[e] + NT - 1) / NT;
+    }
+    part[tid] = sc;
+    __syncthreads();
+    if (tid == 0) {
+        int run = 0;
+        for (int i = 0; i < nth; ++i) { int v = part[i]; part[i] = run; run += v; }
+    }
+    __syncthreads();
+    int base_s = part[tid];
+    __syncthreads();
+    part[tid] = st;
+    __syncthreads();
+    if (tid == 0) {
+        int run = 0;
+        for (int i = 0; i < nth; ++i) { int v = part[i]; part[i] = run; run += v; }
+        *ntiles = run;
+    }
+    __syncthreads();
+    int base_t = part[tid];
+    for (int e = e0; e < e1; ++e) {
+        const int c = cnt[e];
+        off[e] = base_s;
+        toff[e] = base_t;
+        const int nt = (c + NT - 1) / NT;
+        for (int i = 0; i < nt; ++i) tiles[base_t + i] = make_int4(e, base_s + i * NT, min(NT, c - i * NT), 0);
+        base_s += c;
+        base_t += nt;
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += nth) cnt[e] = 0;
+    __syncthreads();
+    for (int s = tid; s < TK; s += nth) {
+        int e = __ldcg(idx + s);
+        if (e < 0 || e >= E) e = 0;
+        const int pos = atomicAdd(&cnt[e], 1);
+        sorted[off[e] + pos] = s;
+    }
+}
+
+// per-64-group sums of one token row (fp32); warp-cooperative
+__device__ __forceinline__ void row_group_sums(const uint16_t *__restrict__ xr, int d, float *__restrict__ out,
+                                               int lane) {
+    for (int g = lane; g < d / 64; g += 32) {
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint4 u = *reinterpret_cast<const uint4 *>(xr + g * 64 + 8 * i);
+            s += bf16lo(u.x) + bf16hi(u.x) + bf16lo(u.y) + bf16hi(u.y) + bf16lo(u.z) + bf16hi(u.z) + bf16lo(u.w) +
+                 bf16hi(u.w);
+        }
+        out[g] = s;
+    }
+}
+
+template <int JMAX>
+__device__ void topk_token(const RouterArgs &a, int t, int lane) {
+    const int E = a.E, k = a.k;
+    float v[JMAX];
+    float m0 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < JMAX; ++j) {
+        const int e = j * 32 + lane;
+        float l = e < E ? __ldcg(a.logits + (size_t)t * E + e) : -INFINITY;
+        v[j] = isnan(l) ? -INFINITY : l;
+        m0 = fmaxf(m0, v[j]);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+    float den = 0.f;
+    if (!a.norm) {
+#pragma unroll
+        for (int j = 0; j < JMAX; ++j) den += v[j] == -INFINITY ? 0.f : expf(v[j] - m0);
+        den = warp_sum(den);
+    }
+    float myv = -INFINITY, top0 = -INFINITY;
+    int myi = 0;
+    for (int r = 0; r < k; ++r) {
+        float b = -INFINITY;
+        unsigned bi = 0xffffffffu;
+#pragma unroll
+        for (int j = 0; j < JMAX; ++j)
+            if (v[j] > b) { b = v[j]; bi = (unsigned)(j * 32 + lane); }
+        float m = b;
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        unsigned sel = __reduce_min_sync(0xffffffffu, b == m ? bi : 0xffffffffu);
+        if (sel == 0xffffffffu) {  // fewer than k values above -inf: lowest unused id, weight 0
+            unsigned cand = 0;
+            while (__any_sync(0xffffffffu, lane < r && (unsigned)myi == cand)) ++cand;
+            sel = cand;
+            m = -INFINITY;
+        } else if ((int)(sel & 31u) == lane) {
+#pragma unroll
+            for (int j = 0; j < JMAX; ++j)
+                if (j == (int)(sel >> 5)) v[j] = -INFINITY;
+        }
+        if (lane == r) { myv = m; myi = (int)sel; }
+        if (r == 0) top0 = m;
+    }
+    float s = 0.f;
+    if (a.norm) {
+        for (int r = 0; r < k; ++r) s += expf(__shfl_sync(0xffffffffu, myv, r) - top0);
+    } else {
+        s = den;
+    }
+    const float off = a.norm ? top0 : m0;
+    if (lane < k) {
+        a.idx[(size_t)t * k + lane] = myi;
+        a.wts[(size_t)t * k + lane] = expf(myv - off) / s * a.scale;
+    }
+}
+
+// grid (ceil(E / 4), ceil(T / TPB)), block 128: warp w computes expert blockIdx.x * 4 + w for TPB tokens.
+template <int TPB, int JMAX>
+__global__ void __launch_bounds__(128) k_router(RouterArgs a) {
+    pdl_launch();
+    pdl_wait();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int e = blockIdx.x * 4 + warp;
+    const int t0 = blockIdx.y * TPB;
+    const int nt = min(TPB, a.T - t0);
+    const int nch = a.d / 8;
+    if (e < a.E) {
+        float acc[TPB];
+#pragma unroll
+        for (int i = 0; i < TPB; ++i) acc[i] = 0.f;
+        const uint16_t *wr = a.wg + (size_t)e * a.d;
+        for (int c = lane; c < nch; c += 32) {
+            const uint4 w = *reinterpret_cast<const uint4 *>(wr + 8 * c);
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int i = 0; i < TPB; ++i) {
+                if (i < nt) {
+                    const uint4 xv = *reinterpret_cast<const uint4 *>(a.x + (size_t)(t0 + i) * a.d + 8 * c);
+                    const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
+                    float s = acc[i];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        s = __fmaf_rn(bf16lo(xx[j]), bf16lo(ww[j]), s);
+                        s = __fmaf_rn(bf16hi(xx[j]), bf16hi(ww[j]), s);
+                    }
+                    acc[i] = s;
+                }
+            }
+        }
+        const float bias = a.bias ? bf2f(a.bias[e]) : 0.f;
+#pragma unroll
+        for (int i = 0; i < TPB; ++i) {
+            float v = acc[i];
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+            if (a.bias) v = __fadd_rn(v, bias);
+            if (lane == 0 && i < nt) a.logits[(size_t)(t0 + i) * a.E + e] = v;
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ int s_last;
+    if (threadIdx.x == 0) {
+        const unsigned prev = atomicAdd(a.cnt + blockIdx.y, 1u);
+        s_last = prev == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int i = warp; i < nt; i += 4) {
+        topk_token<JMAX>(a, t0 + i, lane);
+        if (a.xsum) row_group_sums(a.x + (size_t)(t0 + i) * a.d, a.d, a.xsum + (size_t)(t0 + i) * (a.d / 64), lane);
+    }
+    if (threadIdx.x == 0) a.cnt[blockIdx.y] = 0;
+    if (a.tiles == nullptr) return;
+    // routing step in the last token block to finish
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned prev = atomicAdd(a.cnt_all, 1u);
+        s_last = prev == gridDim.y - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    build_tiles(a.idx, a.T * a.k, a.E, a.NT, a.tiles, a.ntiles, a.sorted, a.err);
+    if (threadIdx.x == 0) *a.cnt_all = 0;
+}
+
+// Harness path (ids given): grid ceil(T / 8), block 256. Per-token x group sums; tile mode: the last CTA
+// builds the tiles.
+__global__ void __launch_bounds__(256) k_prep(PrepArgs a) {
+    pdl_launch();
+    pdl_wait();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int t = blockIdx.x * 8 + warp;
+    if (t < a.T) row_group_sums(a.x + (size_t)t * a.d, a.d, a.xsum + (size_t)t * (a.d / 64), lane);
+    if (a.tiles == nullptr) {
+        // slot mode: only validate ids
+        for (int s = blockIdx.x * 256 + threadIdx.x; s < a.T * a.k; s += gridDim.x * 256) {
+            const int e = a.idx[s];
+            if (e < 0 || e >= a.E) atomicOr(a.err, ERR_EXPERT_ID);
+        }
+        return;
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ int s_last;
+    if (threadIdx.x == 0) {
+        const unsigned prev = atomicAdd(a.cnt_all, 1u);
+        s_last = prev == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    build_tiles(a.idx, a.T * a.k, a.E, a.NT, a.tiles, a.ntiles, a.sorted, a.err);
+    if (threadIdx.x == 0) *a.cnt_all = 0;
+}
+
+template __global__ void k_router<8, 1>(RouterArgs);
+template __global__ void k_router<8, 2>(RouterArgs);
+template __global__ void k_router<8, 4>(RouterArgs);
+template __global__ void k_router<8, 8>(RouterArgs);
+template __global__ void k_router<8, 16>(RouterArgs);
+template __global__ void k_router<8, 32>(RouterArgs);
+
+}  // namespace moeb

@@ -1,0 +1,199 @@
+"""torch-level wrappers over the C ABI (device tensors in, device tensors out, current stream).
+
+Every function here launches CUDA kernels from libmoelab_b200.so; there is no CPU path. Tensors must be
+CUDA, contiguous, with the dtypes documented in include/moelab_b200.h (packed codes are carried in int32 /
+uint8 tensors).
+"""
+import ctypes
+
+import torch
+
+from . import _lib
+
+POLICY_AUTO, POLICY_SLOTS, POLICY_TILES8, POLICY_TILES16 = (_lib.POLICY_AUTO, _lib.POLICY_SLOTS,
+                                                            _lib.POLICY_TILES8, _lib.POLICY_TILES16)
+
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _need(t, dtype, name):
+    if t is None:
+        return
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (moelab_b200 has no CPU path)")
+    if dtype is not None and t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+class Workspace:
+    """Caller-owned scratch for the layer kernels, grown on demand (allocation happens here, in Python,
+    never inside the library). Zeroed once at allocation; the kernels keep its counters zero."""
+
+    def __init__(self, d, f, E, k, device=None):
+        self.d, self.f, self.E, self.k = d, f, E, k
+        self.device = device
+        self.T = 0
+        self.buf = None
+
+    def get(self, T):
+        if T > self.T:
+            Tn = max(T, 2 * self.T, 16)
+            nbytes = _lib.load().moeb_workspace_bytes(Tn, self.d, self.f, self.E, self.k)
+            self.buf = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+            _lib.call("moeb_workspace_init", _p(self.buf), nbytes, _stream())
+            self.T = Tn
+        return self.buf
+
+    def read_error(self):
+        """Sticky device error bits (MOEB_DEVERR_*); synchronises the current stream and clears them."""
+        if self.buf is None:
+            return 0
+        out = ctypes.c_uint(0)
+        _lib.call("moeb_read_error", _p(self.buf), ctypes.byref(out), _stream())
+        return out.value
+
+
+# ------------------------------------------------------------------ quantizers
+def quantize_q4(w):
+    """bf16 [..., N, K] -> (q int32 [..., N, K/8], sb int32 [..., N, K/64]) in the B200 layout."""
+    _need(w, torch.bfloat16, "w")
+    K = w.shape[-1]
+    rows = w.numel() // K
+    q = torch.empty(*w.shape[:-1], K // 8, dtype=torch.int32, device=w.device)
+    sb = torch.empty(*w.shape[:-1], K // 64, dtype=torch.int32, device=w.device)
+    _lib.call("moeb_quantize_q4", _p(w), rows, K, _p(q), _p(sb), _stream())
+    return q, sb
+
+
+def dequant_q4(q, sb):
+    _need(q, torch.int32, "q")
+    _need(sb, torch.int32, "sb")
+    K = q.shape[-1] * 8
+    rows = q.numel() // q.shape[-1]
+    out = torch.empty(*q.shape[:-1], K, dtype=torch.float32, device=q.device)
+    _lib.call("moeb_dequant_q4", _p(q), _p(sb), rows, K, _p(out), _stream())
+    return out
+
+
+def q4_from_mlx(wq, scales, biases):
+    """mlx affine state (uint32 natural nibble order as int32, bf16 scales, bf16 biases) -> (q, sb)."""
+    _need(wq, torch.int32, "wq")
+    _need(scales, torch.bfloat16, "scales")
+    _need(biases, torch.bfloat16, "biases")
+    K = wq.shape[-1] * 8
+    rows = wq.numel() // wq.shape[-1]
+    q = torch.empty_like(wq)
+    sb = torch.empty(*wq.shape[:-1], K // 64, dtype=torch.int32, device=wq.device)
+    _lib.call("moeb_q4_from_mlx", _p(wq), _p(scales), _p(biases), rows, K, _p(q), _p(sb), _stream())
+    return q, sb
+
+
+def quantize_mxfp4(w):
+    """bf16 [..., N, K] -> (q int32 [..., N, K/8], sc uint8 [..., N, K/32]) in the B200 layout."""
+    _need(w, torch.bfloat16, "w")
+    K = w.shape[-1]
+    rows = w.numel() // K
+    q = torch.empty(*w.shape[:-1], K // 8, dtype=torch.int32, device=w.device)
+    sc = torch.empty(*w.shape[:-1], K // 32, dtype=torch.uint8, device=w.device)
+    _lib.call("moeb_quantize_mxfp4", _p(w), rows, K, _p(q), _p(sc), _stream())
+    return q, sc
+
+
+def dequant_mxfp4(q, sc):
+    _need(q, torch.int32, "q")
+    _need(sc, torch.uint8, "sc")
+    K = q.shape[-1] * 8
+    rows = q.numel() // q.shape[-1]
+    out = torch.empty(*q.shape[:-1], K, dtype=torch.float32, device=q.device)
+    _lib.call("moeb_dequant_mxfp4", _p(q), _p(sc), rows, K, _p(out), _stream())
+    return out
+
+
+def mxfp4_from_mlx(wq, scales):
+    _need(wq, torch.int32, "wq")
+    _need(scales, torch.uint8, "scales")
+    K = wq.shape[-1] * 8
+    rows = wq.numel() // wq.shape[-1]
+    q = torch.empty_like(wq)
+    sc = torch.empty_like(scales)
+    _lib.call("moeb_mxfp4_from_mlx", _p(wq), _p(scales), rows, K, _p(q), _p(sc), _stream())
+    return q, sc
+
+
+# ------------------------------------------------------------------ router
+_ROUTER_WS = {}
+
+
+def router(x, gate_w, k, gate_b=None, norm=True, scale=1.0, return_logits=False):
+    """x bf16 [T, d], gate_w bf16 [E, d], gate_b bf16 [E] -> idx int32 [T, k], wts fp32 [T, k] (+ logits)."""
+    _need(x, torch.bfloat16, "x")
+    _need(gate_w, torch.bfloat16, "gate_w")
+    _need(gate_b, torch.bfloat16, "gate_b")
+    T, d = x.shape
+    E = gate_w.shape[0]
+    idx = torch.empty(T, k, dtype=torch.int32, device=x.device)
+    wts = torch.empty(T, k, dtype=torch.float32, device=x.device)
+    logits = torch.empty(T, E, dtype=torch.float32, device=x.device) if return_logits else None
+    key = (x.device, d, E, k)
+    ws = _ROUTER_WS.get(key)
+    if ws is None:
+        ws = _ROUTER_WS[key] = Workspace(d, 64, E, k, x.device)
+    buf = ws.get(max(T, 1))
+    _lib.call("moeb_router", _p(x), _p(gate_w), _p(gate_b), T, d, E, k, int(bool(norm)), float(scale), _p(idx),
+              _p(wts), _p(logits), _p(buf), buf.numel(), _stream())
+    return (idx, wts, logits) if return_logits else (idx, wts)
+
+
+# ------------------------------------------------------------------ experts / layer (int4)
+def _expert_ptrs(state):
+    (qg, sg), (qu, su), (qd, sd) = state["g"], state["u"], state["d"]
+    return [_p(qg), _p(sg), _p(qu), _p(su), _p(qd), _p(sd), _p(state.get("bg")), _p(state.get("bu")),
+            _p(state.get("bd"))]
+
+
+def experts_q4(state, x, idx, wts, act=0, policy=POLICY_AUTO, residual=None):
+    """y = sum_j wts * expert(x) (+ residual), bf16 [T, d]."""
+    _need(x, torch.bfloat16, "x")
+    _need(idx, torch.int32, "idx")
+    _need(wts, torch.float32, "wts")
+    _need(residual, torch.bfloat16, "residual")
+    T, d = x.shape
+    k = idx.shape[1]
+    E, f = state["E"], state["f"]
+    ws = state["ws"]
+    buf = ws.get(max(T, 1))
+    y = torch.empty_like(x)
+    _lib.call("moeb_experts_q4", _p(x), *_expert_ptrs(state), _p(idx), _p(wts), T, d, f, E, k, int(act),
+              int(policy), _p(residual), _p(y), _p(buf), buf.numel(), _stream())
+    return y
+
+
+def layer_q4(state, x, gate_w, k, gate_b=None, norm=True, rscale=1.0, act=0, policy=POLICY_AUTO, residual=None,
+             return_routing=False):
+    """The layer call (x, gate weights, packed experts, k) -> y: router + routing + experts + combine."""
+    _need(x, torch.bfloat16, "x")
+    _need(gate_w, torch.bfloat16, "gate_w")
+    _need(gate_b, torch.bfloat16, "gate_b")
+    _need(residual, torch.bfloat16, "residual")
+    T, d = x.shape
+    E, f = state["E"], state["f"]
+    buf = state["ws"].get(max(T, 1))
+    y = torch.empty_like(x)
+    idx = torch.empty(T, k, dtype=torch.int32, device=x.device) if return_routing else None
+    wts = torch.empty(T, k, dtype=torch.float32, device=x.device) if return_routing else None
+    _lib.call("moeb_layer_q4", _p(x), _p(gate_w), _p(gate_b), int(bool(norm)), float(rscale), *_expert_ptrs(state),
+              T, d, f, E, k, int(act), int(policy), _p(residual), _p(y), _p(idx), _p(wts), _p(buf), buf.numel(),
+              _stream())
+    return (y, idx, wts) if return_routing else y
+
+
+def policy(T, E, k):
+    return _lib.load().moeb_policy(T, E, k)

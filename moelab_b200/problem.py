@@ -1,0 +1,67 @@
+"""Seeded synthetic MoE problems: the input generator side of moelab/problem.py.
+
+Kernel contract (moelab/problem.py:3-10): y = moe(x, w_gate, w_up, w_down, idx, wts) with
+x [T, d], w_gate/w_up [E, f, d], w_down [E, d, f] (out, in), idx [T, k] int32, wts [T, k] float,
+y[t] = sum_j wts[t,j] * down_e(silu(gate_e x_t) * up_e x_t), e = idx[t,j].
+
+make_routing / make_problem restate moelab/problem.py:15-64 call for call (same numpy Generator draws), so a
+seed gives the reference's own inputs; tests/golden pins that. The "trace" mode (recorded Qwen3 routing,
+problem.py:38-50) needs the reference's runs/ data and is not carried here.
+"""
+import numpy as np
+
+
+def make_routing(T, E, k, mode="uniform", rng=None, zipf_a=1.2):
+    rng = rng or np.random.default_rng(0)
+    if mode == "uniform":
+        logits = rng.standard_normal((T, E))
+    elif mode == "zipf":  # skewed popularity over a seeded expert permutation
+        pop = 1.0 / np.arange(1, E + 1) ** zipf_a
+        logits = rng.standard_normal((T, E)) + np.log(pop)[rng.permutation(E)] * 2.0
+    elif mode == "one_hot":  # every token to the same k experts (worst imbalance)
+        logits = np.tile(np.arange(E, 0, -1, dtype=np.float64), (T, 1))
+    elif mode == "round_robin":  # balanced: token t takes experts (t*k + j) % E
+        idx = ((np.arange(T)[:, None] * k + np.arange(k)[None, :]) % E).astype(np.int32)
+        w = rng.random((T, k)).astype(np.float32)
+        return idx, (w / w.sum(1, keepdims=True)).astype(np.float32)
+    else:
+        raise ValueError(mode)
+    idx = np.argsort(-logits, axis=1)[:, :k].astype(np.int32)
+    top = np.take_along_axis(logits, idx, axis=1)
+    w = np.exp(top - top.max(1, keepdims=True))
+    w = (w / w.sum(1, keepdims=True)).astype(np.float32)
+    return idx, w
+
+
+def make_problem(shape, T, routing="uniform", seed=0):
+    rng = np.random.default_rng(seed)
+    d, f, E, k = shape.d, shape.f, shape.E, shape.k
+    s_in, s_hid = 1.0 / np.sqrt(d), 1.0 / np.sqrt(f)
+    p = {
+        "x": rng.standard_normal((T, d)).astype(np.float32),
+        "w_gate": (rng.standard_normal((E, f, d)) * s_in).astype(np.float32),
+        "w_up": (rng.standard_normal((E, f, d)) * s_in).astype(np.float32),
+        "w_down": (rng.standard_normal((E, d, f)) * s_hid).astype(np.float32),
+    }
+    p["idx"], p["wts"] = make_routing(T, E, k, routing, rng)
+    return p
+
+
+def error_metrics(y, y_ref):
+    """moelab/problem.py:88-98, plus max_rowrel = max |err| / row max |ref|."""
+    y = np.asarray(y, dtype=np.float64)
+    r = np.asarray(y_ref, dtype=np.float64)
+    diff = y - r
+    nr = np.linalg.norm(r) + 1e-30
+    rowmax = np.abs(r).max(axis=-1, keepdims=True) + 1e-30
+    return {
+        "rel_fro": float(np.linalg.norm(diff) / nr),
+        "max_abs": float(np.abs(diff).max()) if diff.size else 0.0,
+        "max_rowrel": float((np.abs(diff) / rowmax).max()) if diff.size else 0.0,
+        "cos": float((y * r).sum() / (np.linalg.norm(y) * nr + 1e-30)),
+        "finite": bool(np.isfinite(y).all()),
+    }
+
+
+TOLERANCE = {"float32": 1e-4, "float16": 3e-3, "bfloat16": 2e-2, "q8": 2e-2, "q4": 2e-2}
+ROWREL_TOL = 1e-2  # north star: max |err| <= 1e-2 * row max |ref| for bf16 activations

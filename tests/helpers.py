@@ -1,0 +1,67 @@
+"""Shared test helpers: layout conversion for bit-exact checks, oracle references, error bounds."""
+import os
+
+import numpy as np
+import torch
+
+import oracle
+from moelab_b200.problem import ROWREL_TOL, make_problem
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+Q4_VARIANT = os.path.join(ROOT, "moelab_b200", "variants", "cuda", "b200_q4_moe.py")
+TOL_BF16 = 1e-2  # rel_fro bound used by the reference's bf16 tests (mlx_backend.py:163); outputs also <= ROWREL_TOL
+
+
+def interleave_words(nat):
+    """natural nibble order (element i at nibble i) -> B200 order (pairs (2p, 2p+1) at nibbles p, p+4)."""
+    nat = np.asarray(nat, np.uint32)
+    out = np.zeros_like(nat)
+    for p in range(4):
+        out |= ((nat >> (8 * p)) & 0xF) << (4 * p)
+        out |= ((nat >> (8 * p + 4)) & 0xF) << (4 * (p + 4))
+    return out
+
+
+def deinterleave_words(w):
+    w = np.asarray(w, np.uint32)
+    out = np.zeros_like(w)
+    for p in range(4):
+        out |= ((w >> (4 * p)) & 0xF) << (8 * p)
+        out |= ((w >> (4 * (p + 4))) & 0xF) << (8 * p + 4)
+    return out
+
+
+def u32(t):
+    return t.detach().cpu().numpy().view(np.uint32)
+
+
+def load_variant(path):
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(f"variant_{abs(hash(path))}", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def problem_tensors(shape, T, routing="uniform", seed=0, dtype=torch.bfloat16, device="cuda"):
+    p = make_problem(shape, T, routing, seed)
+    w = [torch.from_numpy(p[n]).to(device, dtype) for n in ("w_gate", "w_up", "w_down")]
+    x = torch.from_numpy(p["x"]).to(device, dtype)
+    return p, w, x, torch.from_numpy(p["idx"]).to(device), torch.from_numpy(p["wts"]).to(device)
+
+
+def ref_from_state(mod, st, x, idx, wts, act=0, bg=None, bu=None, bd=None):
+    """fp64-accumulated oracle output on the variant's own dequantised weights (fp32)."""
+    wg, wu, wd = (t.cpu().numpy() for t in mod.dequant(st))
+    xx = x.float().cpu().numpy()
+    f = lambda t: None if t is None else t.float().cpu().numpy()  # noqa: E731
+    return oracle.moe_forward(xx, wg, wu, wd, idx.cpu().numpy(), wts.float().cpu().numpy(), act=act, bg=f(bg),
+                              bu=f(bu), bd=f(bd))
+
+
+def assert_close(y, ref, tol=TOL_BF16, rowrel=ROWREL_TOL, what=""):
+    e = oracle.error_metrics(y.float().cpu().numpy(), ref)
+    assert e["finite"], (what, e)
+    assert e["rel_fro"] < tol, (what, e)
+    assert e["max_rowrel"] <= rowrel, (what, e)
+    return e

@@ -1,0 +1,52 @@
+"""The C-ABI library loads and exports every symbol include/*.h declares; host-only entry points work without
+a GPU (no compute calls here)."""
+import glob
+import os
+import re
+
+import pytest
+
+from moelab_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        src = re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S)
+        names |= set(re.findall(r"\b(moeb_\w+)\s*\(", src))
+    return names
+
+
+def test_header_matches_binding_table():
+    assert declared_functions() == set(_lib.SIGNATURES), declared_functions() ^ set(_lib.SIGNATURES)
+
+
+def test_library_exports_every_symbol():
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+
+
+def test_host_only_calls():
+    lib = _lib.load()
+    assert lib.moeb_version() == 1
+    # workspace size grows with T and covers h / per-slot partials
+    a = lib.moeb_workspace_bytes(1, 2048, 768, 128, 8)
+    b = lib.moeb_workspace_bytes(256, 2048, 768, 128, 8)
+    assert 0 < a < b
+    assert b >= 256 * 8 * (768 * 2 + 2048 * 4)
+    # dispatcher: decode -> per-slot tiles; high load -> grouped tiles
+    assert lib.moeb_policy(1, 128, 8) == _lib.POLICY_SLOTS
+    assert lib.moeb_policy(4, 128, 8) == _lib.POLICY_SLOTS
+    assert lib.moeb_policy(256, 128, 8) in (_lib.POLICY_TILES8, _lib.POLICY_TILES16)
+    assert lib.moeb_policy(4096, 8, 2) == _lib.POLICY_TILES16
+
+
+def test_bad_shape_is_rejected_before_any_device_work():
+    # idx / wts are non-null dummies: the shape check runs before anything is dereferenced
+    with pytest.raises(_lib.MoebError, match="multiples of 64"):
+        _lib.call("moeb_experts_q4", *([None] * 10), 8, 8, 4, 100, 256, 8, 2, 0, 0, None, None, None, 0, None)
+    with pytest.raises(_lib.MoebError, match="k must be"):
+        _lib.call("moeb_experts_q4", *([None] * 10), 8, 8, 4, 128, 256, 8, 9, 0, 0, None, None, None, 0, None)
