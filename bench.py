@@ -1,0 +1,413 @@
+#!/usr/bin/env python
+"""Benchmark of the quantized MoE-layer forward (moe-lab's hot path) on B200.
+
+Workload: Qwen3-30B-A3B-shaped int4-g64 MoE layer, d=2048, f=768, E=128, k=8,
+weights N(0, 0.02) bf16 quantised to int4 affine g64 (bf16 scale/bias), gate N(0, 0.02), x ~ N(0, 1) bf16,
+routing from the gate (softmax, top-8, renormalised). One step = one layer call (router + routing + grouped
+experts + weighted combine, residual fused) on T tokens per GPU. 16 independent seeded layers are cycled so
+the weights streamed between steps (16 x 340 MB) are far larger than the 126 MB L2.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl reference]
+
+Prints one JSON line (rank 0). value = whole-job tokens/s; the T sweep, per-kernel times and the roofline
+fraction explain it. --impl reference times the reference's CPU torch path (the oracle's port of
+moelab/variants/cuda/torch_loop.py plus the stock torch router) on the same config with all host threads.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+D, F, E, K_TOP = 2048, 768, 128, 8
+W_BITS = 4.5
+WORKLOAD = "qwen3-30b-a3b int4-g64 MoE layer: router + routing + grouped experts + combine (residual fused)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2048)
+    ap.add_argument("--warmup", type=int, default=32)
+    ap.add_argument("--tokens", type=int, default=32)
+    ap.add_argument("--layers", type=int, default=16)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--sweep", default="1,4,32,256", help="extra T values measured after the headline ('' = none)")
+    ap.add_argument("--e2e-steps", type=int, default=256)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bound on the CPU baseline sample")
+    ap.add_argument("--soak-seconds", type=float, default=1.5, help="replays before the timed region (clocks)")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ distributed plumbing
+def dist_init(a):
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(ws, v):
+    if ws == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------ clocks
+CLOCK_Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+           "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+           "clocks_event_reasons.sw_power_cap")
+
+
+class ClockSampler:
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_bench_gpu{gpu_index}.csv")
+
+    def start(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={CLOCK_Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        rows = []
+        for line in open(self.path):
+            p = [x.strip() for x in line.split(",")]
+            if len(p) >= 9:
+                rows.append(p)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows)}
+
+
+# ------------------------------------------------------------------ workload
+def make_layers(n_layers, seed, device):
+    from moelab_b200.variants.cuda import b200_q4_moe as v
+    g = torch.Generator(device=device).manual_seed(seed)
+    layers = []
+    for _ in range(n_layers):
+        mk = lambda *s: (torch.randn(*s, generator=g, device=device) * 0.02).to(torch.bfloat16)  # noqa: E731
+        w = [mk(E, F, D), mk(E, F, D), mk(E, D, F)]
+        st = v.prepare(*w)
+        del w
+        layers.append((st, mk(E, D)))
+    torch.cuda.synchronize()
+    return v, layers
+
+
+def layer_bytes(idx_list, T):
+    """Algorithmic bytes of one layer call (moelab/roofline.py:29-33 with the actual unique experts U, plus the
+    router's gate read): U*3*d*f*w_bits/8 + 2*T*d*2 + 2*T*k*f*2 + E*d*2."""
+    out = []
+    for idx in idx_list:
+        U = int(torch.unique(idx).numel())
+        out.append(U * 3 * D * F * W_BITS / 8 + 2 * T * D * 2 + 2 * T * K_TOP * F * 2 + E * D * 2)
+    return out
+
+
+def gate_up_bytes(idx, T):
+    U = int(torch.unique(idx).numel())
+    return U * 2 * D * F * W_BITS / 8 + T * D * 2 + T * K_TOP * F * 2
+
+
+def down_bytes(idx, T):
+    U = int(torch.unique(idx).numel())
+    return U * D * F * W_BITS / 8 + T * K_TOP * F * 2 + T * D * 2 * 2
+
+
+def capture(v, layers, x0, n_steps, k0=0):
+    """CUDA graph of n_steps layer calls x <- layer_i(x) + x cycling through the layers."""
+    L = len(layers)
+
+    def chain():
+        x = x0
+        for i in range(n_steps):
+            st, gate = layers[(k0 + i) % L]
+            x = v.layer(st, x, gate, K_TOP, residual=x)
+        return x
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        chain()
+    torch.cuda.current_stream().wait_stream(s)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        out = chain()
+    return gr, out
+
+
+def time_graph(gr, ws, reps=1):
+    barrier(ws)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        gr.replay()
+    b.record()
+    b.synchronize()
+    torch.cuda.synchronize()
+    barrier(ws)
+    return a.elapsed_time(b) / 1e3
+
+
+def routing_of_chain(v, layers, x0, n_steps, k0=0):
+    idxs = []
+    x = x0
+    for i in range(n_steps):
+        st, gate = layers[(k0 + i) % len(layers)]
+        y, idx, _ = v.layer(st, x, gate, K_TOP, residual=x, return_routing=True)
+        idxs.append(idx)
+        x = y
+    return idxs
+
+
+def stage_times(v, layers, x0, n_steps):
+    """Per-kernel durations from CUDA events recorded between the stages (router, gate/up, down)."""
+    x = x0
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n_steps)]
+    idxs = []
+    for i in range(n_steps):
+        st, gate = layers[i % len(layers)]
+        y, idx, _ = v.layer(st, x, gate, K_TOP, residual=x, return_routing=True, stage_events=ev[i])
+        idxs.append(idx)
+        x = y
+    torch.cuda.synchronize()
+    r = [ev[i][0].elapsed_time(ev[i][1]) * 1e3 for i in range(n_steps)]
+    gu = [ev[i][1].elapsed_time(ev[i][2]) * 1e3 for i in range(n_steps)]
+    dn = [ev[i][2].elapsed_time(ev[i][3]) * 1e3 for i in range(n_steps)]
+    return r, gu, dn, idxs
+
+
+def measure_T(v, layers, T, ws, rank, n_steps, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x0 = torch.randn(T, D, generator=g, device="cuda").to(torch.bfloat16)
+    gr, _ = capture(v, layers, x0, n_steps)
+    gr.replay()
+    torch.cuda.synchronize()
+    t = max_over_ranks(ws, time_graph(gr, ws))
+    idxs = routing_of_chain(v, layers, x0, n_steps)
+    nb = layer_bytes(idxs, T)
+    us = t / n_steps * 1e6
+    return {"T": T, "us_per_call": round(us, 3), "gbs": round(sum(nb) / t / 1e9, 1),
+            "unique_experts": round(float(np.mean([torch.unique(i).numel() for i in idxs])), 2),
+            "tokens_per_s": round(T * n_steps / t, 1)}
+
+
+# ------------------------------------------------------------------ CPU baseline (reference's CPU torch path)
+def cpu_layer(seed=0):
+    """One Qwen3-30B-shaped layer on the CPU: int4-g64 quantised by the oracle, dequantised to bf16 (the weights
+    the reference's torch path multiplies)."""
+    import oracle
+    g = torch.Generator().manual_seed(seed)
+    mk = lambda *s: (torch.randn(*s, generator=g) * 0.02).to(torch.bfloat16)  # noqa: E731
+    dq = []
+    for shape in ((E, F, D), (E, F, D), (E, D, F)):
+        q, s, b = oracle.q4_quantize(mk(*shape))
+        dq.append(torch.from_numpy(oracle.q4_dequant(q, s, b)).to(torch.bfloat16))
+    return {"wg": dq[0], "wu": dq[1], "wd": dq[2]}, mk(E, D)
+
+
+def cpu_step(s, gate, x):
+    import oracle
+    idx, wts = oracle.torch_router_stock(x, gate, K_TOP)
+    return oracle.torch_loop_run(s, x, idx, wts) + x
+
+
+def cpu_baseline(T, seconds, warmup=1, steps=None):
+    torch.set_num_threads(os.cpu_count() or 1)
+    s, gate = cpu_layer()
+    x = torch.randn(T, D, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+    for _ in range(warmup):
+        x = cpu_step(s, gate, x)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        x = cpu_step(s, gate, x)
+        n += 1
+        el = time.perf_counter() - t0
+        if (steps is not None and (n >= steps or el >= 120.0)) or (steps is None and (el >= seconds or n >= 10000)):
+            break  # the reference arm stops at K steps or 120 s of timed work, whichever comes first
+    return T * n / el, n, el
+
+
+# ------------------------------------------------------------------ main
+def run_reference(a, ws, rank):
+    if rank != 0:
+        return
+    val, n, el = cpu_baseline(a.tokens, a.cpu_seconds, warmup=a.warmup, steps=a.steps)
+    cores = torch.get_num_threads()
+    line = {"metric": "MoE-layer tokens/s", "value": round(val, 2), "unit": "tokens/s", "n_gpus": a.gpus,
+            "steps": n, "warmup": a.warmup, "ms_per_step": round(el / n * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": WORKLOAD, "tokens_per_step": a.tokens, "d": D, "f": F, "E": E, "k": K_TOP,
+                       "layers": 1, "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(val, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": f"{n} layer calls of T={a.tokens} tokens (router + torch_loop) on one "
+                                       f"dequantised layer, {el:.1f} s"},
+            "e2e": {"value": round(val, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    a = parse()
+    ws, rank, local = dist_init(a)
+    if a.impl == "reference":
+        run_reference(a, ws, rank)
+        return
+    from moelab_b200 import roofline
+    peaks = roofline.b200_peaks()
+    T = a.tokens
+    v, layers = make_layers(a.layers, seed=1000 + 7919 * rank, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(5 + rank)
+    x0 = torch.randn(T, D, generator=g, device="cuda").to(torch.bfloat16)
+    # warm-up: W untimed eager steps
+    x = x0
+    for i in range(a.warmup):
+        st, gate = layers[i % len(layers)]
+        x = v.layer(st, x, gate, K_TOP, residual=x)
+    torch.cuda.synchronize()
+    # headline: one CUDA graph of exactly K steps
+    gr, _ = capture(v, layers, x0, a.steps)
+    gr.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    t_soak = time.perf_counter()
+    while time.perf_counter() - t_soak < a.soak_seconds:
+        gr.replay()
+        torch.cuda.synchronize()
+    t = time_graph(gr, ws)
+    ck = clocks.stop()
+    t = max_over_ranks(ws, t)
+    value = ws * T * a.steps / t
+    # per-kernel times and roofline of the dominant kernel (gate/up)
+    n_stage = min(4 * a.layers, a.steps)
+    r_us, gu_us, dn_us, idxs = stage_times(v, layers, x0, n_stage)
+    gu_b = [gate_up_bytes(i, T) for i in idxs]
+    dn_b = [down_bytes(i, T) for i in idxs]
+    gu_ach = sum(gu_b) / (sum(gu_us) * 1e-6) / 1e9
+    dn_ach = sum(dn_b) / (sum(dn_us) * 1e-6) / 1e9
+    lay_b = layer_bytes(idxs, T)
+    lay_ach = sum(lay_b) / (t / a.steps * n_stage) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic_gate_up.json")
+    if os.path.exists(tp):
+        try:
+            traffic = json.load(open(tp)).get(str(T))
+        except (OSError, ValueError):
+            traffic = None
+    sweep = []
+    for Ts in [int(s) for s in a.sweep.split(",") if s.strip()]:
+        sweep.append(measure_T(v, layers, Ts, ws, rank, 2 * a.layers if Ts >= 256 else 4 * a.layers, 77 + Ts))
+    for s_ in sweep:
+        s_["frac_of_hbm_peak"] = round(s_["gbs"] / peaks["hbm_gbs"], 3)
+    # end to end through the public API with host buffers
+    xh = torch.randn(T, D, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16).pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+    for i in range(8):
+        xd = xh.to("cuda", non_blocking=True)
+        st, gate = layers[i % len(layers)]
+        yh.copy_(v.layer(st, xd, gate, K_TOP, residual=xd), non_blocking=True)
+    torch.cuda.synchronize()
+    barrier(ws)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(a.e2e_steps):
+        xd = xh.to("cuda", non_blocking=True)
+        st, gate = layers[i % len(layers)]
+        yh.copy_(v.layer(st, xd, gate, K_TOP, residual=xd), non_blocking=True)
+    e1.record()
+    e1.synchronize()
+    torch.cuda.synchronize()
+    te = max_over_ranks(ws, e0.elapsed_time(e1) / 1e3)
+    e2e = {"value": round(ws * T * a.e2e_steps / te, 1), "unit": "tokens/s", "h2d_bytes_per_step": T * D * 2,
+           "d2h_bytes_per_step": T * D * 2, "us_per_call": round(te / a.e2e_steps * 1e6, 3),
+           "note": "public API v.layer(); pinned host x copied in and y copied out every step, no graph"}
+    cpu = None
+    if rank == 0 and ws == 1:
+        val, n, el = cpu_baseline(T, a.cpu_seconds)
+        cpu = {"value": round(val, 2), "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"{n} layer calls of T={T} tokens (torch router + port of torch_loop.run) on one "
+                         f"dequantised layer, {el:.1f} s"}
+    if rank != 0:
+        return
+    line = {
+        "metric": "MoE-layer tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": ws,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(t / a.steps * 1e3, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) tokens)",
+        "config": {"workload": WORKLOAD, "tokens_per_gpu": T, "d": D, "f": F, "E": E, "k": K_TOP,
+                   "layers": a.layers, "weights_gb_per_gpu": round(a.layers * 3 * E * D * F * W_BITS / 8 / 1e9, 2),
+                   "l2": "inputs larger than L2: 16 independent layers cycled (5.4 GB of expert weights)",
+                   "parallelism": "single" if ws == 1 else f"replicas{ws}", "graph": "one CUDA graph of K steps"},
+        "us_per_call": round(t / a.steps * 1e6, 3),
+        "layer_gbs": round(lay_ach, 1), "layer_frac_of_hbm_peak": round(lay_ach / peaks["hbm_gbs"], 3),
+        "sweep": sweep,
+        "kernels_us": {"router": round(statistics.mean(r_us), 3), "gate_up": round(statistics.mean(gu_us), 3),
+                       "down": round(statistics.mean(dn_us), 3),
+                       "note": "CUDA events between stages (serialised, eager)"},
+        "roofline": {"bound": "hbm", "kernel": "k_gate_up", "achieved": round(gu_ach, 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(gu_ach / peaks["hbm_gbs"], 3), "traffic": traffic,
+                     "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)" if peaks["source"] == "measured"
+                     else "fallback 6650 GB/s",
+                     "algorithmic_bytes_per_launch": round(statistics.mean(gu_b)),
+                     "down_achieved_gbs": round(dn_ach, 1)},
+        "cpu_baseline": cpu, "e2e": e2e, "clocks": ck,
+        "gpu_launches": 3 * a.steps,
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    try:
+        main()
+    finally:
+        if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+            import torch.distributed as dist
+            if dist.is_initialized():
+                dist.destroy_process_group()

@@ -95,14 +95,15 @@ int moeb_experts_q4(const void *x, const void *qg, const void *sbg, const void *
                     const void *residual, void *y, void *ws, size_t ws_bytes, cudaStream_t stream);
 
 /* --- full layer call (x, gate weights, packed expert weights + scales + biases, k) -> y: router, routing
- * step, grouped experts and the weighted combine in one stream-ordered sequence (3-4 launches).
+ * step, grouped experts and the weighted combine in one stream-ordered sequence (3 launches).
  * Replaces the patched MoE block call of moelab/e2e.py:51-69 (router + mod.run). idx_out / wts_out may be
- * NULL (then they live in the workspace). */
+ * NULL (then they live in the workspace). stage_events: NULL, or 4 cudaEvent_t recorded before the router,
+ * after the router, after gate/up and after down (per-kernel timing; recording them serialises the stages). */
 int moeb_layer_q4(const void *x, const void *gate_w, const void *gate_b, int norm, float rscale, const void *qg,
                   const void *sbg, const void *qu, const void *sbu, const void *qd, const void *sbd,
                   const float *bg, const float *bu, const float *bd, int T, int d, int f, int E, int k, int act,
-                  int policy, const void *residual, void *y, int *idx_out, float *wts_out, void *ws,
-                  size_t ws_bytes, cudaStream_t stream);
+                  int policy, const void *residual, void *y, int *idx_out, float *wts_out,
+                  void *const *stage_events, void *ws, size_t ws_bytes, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

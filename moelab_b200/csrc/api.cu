@@ -92,7 +92,7 @@ Layout layout(long Tc, int d, int f, int E, int k) {
     size_t o = 0;
     L.err = o; o += 256;
     L.cnt_all = o; o += 256;
-    L.rcnt = o; o = align256(o + 4 * (size_t)((Tc + 7) / 8));
+    L.rcnt = o; o = align256(o + 4 * (size_t)Tc);  // one counter per router token block (>= 1 token each)
     L.ycnt = o; o = align256(o + 4 * (size_t)Tc * (d / 16));
     L.zero_end = o;
     L.logits = o; o = align256(o + 4 * (size_t)Tc * E);
@@ -146,19 +146,20 @@ int nt_of(int policy) { return policy == MOEB_POLICY_TILES16 ? 16 : 8; }
 struct ExpLaunch {
     void (*gu)(ExpArgs);
     void (*dn)(ExpArgs);
-    int threads;
+    int gu_threads, dn_threads;
 };
 
 ExpLaunch pick_kernels(int fmt, int policy) {
     const bool wide = policy == MOEB_POLICY_TILES16;
     if (fmt == FMT_Q4) {
-        if (wide) return {k_gate_up<FMT_Q4, 2, 4>, k_down<FMT_Q4, 2, 4>, 128};
-        return {k_gate_up<FMT_Q4, 1, 4>, k_down<FMT_Q4, 1, 4>, 128};
+        if (wide) return {k_gate_up<FMT_Q4, 2, 8, 2>, k_down<FMT_Q4, 2, 4, 2>, 256, 128};
+        return {k_gate_up<FMT_Q4, 1, 8, 4>, k_down<FMT_Q4, 1, 4, 4>, 256, 128};
     }
-    return {nullptr, nullptr, 0};
+    return {nullptr, nullptr, 0, 0};
 }
 
-int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaStream_t st) {
+int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaStream_t st,
+                void *const *ev) {
     const long TK = (long)a.T * a.k;
     const int nt = nt_of(policy);
     const long max_tiles = a.tile_mode ? std::min<long>(TK, (long)a.E + TK / nt) : TK;
@@ -167,16 +168,18 @@ int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaS
     const int nsm = sm_count();
     {
         const long units = max_tiles * (a.f / 16);
-        const long cap = (long)occupancy((const void *)K.gu, K.threads, 0) * nsm;
+        const long cap = (long)occupancy((const void *)K.gu, K.gu_threads, 0) * nsm;
         const int grid = (int)std::max<long>(1, std::min(units, cap));
-        if (launch(K.gu, dim3(grid), dim3(K.threads), 0, st, a) != cudaSuccess) return check_launch("gate_up");
+        if (launch(K.gu, dim3(grid), dim3(K.gu_threads), 0, st, a) != cudaSuccess) return check_launch("gate_up");
     }
+    if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[2]), st);
     {
         const long units = max_tiles * (a.d / 16);
-        const long cap = (long)occupancy((const void *)K.dn, K.threads, 0) * nsm;
+        const long cap = (long)occupancy((const void *)K.dn, K.dn_threads, 0) * nsm;
         const int grid = (int)std::max<long>(1, std::min(units, cap));
-        if (launch(K.dn, dim3(grid), dim3(K.threads), 0, st, a) != cudaSuccess) return check_launch("down");
+        if (launch(K.dn, dim3(grid), dim3(K.dn_threads), 0, st, a) != cudaSuccess) return check_launch("down");
     }
+    if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[3]), st);
     (void)L;
     (void)ws;
     return MOEB_OK;
@@ -214,7 +217,10 @@ int launch_router(const void *x, const void *wg, const void *bias, int T, int d,
     r.ntiles = at<int>(ws, L.ntiles);
     r.sorted = at<int>(ws, L.sorted);
     const size_t smem = tiles ? 12 * (size_t)E : 0;
-    if (launch(router_kernel<8>(E), dim3((E + 3) / 4, (T + 7) / 8), dim3(128), smem, st, r) != cudaSuccess)
+    // tokens per CTA: 1 for decode-sized T (more CTAs in flight), 4 above
+    const int tpb = T <= 8 ? 1 : 4;
+    void (*kern)(RouterArgs) = tpb == 1 ? router_kernel<1>(E) : router_kernel<4>(E);
+    if (launch(kern, dim3((E + 3) / 4, (T + tpb - 1) / tpb), dim3(128), smem, st, r) != cudaSuccess)
         return check_launch("router");
     return MOEB_OK;
 }
@@ -325,7 +331,7 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
                           const int *idx, const float *wts, int T, int d, int f, int E, int k, int act, int policy,
                           const void *residual, void *y, void *ws, size_t ws_bytes, cudaStream_t st,
                           const void *gate_w, const void *gate_b, int norm, float rscale, int *idx_out,
-                          float *wts_out) {
+                          float *wts_out, void *const *ev) {
     int rc = check_shape(T, d, f, E, k);
     if (rc) return rc;
     if (act < 0 || act > 2) return fail(MOEB_EINVAL, "act must be 0, 1 or 2%s");
@@ -337,6 +343,7 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
     if (policy != MOEB_POLICY_SLOTS && policy != MOEB_POLICY_TILES8 && policy != MOEB_POLICY_TILES16)
         return fail(MOEB_EINVAL, "unknown policy%s");
     const bool tiles = policy != MOEB_POLICY_SLOTS;
+    if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[0]), st);
     if (gate_w) {  // layer call: router produces ids, weights, x group sums and (tile mode) the tiles
         int *ri = idx_out ? idx_out : at<int>(ws, L.idx);
         float *rw = wts_out ? wts_out : at<float>(ws, L.wts);
@@ -359,6 +366,7 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
         const size_t smem = tiles ? 12 * (size_t)E : 0;
         if (launch(k_prep, dim3((T + 7) / 8), dim3(256), smem, st, p) != cudaSuccess) return check_launch("prep");
     }
+    if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[1]), st);
     ExpArgs a = {};
     a.x = static_cast<const uint16_t *>(x);
     a.xsum = at<float>(ws, L.xsum);
@@ -380,7 +388,9 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
     a.y = static_cast<uint16_t *>(y);
     a.err = at<unsigned>(ws, L.err);
     a.T = T; a.d = d; a.f = f; a.E = E; a.k = k; a.act = act; a.tile_mode = tiles ? 1 : 0;
-    return run_experts(fmt, a, policy, L, ws, st);
+    // down weights are prefetched into L2 while gate/up runs when they are a small share of L2
+    a.dn_prefetch = (long)T * k <= 4L * E ? 1 : 0;
+    return run_experts(fmt, a, policy, L, ws, st, ev);
 }
 
 int moeb_experts_q4(const void *x, const void *qg, const void *sbg, const void *qu, const void *sbu, const void *qd,
@@ -389,17 +399,18 @@ int moeb_experts_q4(const void *x, const void *qg, const void *sbg, const void *
                     void *y, void *ws, size_t ws_bytes, cudaStream_t st) {
     if (!idx || !wts) return fail(MOEB_EINVAL, "idx and wts are required%s");
     return experts_common(FMT_Q4, x, qg, sbg, qu, sbu, qd, sbd, bg, bu, bd, idx, wts, T, d, f, E, k, act, policy,
-                          residual, y, ws, ws_bytes, st, nullptr, nullptr, 0, 1.f, nullptr, nullptr);
+                          residual, y, ws, ws_bytes, st, nullptr, nullptr, 0, 1.f, nullptr, nullptr, nullptr);
 }
 
 int moeb_layer_q4(const void *x, const void *gate_w, const void *gate_b, int norm, float rscale, const void *qg,
                   const void *sbg, const void *qu, const void *sbu, const void *qd, const void *sbd, const float *bg,
                   const float *bu, const float *bd, int T, int d, int f, int E, int k, int act, int policy,
-                  const void *residual, void *y, int *idx_out, float *wts_out, void *ws, size_t ws_bytes,
-                  cudaStream_t st) {
+                  const void *residual, void *y, int *idx_out, float *wts_out, void *const *stage_events, void *ws,
+                  size_t ws_bytes, cudaStream_t st) {
     if (!gate_w) return fail(MOEB_EINVAL, "gate weights are required%s");
     return experts_common(FMT_Q4, x, qg, sbg, qu, sbu, qd, sbd, bg, bu, bd, nullptr, nullptr, T, d, f, E, k, act,
-                          policy, residual, y, ws, ws_bytes, st, gate_w, gate_b, norm, rscale, idx_out, wts_out);
+                          policy, residual, y, ws, ws_bytes, st, gate_w, gate_b, norm, rscale, idx_out, wts_out,
+                          stage_events);
 }
 
 }  // extern "C"

@@ -88,9 +88,21 @@ __device__ __forceinline__ void load_b16(const uint16_t *p, uint32_t (&o)[8]) {
     }
 }
 
+// L2 prefetch of the 16-byte-aligned part of [p, p + bytes), in 4 KB pieces spread over a warp's lanes. The
+// range is shrunk inward to 16-byte boundaries, so nothing outside it is touched.
+__device__ __forceinline__ void prefetch_l2(const void *p, size_t bytes, int lane) {
+    const uintptr_t b = ((uintptr_t)p + 15) & ~(uintptr_t)15, e = ((uintptr_t)p + bytes) & ~(uintptr_t)15;
+    for (uintptr_t q = b + (uintptr_t)lane * 4096; q < e; q += 32 * 4096) {
+        const uint32_t n = (uint32_t)(e - q < 4096 ? e - q : 4096);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(q), "r"(n) : "memory");
+    }
+}
+
 // ------------------------------------------------------------------ gate/up
-template <int FMT, int NT8, int KS>
-__global__ void __launch_bounds__(32 * KS) k_gate_up(ExpArgs a) {
+// GPW = 64-groups per warp per batch: all loads of a batch (codes, scale|bias, activations, group sums) are
+// issued before the first MMA, so one warp keeps GPW * 56 bytes per lane in flight.
+template <int FMT, int NT8, int KS, int GPW>
+__global__ void __launch_bounds__(32 * KS, 2) k_gate_up(ExpArgs a) {
     pdl_launch();
     pdl_wait();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -103,6 +115,13 @@ __global__ void __launch_bounds__(32 * KS) k_gate_up(ExpArgs a) {
     for (int unit = blockIdx.x; unit < n_tiles * RB; unit += gridDim.x) {
         const int tile = unit / RB, rb = unit - tile * RB;
         const TileInfo ti = tile_info(a, tile);
+        // the down projection of this expert streams next: pull this unit's share of it into L2 now
+        if (warp == KS - 1 && a.dn_prefetch) {
+            const int r0 = (int)((long)rb * d / RB), r1 = (int)((long)(rb + 1) * d / RB);
+            const size_t row = (size_t)ti.e * d + r0;
+            prefetch_l2(a.dn.q + row * (f / 8), (size_t)(r1 - r0) * (f / 2), lane);
+            prefetch_l2(a.dn.sb + row * (f / 64), (size_t)(r1 - r0) * (f / 16), lane);
+        }
         const uint16_t *xrow[NT8];
         const float *sxrow[NT8][2];
 #pragma unroll
@@ -125,38 +144,34 @@ __global__ void __launch_bounds__(32 * KS) k_gate_up(ExpArgs a) {
         for (int j = 0; j < NT8; ++j)
 #pragma unroll
             for (int i = 0; i < 4; ++i) Cg[j][i] = Cu[j][i] = 0.f;
-        constexpr int PF = 4;  // groups in flight per warp
-        for (int g0 = g_beg; g0 < g_end; g0 += PF) {
-            uint2 wg0[PF], wg1[PF], wu0[PF], wu1[PF];
-            uint32_t bg0[PF], bg1[PF], bu0[PF], bu1[PF];
+        for (int g0 = g_beg; g0 < g_end; g0 += GPW) {
+            uint2 wg0[GPW], wg1[GPW], wu0[GPW], wu1[GPW];
+            uint32_t bg0[GPW], bg1[GPW], bu0[GPW], bu1[GPW];
+            uint32_t xb[GPW][NT8][8];
+            float sx[GPW][NT8][2];
 #pragma unroll
-            for (int i = 0; i < PF; ++i) {
-                if (g0 + i < g_end) {
-                    const int g = g0 + i;
-                    wg0[i] = ld_stream_u2(qg0 + g * 8);
-                    wg1[i] = ld_stream_u2(qg1 + g * 8);
-                    wu0[i] = ld_stream_u2(qu0 + g * 8);
-                    wu1[i] = ld_stream_u2(qu1 + g * 8);
-                    bg0[i] = ld_stream_u32(sg0 + g);
-                    bg1[i] = ld_stream_u32(sg1 + g);
-                    bu0[i] = ld_stream_u32(su0 + g);
-                    bu1[i] = ld_stream_u32(su1 + g);
+            for (int i = 0; i < GPW; ++i) {
+                const int g = min(g0 + i, g_end - 1);  // clamped: a repeated load, never used
+                wg0[i] = ld_stream_u2(qg0 + g * 8);
+                wg1[i] = ld_stream_u2(qg1 + g * 8);
+                wu0[i] = ld_stream_u2(qu0 + g * 8);
+                wu1[i] = ld_stream_u2(qu1 + g * 8);
+                bg0[i] = ld_stream_u32(sg0 + g);
+                bg1[i] = ld_stream_u32(sg1 + g);
+                bu0[i] = ld_stream_u32(su0 + g);
+                bu1[i] = ld_stream_u32(su1 + g);
+#pragma unroll
+                for (int j = 0; j < NT8; ++j) {
+                    load_b16(xrow[j] ? xrow[j] + g * 64 : nullptr, xb[i][j]);
+                    sx[i][j][0] = sxrow[j][0] ? sxrow[j][0][g] : 0.f;
+                    sx[i][j][1] = sxrow[j][1] ? sxrow[j][1][g] : 0.f;
                 }
             }
 #pragma unroll
-            for (int i = 0; i < PF; ++i) {
+            for (int i = 0; i < GPW; ++i) {
                 if (g0 + i < g_end) {
-                    const int g = g0 + i;
-                    uint32_t xb[NT8][8];
-                    float sx[NT8][2];
-#pragma unroll
-                    for (int j = 0; j < NT8; ++j) {
-                        load_b16(xrow[j] ? xrow[j] + g * 64 : nullptr, xb[j]);
-                        sx[j][0] = sxrow[j][0] ? sxrow[j][0][g] : 0.f;
-                        sx[j][1] = sxrow[j][1] ? sxrow[j][1][g] : 0.f;
-                    }
-                    q4_group<NT8>(wg0[i], wg1[i], bg0[i], bg1[i], xb, sx, Cg);
-                    q4_group<NT8>(wu0[i], wu1[i], bu0[i], bu1[i], xb, sx, Cu);
+                    q4_group<NT8>(wg0[i], wg1[i], bg0[i], bg1[i], xb[i], sx[i], Cg);
+                    q4_group<NT8>(wu0[i], wu1[i], bu0[i], bu1[i], xb[i], sx[i], Cu);
                 }
             }
         }
@@ -177,6 +192,7 @@ __global__ void __launch_bounds__(32 * KS) k_gate_up(ExpArgs a) {
                 for (int i = 0; i < 4; ++i) {
                     gs[i] = red[0][0][j][i][lane];
                     us[i] = red[0][1][j][i][lane];
+#pragma unroll
                     for (int w = 1; w < KS; ++w) {
                         gs[i] += red[w][0][j][i][lane];
                         us[i] += red[w][1][j][i][lane];
@@ -211,8 +227,8 @@ __global__ void __launch_bounds__(32 * KS) k_gate_up(ExpArgs a) {
 }
 
 // ------------------------------------------------------------------ down + combine
-template <int FMT, int NT8, int KS>
-__global__ void __launch_bounds__(32 * KS) k_down(ExpArgs a) {
+template <int FMT, int NT8, int KS, int GPW>
+__global__ void __launch_bounds__(32 * KS, 4) k_down(ExpArgs a) {
     pdl_launch();
     pdl_wait();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -247,36 +263,39 @@ __global__ void __launch_bounds__(32 * KS) k_down(ExpArgs a) {
         for (int j = 0; j < NT8; ++j)
 #pragma unroll
             for (int i = 0; i < 4; ++i) C[j][i] = 0.f;
-        constexpr int PF = 4;
-        for (int g0 = g_beg; g0 < g_end; g0 += PF) {
-            uint2 w0[PF], w1[PF];
-            uint32_t b0[PF], b1[PF];
+        for (int g0 = g_beg; g0 < g_end; g0 += GPW) {
+            uint2 w0[GPW], w1[GPW];
+            uint32_t b0[GPW], b1[GPW];
+            uint32_t hb[GPW][NT8][8];
+            float4 hs[GPW][NT8][2];
 #pragma unroll
-            for (int i = 0; i < PF; ++i) {
-                if (g0 + i < g_end) {
-                    const int g = g0 + i;
-                    w0[i] = ld_stream_u2(qd0 + g * 8);
-                    w1[i] = ld_stream_u2(qd1 + g * 8);
-                    b0[i] = ld_stream_u32(sd0 + g);
-                    b1[i] = ld_stream_u32(sd1 + g);
+            for (int i = 0; i < GPW; ++i) {
+                const int g = min(g0 + i, g_end - 1);
+                w0[i] = ld_stream_u2(qd0 + g * 8);
+                w1[i] = ld_stream_u2(qd1 + g * 8);
+                b0[i] = ld_stream_u32(sd0 + g);
+                b1[i] = ld_stream_u32(sd1 + g);
+#pragma unroll
+                for (int j = 0; j < NT8; ++j) {
+                    load_b16(hrow[j] ? hrow[j] + g * 64 : nullptr, hb[i][j]);
+#pragma unroll
+                    for (int hf = 0; hf < 2; ++hf)
+                        hs[i][j][hf] = hsrow[j][hf] ? *reinterpret_cast<const float4 *>(hsrow[j][hf] + 4 * g)
+                                                    : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
             }
 #pragma unroll
-            for (int i = 0; i < PF; ++i) {
+            for (int i = 0; i < GPW; ++i) {
                 if (g0 + i < g_end) {
-                    const int g = g0 + i;
-                    uint32_t hb[NT8][8];
                     float sx[NT8][2];
 #pragma unroll
-                    for (int j = 0; j < NT8; ++j) {
-                        load_b16(hrow[j] ? hrow[j] + g * 64 : nullptr, hb[j]);
+                    for (int j = 0; j < NT8; ++j)
 #pragma unroll
                         for (int hf = 0; hf < 2; ++hf) {
-                            const float *p = hsrow[j][hf];
-                            sx[j][hf] = p ? (p[4 * g] + p[4 * g + 1]) + (p[4 * g + 2] + p[4 * g + 3]) : 0.f;
+                            const float4 v = hs[i][j][hf];
+                            sx[j][hf] = (v.x + v.y) + (v.z + v.w);
                         }
-                    }
-                    q4_group<NT8>(w0[i], w1[i], b0[i], b1[i], hb, sx, C);
+                    q4_group<NT8>(w0[i], w1[i], b0[i], b1[i], hb[i], sx, C);
                 }
             }
         }
@@ -294,6 +313,7 @@ __global__ void __launch_bounds__(32 * KS) k_down(ExpArgs a) {
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     cs[i] = red[0][j][i][lane];
+#pragma unroll
                     for (int w = 1; w < KS; ++w) cs[i] += red[w][j][i][lane];
                 }
 #pragma unroll
@@ -344,13 +364,9 @@ __global__ void __launch_bounds__(32 * KS) k_down(ExpArgs a) {
     }
 }
 
-#define MOEB_INST(FMT, NT8, KS)                          \
-    template __global__ void k_gate_up<FMT, NT8, KS>(ExpArgs); \
-    template __global__ void k_down<FMT, NT8, KS>(ExpArgs);
-MOEB_INST(FMT_Q4, 1, 4)
-MOEB_INST(FMT_Q4, 2, 4)
-MOEB_INST(FMT_Q4, 1, 8)
-MOEB_INST(FMT_Q4, 2, 8)
-#undef MOEB_INST
+template __global__ void k_gate_up<FMT_Q4, 1, 8, 4>(ExpArgs);
+template __global__ void k_gate_up<FMT_Q4, 2, 8, 2>(ExpArgs);
+template __global__ void k_down<FMT_Q4, 1, 4, 4>(ExpArgs);
+template __global__ void k_down<FMT_Q4, 2, 4, 2>(ExpArgs);
 
 }  // namespace moeb

@@ -62,6 +62,7 @@ struct ExpArgs {
     uint16_t *y;               // [T][d] bf16
     unsigned *err;
     int T, d, f, E, k, act, tile_mode;
+    int dn_prefetch;  // gate/up pulls the down weights of its expert into L2
 };
 
 template <int TPB, int JMAX>
@@ -77,9 +78,9 @@ __global__ void k_fp4_dequant(const uint32_t *qw, const uint8_t *sc, long rows, 
 __global__ void k_fp4_from_mlx(const uint32_t *wq, const uint8_t *scales, long rows, long K, uint32_t *qw,
                                uint8_t *sc);
 
-template <int FMT, int NT8, int KS>
+template <int FMT, int NT8, int KS, int GPW>
 __global__ void k_gate_up(ExpArgs a);
-template <int FMT, int NT8, int KS>
+template <int FMT, int NT8, int KS, int GPW>
 __global__ void k_down(ExpArgs a);
 
 enum { FMT_Q4 = 0, FMT_FP4 = 1 };

@@ -173,19 +173,36 @@ __global__ void __launch_bounds__(128) k_router(RouterArgs a) {
 #pragma unroll
         for (int i = 0; i < TPB; ++i) acc[i] = 0.f;
         const uint16_t *wr = a.wg + (size_t)e * a.d;
-        for (int c = lane; c < nch; c += 32) {
-            const uint4 w = *reinterpret_cast<const uint4 *>(wr + 8 * c);
-            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+        constexpr int U = 4;  // chunks per lane in flight; each (token, expert) still sums chunks in order
+        for (int c0 = lane; c0 < nch; c0 += 32 * U) {
+            uint4 w[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int c = c0 + 32 * u;
+                w[u] = c < nch ? *reinterpret_cast<const uint4 *>(wr + 8 * c) : make_uint4(0, 0, 0, 0);
+            }
 #pragma unroll
             for (int i = 0; i < TPB; ++i) {
                 if (i < nt) {
-                    const uint4 xv = *reinterpret_cast<const uint4 *>(a.x + (size_t)(t0 + i) * a.d + 8 * c);
-                    const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
+                    uint4 xv[U];
+#pragma unroll
+                    for (int u = 0; u < U; ++u) {
+                        const int c = c0 + 32 * u;
+                        xv[u] = c < nch ? *reinterpret_cast<const uint4 *>(a.x + (size_t)(t0 + i) * a.d + 8 * c)
+                                        : make_uint4(0, 0, 0, 0);
+                    }
                     float s = acc[i];
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        s = __fmaf_rn(bf16lo(xx[j]), bf16lo(ww[j]), s);
-                        s = __fmaf_rn(bf16hi(xx[j]), bf16hi(ww[j]), s);
+                    for (int u = 0; u < U; ++u) {
+                        if (c0 + 32 * u < nch) {
+                            const uint32_t xx[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
+                            const uint32_t ww[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                s = __fmaf_rn(bf16lo(xx[j]), bf16lo(ww[j]), s);
+                                s = __fmaf_rn(bf16hi(xx[j]), bf16hi(ww[j]), s);
+                            }
+                        }
                     }
                     acc[i] = s;
                 }
@@ -261,11 +278,15 @@ __global__ void __launch_bounds__(256) k_prep(PrepArgs a) {
     if (threadIdx.x == 0) *a.cnt_all = 0;
 }
 
-template __global__ void k_router<8, 1>(RouterArgs);
-template __global__ void k_router<8, 2>(RouterArgs);
-template __global__ void k_router<8, 4>(RouterArgs);
-template __global__ void k_router<8, 8>(RouterArgs);
-template __global__ void k_router<8, 16>(RouterArgs);
-template __global__ void k_router<8, 32>(RouterArgs);
+#define MOEB_ROUTER_INST(TPB)                          \
+    template __global__ void k_router<TPB, 1>(RouterArgs);  \
+    template __global__ void k_router<TPB, 2>(RouterArgs);  \
+    template __global__ void k_router<TPB, 4>(RouterArgs);  \
+    template __global__ void k_router<TPB, 8>(RouterArgs);  \
+    template __global__ void k_router<TPB, 16>(RouterArgs); \
+    template __global__ void k_router<TPB, 32>(RouterArgs);
+MOEB_ROUTER_INST(1)
+MOEB_ROUTER_INST(4)
+#undef MOEB_ROUTER_INST
 
 }  // namespace moeb

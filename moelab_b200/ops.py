@@ -177,8 +177,9 @@ def experts_q4(state, x, idx, wts, act=0, policy=POLICY_AUTO, residual=None):
 
 
 def layer_q4(state, x, gate_w, k, gate_b=None, norm=True, rscale=1.0, act=0, policy=POLICY_AUTO, residual=None,
-             return_routing=False):
-    """The layer call (x, gate weights, packed experts, k) -> y: router + routing + experts + combine."""
+             return_routing=False, stage_events=None):
+    """The layer call (x, gate weights, packed experts, k) -> y: router + routing + experts + combine.
+    stage_events: optional 4 torch.cuda.Event (before router, after router, after gate/up, after down)."""
     _need(x, torch.bfloat16, "x")
     _need(gate_w, torch.bfloat16, "gate_w")
     _need(gate_b, torch.bfloat16, "gate_b")
@@ -189,9 +190,15 @@ def layer_q4(state, x, gate_w, k, gate_b=None, norm=True, rscale=1.0, act=0, pol
     y = torch.empty_like(x)
     idx = torch.empty(T, k, dtype=torch.int32, device=x.device) if return_routing else None
     wts = torch.empty(T, k, dtype=torch.float32, device=x.device) if return_routing else None
+    evp = None
+    if stage_events is not None:
+        for ev in stage_events:
+            if ev.cuda_event == 0:
+                ev.record()  # creates the underlying cudaEvent_t
+        evp = (ctypes.c_void_p * 4)(*[ctypes.c_void_p(ev.cuda_event) for ev in stage_events])
     _lib.call("moeb_layer_q4", _p(x), _p(gate_w), _p(gate_b), int(bool(norm)), float(rscale), *_expert_ptrs(state),
-              T, d, f, E, k, int(act), int(policy), _p(residual), _p(y), _p(idx), _p(wts), _p(buf), buf.numel(),
-              _stream())
+              T, d, f, E, k, int(act), int(policy), _p(residual), _p(y), _p(idx), _p(wts), evp, _p(buf),
+              buf.numel(), _stream())
     return (y, idx, wts) if return_routing else y
 
 

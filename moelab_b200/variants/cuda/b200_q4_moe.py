@@ -83,11 +83,12 @@ def run_slots(s, x, idx, act=None):
     return y if x.dtype == torch.bfloat16 else y.to(x.dtype)
 
 
-def layer(s, x, gate_w, k, gate_b=None, norm=True, rscale=1.0, act=None, residual=None, return_routing=False):
+def layer(s, x, gate_w, k, gate_b=None, norm=True, rscale=1.0, act=None, residual=None, return_routing=False,
+          stage_events=None):
     act = s.get("act", 0) if act is None else act
     _ws(s, k)
     return ops.layer_q4(s, x, gate_w, k, gate_b=gate_b, norm=norm, rscale=rscale, act=act, policy=_policy(),
-                        residual=residual, return_routing=return_routing)
+                        residual=residual, return_routing=return_routing, stage_events=stage_events)
 
 
 def custom_wins(T, k, E, D, F):
