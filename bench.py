@@ -159,16 +159,25 @@ def down_bytes(idx, T):
     return U * D * F * W_BITS / 8 + T * K_TOP * F * 2 + T * D * 2 * 2
 
 
-def capture(v, layers, x0, n_steps, k0=0):
-    """CUDA graph of n_steps layer calls x <- layer_i(x) + x cycling through the layers."""
+def make_inputs(T, L, seed):
+    """One seeded token batch x_l ~ N(0, 1) per layer. Steps are independent layer calls y = x_l + moe_l(x_l)
+    (no chaining: without the model's norms a chained residual stream grows without bound and would degrade the
+    routing; stream order still serialises the calls)."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return [torch.randn(T, D, generator=g, device="cuda").to(torch.bfloat16) for _ in range(L)]
+
+
+def capture(v, layers, xs, n_steps, k0=0):
+    """CUDA graph of n_steps layer calls cycling through the layers (step i uses layer and input i mod L)."""
     L = len(layers)
 
     def chain():
-        x = x0
+        y = None
         for i in range(n_steps):
             st, gate = layers[(k0 + i) % L]
-            x = v.layer(st, x, gate, K_TOP, residual=x)
-        return x
+            x = xs[(k0 + i) % L]
+            y = v.layer(st, x, gate, K_TOP, residual=x)
+        return y
 
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
@@ -195,27 +204,25 @@ def time_graph(gr, ws, reps=1):
     return a.elapsed_time(b) / 1e3
 
 
-def routing_of_chain(v, layers, x0, n_steps, k0=0):
+def routing_of_chain(v, layers, xs, n_steps, k0=0):
     idxs = []
-    x = x0
     for i in range(n_steps):
         st, gate = layers[(k0 + i) % len(layers)]
-        y, idx, _ = v.layer(st, x, gate, K_TOP, residual=x, return_routing=True)
+        x = xs[(k0 + i) % len(layers)]
+        _, idx, _ = v.layer(st, x, gate, K_TOP, residual=x, return_routing=True)
         idxs.append(idx)
-        x = y
     return idxs
 
 
-def stage_times(v, layers, x0, n_steps):
+def stage_times(v, layers, xs, n_steps):
     """Per-kernel durations from CUDA events recorded between the stages (router, gate/up, down)."""
-    x = x0
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n_steps)]
     idxs = []
     for i in range(n_steps):
         st, gate = layers[i % len(layers)]
-        y, idx, _ = v.layer(st, x, gate, K_TOP, residual=x, return_routing=True, stage_events=ev[i])
+        x = xs[i % len(layers)]
+        _, idx, _ = v.layer(st, x, gate, K_TOP, residual=x, return_routing=True, stage_events=ev[i])
         idxs.append(idx)
-        x = y
     torch.cuda.synchronize()
     r = [ev[i][0].elapsed_time(ev[i][1]) * 1e3 for i in range(n_steps)]
     gu = [ev[i][1].elapsed_time(ev[i][2]) * 1e3 for i in range(n_steps)]
@@ -224,13 +231,12 @@ def stage_times(v, layers, x0, n_steps):
 
 
 def measure_T(v, layers, T, ws, rank, n_steps, seed):
-    g = torch.Generator(device="cuda").manual_seed(seed)
-    x0 = torch.randn(T, D, generator=g, device="cuda").to(torch.bfloat16)
-    gr, _ = capture(v, layers, x0, n_steps)
+    xs = make_inputs(T, len(layers), seed)
+    gr, _ = capture(v, layers, xs, n_steps)
     gr.replay()
     torch.cuda.synchronize()
     t = max_over_ranks(ws, time_graph(gr, ws))
-    idxs = routing_of_chain(v, layers, x0, n_steps)
+    idxs = routing_of_chain(v, layers, xs, n_steps)
     nb = layer_bytes(idxs, T)
     us = t / n_steps * 1e6
     return {"T": T, "us_per_call": round(us, 3), "gbs": round(sum(nb) / t / 1e9, 1),
@@ -255,7 +261,7 @@ def cpu_layer(seed=0):
 def cpu_step(s, gate, x):
     import oracle
     idx, wts = oracle.torch_router_stock(x, gate, K_TOP)
-    return oracle.torch_loop_run(s, x, idx, wts) + x
+    return oracle.torch_loop_run(s, x, idx, wts) + x  # same layer call as the GPU arm: y = x + moe(x)
 
 
 def cpu_baseline(T, seconds, warmup=1, steps=None):
@@ -263,10 +269,10 @@ def cpu_baseline(T, seconds, warmup=1, steps=None):
     s, gate = cpu_layer()
     x = torch.randn(T, D, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
     for _ in range(warmup):
-        x = cpu_step(s, gate, x)
+        cpu_step(s, gate, x)
     n, t0 = 0, time.perf_counter()
     while True:
-        x = cpu_step(s, gate, x)
+        cpu_step(s, gate, x)
         n += 1
         el = time.perf_counter() - t0
         if (steps is not None and (n >= steps or el >= 120.0)) or (steps is None and (el >= seconds or n >= 10000)):
@@ -303,16 +309,14 @@ def main():
     peaks = roofline.b200_peaks()
     T = a.tokens
     v, layers = make_layers(a.layers, seed=1000 + 7919 * rank, device="cuda")
-    g = torch.Generator(device="cuda").manual_seed(5 + rank)
-    x0 = torch.randn(T, D, generator=g, device="cuda").to(torch.bfloat16)
+    xs = make_inputs(T, a.layers, seed=5 + rank)
     # warm-up: W untimed eager steps
-    x = x0
     for i in range(a.warmup):
         st, gate = layers[i % len(layers)]
-        x = v.layer(st, x, gate, K_TOP, residual=x)
+        v.layer(st, xs[i % len(layers)], gate, K_TOP, residual=xs[i % len(layers)])
     torch.cuda.synchronize()
     # headline: one CUDA graph of exactly K steps
-    gr, _ = capture(v, layers, x0, a.steps)
+    gr, _ = capture(v, layers, xs, a.steps)
     gr.replay()
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
@@ -327,13 +331,13 @@ def main():
     value = ws * T * a.steps / t
     # per-kernel times and roofline of the dominant kernel (gate/up)
     n_stage = min(4 * a.layers, a.steps)
-    r_us, gu_us, dn_us, idxs = stage_times(v, layers, x0, n_stage)
+    r_us, gu_us, dn_us, idxs = stage_times(v, layers, xs, n_stage)
     gu_b = [gate_up_bytes(i, T) for i in idxs]
     dn_b = [down_bytes(i, T) for i in idxs]
     gu_ach = sum(gu_b) / (sum(gu_us) * 1e-6) / 1e9
     dn_ach = sum(dn_b) / (sum(dn_us) * 1e-6) / 1e9
-    lay_b = layer_bytes(idxs, T)
-    lay_ach = sum(lay_b) / (t / a.steps * n_stage) / 1e9
+    lay_b = layer_bytes(idxs[:len(layers)], T)  # the graph cycles the same L (layer, input) pairs
+    lay_ach = sum(lay_b) / len(lay_b) / (t / a.steps) / 1e9
     traffic = None
     tp = os.path.join(ROOT, "profiles", "traffic_gate_up.json")
     if os.path.exists(tp):

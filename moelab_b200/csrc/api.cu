@@ -147,15 +147,24 @@ struct ExpLaunch {
     void (*gu)(ExpArgs);
     void (*dn)(ExpArgs);
     int gu_threads, dn_threads;
+    size_t gu_smem, dn_smem;
+    bool per_warp;  // tiles kernels: one unit per warp (4 warps per CTA); slots kernels: one unit per CTA
 };
 
-ExpLaunch pick_kernels(int fmt, int policy) {
-    const bool wide = policy == MOEB_POLICY_TILES16;
-    if (fmt == FMT_Q4) {
-        if (wide) return {k_gate_up<FMT_Q4, 2, 8, 2>, k_down<FMT_Q4, 2, 4, 2>, 256, 128};
-        return {k_gate_up<FMT_Q4, 1, 8, 4>, k_down<FMT_Q4, 1, 4, 4>, 256, 128};
-    }
-    return {nullptr, nullptr, 0, 0};
+ExpLaunch pick_kernels(int fmt, int policy, int d, int f) {
+    if (fmt != FMT_Q4) return {nullptr, nullptr, 0, 0, 0, 0, false};
+    if (policy == MOEB_POLICY_SLOTS)
+        return {k_gate_up_slots<FMT_Q4, 8, 4>, k_down_slots<FMT_Q4, 4, 4>, 256, 128, (size_t)d * 2,
+                (size_t)f * 2 + (size_t)f / 16 * 4, false};
+    if (policy == MOEB_POLICY_TILES16)
+        return {k_gate_up_tiles<FMT_Q4, 2, 1>, k_down_tiles<FMT_Q4, 2, 1>, 128, 128, 0, 0, true};
+    return {k_gate_up_tiles<FMT_Q4, 1, 2>, k_down_tiles<FMT_Q4, 1, 2>, 128, 128, 0, 0, true};
+}
+
+int grid_for(void (*kern)(ExpArgs), int threads, size_t smem, long units, bool per_warp) {
+    const long ctas = per_warp ? (units + threads / 32 - 1) / (threads / 32) : units;
+    const long cap = (long)occupancy((const void *)kern, threads, smem) * sm_count();
+    return (int)std::max<long>(1, std::min(ctas, cap));
 }
 
 int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaStream_t st,
@@ -163,21 +172,19 @@ int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaS
     const long TK = (long)a.T * a.k;
     const int nt = nt_of(policy);
     const long max_tiles = a.tile_mode ? std::min<long>(TK, (long)a.E + TK / nt) : TK;
-    ExpLaunch K = pick_kernels(fmt, policy);
+    ExpLaunch K = pick_kernels(fmt, policy, a.d, a.f);
     if (!K.gu) return fail(MOEB_EUNSUP, "format not supported%s");
-    const int nsm = sm_count();
+    if (K.gu_smem > 48 * 1024 || K.dn_smem > 48 * 1024) return fail(MOEB_EINVAL, "d or f too large for the decode kernels%s");
     {
-        const long units = max_tiles * (a.f / 16);
-        const long cap = (long)occupancy((const void *)K.gu, K.gu_threads, 0) * nsm;
-        const int grid = (int)std::max<long>(1, std::min(units, cap));
-        if (launch(K.gu, dim3(grid), dim3(K.gu_threads), 0, st, a) != cudaSuccess) return check_launch("gate_up");
+        const int grid = grid_for(K.gu, K.gu_threads, K.gu_smem, max_tiles * (a.f / 16), K.per_warp);
+        if (launch(K.gu, dim3(grid), dim3(K.gu_threads), K.gu_smem, st, a) != cudaSuccess)
+            return check_launch("gate_up");
     }
     if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[2]), st);
     {
-        const long units = max_tiles * (a.d / 16);
-        const long cap = (long)occupancy((const void *)K.dn, K.dn_threads, 0) * nsm;
-        const int grid = (int)std::max<long>(1, std::min(units, cap));
-        if (launch(K.dn, dim3(grid), dim3(K.dn_threads), 0, st, a) != cudaSuccess) return check_launch("down");
+        const int grid = grid_for(K.dn, K.dn_threads, K.dn_smem, max_tiles * (a.d / 16), K.per_warp);
+        if (launch(K.dn, dim3(grid), dim3(K.dn_threads), K.dn_smem, st, a) != cudaSuccess)
+            return check_launch("down");
     }
     if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[3]), st);
     (void)L;
@@ -256,8 +263,14 @@ int moeb_read_error(void *ws, unsigned *out, cudaStream_t st) {
 int moeb_policy(int T, int E, int k) { return choose_policy(T, E, k); }
 
 // ------------------------------------------------------------------ quantizers
+static int check_rows(long rows, long K) {
+    if (K <= 0 || K % 64) return fail(MOEB_EINVAL, "K must be a positive multiple of 64%s");
+    if (rows < 0 || rows % 16) return fail(MOEB_EINVAL, "rows must be a multiple of 16 (16-row weight blocks)%s");
+    return MOEB_OK;
+}
+
 int moeb_quantize_q4(const void *w, long rows, long K, void *qw, void *sb, cudaStream_t st) {
-    if (K % 64 || rows < 0) return fail(MOEB_EINVAL, "K must be a multiple of 64%s");
+    if (int rc = check_rows(rows, K)) return rc;
     const long n = rows * (K / 64);
     if (n == 0) return MOEB_OK;
     k_q4_quantize<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(static_cast<const uint16_t *>(w), rows, K,
@@ -266,7 +279,7 @@ int moeb_quantize_q4(const void *w, long rows, long K, void *qw, void *sb, cudaS
 }
 
 int moeb_dequant_q4(const void *qw, const void *sb, long rows, long K, float *out, cudaStream_t st) {
-    if (K % 64 || rows < 0) return fail(MOEB_EINVAL, "K must be a multiple of 64%s");
+    if (int rc = check_rows(rows, K)) return rc;
     const long n = rows * (K / 8);
     if (n == 0) return MOEB_OK;
     k_q4_dequant<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(static_cast<const uint32_t *>(qw),
@@ -276,7 +289,7 @@ int moeb_dequant_q4(const void *qw, const void *sb, long rows, long K, float *ou
 
 int moeb_q4_from_mlx(const void *wq, const void *scales, const void *biases, long rows, long K, void *qw, void *sb,
                      cudaStream_t st) {
-    if (K % 64 || rows < 0) return fail(MOEB_EINVAL, "K must be a multiple of 64%s");
+    if (int rc = check_rows(rows, K)) return rc;
     const long n = rows * (K / 8);
     if (n == 0) return MOEB_OK;
     k_q4_from_mlx<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
@@ -286,7 +299,7 @@ int moeb_q4_from_mlx(const void *wq, const void *scales, const void *biases, lon
 }
 
 int moeb_quantize_mxfp4(const void *w, long rows, long K, void *qw, void *sc, cudaStream_t st) {
-    if (K % 64 || rows < 0) return fail(MOEB_EINVAL, "K must be a multiple of 64%s");
+    if (int rc = check_rows(rows, K)) return rc;
     const long n = rows * (K / 32);
     if (n == 0) return MOEB_OK;
     k_fp4_quantize<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(static_cast<const uint16_t *>(w), rows, K,
@@ -295,7 +308,7 @@ int moeb_quantize_mxfp4(const void *w, long rows, long K, void *qw, void *sc, cu
 }
 
 int moeb_dequant_mxfp4(const void *qw, const void *sc, long rows, long K, float *out, cudaStream_t st) {
-    if (K % 64 || rows < 0) return fail(MOEB_EINVAL, "K must be a multiple of 64%s");
+    if (int rc = check_rows(rows, K)) return rc;
     const long n = rows * (K / 8);
     if (n == 0) return MOEB_OK;
     k_fp4_dequant<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(static_cast<const uint32_t *>(qw),
@@ -304,7 +317,7 @@ int moeb_dequant_mxfp4(const void *qw, const void *sc, long rows, long K, float 
 }
 
 int moeb_mxfp4_from_mlx(const void *wq, const void *scales, long rows, long K, void *qw, void *sc, cudaStream_t st) {
-    if (K % 64 || rows < 0) return fail(MOEB_EINVAL, "K must be a multiple of 64%s");
+    if (int rc = check_rows(rows, K)) return rc;
     const long n = rows * (K / 8);
     if (n == 0) return MOEB_OK;
     k_fp4_from_mlx<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(static_cast<const uint32_t *>(wq),

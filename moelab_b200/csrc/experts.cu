@@ -1,24 +1,25 @@
-// Grouped expert kernels, warp-MMA path (all loads; the HBM-bound regime).
+// Grouped expert kernels, warp-MMA path (the HBM-bound regime).
 //
-// Work unit = (tile, 16-row block). A tile is up to 8 * NT8 slots routed to one expert (tile mode, built by
-// the routing step) or exactly one slot (slot mode, T*k small). The CTA's KS warps split K; each warp runs
-// m16n8k16 bf16 MMAs with
-//   A = 16 weight rows x 16 k, the raw int4 codes as exact bf16 (128 + q, one lop3 per two codes), loaded
-//       straight from HBM into the MMA fragment (8 bytes per row per 64-group per thread);
-//   B = the tile's activations (x rows for gate/up, h rows for down), 16 contiguous elements per thread;
-// and promotes every 64-wide scale group in fp32: C += s * P + (b - 128 s) * sum(x_group)
-// (the same algebra as the reference's raw-code MMA, metal_q4_tiles_v2.py:255-262), so the result equals the
-// dot product with the fp32-dequantised weights w = s*q + b up to fp32 rounding.
+// Math. m16n8k16 bf16 MMAs with
+//   A = 16 weight rows x 16 k: the raw int4 codes as exact bf16 (128 + q, one lop3 per two codes), read from the
+//       fragment-major weight layout (quant.cu) with one coalesced 16-byte load per lane per 64-group;
+//   B = the activations (x rows for gate/up, h rows for down), 16 contiguous elements per lane per group;
+// and every 64-wide scale group is promoted in fp32: C += s * P + (b - 128 s) * sum(x_group), the algebra of the
+// reference's raw-code MMA (metal_q4_tiles_v2.py:255-262), so the result is the dot product with the
+// fp32-dequantised weights w = s*q + b up to fp32 rounding.
+// K permutation: inside a 64-group, MMA k-step s / fragment half hf / lane-in-quad c address the physical
+// elements 16c + 4s + 2hf + {0,1}, for A and B alike (a bijection of the group).
 //
-// K permutation: inside each 64-group, MMA k-step s / fragment half hf / lane-in-quad c address the physical
-// elements 16c + 4s + 2hf + {0,1}, for A and B alike (a bijection of the group), so every thread reads 16
-// contiguous activations and two contiguous 32-bit code words per row.
-//
+// Two launch shapes over work units (tile, 16-row block):
+//   *_slots (decode, one slot per tile): one CTA per unit, the KS warps split K with every load issued up
+//     front, the token's activation row staged in shared memory, fixed-order split-K reduction.
+//   *_tiles (slots grouped by expert into tiles of 8*NT8): one warp per unit over the whole K, a register
+//     double-buffered load pipeline, and a per-warp epilogue (no CTA barriers).
 // gate/up (reference GATE_UP_SRC metal_q4_decode_v4.py:67-93, GATE_UP_E_SRC metal_q4_tiles_v2.py:179-275):
-//   h[slot][r] = bf16(act(g + bg, u + bu)), plus hsum[slot][r/16] = sum of the 16 bf16 h values of the block
+//   h[slot][r] = bf16(act(g + bg, u + bu)); hsum[slot][r/16] = sum of the block's 16 bf16 h values.
 // down + combine (DOWN_SRC metal_q4_decode_v4.py:95-144, DOWN_E_SRC + COMBINE_SRC metal_q4_tiles_v2.py):
-//   yp[slot][r] = w_slot * (Wd h + bd), then the last CTA to finish a (token, 16-row block) sums the k slots
-//   in fixed slot order j = 0..k-1 (deterministic, no float atomics), adds the optional residual, writes y.
+//   yp[slot][r] = w_slot * (Wd h + bd); the last unit to finish a (token, 16-row block) sums its k slots in
+//   fixed order j = 0..k-1 (deterministic, no float atomics), adds the optional residual and writes y.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -49,25 +50,24 @@ __device__ __forceinline__ int tile_slot(const ExpArgs &a, const TileInfo &ti, i
     return a.tile_mode ? a.sorted[ti.start + col] : ti.start;
 }
 
-// One 64-group of one projection: 4 k-steps x NT8 column tiles into P (zeroed here), then promotion into C.
+// One 64-group of one projection: 4 k-steps x NT8 column tiles into P, then promotion into C.
+// w: {row gq: word 2c, 2c+1; row gq+8: word 2c, 2c+1}; sb: {row gq, row gq+8} scale|bias.
 template <int NT8>
-__device__ __forceinline__ void q4_group(const uint2 w0, const uint2 w1, const uint32_t sb0, const uint32_t sb1,
-                                         const uint32_t (&xb)[NT8][8], const float (&sx)[NT8][2],
-                                         float (&C)[NT8][4]) {
+__device__ __forceinline__ void q4_group(const uint4 w, const uint2 sb, const uint32_t (&xb)[NT8][8],
+                                         const float (&sx)[NT8][2], float (&C)[NT8][4]) {
     float P[NT8][4];
 #pragma unroll
     for (int j = 0; j < NT8; ++j) P[j][0] = P[j][1] = P[j][2] = P[j][3] = 0.f;
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
-        // pair index i = 2s + hf -> word (i / 4) of the row's two words, nibble pair i % 4
-        const uint32_t wa0 = (s < 2) ? w0.x : w0.y, wa1 = (s < 2) ? w1.x : w1.y;
+        const uint32_t wa0 = (s < 2) ? w.x : w.y, wa1 = (s < 2) ? w.z : w.w;
         const int p0 = (2 * s) & 3, p1 = (2 * s + 1) & 3;
         const uint32_t A[4] = {q4pair(wa0, p0), q4pair(wa1, p0), q4pair(wa0, p1), q4pair(wa1, p1)};
 #pragma unroll
         for (int j = 0; j < NT8; ++j) mma_bf16(P[j], A, xb[j][2 * s], xb[j][2 * s + 1]);
     }
-    const float s0 = bf16lo(sb0), s1 = bf16lo(sb1);
-    const float b0 = __fmaf_rn(-128.f, s0, bf16hi(sb0)), b1 = __fmaf_rn(-128.f, s1, bf16hi(sb1));
+    const float s0 = bf16lo(sb.x), s1 = bf16lo(sb.y);
+    const float b0 = __fmaf_rn(-128.f, s0, bf16hi(sb.x)), b1 = __fmaf_rn(-128.f, s1, bf16hi(sb.y));
 #pragma unroll
     for (int j = 0; j < NT8; ++j) {
         C[j][0] = __fmaf_rn(s0, P[j][0], __fmaf_rn(b0, sx[j][0], C[j][0]));
@@ -98,30 +98,304 @@ __device__ __forceinline__ void prefetch_l2(const void *p, size_t bytes, int lan
     }
 }
 
-// ------------------------------------------------------------------ gate/up
-// GPW = 64-groups per warp per batch: all loads of a batch (codes, scale|bias, activations, group sums) are
-// issued before the first MMA, so one warp keeps GPW * 56 bytes per lane in flight.
-template <int FMT, int NT8, int KS, int GPW>
-__global__ void __launch_bounds__(32 * KS, 2) k_gate_up(ExpArgs a) {
+// Pull the share [rb/RB, (rb+1)/RB) of expert e's down projection into L2 (it streams right after gate/up).
+__device__ __forceinline__ void prefetch_down(const ExpArgs &a, int e, int rb, int RB, int lane) {
+    const int rb0 = (int)((long)rb * (a.d / 16) / RB), rb1 = (int)((long)(rb + 1) * (a.d / 16) / RB);
+    if (rb1 <= rb0) return;
+    const size_t blk = (size_t)e * (a.d / 16) + rb0;
+    prefetch_l2(a.dn.q + blk * (size_t)(a.f / 64) * 128, (size_t)(rb1 - rb0) * (a.f / 64) * 512, lane);
+    prefetch_l2(a.dn.sb + blk * (size_t)(a.f / 64) * 16, (size_t)(rb1 - rb0) * (a.f / 64) * 64, lane);
+}
+
+// Weights of one (16-row block, 64-group) for this lane.
+__device__ __forceinline__ uint4 ld_w(const QProj &P, size_t blk, int G, int g, int lane) {
+    return ld_stream_u4(P.q + ((blk * G + g) * 32 + lane) * 4);
+}
+__device__ __forceinline__ uint2 ld_sb(const QProj &P, size_t blk, int G, int g, int gq) {
+    return ld_stream_u2(P.sb + ((blk * G + g) * 8 + gq) * 2);
+}
+
+// gate/up epilogue for one column tile j of a unit: bias, activation, bf16 h, block sums.
+template <int NT8>
+__device__ __forceinline__ void gate_up_store(const ExpArgs &a, const TileInfo &ti, int rb, int j,
+                                              const float (&gs)[4], const float (&us)[4], int lane) {
+    const int gq = lane >> 2, c = lane & 3, f = a.f;
+    const int r0 = rb * 16 + gq, r1 = r0 + 8;
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+        const int slot = tile_slot(a, ti, j * 8 + 2 * c + hf);
+        float g0v = gs[hf], g1v = gs[2 + hf], u0v = us[hf], u1v = us[2 + hf];
+        if (a.bg) {
+            g0v += a.bg[(size_t)ti.e * f + r0];
+            g1v += a.bg[(size_t)ti.e * f + r1];
+            u0v += a.bu[(size_t)ti.e * f + r0];
+            u1v += a.bu[(size_t)ti.e * f + r1];
+        }
+        const uint16_t h0 = f2bf(act_glu(a.act, g0v, u0v)), h1 = f2bf(act_glu(a.act, g1v, u1v));
+        float part = slot >= 0 ? bf2f(h0) + bf2f(h1) : 0.f;
+        part += __shfl_xor_sync(0xffffffffu, part, 4);
+        part += __shfl_xor_sync(0xffffffffu, part, 8);
+        part += __shfl_xor_sync(0xffffffffu, part, 16);
+        if (slot >= 0) {
+            a.h[(size_t)slot * f + r0] = h0;
+            a.h[(size_t)slot * f + r1] = h1;
+            if (gq == 0) a.hsum[(size_t)slot * (f / 16) + rb] = part;
+        }
+    }
+}
+
+// down epilogue of one warp: write the weighted per-slot rows, arrive on the (token, row block) counters and
+// combine every token this arrival completed. Warp-synchronous; no CTA barrier.
+template <int NT8>
+__device__ __forceinline__ void down_store_combine(const ExpArgs &a, const TileInfo &ti, int rb,
+                                                   const float (&C)[NT8][4], int lane) {
+    const int gq = lane >> 2, c = lane & 3, d = a.d, k = a.k, RB = d >> 4;
+    const int r0 = rb * 16 + gq, r1 = r0 + 8;
+#pragma unroll
+    for (int j = 0; j < NT8; ++j)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+            const int slot = tile_slot(a, ti, j * 8 + 2 * c + hf);
+            if (slot >= 0) {
+                const int e_raw = a.idx[slot];
+                const float wsl = (e_raw >= 0 && e_raw < a.E) ? a.wts[slot] : 0.f;
+                float v0 = C[j][hf], v1 = C[j][2 + hf];
+                if (a.bd) {
+                    v0 += a.bd[(size_t)ti.e * d + r0];
+                    v1 += a.bd[(size_t)ti.e * d + r1];
+                }
+                a.yp[(size_t)slot * d + r0] = wsl * v0;
+                a.yp[(size_t)slot * d + r1] = wsl * v1;
+            }
+        }
+    __threadfence();
+    __syncwarp();
+    int tok = -1;
+    bool done = false;
+    if (lane < 8 * NT8) {
+        const int slot = tile_slot(a, ti, lane);
+        if (slot >= 0) {
+            tok = slot / k;
+            done = atomicAdd(a.ycnt + (size_t)tok * RB + rb, 1u) == (unsigned)(k - 1);
+        }
+    }
+    unsigned m = __ballot_sync(0xffffffffu, done);
+    if (m) __threadfence();
+    while (m) {
+        const int src = __ffs(m) - 1;
+        m &= m - 1;
+        const int t = __shfl_sync(0xffffffffu, tok, src);
+        if (lane < 16) {
+            const int r = rb * 16 + lane;
+            float acc = 0.f;
+            for (int jj = 0; jj < k; ++jj) acc += __ldcg(a.yp + ((size_t)t * k + jj) * d + r);
+            if (a.residual) acc += bf2f(a.residual[(size_t)t * d + r]);
+            a.y[(size_t)t * d + r] = f2bf(acc);
+        }
+        if (lane == 0) a.ycnt[(size_t)t * RB + rb] = 0u;
+    }
+}
+
+// ================================================================== slot mode (decode)
+// One CTA per (slot, 16-row block); KS warps split the K groups; GPW groups per warp are loaded at once.
+template <int FMT, int KS, int GPW>
+__global__ void __launch_bounds__(32 * KS, 3) k_gate_up_slots(ExpArgs a) {
     pdl_launch();
     pdl_wait();
+    extern __shared__ uint4 xs4[];  // the slot's x row, d bf16
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int gq = lane >> 2, c = lane & 3;
     const int d = a.d, f = a.f;
     const int RB = f >> 4, G = d >> 6;
-    const int n_tiles = a.tile_mode ? *a.ntiles : a.T * a.k;
     const int g_beg = warp * G / KS, g_end = (warp + 1) * G / KS;
-    __shared__ float red[KS][2][NT8][4][32];
-    for (int unit = blockIdx.x; unit < n_tiles * RB; unit += gridDim.x) {
+    __shared__ float red[KS][2][4][32];
+    const uint16_t *xs = reinterpret_cast<const uint16_t *>(xs4);
+    for (int unit = blockIdx.x; unit < a.T * a.k * RB; unit += gridDim.x) {
+        const int slot = unit / RB, rb = unit - slot * RB;
+        const TileInfo ti = tile_info(a, slot);
+        const size_t blk = (size_t)ti.e * RB + rb;
+        if (warp == KS - 1 && a.dn_prefetch) prefetch_down(a, ti.e, rb, RB, lane);
+        const uint4 *xsrc = reinterpret_cast<const uint4 *>(a.x + (size_t)(slot / a.k) * d);
+        for (int i = threadIdx.x; i < d / 8; i += 32 * KS) xs4[i] = xsrc[i];
+        const float *sxr = a.xsum + (size_t)(slot / a.k) * G;
+        float Cg[1][4] = {{0.f, 0.f, 0.f, 0.f}}, Cu[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+        bool synced = false;
+        for (int g0 = g_beg; g0 < g_end; g0 += GPW) {
+            uint4 wg[GPW], wu[GPW];
+            uint2 bg[GPW], bu[GPW];
+#pragma unroll
+            for (int i = 0; i < GPW; ++i) {
+                const int g = min(g0 + i, g_end - 1);  // clamped: a repeated load, never used
+                wg[i] = ld_w(a.g, blk, G, g, lane);
+                wu[i] = ld_w(a.u, blk, G, g, lane);
+                bg[i] = ld_sb(a.g, blk, G, g, gq);
+                bu[i] = ld_sb(a.u, blk, G, g, gq);
+            }
+            if (!synced) {
+                __syncthreads();  // x row staged (weights already in flight)
+                synced = true;
+            }
+#pragma unroll
+            for (int i = 0; i < GPW; ++i) {
+                if (g0 + i < g_end) {
+                    const int g = g0 + i;
+                    uint32_t xb[1][8];
+                    load_b16(gq == 0 ? xs + g * 64 + 16 * c : nullptr, xb[0]);
+                    const float sx[1][2] = {{c == 0 ? sxr[g] : 0.f, 0.f}};
+                    q4_group<1>(wg[i], bg[i], xb, sx, Cg);
+                    q4_group<1>(wu[i], bu[i], xb, sx, Cu);
+                }
+            }
+        }
+        if (!synced) __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            red[warp][0][i][lane] = Cg[0][i];
+            red[warp][1][i][lane] = Cu[0][i];
+        }
+        __syncthreads();
+        if (warp == 0) {
+            float gs[4], us[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                gs[i] = red[0][0][i][lane];
+                us[i] = red[0][1][i][lane];
+#pragma unroll
+                for (int w = 1; w < KS; ++w) {
+                    gs[i] += red[w][0][i][lane];
+                    us[i] += red[w][1][i][lane];
+                }
+            }
+            gate_up_store<1>(a, ti, rb, 0, gs, us, lane);
+        }
+        __syncthreads();
+    }
+}
+
+template <int FMT, int KS, int GPW>
+__global__ void __launch_bounds__(32 * KS, 8) k_down_slots(ExpArgs a) {
+    pdl_launch();
+    pdl_wait();
+    extern __shared__ uint4 hs4[];  // the slot's h row (f bf16) followed by its f/16 block sums
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gq = lane >> 2, c = lane & 3;
+    const int d = a.d, f = a.f;
+    const int RB = d >> 4, G = f >> 6;
+    const int g_beg = warp * G / KS, g_end = (warp + 1) * G / KS;
+    __shared__ float red[KS][4][32];
+    const uint16_t *hs = reinterpret_cast<const uint16_t *>(hs4);
+    const float *hsum_s = reinterpret_cast<const float *>(hs4 + f / 8);
+    for (int unit = blockIdx.x; unit < a.T * a.k * RB; unit += gridDim.x) {
+        const int slot = unit / RB, rb = unit - slot * RB;
+        const TileInfo ti = tile_info(a, slot);
+        const size_t blk = (size_t)ti.e * RB + rb;
+        const uint4 *hsrc = reinterpret_cast<const uint4 *>(a.h + (size_t)slot * f);
+        for (int i = threadIdx.x; i < f / 8; i += 32 * KS) hs4[i] = hsrc[i];
+        const uint4 *ssrc = reinterpret_cast<const uint4 *>(a.hsum + (size_t)slot * (f / 16));
+        for (int i = threadIdx.x; i < f / 64; i += 32 * KS) hs4[f / 8 + i] = ssrc[i];
+        float C[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+        bool synced = false;
+        for (int g0 = g_beg; g0 < g_end; g0 += GPW) {
+            uint4 w[GPW];
+            uint2 b[GPW];
+#pragma unroll
+            for (int i = 0; i < GPW; ++i) {
+                const int g = min(g0 + i, g_end - 1);
+                w[i] = ld_w(a.dn, blk, G, g, lane);
+                b[i] = ld_sb(a.dn, blk, G, g, gq);
+            }
+            if (!synced) {
+                __syncthreads();
+                synced = true;
+            }
+#pragma unroll
+            for (int i = 0; i < GPW; ++i) {
+                if (g0 + i < g_end) {
+                    const int g = g0 + i;
+                    uint32_t hb[1][8];
+                    load_b16(gq == 0 ? hs + g * 64 + 16 * c : nullptr, hb[0]);
+                    const float4 v = *reinterpret_cast<const float4 *>(hsum_s + 4 * g);
+                    const float sx[1][2] = {{c == 0 ? (v.x + v.y) + (v.z + v.w) : 0.f, 0.f}};
+                    q4_group<1>(w[i], b[i], hb, sx, C);
+                }
+            }
+        }
+        if (!synced) __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) red[warp][i][lane] = C[0][i];
+        __syncthreads();
+        if (warp == 0) {
+            float cs[1][4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                cs[0][i] = red[0][i][lane];
+#pragma unroll
+                for (int w = 1; w < KS; ++w) cs[0][i] += red[w][i][lane];
+            }
+            down_store_combine<1>(a, ti, rb, cs, lane);
+        }
+        __syncthreads();
+    }
+}
+
+// ================================================================== tile mode
+// One warp per (tile, 16-row block) over the whole K; loads run one GPW-group batch ahead of the MMAs.
+template <int NT8, int GPW>
+struct GUBatch {
+    uint4 wg[GPW], wu[GPW];
+    uint2 bg[GPW], bu[GPW];
+    uint32_t xb[GPW][NT8][8];
+    float sx[GPW][NT8][2];
+};
+
+template <int NT8, int GPW>
+__device__ __forceinline__ void gu_load(GUBatch<NT8, GPW> &B, const ExpArgs &a, size_t blk, int G, int g0,
+                                        const uint16_t *const (&xrow)[NT8], const float *const (&sxrow)[NT8][2],
+                                        int lane) {
+    const int gq = lane >> 2;
+#pragma unroll
+    for (int i = 0; i < GPW; ++i) {
+        const int g = min(g0 + i, G - 1);
+        B.wg[i] = ld_w(a.g, blk, G, g, lane);
+        B.wu[i] = ld_w(a.u, blk, G, g, lane);
+        B.bg[i] = ld_sb(a.g, blk, G, g, gq);
+        B.bu[i] = ld_sb(a.u, blk, G, g, gq);
+#pragma unroll
+        for (int j = 0; j < NT8; ++j) {
+            load_b16(xrow[j] ? xrow[j] + g * 64 : nullptr, B.xb[i][j]);
+            B.sx[i][j][0] = sxrow[j][0] ? sxrow[j][0][g] : 0.f;
+            B.sx[i][j][1] = sxrow[j][1] ? sxrow[j][1][g] : 0.f;
+        }
+    }
+}
+
+template <int NT8, int GPW>
+__device__ __forceinline__ void gu_compute(const GUBatch<NT8, GPW> &B, int g0, int G, float (&Cg)[NT8][4],
+                                           float (&Cu)[NT8][4]) {
+#pragma unroll
+    for (int i = 0; i < GPW; ++i) {
+        if (g0 + i < G) {
+            q4_group<NT8>(B.wg[i], B.bg[i], B.xb[i], B.sx[i], Cg);
+            q4_group<NT8>(B.wu[i], B.bu[i], B.xb[i], B.sx[i], Cu);
+        }
+    }
+}
+
+template <int FMT, int NT8, int GPW>
+__global__ void __launch_bounds__(128) k_gate_up_tiles(ExpArgs a) {
+    pdl_launch();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int gq = lane >> 2, c = lane & 3;
+    const int d = a.d, f = a.f;
+    const int RB = f >> 4, G = d >> 6;
+    const int n_units = *a.ntiles * RB;
+    const int nwarps = gridDim.x * 4;
+    for (int unit = blockIdx.x * 4 + (threadIdx.x >> 5); unit < n_units; unit += nwarps) {
         const int tile = unit / RB, rb = unit - tile * RB;
         const TileInfo ti = tile_info(a, tile);
-        // the down projection of this expert streams next: pull this unit's share of it into L2 now
-        if (warp == KS - 1 && a.dn_prefetch) {
-            const int r0 = (int)((long)rb * d / RB), r1 = (int)((long)(rb + 1) * d / RB);
-            const size_t row = (size_t)ti.e * d + r0;
-            prefetch_l2(a.dn.q + row * (f / 8), (size_t)(r1 - r0) * (f / 2), lane);
-            prefetch_l2(a.dn.sb + row * (f / 64), (size_t)(r1 - r0) * (f / 16), lane);
-        }
+        const size_t blk = (size_t)ti.e * RB + rb;
+        if (a.dn_prefetch) prefetch_down(a, ti.e, rb, RB, lane);
         const uint16_t *xrow[NT8];
         const float *sxrow[NT8][2];
 #pragma unroll
@@ -134,115 +408,87 @@ __global__ void __launch_bounds__(32 * KS, 2) k_gate_up(ExpArgs a) {
                 sxrow[j][hf] = sc_ >= 0 ? a.xsum + (size_t)(sc_ / a.k) * G : nullptr;
             }
         }
-        const size_t row0 = (size_t)ti.e * f + rb * 16 + gq;
-        const uint32_t *qg0 = a.g.q + row0 * (d / 8) + 2 * c, *qg1 = qg0 + 8 * (size_t)(d / 8);
-        const uint32_t *qu0 = a.u.q + row0 * (d / 8) + 2 * c, *qu1 = qu0 + 8 * (size_t)(d / 8);
-        const uint32_t *sg0 = a.g.sb + row0 * G, *sg1 = sg0 + 8 * (size_t)G;
-        const uint32_t *su0 = a.u.sb + row0 * G, *su1 = su0 + 8 * (size_t)G;
         float Cg[NT8][4], Cu[NT8][4];
 #pragma unroll
         for (int j = 0; j < NT8; ++j)
 #pragma unroll
             for (int i = 0; i < 4; ++i) Cg[j][i] = Cu[j][i] = 0.f;
-        for (int g0 = g_beg; g0 < g_end; g0 += GPW) {
-            uint2 wg0[GPW], wg1[GPW], wu0[GPW], wu1[GPW];
-            uint32_t bg0[GPW], bg1[GPW], bu0[GPW], bu1[GPW];
-            uint32_t xb[GPW][NT8][8];
-            float sx[GPW][NT8][2];
-#pragma unroll
-            for (int i = 0; i < GPW; ++i) {
-                const int g = min(g0 + i, g_end - 1);  // clamped: a repeated load, never used
-                wg0[i] = ld_stream_u2(qg0 + g * 8);
-                wg1[i] = ld_stream_u2(qg1 + g * 8);
-                wu0[i] = ld_stream_u2(qu0 + g * 8);
-                wu1[i] = ld_stream_u2(qu1 + g * 8);
-                bg0[i] = ld_stream_u32(sg0 + g);
-                bg1[i] = ld_stream_u32(sg1 + g);
-                bu0[i] = ld_stream_u32(su0 + g);
-                bu1[i] = ld_stream_u32(su1 + g);
-#pragma unroll
-                for (int j = 0; j < NT8; ++j) {
-                    load_b16(xrow[j] ? xrow[j] + g * 64 : nullptr, xb[i][j]);
-                    sx[i][j][0] = sxrow[j][0] ? sxrow[j][0][g] : 0.f;
-                    sx[i][j][1] = sxrow[j][1] ? sxrow[j][1][g] : 0.f;
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < GPW; ++i) {
-                if (g0 + i < g_end) {
-                    q4_group<NT8>(wg0[i], wg1[i], bg0[i], bg1[i], xb[i], sx[i], Cg);
-                    q4_group<NT8>(wu0[i], wu1[i], bu0[i], bu1[i], xb[i], sx[i], Cu);
-                }
+        GUBatch<NT8, GPW> A, B;
+        gu_load(A, a, blk, G, 0, xrow, sxrow, lane);
+        for (int g0 = 0; g0 < G; g0 += 2 * GPW) {
+            if (g0 + GPW < G) gu_load(B, a, blk, G, g0 + GPW, xrow, sxrow, lane);
+            gu_compute(A, g0, G, Cg, Cu);
+            if (g0 + GPW < G) {
+                if (g0 + 2 * GPW < G) gu_load(A, a, blk, G, g0 + 2 * GPW, xrow, sxrow, lane);
+                gu_compute(B, g0 + GPW, G, Cg, Cu);
             }
         }
-        // split-K reduction in fixed warp order
 #pragma unroll
-        for (int j = 0; j < NT8; ++j)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                red[warp][0][j][i][lane] = Cg[j][i];
-                red[warp][1][j][i][lane] = Cu[j][i];
-            }
-        __syncthreads();
-        if (warp == 0) {
-#pragma unroll
-            for (int j = 0; j < NT8; ++j) {
-                float gs[4], us[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    gs[i] = red[0][0][j][i][lane];
-                    us[i] = red[0][1][j][i][lane];
-#pragma unroll
-                    for (int w = 1; w < KS; ++w) {
-                        gs[i] += red[w][0][j][i][lane];
-                        us[i] += red[w][1][j][i][lane];
-                    }
-                }
-                const int r0 = rb * 16 + gq, r1 = r0 + 8;
-#pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-                    const int slot = tile_slot(a, ti, j * 8 + 2 * c + hf);
-                    float g0v = gs[hf], g1v = gs[2 + hf], u0v = us[hf], u1v = us[2 + hf];
-                    if (a.bg) {
-                        g0v += a.bg[(size_t)ti.e * f + r0];
-                        g1v += a.bg[(size_t)ti.e * f + r1];
-                        u0v += a.bu[(size_t)ti.e * f + r0];
-                        u1v += a.bu[(size_t)ti.e * f + r1];
-                    }
-                    const uint16_t h0 = f2bf(act_glu(a.act, g0v, u0v)), h1 = f2bf(act_glu(a.act, g1v, u1v));
-                    float part = slot >= 0 ? bf2f(h0) + bf2f(h1) : 0.f;
-                    part += __shfl_xor_sync(0xffffffffu, part, 4);
-                    part += __shfl_xor_sync(0xffffffffu, part, 8);
-                    part += __shfl_xor_sync(0xffffffffu, part, 16);
-                    if (slot >= 0) {
-                        a.h[(size_t)slot * f + r0] = h0;
-                        a.h[(size_t)slot * f + r1] = h1;
-                        if (gq == 0) a.hsum[(size_t)slot * (f / 16) + rb] = part;
-                    }
-                }
-            }
-        }
-        __syncthreads();
+        for (int j = 0; j < NT8; ++j) gate_up_store<NT8>(a, ti, rb, j, Cg[j], Cu[j], lane);
     }
 }
 
-// ------------------------------------------------------------------ down + combine
-template <int FMT, int NT8, int KS, int GPW>
-__global__ void __launch_bounds__(32 * KS, 4) k_down(ExpArgs a) {
+template <int NT8, int GPW>
+struct DNBatch {
+    uint4 w[GPW];
+    uint2 b[GPW];
+    uint32_t hb[GPW][NT8][8];
+    float4 hs[GPW][NT8][2];
+};
+
+template <int NT8, int GPW>
+__device__ __forceinline__ void dn_load(DNBatch<NT8, GPW> &B, const ExpArgs &a, size_t blk, int G, int g0,
+                                        const uint16_t *const (&hrow)[NT8], const float *const (&hsrow)[NT8][2],
+                                        int lane) {
+    const int gq = lane >> 2;
+#pragma unroll
+    for (int i = 0; i < GPW; ++i) {
+        const int g = min(g0 + i, G - 1);
+        B.w[i] = ld_w(a.dn, blk, G, g, lane);
+        B.b[i] = ld_sb(a.dn, blk, G, g, gq);
+#pragma unroll
+        for (int j = 0; j < NT8; ++j) {
+            load_b16(hrow[j] ? hrow[j] + g * 64 : nullptr, B.hb[i][j]);
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf)
+                B.hs[i][j][hf] = hsrow[j][hf] ? *reinterpret_cast<const float4 *>(hsrow[j][hf] + 4 * g)
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+}
+
+template <int NT8, int GPW>
+__device__ __forceinline__ void dn_compute(const DNBatch<NT8, GPW> &B, int g0, int G, float (&C)[NT8][4]) {
+#pragma unroll
+    for (int i = 0; i < GPW; ++i) {
+        if (g0 + i < G) {
+            float sx[NT8][2];
+#pragma unroll
+            for (int j = 0; j < NT8; ++j)
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    const float4 v = B.hs[i][j][hf];
+                    sx[j][hf] = (v.x + v.y) + (v.z + v.w);
+                }
+            q4_group<NT8>(B.w[i], B.b[i], B.hb[i], sx, C);
+        }
+    }
+}
+
+template <int FMT, int NT8, int GPW>
+__global__ void __launch_bounds__(128) k_down_tiles(ExpArgs a) {
     pdl_launch();
     pdl_wait();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
     const int gq = lane >> 2, c = lane & 3;
-    const int d = a.d, f = a.f, k = a.k;
+    const int d = a.d, f = a.f;
     const int RB = d >> 4, G = f >> 6;
-    const int n_tiles = a.tile_mode ? *a.ntiles : a.T * a.k;
-    const int g_beg = warp * G / KS, g_end = (warp + 1) * G / KS;
-    __shared__ float red[KS][NT8][4][32];
-    __shared__ int s_done[8 * NT8];
-    __shared__ int s_ndone;
-    for (int unit = blockIdx.x; unit < n_tiles * RB; unit += gridDim.x) {
+    const int n_units = *a.ntiles * RB;
+    const int nwarps = gridDim.x * 4;
+    for (int unit = blockIdx.x * 4 + (threadIdx.x >> 5); unit < n_units; unit += nwarps) {
         const int tile = unit / RB, rb = unit - tile * RB;
         const TileInfo ti = tile_info(a, tile);
+        const size_t blk = (size_t)ti.e * RB + rb;
         const uint16_t *hrow[NT8];
         const float *hsrow[NT8][2];
 #pragma unroll
@@ -255,118 +501,30 @@ __global__ void __launch_bounds__(32 * KS, 4) k_down(ExpArgs a) {
                 hsrow[j][hf] = sc_ >= 0 ? a.hsum + (size_t)sc_ * (f / 16) : nullptr;
             }
         }
-        const size_t row0 = (size_t)ti.e * d + rb * 16 + gq;
-        const uint32_t *qd0 = a.dn.q + row0 * (f / 8) + 2 * c, *qd1 = qd0 + 8 * (size_t)(f / 8);
-        const uint32_t *sd0 = a.dn.sb + row0 * G, *sd1 = sd0 + 8 * (size_t)G;
         float C[NT8][4];
 #pragma unroll
         for (int j = 0; j < NT8; ++j)
 #pragma unroll
             for (int i = 0; i < 4; ++i) C[j][i] = 0.f;
-        for (int g0 = g_beg; g0 < g_end; g0 += GPW) {
-            uint2 w0[GPW], w1[GPW];
-            uint32_t b0[GPW], b1[GPW];
-            uint32_t hb[GPW][NT8][8];
-            float4 hs[GPW][NT8][2];
-#pragma unroll
-            for (int i = 0; i < GPW; ++i) {
-                const int g = min(g0 + i, g_end - 1);
-                w0[i] = ld_stream_u2(qd0 + g * 8);
-                w1[i] = ld_stream_u2(qd1 + g * 8);
-                b0[i] = ld_stream_u32(sd0 + g);
-                b1[i] = ld_stream_u32(sd1 + g);
-#pragma unroll
-                for (int j = 0; j < NT8; ++j) {
-                    load_b16(hrow[j] ? hrow[j] + g * 64 : nullptr, hb[i][j]);
-#pragma unroll
-                    for (int hf = 0; hf < 2; ++hf)
-                        hs[i][j][hf] = hsrow[j][hf] ? *reinterpret_cast<const float4 *>(hsrow[j][hf] + 4 * g)
-                                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < GPW; ++i) {
-                if (g0 + i < g_end) {
-                    float sx[NT8][2];
-#pragma unroll
-                    for (int j = 0; j < NT8; ++j)
-#pragma unroll
-                        for (int hf = 0; hf < 2; ++hf) {
-                            const float4 v = hs[i][j][hf];
-                            sx[j][hf] = (v.x + v.y) + (v.z + v.w);
-                        }
-                    q4_group<NT8>(w0[i], w1[i], b0[i], b1[i], hb[i], sx, C);
-                }
+        DNBatch<NT8, GPW> A, B;
+        dn_load(A, a, blk, G, 0, hrow, hsrow, lane);
+        for (int g0 = 0; g0 < G; g0 += 2 * GPW) {
+            if (g0 + GPW < G) dn_load(B, a, blk, G, g0 + GPW, hrow, hsrow, lane);
+            dn_compute(A, g0, G, C);
+            if (g0 + GPW < G) {
+                if (g0 + 2 * GPW < G) dn_load(A, a, blk, G, g0 + 2 * GPW, hrow, hsrow, lane);
+                dn_compute(B, g0 + GPW, G, C);
             }
         }
-#pragma unroll
-        for (int j = 0; j < NT8; ++j)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) red[warp][j][i][lane] = C[j][i];
-        if (threadIdx.x == 0) s_ndone = 0;
-        __syncthreads();
-        if (warp == 0) {
-            const int r0 = rb * 16 + gq, r1 = r0 + 8;
-#pragma unroll
-            for (int j = 0; j < NT8; ++j) {
-                float cs[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    cs[i] = red[0][j][i][lane];
-#pragma unroll
-                    for (int w = 1; w < KS; ++w) cs[i] += red[w][j][i][lane];
-                }
-#pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-                    const int slot = tile_slot(a, ti, j * 8 + 2 * c + hf);
-                    if (slot >= 0) {
-                        const int e_raw = a.idx[slot];
-                        const float wsl = (e_raw >= 0 && e_raw < a.E) ? a.wts[slot] : 0.f;
-                        float v0 = cs[hf], v1 = cs[2 + hf];
-                        if (a.bd) {
-                            v0 += a.bd[(size_t)ti.e * d + r0];
-                            v1 += a.bd[(size_t)ti.e * d + r1];
-                        }
-                        a.yp[(size_t)slot * d + r0] = wsl * v0;
-                        a.yp[(size_t)slot * d + r1] = wsl * v1;
-                    }
-                }
-            }
-            __threadfence();
-        }
-        __syncthreads();
-        // one arrival per slot column on its (token, row block) counter; the last arrival combines
-        if (threadIdx.x < 8 * NT8) {
-            const int slot = tile_slot(a, ti, threadIdx.x);
-            if (slot >= 0) {
-                const int t = slot / k;
-                const unsigned prev = atomicAdd(a.ycnt + (size_t)t * RB + rb, 1u);
-                if (prev == (unsigned)(k - 1)) s_done[atomicAdd(&s_ndone, 1)] = t;
-            }
-        }
-        __syncthreads();
-        const int nd = s_ndone;
-        if (nd > 0) {
-            __threadfence();
-            for (int m = warp; m < nd; m += KS) {
-                const int t = s_done[m];
-                if (lane < 16) {
-                    const int r = rb * 16 + lane;
-                    float acc = 0.f;
-                    for (int j = 0; j < k; ++j) acc += __ldcg(a.yp + ((size_t)t * k + j) * d + r);
-                    if (a.residual) acc += bf2f(a.residual[(size_t)t * d + r]);
-                    a.y[(size_t)t * d + r] = f2bf(acc);
-                }
-                if (lane == 0) a.ycnt[(size_t)t * RB + rb] = 0u;
-            }
-        }
-        __syncthreads();
+        down_store_combine<NT8>(a, ti, rb, C, lane);
     }
 }
 
-template __global__ void k_gate_up<FMT_Q4, 1, 8, 4>(ExpArgs);
-template __global__ void k_gate_up<FMT_Q4, 2, 8, 2>(ExpArgs);
-template __global__ void k_down<FMT_Q4, 1, 4, 4>(ExpArgs);
-template __global__ void k_down<FMT_Q4, 2, 4, 2>(ExpArgs);
+template __global__ void k_gate_up_slots<FMT_Q4, 8, 4>(ExpArgs);
+template __global__ void k_down_slots<FMT_Q4, 4, 4>(ExpArgs);
+template __global__ void k_gate_up_tiles<FMT_Q4, 1, 2>(ExpArgs);
+template __global__ void k_gate_up_tiles<FMT_Q4, 2, 1>(ExpArgs);
+template __global__ void k_down_tiles<FMT_Q4, 1, 2>(ExpArgs);
+template __global__ void k_down_tiles<FMT_Q4, 2, 1>(ExpArgs);
 
 }  // namespace moeb

@@ -78,10 +78,14 @@ __global__ void k_fp4_dequant(const uint32_t *qw, const uint8_t *sc, long rows, 
 __global__ void k_fp4_from_mlx(const uint32_t *wq, const uint8_t *scales, long rows, long K, uint32_t *qw,
                                uint8_t *sc);
 
-template <int FMT, int NT8, int KS, int GPW>
-__global__ void k_gate_up(ExpArgs a);
-template <int FMT, int NT8, int KS, int GPW>
-__global__ void k_down(ExpArgs a);
+template <int FMT, int KS, int GPW>
+__global__ void k_gate_up_slots(ExpArgs a);
+template <int FMT, int KS, int GPW>
+__global__ void k_down_slots(ExpArgs a);
+template <int FMT, int NT8, int GPW>
+__global__ void k_gate_up_tiles(ExpArgs a);
+template <int FMT, int NT8, int GPW>
+__global__ void k_down_tiles(ExpArgs a);
 
 enum { FMT_Q4 = 0, FMT_FP4 = 1 };
 

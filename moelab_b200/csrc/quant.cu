@@ -1,15 +1,21 @@
 // Weight formats: int4 affine g64 and MXFP4, quantized on the GPU into the B200 layout.
 //
-// int4 (reference state: moelab/variants/mlx/metal_q4_moe.py:32-39, W_BITS 4.5):
-//   qw  uint32 [rows][K/8]   word j holds elements 8j..8j+7; nibble p (p < 4) = element 8j+2p,
-//                            nibble p+4 = element 8j+2p+1, so `(w >> 4p) & 0x000F000F` yields the
-//                            consecutive pair (8j+2p, 8j+2p+1) as two bf16 lanes (see q4pair).
-//   sb  uint32 [rows][K/64]  bf16 scale in the low half, bf16 bias in the high half (one load per group).
-// MXFP4 (metal_mxfp4_moe.py:1-12, :448-455, W_BITS 4.25):
-//   qw  uint32 [rows][K/8]   same nibble interleave, E2M1 codes (sign bit 3, exponent bits 1-2, mantissa 0)
-//   sc  uint8  [rows][K/32]  E8M0 scale bytes
+// Reference state (moelab/variants/mlx/metal_q4_moe.py:32-39, W_BITS 4.5; metal_mxfp4_moe.py:448-455, W_BITS
+// 4.25): uint32 [rows][K/8] with element 8j+i at bits 4i of word j, scales (and biases) per group.
+//
+// B200 layout ("fragment-major"): rows are taken in blocks of 16 (rows never straddle experts since
+// N % 16 == 0) and K in groups of 64. Each (row block, group) is one contiguous 512-byte block holding, for
+// warp lane L = 4*gq + c, the uint4 {row gq: word 2c, word 2c+1; row gq+8: word 2c, word 2c+1} - exactly the
+// m16n8k16 A fragments of that lane for the 4 k-steps of the group (the k permutation is described in
+// experts.cu). A warp therefore reads a whole A operand with one coalesced 16-byte load per lane. Inside
+// each word the nibbles are interleaved: nibble p (p < 4) = element 2p, nibble p+4 = element 2p+1, so
+// `(w >> 4p) & 0x000F000F` yields the consecutive pair (2p, 2p+1) as two bf16 lanes (q4pair).
+//   int4  q  uint32 [E*N/16][K/64][32][4]
+//         sb uint32 [E*N/16][K/64][8][2]  (gq, upper) -> bf16 scale | bf16 bias << 16
+//   MXFP4 q  same as int4 (E2M1 codes: sign bit 3, exponent bits 1-2, mantissa bit 0)
+//         sc uint8  [E*N/16][K/64][8][2][2] (gq, upper, 32-half) -> E8M0 byte
 // The quantizers follow the CPU oracle (oracle/moe_oracle.c) operation for operation, so GPU and CPU agree
-// bit for bit on the packed tensors.
+// bit for bit on the codes, scales and biases.
 #include "common.cuh"
 
 namespace moeb {
@@ -23,6 +29,23 @@ __device__ __forceinline__ uint32_t interleave_word(uint32_t nat) {
         r |= ((nat >> (8 * p + 4)) & 0xfu) << (4 * (p + 4));
     }
     return r;
+}
+
+// word index of (row, k-word j) in the fragment-major layout
+__device__ __forceinline__ long fm_word(long row, long j, long K) {
+    const long rb = row >> 4, rr = row & 15, g = j >> 3, jj = j & 7;
+    const long lane = (rr & 7) * 4 + (jj >> 1);
+    return ((rb * (K / 64) + g) * 32 + lane) * 4 + (rr >> 3) * 2 + (jj & 1);
+}
+// index of (row, 64-group g) in the scale|bias array
+__device__ __forceinline__ long fm_sb(long row, long g, long K) {
+    const long rb = row >> 4, rr = row & 15;
+    return ((rb * (K / 64) + g) * 8 + (rr & 7)) * 2 + (rr >> 3);
+}
+// index of (row, 32-group h) in the MXFP4 scale-byte array
+__device__ __forceinline__ long fm_sc(long row, long h, long K) {
+    const long rb = row >> 4, rr = row & 15;
+    return (((rb * (K / 64) + (h >> 1)) * 8 + (rr & 7)) * 2 + (rr >> 3)) * 2 + (h & 1);
 }
 
 __device__ __forceinline__ uint32_t deinterleave_word(uint32_t w) {
@@ -71,7 +94,6 @@ __global__ void k_q4_quantize(const uint16_t *__restrict__ w, long rows, long K,
         scale = __fdiv_rn(edge, q0);
         bias = edge;
     }
-    uint32_t *dst = qw + r * (K / 8) + g * 8;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         uint32_t nat = 0;
@@ -81,9 +103,9 @@ __global__ void k_q4_quantize(const uint16_t *__restrict__ w, long rows, long K,
             q = q < 0.0f ? 0.0f : (q > 15.0f ? 15.0f : q);
             nat |= ((uint32_t)q & 0xfu) << (4 * i);
         }
-        dst[j] = interleave_word(nat);
+        qw[fm_word(r, g * 8 + j, K)] = interleave_word(nat);
     }
-    sb[r * ng + g] = (uint32_t)f2bf(scale) | ((uint32_t)f2bf(bias) << 16);
+    sb[fm_sb(r, g, K)] = (uint32_t)f2bf(scale) | ((uint32_t)f2bf(bias) << 16);
 }
 
 // fp32 dequant in natural element order: w = fmaf(scale, q, bias). One thread per packed word.
@@ -93,8 +115,8 @@ __global__ void k_q4_dequant(const uint32_t *__restrict__ qw, const uint32_t *__
     const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= rows * nw) return;
     const long r = gid / nw, j = gid - r * nw;
-    const uint32_t nat = deinterleave_word(qw[gid]);
-    const uint32_t s_b = sb[r * (K / 64) + j / 8];
+    const uint32_t nat = deinterleave_word(qw[fm_word(r, j, K)]);
+    const uint32_t s_b = sb[fm_sb(r, j / 8, K)];
     const float s = bf16lo(s_b), b = bf16hi(s_b);
     float4 o0, o1;
     float *o = reinterpret_cast<float *>(&o0);
@@ -115,11 +137,11 @@ __global__ void k_q4_from_mlx(const uint32_t *__restrict__ wq, const uint16_t *_
     const long nw = K / 8;
     const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= rows * nw) return;
-    qw[gid] = interleave_word(wq[gid]);
     const long r = gid / nw, j = gid - r * nw;
+    qw[fm_word(r, j, K)] = interleave_word(wq[gid]);
     if ((j & 7) == 0) {
         const long gi = r * (K / 64) + j / 8;
-        sb[gi] = (uint32_t)scales[gi] | ((uint32_t)biases[gi] << 16);
+        sb[fm_sb(r, j / 8, K)] = (uint32_t)scales[gi] | ((uint32_t)biases[gi] << 16);
     }
 }
 
@@ -165,15 +187,14 @@ __global__ void k_fp4_quantize(const uint16_t *__restrict__ w, long rows, long K
     }
     e = e < -127 ? -127 : (e > 127 ? 127 : e);
     const float inv = ldexpf(1.0f, -e);
-    uint32_t *dst = qw + r * (K / 8) + g * 4;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         uint32_t nat = 0;
 #pragma unroll
         for (int i = 0; i < 8; ++i) nat |= e2m1_round(__fmul_rn(v[8 * j + i], inv)) << (4 * i);
-        dst[j] = interleave_word(nat);
+        qw[fm_word(r, g * 4 + j, K)] = interleave_word(nat);
     }
-    sc[r * ng + g] = (uint8_t)(e + 127);
+    sc[fm_sc(r, g, K)] = (uint8_t)(e + 127);
 }
 
 __device__ __forceinline__ float e2m1_value(uint32_t c) {
@@ -188,8 +209,8 @@ __global__ void k_fp4_dequant(const uint32_t *__restrict__ qw, const uint8_t *__
     const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= rows * nw) return;
     const long r = gid / nw, j = gid - r * nw;
-    const uint32_t nat = deinterleave_word(qw[gid]);
-    const int ex = (int)sc[r * (K / 32) + j / 4] - 127;
+    const uint32_t nat = deinterleave_word(qw[fm_word(r, j, K)]);
+    const int ex = (int)sc[fm_sc(r, j / 4, K)] - 127;
     float *dst = out + r * K + j * 8;
 #pragma unroll
     for (int i = 0; i < 8; ++i) dst[i] = ldexpf(e2m1_value((nat >> (4 * i)) & 0xfu), ex);
@@ -200,9 +221,9 @@ __global__ void k_fp4_from_mlx(const uint32_t *__restrict__ wq, const uint8_t *_
     const long nw = K / 8;
     const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= rows * nw) return;
-    qw[gid] = interleave_word(wq[gid]);
     const long r = gid / nw, j = gid - r * nw;
-    if ((j & 3) == 0) sc[r * (K / 32) + j / 4] = scales[r * (K / 32) + j / 4];
+    qw[fm_word(r, j, K)] = interleave_word(wq[gid]);
+    if ((j & 3) == 0) sc[fm_sc(r, j / 4, K)] = scales[r * (K / 32) + j / 4];
 }
 
 }  // namespace moeb

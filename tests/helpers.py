@@ -31,6 +31,40 @@ def deinterleave_words(w):
     return out
 
 
+def fm_q_index(rows, K):
+    """Flat word index in the fragment-major layout of every (row, k-word j) of a natural [rows, K/8] array."""
+    r = np.arange(rows)[:, None]
+    j = np.arange(K // 8)[None, :]
+    rb, rr, g, jj = r // 16, r % 16, j // 8, j % 8
+    lane = (rr % 8) * 4 + jj // 2
+    return ((rb * (K // 64) + g) * 32 + lane) * 4 + (rr // 8) * 2 + (jj % 2)
+
+
+def to_b200_q4(qw, s, b):
+    """oracle (natural mlx) int4 state -> flat B200 arrays (q words, sb words)."""
+    rows, K = qw.shape[0], qw.shape[1] * 8
+    q = np.zeros(rows * K // 8, np.uint32)
+    q[fm_q_index(rows, K)] = interleave_words(qw)
+    r = np.arange(rows)[:, None]
+    g = np.arange(K // 64)[None, :]
+    sbi = ((r // 16 * (K // 64) + g) * 8 + (r % 16) % 8) * 2 + (r % 16) // 8
+    sb = np.zeros(rows * K // 64, np.uint32)
+    sb[sbi] = s.astype(np.uint32) | (b.astype(np.uint32) << 16)
+    return q, sb
+
+
+def to_b200_fp4(qw, sc):
+    rows, K = qw.shape[0], qw.shape[1] * 8
+    q = np.zeros(rows * K // 8, np.uint32)
+    q[fm_q_index(rows, K)] = interleave_words(qw)
+    r = np.arange(rows)[:, None]
+    h = np.arange(K // 32)[None, :]
+    sci = (((r // 16 * (K // 64) + h // 2) * 8 + (r % 16) % 8) * 2 + (r % 16) // 8) * 2 + h % 2
+    out = np.zeros(rows * K // 32, np.uint8)
+    out[sci] = sc
+    return q, out
+
+
 def u32(t):
     return t.detach().cpu().numpy().view(np.uint32)
 

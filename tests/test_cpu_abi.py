@@ -50,3 +50,18 @@ def test_bad_shape_is_rejected_before_any_device_work():
         _lib.call("moeb_experts_q4", *([None] * 10), 8, 8, 4, 100, 256, 8, 2, 0, 0, None, None, None, 0, None)
     with pytest.raises(_lib.MoebError, match="k must be"):
         _lib.call("moeb_experts_q4", *([None] * 10), 8, 8, 4, 128, 256, 8, 9, 0, 0, None, None, None, 0, None)
+
+
+def test_fragment_major_layout_is_a_permutation():
+    """The numpy model of the B200 weight layout (used by the bit-exact GPU tests) is a bijection."""
+    import numpy as np
+
+    from helpers import fm_q_index, to_b200_q4
+    for rows, K in [(16, 64), (48, 256), (32, 2880 // 64 * 64)]:
+        idx = fm_q_index(rows, K).ravel()
+        assert np.array_equal(np.sort(idx), np.arange(rows * K // 8))
+    rng = np.random.default_rng(0)
+    qw = rng.integers(0, 2**32, (32, 64), dtype=np.uint32)
+    s = rng.integers(0, 2**16, (32, 8), dtype=np.uint16)
+    q, sb = to_b200_q4(qw, s, s)
+    assert q.shape == (32 * 64,) and sb.shape == (32 * 8,)

@@ -10,8 +10,8 @@ import pytest
 import torch
 
 import oracle
-from helpers import (Q4_VARIANT, assert_close, deinterleave_words, interleave_words, load_variant,
-                     problem_tensors, ref_from_state, u32)
+from helpers import (Q4_VARIANT, assert_close, load_variant, problem_tensors, ref_from_state, to_b200_fp4,
+                     to_b200_q4, u32)
 from moelab_b200 import ops
 from moelab_b200.shapes import MoEShape
 
@@ -34,7 +34,7 @@ def policy(request, mod, monkeypatch):
 
 
 # ------------------------------------------------------------------ formats
-@pytest.mark.parametrize("rows,K", [(8, 64), (96, 256), (130, 2048), (7, 1408)])
+@pytest.mark.parametrize("rows,K", [(16, 64), (96, 256), (144, 2048), (16, 1408)])
 def test_quantize_q4_bit_exact(rows, K):
     g = torch.Generator(device="cuda").manual_seed(rows + K)
     w = (torch.randn(rows, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
@@ -42,9 +42,9 @@ def test_quantize_q4_bit_exact(rows, K):
     w[1, :64] = torch.linspace(-1, 1, 64, device="cuda").to(torch.bfloat16)
     q, sb = ops.quantize_q4(w)
     qw, s, b = oracle.q4_quantize(w)
-    np.testing.assert_array_equal(u32(q), interleave_words(qw))
-    np.testing.assert_array_equal(u32(sb) & 0xFFFF, s)
-    np.testing.assert_array_equal(u32(sb) >> 16, b)
+    ref_q, ref_sb = to_b200_q4(qw, s, b)
+    np.testing.assert_array_equal(u32(q).reshape(-1), ref_q)
+    np.testing.assert_array_equal(u32(sb).reshape(-1), ref_sb)
     np.testing.assert_array_equal(ops.dequant_q4(q, sb).cpu().numpy(), oracle.q4_dequant(qw, s, b))
 
 
@@ -56,10 +56,10 @@ def test_q4_from_mlx_layout():
     q, sb = ops.q4_from_mlx(dev(qw, np.int32), dev(s, np.int16).view(torch.bfloat16), dev(b, np.int16).view(torch.bfloat16))
     q2, sb2 = ops.quantize_q4(w)
     assert torch.equal(q, q2) and torch.equal(sb, sb2)
-    np.testing.assert_array_equal(deinterleave_words(u32(q)), qw)
+    np.testing.assert_array_equal(u32(q).reshape(-1), to_b200_q4(qw, s, b)[0])
 
 
-@pytest.mark.parametrize("rows,K", [(8, 64), (64, 2880), (33, 256)])
+@pytest.mark.parametrize("rows,K", [(16, 64), (64, 2880), (48, 256)])
 @pytest.mark.parametrize("mult", [1.0, 256.0])
 def test_quantize_mxfp4_bit_exact(rows, K, mult):
     g = torch.Generator(device="cuda").manual_seed(rows * 7 + K)
@@ -67,8 +67,9 @@ def test_quantize_mxfp4_bit_exact(rows, K, mult):
     w[0, :32] = 0
     q, sc = ops.quantize_mxfp4(w)
     qw, s = oracle.mxfp4_quantize(w)
-    np.testing.assert_array_equal(u32(q), interleave_words(qw))
-    np.testing.assert_array_equal(sc.cpu().numpy(), s)
+    ref_q, ref_sc = to_b200_fp4(qw, s)
+    np.testing.assert_array_equal(u32(q).reshape(-1), ref_q)
+    np.testing.assert_array_equal(sc.cpu().numpy().reshape(-1), ref_sc)
     np.testing.assert_array_equal(ops.dequant_mxfp4(q, sc).cpu().numpy(), oracle.mxfp4_dequant(qw, s))
     if mult > 1:
         assert int(s.max()) >= 129  # the large-E8M0 regime of tests/test_mxfp4_large_scales.py
@@ -303,6 +304,12 @@ def test_layer_qwen3_shape(mod, policy, T):
     # residual fused into the combine: y2 = bf16(x + moe(x))
     y2 = mod.layer(st, x, gate, sh.k, residual=x)
     assert_close(y2, ref_from_state(mod, st, x, idx, wts) + x.float().cpu().numpy())
+
+
+def test_rows_not_multiple_of_16_rejected():
+    w = torch.zeros(8, 64, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ops._lib.MoebError, match="multiple of 16"):
+        ops.quantize_q4(w)
 
 
 def test_invalid_expert_ids_flagged(mod):
