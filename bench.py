@@ -239,9 +239,11 @@ def measure_T(v, layers, T, ws, rank, n_steps, seed):
     idxs = routing_of_chain(v, layers, xs, n_steps)
     nb = layer_bytes(idxs, T)
     us = t / n_steps * 1e6
+    r_us, gu_us, dn_us, _ = stage_times(v, layers, xs, len(layers))
     return {"T": T, "us_per_call": round(us, 3), "gbs": round(sum(nb) / t / 1e9, 1),
             "unique_experts": round(float(np.mean([torch.unique(i).numel() for i in idxs])), 2),
-            "tokens_per_s": round(T * n_steps / t, 1)}
+            "tokens_per_s": round(T * n_steps / t, 1),
+            "stage_us": [round(statistics.mean(x), 2) for x in (r_us, gu_us, dn_us)]}
 
 
 # ------------------------------------------------------------------ CPU baseline (reference's CPU torch path)

@@ -157,8 +157,23 @@ ExpLaunch pick_kernels(int fmt, int policy, int d, int f) {
         return {k_gate_up_slots<FMT_Q4, 8, 4>, k_down_slots<FMT_Q4, 4, 4>, 256, 128, (size_t)d * 2,
                 (size_t)f * 2 + (size_t)f / 16 * 4, false};
     if (policy == MOEB_POLICY_TILES16)
-        return {k_gate_up_tiles<FMT_Q4, 2, 1>, k_down_tiles<FMT_Q4, 2, 1>, 128, 128, 0, 0, true};
-    return {k_gate_up_tiles<FMT_Q4, 1, 2>, k_down_tiles<FMT_Q4, 1, 2>, 128, 128, 0, 0, true};
+        return {k_gate_up_tiles<FMT_Q4, 2, 3, 2>, k_down_tiles<FMT_Q4, 2, 4, 1>, 128, 128, gate_up_tiles_smem(2, 3, 2),
+                down_tiles_smem(2, 4, 1), true};
+    return {k_gate_up_tiles<FMT_Q4, 1, 4, 2>, k_down_tiles<FMT_Q4, 1, 4, 2>, 128, 128, gate_up_tiles_smem(1, 4, 2),
+            down_tiles_smem(1, 4, 2), true};
+}
+
+// Opt a kernel in to more than 48 KB of dynamic shared memory (once per kernel).
+bool allow_smem(const void *fn, size_t bytes) {
+    if (bytes <= 48 * 1024) return true;
+    static std::mutex mu;
+    static std::unordered_map<const void *, size_t> done;
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = done.find(fn);
+    if (it != done.end() && it->second >= bytes) return true;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess) return false;
+    done[fn] = bytes;
+    return true;
 }
 
 int grid_for(void (*kern)(ExpArgs), int threads, size_t smem, long units, bool per_warp) {
@@ -174,7 +189,10 @@ int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaS
     const long max_tiles = a.tile_mode ? std::min<long>(TK, (long)a.E + TK / nt) : TK;
     ExpLaunch K = pick_kernels(fmt, policy, a.d, a.f);
     if (!K.gu) return fail(MOEB_EUNSUP, "format not supported%s");
-    if (K.gu_smem > 48 * 1024 || K.dn_smem > 48 * 1024) return fail(MOEB_EINVAL, "d or f too large for the decode kernels%s");
+    if (!K.per_warp && (K.gu_smem > 48 * 1024 || K.dn_smem > 48 * 1024))
+        return fail(MOEB_EINVAL, "d or f too large for the decode kernels%s");
+    if (!allow_smem((const void *)K.gu, K.gu_smem) || !allow_smem((const void *)K.dn, K.dn_smem))
+        return check_launch("cudaFuncSetAttribute");
     {
         const int grid = grid_for(K.gu, K.gu_threads, K.gu_smem, max_tiles * (a.f / 16), K.per_warp);
         if (launch(K.gu, dim3(grid), dim3(K.gu_threads), K.gu_smem, st, a) != cudaSuccess)
@@ -192,15 +210,15 @@ int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaS
     return MOEB_OK;
 }
 
-template <int TPB>
+template <int TPB, int U>
 void (*router_kernel(int E))(RouterArgs) {
     const int J = (E + 31) / 32;
-    if (J <= 1) return k_router<TPB, 1>;
-    if (J <= 2) return k_router<TPB, 2>;
-    if (J <= 4) return k_router<TPB, 4>;
-    if (J <= 8) return k_router<TPB, 8>;
-    if (J <= 16) return k_router<TPB, 16>;
-    return k_router<TPB, 32>;
+    if (J <= 1) return k_router<TPB, 1, U>;
+    if (J <= 2) return k_router<TPB, 2, U>;
+    if (J <= 4) return k_router<TPB, 4, U>;
+    if (J <= 8) return k_router<TPB, 8, U>;
+    if (J <= 16) return k_router<TPB, 16, U>;
+    return k_router<TPB, 32, U>;
 }
 
 int launch_router(const void *x, const void *wg, const void *bias, int T, int d, int E, int k, int norm,
@@ -223,10 +241,10 @@ int launch_router(const void *x, const void *wg, const void *bias, int T, int d,
     r.tiles = tiles ? at<int4>(ws, L.tiles) : nullptr;
     r.ntiles = at<int>(ws, L.ntiles);
     r.sorted = at<int>(ws, L.sorted);
-    const size_t smem = tiles ? 12 * (size_t)E : 0;
-    // tokens per CTA: 1 for decode-sized T (more CTAs in flight), 4 above
-    const int tpb = T <= 8 ? 1 : 4;
-    void (*kern)(RouterArgs) = tpb == 1 ? router_kernel<1>(E) : router_kernel<4>(E);
+    const size_t smem = tiles ? 8 * (size_t)E : 0;
+    // tokens per CTA: 1 up to T = 64 (more CTAs in flight, the gate row re-read from L2), 4 above
+    const int tpb = T <= 64 ? 1 : 4;
+    void (*kern)(RouterArgs) = tpb == 1 ? router_kernel<1, 8>(E) : router_kernel<4, 4>(E);
     if (launch(kern, dim3((E + 3) / 4, (T + tpb - 1) / tpb), dim3(128), smem, st, r) != cudaSuccess)
         return check_launch("router");
     return MOEB_OK;

@@ -64,6 +64,24 @@ MOEB_DEV uint32_t q4pair(uint32_t w, int p) {
     return r;
 }
 
+// Ampere-style asynchronous global->shared copies (per lane, no register staging). A false predicate copies
+// nothing and zero-fills the destination; the source must still be a valid address.
+MOEB_DEV void cp_async16(void *smem, const void *gmem, bool pred = true) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(pred ? 16 : 0) : "memory");
+}
+MOEB_DEV void cp_async8(void *smem, const void *gmem, bool pred = true) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(s), "l"(gmem), "r"(pred ? 8 : 0) : "memory");
+}
+MOEB_DEV void cp_async4(void *smem, const void *gmem, bool pred = true) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(s), "l"(gmem), "r"(pred ? 4 : 0) : "memory");
+}
+MOEB_DEV void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+MOEB_DEV void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 MOEB_DEV float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

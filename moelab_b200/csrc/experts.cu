@@ -339,192 +339,248 @@ __global__ void __launch_bounds__(32 * KS, 8) k_down_slots(ExpArgs a) {
 }
 
 // ================================================================== tile mode
-// One warp per (tile, 16-row block) over the whole K; loads run one GPW-group batch ahead of the MMAs.
-template <int NT8, int GPW>
-struct GUBatch {
-    uint4 wg[GPW], wu[GPW];
-    uint2 bg[GPW], bu[GPW];
-    uint32_t xb[GPW][NT8][8];
-    float sx[GPW][NT8][2];
+// One warp per (tile, 16-row block) over the whole K. Each warp owns a ring of NS shared-memory stages of GPS
+// groups; every lane cp.async-copies its own fragment bytes (weights, scale|bias, activations, group sums) into
+// a lane-major slot, so NS-1 stages stay in flight without holding registers and the MMA loop reads
+// shared memory only. The stage sequence runs across unit boundaries (the next unit's first groups are
+// already loading while the current unit finishes).
+template <int NT8>
+struct GUFields {  // uint4 slots per lane per group
+    static constexpr int W_G = 0, W_U = 1, SB = 2, X = 3, SX = 3 + 2 * NT8, N = 3 + 2 * NT8 + (NT8 + 1) / 2;
+};
+template <int NT8>
+struct DNFields {
+    static constexpr int W = 0, SB = 1, H = 2, HS = 2 + 2 * NT8, N = 2 + 4 * NT8;
 };
 
-template <int NT8, int GPW>
-__device__ __forceinline__ void gu_load(GUBatch<NT8, GPW> &B, const ExpArgs &a, size_t blk, int G, int g0,
-                                        const uint16_t *const (&xrow)[NT8], const float *const (&sxrow)[NT8][2],
-                                        int lane) {
-    const int gq = lane >> 2;
+// Per-lane view of the producer's current unit.
+template <int NT8>
+struct UnitSrc {
+    int unit = -1;
+    TileInfo ti;
+    size_t blk;
+    const uint16_t *row[NT8];     // activation row of B column gq of each n8 tile (x or h), or null
+    const float *srow[NT8][2];    // group-sum rows of C columns 2c, 2c+1 (xsum or hsum), or null
+};
+
+template <int NT8, bool DOWN>
+__device__ __forceinline__ void unit_src(UnitSrc<NT8> &u, const ExpArgs &a, int unit, int RB, int lane) {
+    const int gq = lane >> 2, c = lane & 3;
+    u.unit = unit;
+    const int tile = unit / RB, rb = unit - tile * RB;
+    u.ti = tile_info(a, tile);
+    u.blk = (size_t)u.ti.e * RB + rb;
 #pragma unroll
-    for (int i = 0; i < GPW; ++i) {
-        const int g = min(g0 + i, G - 1);
-        B.wg[i] = ld_w(a.g, blk, G, g, lane);
-        B.wu[i] = ld_w(a.u, blk, G, g, lane);
-        B.bg[i] = ld_sb(a.g, blk, G, g, gq);
-        B.bu[i] = ld_sb(a.u, blk, G, g, gq);
+    for (int j = 0; j < NT8; ++j) {
+        const int sb_ = tile_slot(a, u.ti, j * 8 + gq);
+        if (DOWN) u.row[j] = sb_ >= 0 ? a.h + (size_t)sb_ * a.f + 16 * c : nullptr;
+        else u.row[j] = sb_ >= 0 ? a.x + (size_t)(sb_ / a.k) * a.d + 16 * c : nullptr;
 #pragma unroll
-        for (int j = 0; j < NT8; ++j) {
-            load_b16(xrow[j] ? xrow[j] + g * 64 : nullptr, B.xb[i][j]);
-            B.sx[i][j][0] = sxrow[j][0] ? sxrow[j][0][g] : 0.f;
-            B.sx[i][j][1] = sxrow[j][1] ? sxrow[j][1][g] : 0.f;
+        for (int hf = 0; hf < 2; ++hf) {
+            const int sc_ = tile_slot(a, u.ti, j * 8 + 2 * c + hf);
+            if (DOWN) u.srow[j][hf] = sc_ >= 0 ? a.hsum + (size_t)sc_ * (a.f / 16) : nullptr;
+            else u.srow[j][hf] = sc_ >= 0 ? a.xsum + (size_t)(sc_ / a.k) * (a.d / 64) : nullptr;
         }
     }
 }
 
-template <int NT8, int GPW>
-__device__ __forceinline__ void gu_compute(const GUBatch<NT8, GPW> &B, int g0, int G, float (&Cg)[NT8][4],
-                                           float (&Cu)[NT8][4]) {
-#pragma unroll
-    for (int i = 0; i < GPW; ++i) {
-        if (g0 + i < G) {
-            q4_group<NT8>(B.wg[i], B.bg[i], B.xb[i], B.sx[i], Cg);
-            q4_group<NT8>(B.wu[i], B.bu[i], B.xb[i], B.sx[i], Cu);
-        }
-    }
-}
-
-template <int FMT, int NT8, int GPW>
+template <int FMT, int NT8, int NS, int GPS>
 __global__ void __launch_bounds__(128) k_gate_up_tiles(ExpArgs a) {
+    using FL = GUFields<NT8>;
     pdl_launch();
     pdl_wait();
-    const int lane = threadIdx.x & 31;
-    const int gq = lane >> 2, c = lane & 3;
-    const int d = a.d, f = a.f;
-    const int RB = f >> 4, G = d >> 6;
-    const int n_units = *a.ntiles * RB;
-    const int nwarps = gridDim.x * 4;
-    for (int unit = blockIdx.x * 4 + (threadIdx.x >> 5); unit < n_units; unit += nwarps) {
-        const int tile = unit / RB, rb = unit - tile * RB;
-        const TileInfo ti = tile_info(a, tile);
-        const size_t blk = (size_t)ti.e * RB + rb;
-        if (a.dn_prefetch) prefetch_down(a, ti.e, rb, RB, lane);
-        const uint16_t *xrow[NT8];
-        const float *sxrow[NT8][2];
-#pragma unroll
-        for (int j = 0; j < NT8; ++j) {
-            const int sb_ = tile_slot(a, ti, j * 8 + gq);
-            xrow[j] = sb_ >= 0 ? a.x + (size_t)(sb_ / a.k) * d + 16 * c : nullptr;
-#pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-                const int sc_ = tile_slot(a, ti, j * 8 + 2 * c + hf);
-                sxrow[j][hf] = sc_ >= 0 ? a.xsum + (size_t)(sc_ / a.k) * G : nullptr;
-            }
-        }
-        float Cg[NT8][4], Cu[NT8][4];
-#pragma unroll
-        for (int j = 0; j < NT8; ++j)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) Cg[j][i] = Cu[j][i] = 0.f;
-        GUBatch<NT8, GPW> A, B;
-        gu_load(A, a, blk, G, 0, xrow, sxrow, lane);
-        for (int g0 = 0; g0 < G; g0 += 2 * GPW) {
-            if (g0 + GPW < G) gu_load(B, a, blk, G, g0 + GPW, xrow, sxrow, lane);
-            gu_compute(A, g0, G, Cg, Cu);
-            if (g0 + GPW < G) {
-                if (g0 + 2 * GPW < G) gu_load(A, a, blk, G, g0 + 2 * GPW, xrow, sxrow, lane);
-                gu_compute(B, g0 + GPW, G, Cg, Cu);
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < NT8; ++j) gate_up_store<NT8>(a, ti, rb, j, Cg[j], Cu[j], lane);
-    }
-}
-
-template <int NT8, int GPW>
-struct DNBatch {
-    uint4 w[GPW];
-    uint2 b[GPW];
-    uint32_t hb[GPW][NT8][8];
-    float4 hs[GPW][NT8][2];
-};
-
-template <int NT8, int GPW>
-__device__ __forceinline__ void dn_load(DNBatch<NT8, GPW> &B, const ExpArgs &a, size_t blk, int G, int g0,
-                                        const uint16_t *const (&hrow)[NT8], const float *const (&hsrow)[NT8][2],
-                                        int lane) {
+    extern __shared__ uint4 smem_ring[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int gq = lane >> 2;
+    const int RB = a.f >> 4, G = a.d >> 6;
+    const int SPU = (G + GPS - 1) / GPS;  // stages per unit
+    const int n_units = *a.ntiles * RB;
+    const int w0 = blockIdx.x * 4 + warp, nw = gridDim.x * 4;
+    const int my_units = w0 < n_units ? (n_units - w0 + nw - 1) / nw : 0;
+    const int total = my_units * SPU;
+    uint4 *ring = smem_ring + (size_t)warp * NS * GPS * FL::N * 32;
+    UnitSrc<NT8> P;  // producer's unit
+    auto issue = [&](int k) {
+        if (k < total) {
+            const int unit = w0 + (k / SPU) * nw, gb = (k % SPU) * GPS;
+            if (unit != P.unit) {
+                unit_src<NT8, false>(P, a, unit, RB, lane);
+                if (gb == 0 && a.dn_prefetch) prefetch_down(a, P.ti.e, unit % RB, RB, lane);
+            }
+            uint4 *st = ring + (size_t)(k % NS) * GPS * FL::N * 32;
 #pragma unroll
-    for (int i = 0; i < GPW; ++i) {
-        const int g = min(g0 + i, G - 1);
-        B.w[i] = ld_w(a.dn, blk, G, g, lane);
-        B.b[i] = ld_sb(a.dn, blk, G, g, gq);
+            for (int i = 0; i < GPS; ++i) {
+                const int g = min(gb + i, G - 1);
+                uint4 *sl = st + i * FL::N * 32 + lane;
+                cp_async16(sl + FL::W_G * 32, a.g.q + ((P.blk * G + g) * 32 + lane) * 4);
+                cp_async16(sl + FL::W_U * 32, a.u.q + ((P.blk * G + g) * 32 + lane) * 4);
+                cp_async8(sl + FL::SB * 32, a.g.sb + ((P.blk * G + g) * 8 + gq) * 2);
+                cp_async8(reinterpret_cast<uint2 *>(sl + FL::SB * 32) + 1, a.u.sb + ((P.blk * G + g) * 8 + gq) * 2);
 #pragma unroll
-        for (int j = 0; j < NT8; ++j) {
-            load_b16(hrow[j] ? hrow[j] + g * 64 : nullptr, B.hb[i][j]);
+                for (int j = 0; j < NT8; ++j) {
+                    const bool ok = P.row[j] != nullptr;
+                    const uint16_t *src = ok ? P.row[j] + g * 64 : a.x;
+                    cp_async16(sl + (FL::X + 2 * j) * 32, src, ok);
+                    cp_async16(sl + (FL::X + 2 * j + 1) * 32, src + 8, ok);
+                    float *sxd = reinterpret_cast<float *>(sl + (FL::SX + j / 2) * 32) + 2 * (j & 1);
+                    cp_async4(sxd, P.srow[j][0] ? P.srow[j][0] + g : a.xsum, P.srow[j][0] != nullptr);
+                    cp_async4(sxd + 1, P.srow[j][1] ? P.srow[j][1] + g : a.xsum, P.srow[j][1] != nullptr);
+                }
+            }
+        }
+        cp_commit();
+    };
+    for (int k = 0; k < NS - 1; ++k) issue(k);
+    float Cg[NT8][4], Cu[NT8][4];
 #pragma unroll
-            for (int hf = 0; hf < 2; ++hf)
-                B.hs[i][j][hf] = hsrow[j][hf] ? *reinterpret_cast<const float4 *>(hsrow[j][hf] + 4 * g)
-                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < NT8; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) Cg[j][i] = Cu[j][i] = 0.f;
+    for (int k = 0; k < total; ++k) {
+        issue(k + NS - 1);
+        cp_wait<NS - 1>();
+        __syncwarp();
+        const uint4 *st = ring + (size_t)(k % NS) * GPS * FL::N * 32;
+        const int gb = (k % SPU) * GPS;
+#pragma unroll
+        for (int i = 0; i < GPS; ++i) {
+            if (gb + i < G) {
+                const uint4 *sl = st + i * FL::N * 32 + lane;
+                const uint4 wg = sl[FL::W_G * 32], wu = sl[FL::W_U * 32], sb = sl[FL::SB * 32];
+                uint32_t xb[NT8][8];
+                float sx[NT8][2];
+#pragma unroll
+                for (int j = 0; j < NT8; ++j) {
+                    const uint4 x0 = sl[(FL::X + 2 * j) * 32], x1 = sl[(FL::X + 2 * j + 1) * 32];
+                    xb[j][0] = x0.x; xb[j][1] = x0.y; xb[j][2] = x0.z; xb[j][3] = x0.w;
+                    xb[j][4] = x1.x; xb[j][5] = x1.y; xb[j][6] = x1.z; xb[j][7] = x1.w;
+                    const float *sxp = reinterpret_cast<const float *>(sl + (FL::SX + j / 2) * 32) + 2 * (j & 1);
+                    sx[j][0] = sxp[0];
+                    sx[j][1] = sxp[1];
+                }
+                q4_group<NT8>(wg, make_uint2(sb.x, sb.y), xb, sx, Cg);
+                q4_group<NT8>(wu, make_uint2(sb.z, sb.w), xb, sx, Cu);
+            }
+        }
+        __syncwarp();  // the slot is refilled by a later issue()
+        if (k % SPU == SPU - 1) {
+            const int unit = w0 + (k / SPU) * nw;
+            const int tile = unit / RB, rb = unit - tile * RB;
+            const TileInfo ti = tile_info(a, tile);
+#pragma unroll
+            for (int j = 0; j < NT8; ++j) {
+                gate_up_store<NT8>(a, ti, rb, j, Cg[j], Cu[j], lane);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) Cg[j][i] = Cu[j][i] = 0.f;
+            }
         }
     }
+    cp_wait<0>();
 }
 
-template <int NT8, int GPW>
-__device__ __forceinline__ void dn_compute(const DNBatch<NT8, GPW> &B, int g0, int G, float (&C)[NT8][4]) {
+template <int FMT, int NT8, int NS, int GPS>
+__global__ void __launch_bounds__(128) k_down_tiles(ExpArgs a) {
+    using FL = DNFields<NT8>;
+    pdl_launch();
+    pdl_wait();
+    extern __shared__ uint4 smem_ring[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gq = lane >> 2;
+    const int RB = a.d >> 4, G = a.f >> 6;
+    const int SPU = (G + GPS - 1) / GPS;
+    const int n_units = *a.ntiles * RB;
+    const int w0 = blockIdx.x * 4 + warp, nw = gridDim.x * 4;
+    const int my_units = w0 < n_units ? (n_units - w0 + nw - 1) / nw : 0;
+    const int total = my_units * SPU;
+    uint4 *ring = smem_ring + (size_t)warp * NS * GPS * FL::N * 32;
+    UnitSrc<NT8> P;
+    auto issue = [&](int k) {
+        if (k < total) {
+            const int unit = w0 + (k / SPU) * nw, gb = (k % SPU) * GPS;
+            if (unit != P.unit) unit_src<NT8, true>(P, a, unit, RB, lane);
+            uint4 *st = ring + (size_t)(k % NS) * GPS * FL::N * 32;
 #pragma unroll
-    for (int i = 0; i < GPW; ++i) {
-        if (g0 + i < G) {
-            float sx[NT8][2];
+            for (int i = 0; i < GPS; ++i) {
+                const int g = min(gb + i, G - 1);
+                uint4 *sl = st + i * FL::N * 32 + lane;
+                cp_async16(sl + FL::W * 32, a.dn.q + ((P.blk * G + g) * 32 + lane) * 4);
+                cp_async8(sl + FL::SB * 32, a.dn.sb + ((P.blk * G + g) * 8 + gq) * 2);
+#pragma unroll
+                for (int j = 0; j < NT8; ++j) {
+                    const bool ok = P.row[j] != nullptr;
+                    const uint16_t *src = ok ? P.row[j] + g * 64 : a.h;
+                    cp_async16(sl + (FL::H + 2 * j) * 32, src, ok);
+                    cp_async16(sl + (FL::H + 2 * j + 1) * 32, src + 8, ok);
+#pragma unroll
+                    for (int hf = 0; hf < 2; ++hf) {
+                        const bool okh = P.srow[j][hf] != nullptr;
+                        cp_async16(sl + (FL::HS + 2 * j + hf) * 32, okh ? P.srow[j][hf] + 4 * g : a.hsum, okh);
+                    }
+                }
+            }
+        }
+        cp_commit();
+    };
+    for (int k = 0; k < NS - 1; ++k) issue(k);
+    float C[NT8][4];
+#pragma unroll
+    for (int j = 0; j < NT8; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) C[j][i] = 0.f;
+    for (int k = 0; k < total; ++k) {
+        issue(k + NS - 1);
+        cp_wait<NS - 1>();
+        __syncwarp();
+        const uint4 *st = ring + (size_t)(k % NS) * GPS * FL::N * 32;
+        const int gb = (k % SPU) * GPS;
+#pragma unroll
+        for (int i = 0; i < GPS; ++i) {
+            if (gb + i < G) {
+                const uint4 *sl = st + i * FL::N * 32 + lane;
+                const uint4 w = sl[FL::W * 32];
+                const uint2 sb = *reinterpret_cast<const uint2 *>(sl + FL::SB * 32);
+                uint32_t hb[NT8][8];
+                float sx[NT8][2];
+#pragma unroll
+                for (int j = 0; j < NT8; ++j) {
+                    const uint4 h0 = sl[(FL::H + 2 * j) * 32], h1 = sl[(FL::H + 2 * j + 1) * 32];
+                    hb[j][0] = h0.x; hb[j][1] = h0.y; hb[j][2] = h0.z; hb[j][3] = h0.w;
+                    hb[j][4] = h1.x; hb[j][5] = h1.y; hb[j][6] = h1.z; hb[j][7] = h1.w;
+#pragma unroll
+                    for (int hf = 0; hf < 2; ++hf) {
+                        const float4 v = *reinterpret_cast<const float4 *>(sl + (FL::HS + 2 * j + hf) * 32);
+                        sx[j][hf] = (v.x + v.y) + (v.z + v.w);
+                    }
+                }
+                q4_group<NT8>(w, sb, hb, sx, C);
+            }
+        }
+        __syncwarp();
+        if (k % SPU == SPU - 1) {
+            const int unit = w0 + (k / SPU) * nw;
+            const int tile = unit / RB, rb = unit - tile * RB;
+            const TileInfo ti = tile_info(a, tile);
+            down_store_combine<NT8>(a, ti, rb, C, lane);
 #pragma unroll
             for (int j = 0; j < NT8; ++j)
 #pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-                    const float4 v = B.hs[i][j][hf];
-                    sx[j][hf] = (v.x + v.y) + (v.z + v.w);
-                }
-            q4_group<NT8>(B.w[i], B.b[i], B.hb[i], sx, C);
+                for (int i = 0; i < 4; ++i) C[j][i] = 0.f;
         }
     }
+    cp_wait<0>();
 }
 
-template <int FMT, int NT8, int GPW>
-__global__ void __launch_bounds__(128) k_down_tiles(ExpArgs a) {
-    pdl_launch();
-    pdl_wait();
-    const int lane = threadIdx.x & 31;
-    const int gq = lane >> 2, c = lane & 3;
-    const int d = a.d, f = a.f;
-    const int RB = d >> 4, G = f >> 6;
-    const int n_units = *a.ntiles * RB;
-    const int nwarps = gridDim.x * 4;
-    for (int unit = blockIdx.x * 4 + (threadIdx.x >> 5); unit < n_units; unit += nwarps) {
-        const int tile = unit / RB, rb = unit - tile * RB;
-        const TileInfo ti = tile_info(a, tile);
-        const size_t blk = (size_t)ti.e * RB + rb;
-        const uint16_t *hrow[NT8];
-        const float *hsrow[NT8][2];
-#pragma unroll
-        for (int j = 0; j < NT8; ++j) {
-            const int sb_ = tile_slot(a, ti, j * 8 + gq);
-            hrow[j] = sb_ >= 0 ? a.h + (size_t)sb_ * f + 16 * c : nullptr;
-#pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-                const int sc_ = tile_slot(a, ti, j * 8 + 2 * c + hf);
-                hsrow[j][hf] = sc_ >= 0 ? a.hsum + (size_t)sc_ * (f / 16) : nullptr;
-            }
-        }
-        float C[NT8][4];
-#pragma unroll
-        for (int j = 0; j < NT8; ++j)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) C[j][i] = 0.f;
-        DNBatch<NT8, GPW> A, B;
-        dn_load(A, a, blk, G, 0, hrow, hsrow, lane);
-        for (int g0 = 0; g0 < G; g0 += 2 * GPW) {
-            if (g0 + GPW < G) dn_load(B, a, blk, G, g0 + GPW, hrow, hsrow, lane);
-            dn_compute(A, g0, G, C);
-            if (g0 + GPW < G) {
-                if (g0 + 2 * GPW < G) dn_load(A, a, blk, G, g0 + 2 * GPW, hrow, hsrow, lane);
-                dn_compute(B, g0 + GPW, G, C);
-            }
-        }
-        down_store_combine<NT8>(a, ti, rb, C, lane);
-    }
+// shared-memory bytes of the tile kernels (4 warps per CTA)
+size_t gate_up_tiles_smem(int nt8, int ns, int gps) {
+    return (size_t)4 * ns * gps * (3 + 2 * nt8 + (nt8 + 1) / 2) * 32 * 16;
 }
+size_t down_tiles_smem(int nt8, int ns, int gps) { return (size_t)4 * ns * gps * (2 + 4 * nt8) * 32 * 16; }
 
 template __global__ void k_gate_up_slots<FMT_Q4, 8, 4>(ExpArgs);
 template __global__ void k_down_slots<FMT_Q4, 4, 4>(ExpArgs);
-template __global__ void k_gate_up_tiles<FMT_Q4, 1, 2>(ExpArgs);
-template __global__ void k_gate_up_tiles<FMT_Q4, 2, 1>(ExpArgs);
-template __global__ void k_down_tiles<FMT_Q4, 1, 2>(ExpArgs);
-template __global__ void k_down_tiles<FMT_Q4, 2, 1>(ExpArgs);
+template __global__ void k_gate_up_tiles<FMT_Q4, 1, 4, 2>(ExpArgs);
+template __global__ void k_gate_up_tiles<FMT_Q4, 2, 3, 2>(ExpArgs);
+template __global__ void k_down_tiles<FMT_Q4, 1, 4, 2>(ExpArgs);
+template __global__ void k_down_tiles<FMT_Q4, 2, 4, 1>(ExpArgs);
 
 }  // namespace moeb

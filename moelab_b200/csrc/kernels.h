@@ -65,7 +65,7 @@ struct ExpArgs {
     int dn_prefetch;  // gate/up pulls the down weights of its expert into L2
 };
 
-template <int TPB, int JMAX>
+template <int TPB, int JMAX, int U>
 __global__ void k_router(RouterArgs a);
 __global__ void k_prep(PrepArgs a);
 
@@ -82,10 +82,12 @@ template <int FMT, int KS, int GPW>
 __global__ void k_gate_up_slots(ExpArgs a);
 template <int FMT, int KS, int GPW>
 __global__ void k_down_slots(ExpArgs a);
-template <int FMT, int NT8, int GPW>
+template <int FMT, int NT8, int NS, int GPS>
 __global__ void k_gate_up_tiles(ExpArgs a);
-template <int FMT, int NT8, int GPW>
+template <int FMT, int NT8, int NS, int GPS>
 __global__ void k_down_tiles(ExpArgs a);
+size_t gate_up_tiles_smem(int nt8, int ns, int gps);
+size_t down_tiles_smem(int nt8, int ns, int gps);
 
 enum { FMT_Q4 = 0, FMT_FP4 = 1 };
 

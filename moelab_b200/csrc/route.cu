@@ -19,15 +19,43 @@
 namespace moeb {
 
 // ------------------------------------------------------------------ tile builder (one CTA)
+// Exclusive scan over the CTA (blockDim.x <= 1024): warp shuffles, then one warp over the warp totals.
+__device__ __forceinline__ int block_exclusive_scan(int v, int *total) {
+    __shared__ int wsum[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    int inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += n;
+    }
+    if (lane == 31) wsum[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < nw ? wsum[lane] : 0;
+        int winc = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, winc, o);
+            if (lane >= o) winc += n;
+        }
+        if (lane < nw) wsum[lane] = winc - w;
+        if (lane == 31) wsum[31] = winc;  // nw <= 32; lane 31 holds the grand total
+    }
+    __syncthreads();
+    const int r = wsum[warp] + inc - v;
+    *total = wsum[31];
+    __syncthreads();
+    return r;
+}
+
 // Counting sort of the TK slots by expert. Slot order inside an expert follows atomic arrival; this does not
 // change any result (every slot is its own MMA column and the combine sums slots in fixed j order).
 __device__ void build_tiles(const int *__restrict__ idx, int TK, int E, int NT, int4 *__restrict__ tiles,
                             int *__restrict__ ntiles, int *__restrict__ sorted, unsigned *__restrict__ err) {
     extern __shared__ int smem[];
-    int *cnt = smem;           // [E]
-    int *off = smem + E;       // [E]
-    int *toff = smem + 2 * E;  // [E]
-    __shared__ int part[1024];
+    int *cnt = smem;      // [E]
+    int *off = smem + E;  // [E]
     const int tid = threadIdx.x, nth = blockDim.x;
     for (int e = tid; e < E; e += nth) cnt[e] = 0;
     __syncthreads();
@@ -39,36 +67,21 @@ __device__ void build_tiles(const int *__restrict__ idx, int TK, int E, int NT, 
     }
     if (bad) atomicOr(err, ERR_EXPERT_ID);
     __syncthreads();
-    // exclusive scans of slot counts and tile counts (thread-chunked, then a serial pass over the partials)
+    // each thread owns a contiguous chunk of experts; two CTA-wide scans give slot and tile offsets
     const int per = (E + nth - 1) / nth;
-    const int e0 = tid * per, e1 = min(E, e0 + per);
+    const int e0 = min(E, tid * per), e1 = min(E, e0 + per);
     int sc = 0, st = 0;
     for (int e = e0; e < e1; ++e) {
         sc += cnt[e];
         st += (cnt[e] + NT - 1) / NT;
     }
-    part[tid] = sc;
-    __syncthreads();
-    if (tid == 0) {
-        int run = 0;
-        for (int i = 0; i < nth; ++i) { int v = part[i]; part[i] = run; run += v; }
-    }
-    __syncthreads();
-    int base_s = part[tid];
-    __syncthreads();
-    part[tid] = st;
-    __syncthreads();
-    if (tid == 0) {
-        int run = 0;
-        for (int i = 0; i < nth; ++i) { int v = part[i]; part[i] = run; run += v; }
-        *ntiles = run;
-    }
-    __syncthreads();
-    int base_t = part[tid];
+    int tot_s, tot_t;
+    int base_s = block_exclusive_scan(sc, &tot_s);
+    int base_t = block_exclusive_scan(st, &tot_t);
+    if (tid == 0) *ntiles = tot_t;
     for (int e = e0; e < e1; ++e) {
         const int c = cnt[e];
         off[e] = base_s;
-        toff[e] = base_t;
         const int nt = (c + NT - 1) / NT;
         for (int i = 0; i < nt; ++i) tiles[base_t + i] = make_int4(e, base_s + i * NT, min(NT, c - i * NT), 0);
         base_s += c;
@@ -159,7 +172,9 @@ __device__ void topk_token(const RouterArgs &a, int t, int lane) {
 }
 
 // grid (ceil(E / 4), ceil(T / TPB)), block 128: warp w computes expert blockIdx.x * 4 + w for TPB tokens.
-template <int TPB, int JMAX>
+// Each lane loads U chunks of the gate row and of every token row at once, then runs the fmaf chains; warp 0 of
+// the first expert block also turns its x registers into the per-64-group sums.
+template <int TPB, int JMAX, int U>
 __global__ void __launch_bounds__(128) k_router(RouterArgs a) {
     pdl_launch();
     pdl_wait();
@@ -168,43 +183,53 @@ __global__ void __launch_bounds__(128) k_router(RouterArgs a) {
     const int t0 = blockIdx.y * TPB;
     const int nt = min(TPB, a.T - t0);
     const int nch = a.d / 8;
+    const bool do_xsum = a.xsum != nullptr && blockIdx.x == 0 && warp == 0;
     if (e < a.E) {
         float acc[TPB];
 #pragma unroll
         for (int i = 0; i < TPB; ++i) acc[i] = 0.f;
         const uint16_t *wr = a.wg + (size_t)e * a.d;
-        constexpr int U = 4;  // chunks per lane in flight; each (token, expert) still sums chunks in order
-        for (int c0 = lane; c0 < nch; c0 += 32 * U) {
-            uint4 w[U];
+        for (int c0 = lane; c0 - lane < nch; c0 += 32 * U) {  // same trip count on every lane (shuffles below)
+            uint4 w[U], xv[TPB][U];
 #pragma unroll
             for (int u = 0; u < U; ++u) {
-                const int c = c0 + 32 * u;
-                w[u] = c < nch ? *reinterpret_cast<const uint4 *>(wr + 8 * c) : make_uint4(0, 0, 0, 0);
+                const int c = min(c0 + 32 * u, nch - 1);  // clamped: a repeated load, never used
+                w[u] = *reinterpret_cast<const uint4 *>(wr + 8 * c);
+#pragma unroll
+                for (int i = 0; i < TPB; ++i)
+                    xv[i][u] = *reinterpret_cast<const uint4 *>(a.x + (size_t)(t0 + min(i, nt - 1)) * a.d + 8 * c);
             }
 #pragma unroll
             for (int i = 0; i < TPB; ++i) {
-                if (i < nt) {
-                    uint4 xv[U];
+                float s = acc[i];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    if (c0 + 32 * u < nch) {
+                        const uint32_t xx[4] = {xv[i][u].x, xv[i][u].y, xv[i][u].z, xv[i][u].w};
+                        const uint32_t ww[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            s = __fmaf_rn(bf16lo(xx[j]), bf16lo(ww[j]), s);
+                            s = __fmaf_rn(bf16hi(xx[j]), bf16hi(ww[j]), s);
+                        }
+                    }
+                }
+                acc[i] = s;
+            }
+            if (do_xsum) {  // chunk c of lane l covers group c / 8: 8 consecutive lanes share a group
+#pragma unroll
+                for (int i = 0; i < TPB; ++i) {
 #pragma unroll
                     for (int u = 0; u < U; ++u) {
                         const int c = c0 + 32 * u;
-                        xv[u] = c < nch ? *reinterpret_cast<const uint4 *>(a.x + (size_t)(t0 + i) * a.d + 8 * c)
-                                        : make_uint4(0, 0, 0, 0);
+                        const uint4 v = xv[i][u];
+                        float p = bf16lo(v.x) + bf16hi(v.x) + bf16lo(v.y) + bf16hi(v.y) + bf16lo(v.z) +
+                                  bf16hi(v.z) + bf16lo(v.w) + bf16hi(v.w);
+                        p += __shfl_xor_sync(0xffffffffu, p, 1);
+                        p += __shfl_xor_sync(0xffffffffu, p, 2);
+                        p += __shfl_xor_sync(0xffffffffu, p, 4);
+                        if (i < nt && c < nch && (lane & 7) == 0) a.xsum[(size_t)(t0 + i) * (a.d / 64) + c / 8] = p;
                     }
-                    float s = acc[i];
-#pragma unroll
-                    for (int u = 0; u < U; ++u) {
-                        if (c0 + 32 * u < nch) {
-                            const uint32_t xx[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
-                            const uint32_t ww[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                s = __fmaf_rn(bf16lo(xx[j]), bf16lo(ww[j]), s);
-                                s = __fmaf_rn(bf16hi(xx[j]), bf16hi(ww[j]), s);
-                            }
-                        }
-                    }
-                    acc[i] = s;
                 }
             }
         }
@@ -228,10 +253,7 @@ __global__ void __launch_bounds__(128) k_router(RouterArgs a) {
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    for (int i = warp; i < nt; i += 4) {
-        topk_token<JMAX>(a, t0 + i, lane);
-        if (a.xsum) row_group_sums(a.x + (size_t)(t0 + i) * a.d, a.d, a.xsum + (size_t)(t0 + i) * (a.d / 64), lane);
-    }
+    for (int i = warp; i < nt; i += 4) topk_token<JMAX>(a, t0 + i, lane);
     if (threadIdx.x == 0) a.cnt[blockIdx.y] = 0;
     if (a.tiles == nullptr) return;
     // routing step in the last token block to finish
@@ -278,15 +300,15 @@ __global__ void __launch_bounds__(256) k_prep(PrepArgs a) {
     if (threadIdx.x == 0) *a.cnt_all = 0;
 }
 
-#define MOEB_ROUTER_INST(TPB)                          \
-    template __global__ void k_router<TPB, 1>(RouterArgs);  \
-    template __global__ void k_router<TPB, 2>(RouterArgs);  \
-    template __global__ void k_router<TPB, 4>(RouterArgs);  \
-    template __global__ void k_router<TPB, 8>(RouterArgs);  \
-    template __global__ void k_router<TPB, 16>(RouterArgs); \
-    template __global__ void k_router<TPB, 32>(RouterArgs);
-MOEB_ROUTER_INST(1)
-MOEB_ROUTER_INST(4)
+#define MOEB_ROUTER_INST(TPB, U)                          \
+    template __global__ void k_router<TPB, 1, U>(RouterArgs);  \
+    template __global__ void k_router<TPB, 2, U>(RouterArgs);  \
+    template __global__ void k_router<TPB, 4, U>(RouterArgs);  \
+    template __global__ void k_router<TPB, 8, U>(RouterArgs);  \
+    template __global__ void k_router<TPB, 16, U>(RouterArgs); \
+    template __global__ void k_router<TPB, 32, U>(RouterArgs);
+MOEB_ROUTER_INST(1, 8)
+MOEB_ROUTER_INST(4, 4)
 #undef MOEB_ROUTER_INST
 
 }  // namespace moeb
