@@ -141,7 +141,8 @@ int choose_policy(int T, int E, int k) {
     return load <= 6.0 ? MOEB_POLICY_TILES8 : MOEB_POLICY_TILES16;
 }
 
-int nt_of(int policy) { return policy == MOEB_POLICY_TILES16 ? 16 : 8; }
+int nt_of(int policy) { return (policy == MOEB_POLICY_TILES16 || policy == MOEB_POLICY_TILES16_RING) ? 16 : 8; }
+bool is_tiles(int policy) { return policy >= MOEB_POLICY_TILES8 && policy <= MOEB_POLICY_TILES16_RING; }
 
 struct ExpLaunch {
     void (*gu)(ExpArgs);
@@ -156,11 +157,15 @@ ExpLaunch pick_kernels(int fmt, int policy, int d, int f) {
     if (policy == MOEB_POLICY_SLOTS)
         return {k_gate_up_slots<FMT_Q4, 8, 4>, k_down_slots<FMT_Q4, 4, 4>, 256, 128, (size_t)d * 2,
                 (size_t)f * 2 + (size_t)f / 16 * 4, false};
-    if (policy == MOEB_POLICY_TILES16)
+    if (policy == MOEB_POLICY_TILES16_RING)
         return {k_gate_up_tiles<FMT_Q4, 2, 3, 2>, k_down_tiles<FMT_Q4, 2, 4, 1>, 128, 128, gate_up_tiles_smem(2, 3, 2),
                 down_tiles_smem(2, 4, 1), true};
-    return {k_gate_up_tiles<FMT_Q4, 1, 4, 2>, k_down_tiles<FMT_Q4, 1, 4, 2>, 128, 128, gate_up_tiles_smem(1, 4, 2),
-            down_tiles_smem(1, 4, 2), true};
+    if (policy == MOEB_POLICY_TILES8_RING)
+        return {k_gate_up_tiles<FMT_Q4, 1, 4, 2>, k_down_tiles<FMT_Q4, 1, 4, 2>, 128, 128, gate_up_tiles_smem(1, 4, 2),
+                down_tiles_smem(1, 4, 2), true};
+    if (policy == MOEB_POLICY_TILES16)
+        return {k_gate_up_tiles_reg<FMT_Q4, 2, 1>, k_down_tiles_reg<FMT_Q4, 2, 1>, 128, 128, 0, 0, true};
+    return {k_gate_up_tiles_reg<FMT_Q4, 1, 2>, k_down_tiles_reg<FMT_Q4, 1, 2>, 128, 128, 0, 0, true};
 }
 
 // Opt a kernel in to more than 48 KB of dynamic shared memory (once per kernel).
@@ -236,7 +241,7 @@ int launch_router(const void *x, const void *wg, const void *bias, int T, int d,
     r.cnt = at<unsigned>(ws, L.rcnt);
     r.cnt_all = at<unsigned>(ws, L.cnt_all);
     r.err = at<unsigned>(ws, L.err);
-    const bool tiles = policy == MOEB_POLICY_TILES8 || policy == MOEB_POLICY_TILES16;
+    const bool tiles = is_tiles(policy);
     r.NT = nt_of(policy);
     r.tiles = tiles ? at<int4>(ws, L.tiles) : nullptr;
     r.ntiles = at<int>(ws, L.ntiles);
@@ -371,8 +376,7 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
     if (cap < T) return fail(MOEB_EINVAL, "workspace too small for T tokens%s");
     const Layout L = layout(cap, d, f, E, k);
     if (policy == MOEB_POLICY_AUTO) policy = choose_policy(T, E, k);
-    if (policy != MOEB_POLICY_SLOTS && policy != MOEB_POLICY_TILES8 && policy != MOEB_POLICY_TILES16)
-        return fail(MOEB_EINVAL, "unknown policy%s");
+    if (policy != MOEB_POLICY_SLOTS && !is_tiles(policy)) return fail(MOEB_EINVAL, "unknown policy%s");
     const bool tiles = policy != MOEB_POLICY_SLOTS;
     if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[0]), st);
     if (gate_w) {  // layer call: router produces ids, weights, x group sums and (tile mode) the tiles
@@ -394,7 +398,7 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
         p.ntiles = at<int>(ws, L.ntiles);
         p.sorted = at<int>(ws, L.sorted);
         p.err = at<unsigned>(ws, L.err);
-        const size_t smem = tiles ? 12 * (size_t)E : 0;
+        const size_t smem = tiles ? 8 * (size_t)E : 0;
         if (launch(k_prep, dim3((T + 7) / 8), dim3(256), smem, st, p) != cudaSuccess) return check_launch("prep");
     }
     if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[1]), st);

@@ -168,7 +168,8 @@ __device__ __forceinline__ void down_store_combine(const ExpArgs &a, const TileI
                 a.yp[(size_t)slot * d + r1] = wsl * v1;
             }
         }
-    __threadfence();
+    __syncwarp();
+    if (lane == 0) __threadfence();  // cumulative over the warp's writes ordered by the __syncwarp
     __syncwarp();
     int tok = -1;
     bool done = false;
@@ -180,7 +181,10 @@ __device__ __forceinline__ void down_store_combine(const ExpArgs &a, const TileI
         }
     }
     unsigned m = __ballot_sync(0xffffffffu, done);
-    if (m) __threadfence();
+    if (m) {
+        if (lane == 0) __threadfence();
+        __syncwarp();
+    }
     while (m) {
         const int src = __ffs(m) - 1;
         m &= m - 1;
@@ -335,6 +339,189 @@ __global__ void __launch_bounds__(32 * KS, 8) k_down_slots(ExpArgs a) {
             down_store_combine<1>(a, ti, rb, cs, lane);
         }
         __syncthreads();
+    }
+}
+
+// ================================================================== tile mode, register pipeline
+// One warp per (tile, 16-row block) over the whole K; loads run one GPW-group batch ahead of the MMAs in
+// registers (no shared memory), so more warps fit per SM than with the cp.async ring below.
+template <int NT8, int GPW>
+struct GUBatch {
+    uint4 wg[GPW], wu[GPW];
+    uint2 bg[GPW], bu[GPW];
+    uint32_t xb[GPW][NT8][8];
+    float sx[GPW][NT8][2];
+};
+
+template <int NT8, int GPW>
+__device__ __forceinline__ void gu_load(GUBatch<NT8, GPW> &B, const ExpArgs &a, size_t blk, int G, int g0,
+                                        const uint16_t *const (&xrow)[NT8], const float *const (&sxrow)[NT8][2],
+                                        int lane) {
+    const int gq = lane >> 2;
+#pragma unroll
+    for (int i = 0; i < GPW; ++i) {
+        const int g = min(g0 + i, G - 1);
+        B.wg[i] = ld_w(a.g, blk, G, g, lane);
+        B.wu[i] = ld_w(a.u, blk, G, g, lane);
+        B.bg[i] = ld_sb(a.g, blk, G, g, gq);
+        B.bu[i] = ld_sb(a.u, blk, G, g, gq);
+#pragma unroll
+        for (int j = 0; j < NT8; ++j) {
+            load_b16(xrow[j] ? xrow[j] + g * 64 : nullptr, B.xb[i][j]);
+            B.sx[i][j][0] = sxrow[j][0] ? sxrow[j][0][g] : 0.f;
+            B.sx[i][j][1] = sxrow[j][1] ? sxrow[j][1][g] : 0.f;
+        }
+    }
+}
+
+template <int NT8, int GPW>
+__device__ __forceinline__ void gu_compute(const GUBatch<NT8, GPW> &B, int g0, int G, float (&Cg)[NT8][4],
+                                           float (&Cu)[NT8][4]) {
+#pragma unroll
+    for (int i = 0; i < GPW; ++i) {
+        if (g0 + i < G) {
+            q4_group<NT8>(B.wg[i], B.bg[i], B.xb[i], B.sx[i], Cg);
+            q4_group<NT8>(B.wu[i], B.bu[i], B.xb[i], B.sx[i], Cu);
+        }
+    }
+}
+
+template <int FMT, int NT8, int GPW>
+__global__ void __launch_bounds__(128) k_gate_up_tiles_reg(ExpArgs a) {
+    pdl_launch();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int gq = lane >> 2, c = lane & 3;
+    const int d = a.d, f = a.f;
+    const int RB = f >> 4, G = d >> 6;
+    const int n_units = *a.ntiles * RB;
+    const int nwarps = gridDim.x * 4;
+    for (int unit = blockIdx.x * 4 + (threadIdx.x >> 5); unit < n_units; unit += nwarps) {
+        const int tile = unit / RB, rb = unit - tile * RB;
+        const TileInfo ti = tile_info(a, tile);
+        const size_t blk = (size_t)ti.e * RB + rb;
+        if (a.dn_prefetch) prefetch_down(a, ti.e, rb, RB, lane);
+        const uint16_t *xrow[NT8];
+        const float *sxrow[NT8][2];
+#pragma unroll
+        for (int j = 0; j < NT8; ++j) {
+            const int sb_ = tile_slot(a, ti, j * 8 + gq);
+            xrow[j] = sb_ >= 0 ? a.x + (size_t)(sb_ / a.k) * d + 16 * c : nullptr;
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                const int sc_ = tile_slot(a, ti, j * 8 + 2 * c + hf);
+                sxrow[j][hf] = sc_ >= 0 ? a.xsum + (size_t)(sc_ / a.k) * G : nullptr;
+            }
+        }
+        float Cg[NT8][4], Cu[NT8][4];
+#pragma unroll
+        for (int j = 0; j < NT8; ++j)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) Cg[j][i] = Cu[j][i] = 0.f;
+        GUBatch<NT8, GPW> A, B;
+        gu_load(A, a, blk, G, 0, xrow, sxrow, lane);
+        for (int g0 = 0; g0 < G; g0 += 2 * GPW) {
+            if (g0 + GPW < G) gu_load(B, a, blk, G, g0 + GPW, xrow, sxrow, lane);
+            gu_compute(A, g0, G, Cg, Cu);
+            if (g0 + GPW < G) {
+                if (g0 + 2 * GPW < G) gu_load(A, a, blk, G, g0 + 2 * GPW, xrow, sxrow, lane);
+                gu_compute(B, g0 + GPW, G, Cg, Cu);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < NT8; ++j) gate_up_store<NT8>(a, ti, rb, j, Cg[j], Cu[j], lane);
+    }
+}
+
+template <int NT8, int GPW>
+struct DNBatch {
+    uint4 w[GPW];
+    uint2 b[GPW];
+    uint32_t hb[GPW][NT8][8];
+    float4 hs[GPW][NT8][2];
+};
+
+template <int NT8, int GPW>
+__device__ __forceinline__ void dn_load(DNBatch<NT8, GPW> &B, const ExpArgs &a, size_t blk, int G, int g0,
+                                        const uint16_t *const (&hrow)[NT8], const float *const (&hsrow)[NT8][2],
+                                        int lane) {
+    const int gq = lane >> 2;
+#pragma unroll
+    for (int i = 0; i < GPW; ++i) {
+        const int g = min(g0 + i, G - 1);
+        B.w[i] = ld_w(a.dn, blk, G, g, lane);
+        B.b[i] = ld_sb(a.dn, blk, G, g, gq);
+#pragma unroll
+        for (int j = 0; j < NT8; ++j) {
+            load_b16(hrow[j] ? hrow[j] + g * 64 : nullptr, B.hb[i][j]);
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf)
+                B.hs[i][j][hf] = hsrow[j][hf] ? *reinterpret_cast<const float4 *>(hsrow[j][hf] + 4 * g)
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+}
+
+template <int NT8, int GPW>
+__device__ __forceinline__ void dn_compute(const DNBatch<NT8, GPW> &B, int g0, int G, float (&C)[NT8][4]) {
+#pragma unroll
+    for (int i = 0; i < GPW; ++i) {
+        if (g0 + i < G) {
+            float sx[NT8][2];
+#pragma unroll
+            for (int j = 0; j < NT8; ++j)
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    const float4 v = B.hs[i][j][hf];
+                    sx[j][hf] = (v.x + v.y) + (v.z + v.w);
+                }
+            q4_group<NT8>(B.w[i], B.b[i], B.hb[i], sx, C);
+        }
+    }
+}
+
+template <int FMT, int NT8, int GPW>
+__global__ void __launch_bounds__(128) k_down_tiles_reg(ExpArgs a) {
+    pdl_launch();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int gq = lane >> 2, c = lane & 3;
+    const int d = a.d, f = a.f;
+    const int RB = d >> 4, G = f >> 6;
+    const int n_units = *a.ntiles * RB;
+    const int nwarps = gridDim.x * 4;
+    for (int unit = blockIdx.x * 4 + (threadIdx.x >> 5); unit < n_units; unit += nwarps) {
+        const int tile = unit / RB, rb = unit - tile * RB;
+        const TileInfo ti = tile_info(a, tile);
+        const size_t blk = (size_t)ti.e * RB + rb;
+        const uint16_t *hrow[NT8];
+        const float *hsrow[NT8][2];
+#pragma unroll
+        for (int j = 0; j < NT8; ++j) {
+            const int sb_ = tile_slot(a, ti, j * 8 + gq);
+            hrow[j] = sb_ >= 0 ? a.h + (size_t)sb_ * f + 16 * c : nullptr;
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                const int sc_ = tile_slot(a, ti, j * 8 + 2 * c + hf);
+                hsrow[j][hf] = sc_ >= 0 ? a.hsum + (size_t)sc_ * (f / 16) : nullptr;
+            }
+        }
+        float C[NT8][4];
+#pragma unroll
+        for (int j = 0; j < NT8; ++j)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) C[j][i] = 0.f;
+        DNBatch<NT8, GPW> A, B;
+        dn_load(A, a, blk, G, 0, hrow, hsrow, lane);
+        for (int g0 = 0; g0 < G; g0 += 2 * GPW) {
+            if (g0 + GPW < G) dn_load(B, a, blk, G, g0 + GPW, hrow, hsrow, lane);
+            dn_compute(A, g0, G, C);
+            if (g0 + GPW < G) {
+                if (g0 + 2 * GPW < G) dn_load(A, a, blk, G, g0 + 2 * GPW, hrow, hsrow, lane);
+                dn_compute(B, g0 + GPW, G, C);
+            }
+        }
+        down_store_combine<NT8>(a, ti, rb, C, lane);
     }
 }
 
@@ -578,6 +765,10 @@ size_t down_tiles_smem(int nt8, int ns, int gps) { return (size_t)4 * ns * gps *
 
 template __global__ void k_gate_up_slots<FMT_Q4, 8, 4>(ExpArgs);
 template __global__ void k_down_slots<FMT_Q4, 4, 4>(ExpArgs);
+template __global__ void k_gate_up_tiles_reg<FMT_Q4, 1, 2>(ExpArgs);
+template __global__ void k_gate_up_tiles_reg<FMT_Q4, 2, 1>(ExpArgs);
+template __global__ void k_down_tiles_reg<FMT_Q4, 1, 2>(ExpArgs);
+template __global__ void k_down_tiles_reg<FMT_Q4, 2, 1>(ExpArgs);
 template __global__ void k_gate_up_tiles<FMT_Q4, 1, 4, 2>(ExpArgs);
 template __global__ void k_gate_up_tiles<FMT_Q4, 2, 3, 2>(ExpArgs);
 template __global__ void k_down_tiles<FMT_Q4, 1, 4, 2>(ExpArgs);

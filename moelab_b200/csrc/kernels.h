@@ -86,6 +86,10 @@ template <int FMT, int NT8, int NS, int GPS>
 __global__ void k_gate_up_tiles(ExpArgs a);
 template <int FMT, int NT8, int NS, int GPS>
 __global__ void k_down_tiles(ExpArgs a);
+template <int FMT, int NT8, int GPW>
+__global__ void k_gate_up_tiles_reg(ExpArgs a);
+template <int FMT, int NT8, int GPW>
+__global__ void k_down_tiles_reg(ExpArgs a);
 size_t gate_up_tiles_smem(int nt8, int ns, int gps);
 size_t down_tiles_smem(int nt8, int ns, int gps);
 

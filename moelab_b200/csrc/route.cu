@@ -243,29 +243,31 @@ __global__ void __launch_bounds__(128) k_router(RouterArgs a) {
             if (lane == 0 && i < nt) a.logits[(size_t)(t0 + i) * a.E + e] = v;
         }
     }
-    __threadfence();
-    __syncthreads();
+    // last-arriver hand-off: the barrier orders the CTA's logits before thread 0's fence (cumulative), the
+    // counter picks the last CTA of the token block, whose thread 0 fences again before the reads
     __shared__ int s_last;
+    __syncthreads();
     if (threadIdx.x == 0) {
+        __threadfence();
         const unsigned prev = atomicAdd(a.cnt + blockIdx.y, 1u);
         s_last = prev == gridDim.x - 1;
+        if (s_last) __threadfence();
     }
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
     for (int i = warp; i < nt; i += 4) topk_token<JMAX>(a, t0 + i, lane);
     if (threadIdx.x == 0) a.cnt[blockIdx.y] = 0;
     if (a.tiles == nullptr) return;
     // routing step in the last token block to finish
-    __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
+        __threadfence();
         const unsigned prev = atomicAdd(a.cnt_all, 1u);
         s_last = prev == gridDim.y - 1;
+        if (s_last) __threadfence();
     }
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
     build_tiles(a.idx, a.T * a.k, a.E, a.NT, a.tiles, a.ntiles, a.sorted, a.err);
     if (threadIdx.x == 0) *a.cnt_all = 0;
 }
@@ -286,16 +288,16 @@ __global__ void __launch_bounds__(256) k_prep(PrepArgs a) {
         }
         return;
     }
-    __threadfence();
-    __syncthreads();
     __shared__ int s_last;
+    __syncthreads();
     if (threadIdx.x == 0) {
+        __threadfence();
         const unsigned prev = atomicAdd(a.cnt_all, 1u);
         s_last = prev == gridDim.x - 1;
+        if (s_last) __threadfence();
     }
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
     build_tiles(a.idx, a.T * a.k, a.E, a.NT, a.tiles, a.ntiles, a.sorted, a.err);
     if (threadIdx.x == 0) *a.cnt_all = 0;
 }
