@@ -43,8 +43,8 @@ typedef struct CUstream_st *cudaStream_t;
 #define MOEB_POLICY_SLOTS 1   /* one tile per slot, no routing step (decode) */
 #define MOEB_POLICY_TILES8 2  /* slots grouped by expert, tiles of <= 8 slots */
 #define MOEB_POLICY_TILES16 3 /* tiles of <= 16 slots */
-#define MOEB_POLICY_TILES8_RING 4  /* tiles of <= 8 slots, weights streamed through a per-warp cp.async ring */
-#define MOEB_POLICY_TILES16_RING 5 /* tiles of <= 16 slots, cp.async ring */
+#define MOEB_POLICY_TILES8_RING 4  /* tiles of <= 8 slots, weights streamed by TMA into a per-warp ring */
+#define MOEB_POLICY_TILES16_RING 5 /* tiles of <= 16 slots, TMA ring */
 
 /* device error bits readable with moeb_read_error */
 #define MOEB_DEVERR_EXPERT_ID 1u /* an expert id outside [0, E) was given; that slot contributed nothing */

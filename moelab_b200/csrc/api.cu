@@ -158,11 +158,11 @@ ExpLaunch pick_kernels(int fmt, int policy, int d, int f) {
         return {k_gate_up_slots<FMT_Q4, 8, 4>, k_down_slots<FMT_Q4, 4, 4>, 256, 128, (size_t)d * 2,
                 (size_t)f * 2 + (size_t)f / 16 * 4, false};
     if (policy == MOEB_POLICY_TILES16_RING)
-        return {k_gate_up_tiles<FMT_Q4, 2, 3, 2>, k_down_tiles<FMT_Q4, 2, 4, 1>, 128, 128, gate_up_tiles_smem(2, 3, 2),
-                down_tiles_smem(2, 4, 1), true};
+        return {k_gate_up_tiles<FMT_Q4, 2, 3, 8>, k_down_tiles<FMT_Q4, 2, 3, 8>, 128, 128, gate_up_tiles_smem(2, 3, 8),
+                down_tiles_smem(2, 3, 8), true};
     if (policy == MOEB_POLICY_TILES8_RING)
-        return {k_gate_up_tiles<FMT_Q4, 1, 4, 2>, k_down_tiles<FMT_Q4, 1, 4, 2>, 128, 128, gate_up_tiles_smem(1, 4, 2),
-                down_tiles_smem(1, 4, 2), true};
+        return {k_gate_up_tiles<FMT_Q4, 1, 3, 8>, k_down_tiles<FMT_Q4, 1, 3, 8>, 128, 128, gate_up_tiles_smem(1, 3, 8),
+                down_tiles_smem(1, 3, 8), true};
     if (policy == MOEB_POLICY_TILES16)
         return {k_gate_up_tiles_reg<FMT_Q4, 2, 1>, k_down_tiles_reg<FMT_Q4, 2, 1>, 128, 128, 0, 0, true};
     return {k_gate_up_tiles_reg<FMT_Q4, 1, 2>, k_down_tiles_reg<FMT_Q4, 1, 2>, 128, 128, 0, 0, true};
@@ -423,8 +423,13 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
     a.y = static_cast<uint16_t *>(y);
     a.err = at<unsigned>(ws, L.err);
     a.T = T; a.d = d; a.f = f; a.E = E; a.k = k; a.act = act; a.tile_mode = tiles ? 1 : 0;
-    // down weights are prefetched into L2 while gate/up runs when they are a small share of L2
-    a.dn_prefetch = (long)T * k <= 4L * E ? 1 : 0;
+    // the down weights of the routed experts are prefetched into L2 while gate/up runs only when gate/up,
+    // down and the prefetch all fit comfortably in L2 (otherwise the gate/up stream evicts them again)
+    {
+        const double U = std::min<double>(E, (double)T * k);
+        const double layer_bytes = U * 3.0 * d * f * 4.5 / 8.0;
+        a.dn_prefetch = layer_bytes < 48.0 * (1 << 20) ? 1 : 0;
+    }
     return run_experts(fmt, a, policy, L, ws, st, ev);
 }
 

@@ -90,21 +90,22 @@ __device__ __forceinline__ void load_b16(const uint16_t *p, uint32_t (&o)[8]) {
 
 // L2 prefetch of the 16-byte-aligned part of [p, p + bytes), in 4 KB pieces spread over a warp's lanes. The
 // range is shrunk inward to 16-byte boundaries, so nothing outside it is touched.
-__device__ __forceinline__ void prefetch_l2(const void *p, size_t bytes, int lane) {
+__device__ __forceinline__ void prefetch_l2(const void *p, size_t bytes, int lane, int nlanes = 32) {
     const uintptr_t b = ((uintptr_t)p + 15) & ~(uintptr_t)15, e = ((uintptr_t)p + bytes) & ~(uintptr_t)15;
-    for (uintptr_t q = b + (uintptr_t)lane * 4096; q < e; q += 32 * 4096) {
+    for (uintptr_t q = b + (uintptr_t)lane * 4096; q < e; q += (uintptr_t)nlanes * 4096) {
         const uint32_t n = (uint32_t)(e - q < 4096 ? e - q : 4096);
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(q), "r"(n) : "memory");
     }
 }
 
 // Pull the share [rb/RB, (rb+1)/RB) of expert e's down projection into L2 (it streams right after gate/up).
-__device__ __forceinline__ void prefetch_down(const ExpArgs &a, int e, int rb, int RB, int lane) {
+// Called by `nlanes` lanes of a warp (lane in [0, nlanes)).
+__device__ __forceinline__ void prefetch_down(const ExpArgs &a, int e, int rb, int RB, int lane, int nlanes = 32) {
     const int rb0 = (int)((long)rb * (a.d / 16) / RB), rb1 = (int)((long)(rb + 1) * (a.d / 16) / RB);
     if (rb1 <= rb0) return;
     const size_t blk = (size_t)e * (a.d / 16) + rb0;
-    prefetch_l2(a.dn.q + blk * (size_t)(a.f / 64) * 128, (size_t)(rb1 - rb0) * (a.f / 64) * 512, lane);
-    prefetch_l2(a.dn.sb + blk * (size_t)(a.f / 64) * 16, (size_t)(rb1 - rb0) * (a.f / 64) * 64, lane);
+    prefetch_l2(a.dn.q + blk * (size_t)(a.f / 64) * 128, (size_t)(rb1 - rb0) * (a.f / 64) * 512, lane, nlanes);
+    prefetch_l2(a.dn.sb + blk * (size_t)(a.f / 64) * 16, (size_t)(rb1 - rb0) * (a.f / 64) * 64, lane, nlanes);
 }
 
 // Weights of one (16-row block, 64-group) for this lane.
@@ -525,29 +526,20 @@ __global__ void __launch_bounds__(128) k_down_tiles_reg(ExpArgs a) {
     }
 }
 
-// ================================================================== tile mode
-// One warp per (tile, 16-row block) over the whole K. Each warp owns a ring of NS shared-memory stages of GPS
-// groups; every lane cp.async-copies its own fragment bytes (weights, scale|bias, activations, group sums) into
-// a lane-major slot, so NS-1 stages stay in flight without holding registers and the MMA loop reads
-// shared memory only. The stage sequence runs across unit boundaries (the next unit's first groups are
-// already loading while the current unit finishes).
-template <int NT8>
-struct GUFields {  // uint4 slots per lane per group
-    static constexpr int W_G = 0, W_U = 1, SB = 2, X = 3, SX = 3 + 2 * NT8, N = 3 + 2 * NT8 + (NT8 + 1) / 2;
-};
-template <int NT8>
-struct DNFields {
-    static constexpr int W = 0, SB = 1, H = 2, HS = 2 + 2 * NT8, N = 2 + 4 * NT8;
-};
-
-// Per-lane view of the producer's current unit.
+// ================================================================== tile mode, TMA ring
+// One warp per (tile, 16-row block) over the whole K. In the fragment-major layout a unit's codes for groups
+// [g0, g0 + SG) are one contiguous block per projection (and likewise the scale|bias words), so lane 0 of each
+// warp streams whole stages with 1-D TMA bulk copies (evict-first in L2) into a ring of NS shared-memory stages
+// completing on per-stage mbarriers; the warp's MMAs read the ring. Activations and group sums (L2-resident,
+// reused by every row block of a tile) come through plain loads one group ahead. Every wait is bounded: on a
+// timeout the warp records MOEB_DEVERR_TIMEOUT and stops issuing.
 template <int NT8>
 struct UnitSrc {
     int unit = -1;
     TileInfo ti;
     size_t blk;
-    const uint16_t *row[NT8];     // activation row of B column gq of each n8 tile (x or h), or null
-    const float *srow[NT8][2];    // group-sum rows of C columns 2c, 2c+1 (xsum or hsum), or null
+    const uint16_t *row[NT8];   // activation row of B column gq of each n8 tile (x or h), or null
+    const float *srow[NT8][2];  // group-sum rows of C columns 2c, 2c+1 (xsum or hsum), or null
 };
 
 template <int NT8, bool DOWN>
@@ -571,197 +563,171 @@ __device__ __forceinline__ void unit_src(UnitSrc<NT8> &u, const ExpArgs &a, int 
     }
 }
 
-template <int FMT, int NT8, int NS, int GPS>
-__global__ void __launch_bounds__(128) k_gate_up_tiles(ExpArgs a) {
-    using FL = GUFields<NT8>;
-    pdl_launch();
-    pdl_wait();
-    extern __shared__ uint4 smem_ring[];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int gq = lane >> 2;
-    const int RB = a.f >> 4, G = a.d >> 6;
-    const int SPU = (G + GPS - 1) / GPS;  // stages per unit
-    const int n_units = *a.ntiles * RB;
-    const int w0 = blockIdx.x * 4 + warp, nw = gridDim.x * 4;
-    const int my_units = w0 < n_units ? (n_units - w0 + nw - 1) / nw : 0;
-    const int total = my_units * SPU;
-    uint4 *ring = smem_ring + (size_t)warp * NS * GPS * FL::N * 32;
-    UnitSrc<NT8> P;  // producer's unit
-    auto issue = [&](int k) {
-        if (k < total) {
-            const int unit = w0 + (k / SPU) * nw, gb = (k % SPU) * GPS;
-            if (unit != P.unit) {
-                unit_src<NT8, false>(P, a, unit, RB, lane);
-                if (gb == 0 && a.dn_prefetch) prefetch_down(a, P.ti.e, unit % RB, RB, lane);
-            }
-            uint4 *st = ring + (size_t)(k % NS) * GPS * FL::N * 32;
+// B operand (16 activations per lane) and the two group sums of one group.
+template <int NT8, bool DOWN>
+__device__ __forceinline__ void load_act(const UnitSrc<NT8> &u, int g, uint32_t (&xb)[NT8][8], float (&sx)[NT8][2]) {
 #pragma unroll
-            for (int i = 0; i < GPS; ++i) {
-                const int g = min(gb + i, G - 1);
-                uint4 *sl = st + i * FL::N * 32 + lane;
-                cp_async16(sl + FL::W_G * 32, a.g.q + ((P.blk * G + g) * 32 + lane) * 4);
-                cp_async16(sl + FL::W_U * 32, a.u.q + ((P.blk * G + g) * 32 + lane) * 4);
-                cp_async8(sl + FL::SB * 32, a.g.sb + ((P.blk * G + g) * 8 + gq) * 2);
-                cp_async8(reinterpret_cast<uint2 *>(sl + FL::SB * 32) + 1, a.u.sb + ((P.blk * G + g) * 8 + gq) * 2);
+    for (int j = 0; j < NT8; ++j) {
+        load_b16(u.row[j] ? u.row[j] + g * 64 : nullptr, xb[j]);
 #pragma unroll
-                for (int j = 0; j < NT8; ++j) {
-                    const bool ok = P.row[j] != nullptr;
-                    const uint16_t *src = ok ? P.row[j] + g * 64 : a.x;
-                    cp_async16(sl + (FL::X + 2 * j) * 32, src, ok);
-                    cp_async16(sl + (FL::X + 2 * j + 1) * 32, src + 8, ok);
-                    float *sxd = reinterpret_cast<float *>(sl + (FL::SX + j / 2) * 32) + 2 * (j & 1);
-                    cp_async4(sxd, P.srow[j][0] ? P.srow[j][0] + g : a.xsum, P.srow[j][0] != nullptr);
-                    cp_async4(sxd + 1, P.srow[j][1] ? P.srow[j][1] + g : a.xsum, P.srow[j][1] != nullptr);
+        for (int hf = 0; hf < 2; ++hf) {
+            const float *p = u.srow[j][hf];
+            if (DOWN) {
+                if (p) {
+                    const float4 v = *reinterpret_cast<const float4 *>(p + 4 * g);
+                    sx[j][hf] = (v.x + v.y) + (v.z + v.w);
+                } else {
+                    sx[j][hf] = 0.f;
                 }
-            }
-        }
-        cp_commit();
-    };
-    for (int k = 0; k < NS - 1; ++k) issue(k);
-    float Cg[NT8][4], Cu[NT8][4];
-#pragma unroll
-    for (int j = 0; j < NT8; ++j)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) Cg[j][i] = Cu[j][i] = 0.f;
-    for (int k = 0; k < total; ++k) {
-        issue(k + NS - 1);
-        cp_wait<NS - 1>();
-        __syncwarp();
-        const uint4 *st = ring + (size_t)(k % NS) * GPS * FL::N * 32;
-        const int gb = (k % SPU) * GPS;
-#pragma unroll
-        for (int i = 0; i < GPS; ++i) {
-            if (gb + i < G) {
-                const uint4 *sl = st + i * FL::N * 32 + lane;
-                const uint4 wg = sl[FL::W_G * 32], wu = sl[FL::W_U * 32], sb = sl[FL::SB * 32];
-                uint32_t xb[NT8][8];
-                float sx[NT8][2];
-#pragma unroll
-                for (int j = 0; j < NT8; ++j) {
-                    const uint4 x0 = sl[(FL::X + 2 * j) * 32], x1 = sl[(FL::X + 2 * j + 1) * 32];
-                    xb[j][0] = x0.x; xb[j][1] = x0.y; xb[j][2] = x0.z; xb[j][3] = x0.w;
-                    xb[j][4] = x1.x; xb[j][5] = x1.y; xb[j][6] = x1.z; xb[j][7] = x1.w;
-                    const float *sxp = reinterpret_cast<const float *>(sl + (FL::SX + j / 2) * 32) + 2 * (j & 1);
-                    sx[j][0] = sxp[0];
-                    sx[j][1] = sxp[1];
-                }
-                q4_group<NT8>(wg, make_uint2(sb.x, sb.y), xb, sx, Cg);
-                q4_group<NT8>(wu, make_uint2(sb.z, sb.w), xb, sx, Cu);
-            }
-        }
-        __syncwarp();  // the slot is refilled by a later issue()
-        if (k % SPU == SPU - 1) {
-            const int unit = w0 + (k / SPU) * nw;
-            const int tile = unit / RB, rb = unit - tile * RB;
-            const TileInfo ti = tile_info(a, tile);
-#pragma unroll
-            for (int j = 0; j < NT8; ++j) {
-                gate_up_store<NT8>(a, ti, rb, j, Cg[j], Cu[j], lane);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) Cg[j][i] = Cu[j][i] = 0.f;
+            } else {
+                sx[j][hf] = p ? p[g] : 0.f;
             }
         }
     }
-    cp_wait<0>();
 }
 
-template <int FMT, int NT8, int NS, int GPS>
-__global__ void __launch_bounds__(128) k_down_tiles(ExpArgs a) {
-    using FL = DNFields<NT8>;
-    pdl_launch();
-    pdl_wait();
-    extern __shared__ uint4 smem_ring[];
+// NP projections (2 for gate/up, 1 for down) of SG groups per stage
+template <int NP, int SG>
+struct RingStage {
+    static constexpr int Q_BYTES = SG * 512, SB_BYTES = SG * 64;
+    static constexpr int BYTES = NP * (Q_BYTES + SB_BYTES);
+};
+
+template <int FMT, int NT8, int NS, int SG, bool DOWN>
+__device__ __forceinline__ void tiles_tma_body(const ExpArgs &a) {
+    constexpr int NP = DOWN ? 1 : 2;
+    using RS = RingStage<NP, SG>;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int gq = lane >> 2;
-    const int RB = a.d >> 4, G = a.f >> 6;
-    const int SPU = (G + GPS - 1) / GPS;
+    const int RB = DOWN ? (a.d >> 4) : (a.f >> 4);
+    const int G = DOWN ? (a.f >> 6) : (a.d >> 6);
+    const int SPU = (G + SG - 1) / SG;  // stages per unit
     const int n_units = *a.ntiles * RB;
     const int w0 = blockIdx.x * 4 + warp, nw = gridDim.x * 4;
     const int my_units = w0 < n_units ? (n_units - w0 + nw - 1) / nw : 0;
     const int total = my_units * SPU;
-    uint4 *ring = smem_ring + (size_t)warp * NS * GPS * FL::N * 32;
-    UnitSrc<NT8> P;
-    auto issue = [&](int k) {
-        if (k < total) {
-            const int unit = w0 + (k / SPU) * nw, gb = (k % SPU) * GPS;
-            if (unit != P.unit) unit_src<NT8, true>(P, a, unit, RB, lane);
-            uint4 *st = ring + (size_t)(k % NS) * GPS * FL::N * 32;
-#pragma unroll
-            for (int i = 0; i < GPS; ++i) {
-                const int g = min(gb + i, G - 1);
-                uint4 *sl = st + i * FL::N * 32 + lane;
-                cp_async16(sl + FL::W * 32, a.dn.q + ((P.blk * G + g) * 32 + lane) * 4);
-                cp_async8(sl + FL::SB * 32, a.dn.sb + ((P.blk * G + g) * 8 + gq) * 2);
-#pragma unroll
-                for (int j = 0; j < NT8; ++j) {
-                    const bool ok = P.row[j] != nullptr;
-                    const uint16_t *src = ok ? P.row[j] + g * 64 : a.h;
-                    cp_async16(sl + (FL::H + 2 * j) * 32, src, ok);
-                    cp_async16(sl + (FL::H + 2 * j + 1) * 32, src + 8, ok);
-#pragma unroll
-                    for (int hf = 0; hf < 2; ++hf) {
-                        const bool okh = P.srow[j][hf] != nullptr;
-                        cp_async16(sl + (FL::HS + 2 * j + hf) * 32, okh ? P.srow[j][hf] + 4 * g : a.hsum, okh);
-                    }
-                }
-            }
+    unsigned char *ring = smem_raw + (size_t)warp * NS * RS::BYTES;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem_raw + 4 * NS * RS::BYTES) + warp * NS;
+    const QProj P0 = DOWN ? a.dn : a.g, P1 = a.u;
+    const uint64_t pol = l2_evict_first_policy();
+    if (lane == 0) {
+        for (int i = 0; i < NS; ++i) mbar_init(bar + i, 1);
+        mbar_fence_init();
+    }
+    __syncwarp();
+    int p_unit = -1;
+    size_t p_blk = 0;
+    auto issue = [&](int k) {  // lane 0 only
+        if (k >= total) return;
+        const int unit = w0 + (k / SPU) * nw, g0 = (k % SPU) * SG;
+        if (unit != p_unit) {
+            p_unit = unit;
+            const int tile = unit / RB;
+            int e = a.tile_mode ? a.tiles[tile].x : a.idx[tile];
+            if (e < 0 || e >= a.E) e = 0;
+            p_blk = (size_t)e * RB + (unit - tile * RB);
+            if (!DOWN && g0 == 0 && a.dn_prefetch) prefetch_down(a, e, unit - tile * RB, RB, 0, 1);
         }
-        cp_commit();
+        const int ng = min(SG, G - g0);
+        uint64_t *b = bar + (k % NS);
+        unsigned char *st = ring + (size_t)(k % NS) * RS::BYTES;
+        mbar_expect_tx(b, (unsigned)(NP * ng * (512 + 64)));
+#pragma unroll
+        for (int p = 0; p < NP; ++p) {
+            const QProj &PP = p == 0 ? P0 : P1;
+            tma_load_1d(st + p * RS::Q_BYTES, PP.q + (p_blk * G + g0) * 128, ng * 512, b, pol);
+            tma_load_1d(st + NP * RS::Q_BYTES + p * RS::SB_BYTES, PP.sb + (p_blk * G + g0) * 16, ng * 64, b, pol);
+        }
     };
-    for (int k = 0; k < NS - 1; ++k) issue(k);
-    float C[NT8][4];
+    if (lane == 0)
+        for (int k = 0; k < NS - 1; ++k) issue(k);
+    UnitSrc<NT8> U;
+    float C0[NT8][4], C1[NT8][4];
 #pragma unroll
     for (int j = 0; j < NT8; ++j)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) C[j][i] = 0.f;
-    for (int k = 0; k < total; ++k) {
-        issue(k + NS - 1);
-        cp_wait<NS - 1>();
-        __syncwarp();
-        const uint4 *st = ring + (size_t)(k % NS) * GPS * FL::N * 32;
-        const int gb = (k % SPU) * GPS;
+        for (int i = 0; i < 4; ++i) C0[j][i] = C1[j][i] = 0.f;
+    uint32_t xb[NT8][8];
+    float sx[NT8][2];
+    bool ok = true;
+    for (int k = 0; k < total && ok; ++k) {
+        if (lane == 0) issue(k + NS - 1);
+        const int unit = w0 + (k / SPU) * nw, g0 = (k % SPU) * SG;
+        if (g0 == 0) {
+            unit_src<NT8, DOWN>(U, a, unit, RB, lane);
+            load_act<NT8, DOWN>(U, 0, xb, sx);
+        }
+        ok = mbar_wait_bounded(bar + (k % NS), (unsigned)((k / NS) & 1));
+        if (!ok) {
+            if (lane == 0) atomicOr(a.err, ERR_TIMEOUT);
+            break;
+        }
+        const unsigned char *st = ring + (size_t)(k % NS) * RS::BYTES;
+        const int ng = min(SG, G - g0);
+#pragma unroll 1
+        for (int i = 0; i < ng; ++i) {
+            uint32_t xn[NT8][8];
+            float sn[NT8][2];
+            if (g0 + i + 1 < G) load_act<NT8, DOWN>(U, g0 + i + 1, xn, sn);  // next group's activations
+            const uint4 w0v = reinterpret_cast<const uint4 *>(st)[i * 32 + lane];
+            const uint2 s0v = reinterpret_cast<const uint2 *>(st + NP * RS::Q_BYTES)[i * 8 + (lane >> 2)];
+            q4_group<NT8>(w0v, s0v, xb, sx, C0);
+            if (!DOWN) {
+                const uint4 w1v = reinterpret_cast<const uint4 *>(st + RS::Q_BYTES)[i * 32 + lane];
+                const uint2 s1v = reinterpret_cast<const uint2 *>(st + NP * RS::Q_BYTES + RS::SB_BYTES)[i * 8 + (lane >> 2)];
+                q4_group<NT8>(w1v, s1v, xb, sx, C1);
+            }
 #pragma unroll
-        for (int i = 0; i < GPS; ++i) {
-            if (gb + i < G) {
-                const uint4 *sl = st + i * FL::N * 32 + lane;
-                const uint4 w = sl[FL::W * 32];
-                const uint2 sb = *reinterpret_cast<const uint2 *>(sl + FL::SB * 32);
-                uint32_t hb[NT8][8];
-                float sx[NT8][2];
+            for (int j = 0; j < NT8; ++j) {
 #pragma unroll
-                for (int j = 0; j < NT8; ++j) {
-                    const uint4 h0 = sl[(FL::H + 2 * j) * 32], h1 = sl[(FL::H + 2 * j + 1) * 32];
-                    hb[j][0] = h0.x; hb[j][1] = h0.y; hb[j][2] = h0.z; hb[j][3] = h0.w;
-                    hb[j][4] = h1.x; hb[j][5] = h1.y; hb[j][6] = h1.z; hb[j][7] = h1.w;
-#pragma unroll
-                    for (int hf = 0; hf < 2; ++hf) {
-                        const float4 v = *reinterpret_cast<const float4 *>(sl + (FL::HS + 2 * j + hf) * 32);
-                        sx[j][hf] = (v.x + v.y) + (v.z + v.w);
-                    }
-                }
-                q4_group<NT8>(w, sb, hb, sx, C);
+                for (int q = 0; q < 8; ++q) xb[j][q] = xn[j][q];
+                sx[j][0] = sn[j][0];
+                sx[j][1] = sn[j][1];
             }
         }
-        __syncwarp();
+        __syncwarp();  // every lane is done with this stage before lane 0 refills it
         if (k % SPU == SPU - 1) {
-            const int unit = w0 + (k / SPU) * nw;
-            const int tile = unit / RB, rb = unit - tile * RB;
-            const TileInfo ti = tile_info(a, tile);
-            down_store_combine<NT8>(a, ti, rb, C, lane);
+            const int rb = unit - (unit / RB) * RB;
+            if (DOWN) {
+                down_store_combine<NT8>(a, U.ti, rb, C0, lane);
+            } else {
+#pragma unroll
+                for (int j = 0; j < NT8; ++j) gate_up_store<NT8>(a, U.ti, rb, j, C0[j], C1[j], lane);
+            }
 #pragma unroll
             for (int j = 0; j < NT8; ++j)
 #pragma unroll
-                for (int i = 0; i < 4; ++i) C[j][i] = 0.f;
+                for (int i = 0; i < 4; ++i) C0[j][i] = C1[j][i] = 0.f;
         }
     }
-    cp_wait<0>();
+    if (!ok) {  // drain: give every issued stage a bounded chance to land before the CTA exits
+        for (int k = 0; k < NS; ++k) mbar_wait_bounded(bar + k, 0u, 1u << 12), mbar_wait_bounded(bar + k, 1u, 1u << 12);
+    }
 }
 
-// shared-memory bytes of the tile kernels (4 warps per CTA)
-size_t gate_up_tiles_smem(int nt8, int ns, int gps) {
-    return (size_t)4 * ns * gps * (3 + 2 * nt8 + (nt8 + 1) / 2) * 32 * 16;
+template <int FMT, int NT8, int NS, int SG>
+__global__ void __launch_bounds__(128) k_gate_up_tiles(ExpArgs a) {
+    pdl_launch();
+    pdl_wait();
+    tiles_tma_body<FMT, NT8, NS, SG, false>(a);
 }
-size_t down_tiles_smem(int nt8, int ns, int gps) { return (size_t)4 * ns * gps * (2 + 4 * nt8) * 32 * 16; }
+
+template <int FMT, int NT8, int NS, int SG>
+__global__ void __launch_bounds__(128) k_down_tiles(ExpArgs a) {
+    pdl_launch();
+    pdl_wait();
+    tiles_tma_body<FMT, NT8, NS, SG, true>(a);
+}
+
+// shared-memory bytes of the TMA-ring tile kernels (4 warps per CTA, plus one mbarrier per stage and warp)
+size_t gate_up_tiles_smem(int nt8, int ns, int sg) {
+    (void)nt8;
+    return (size_t)4 * ns * 2 * sg * (512 + 64) + 4 * ns * 8;
+}
+size_t down_tiles_smem(int nt8, int ns, int sg) {
+    (void)nt8;
+    return (size_t)4 * ns * sg * (512 + 64) + 4 * ns * 8;
+}
 
 template __global__ void k_gate_up_slots<FMT_Q4, 8, 4>(ExpArgs);
 template __global__ void k_down_slots<FMT_Q4, 4, 4>(ExpArgs);
@@ -769,9 +735,9 @@ template __global__ void k_gate_up_tiles_reg<FMT_Q4, 1, 2>(ExpArgs);
 template __global__ void k_gate_up_tiles_reg<FMT_Q4, 2, 1>(ExpArgs);
 template __global__ void k_down_tiles_reg<FMT_Q4, 1, 2>(ExpArgs);
 template __global__ void k_down_tiles_reg<FMT_Q4, 2, 1>(ExpArgs);
-template __global__ void k_gate_up_tiles<FMT_Q4, 1, 4, 2>(ExpArgs);
-template __global__ void k_gate_up_tiles<FMT_Q4, 2, 3, 2>(ExpArgs);
-template __global__ void k_down_tiles<FMT_Q4, 1, 4, 2>(ExpArgs);
-template __global__ void k_down_tiles<FMT_Q4, 2, 4, 1>(ExpArgs);
+template __global__ void k_gate_up_tiles<FMT_Q4, 1, 3, 8>(ExpArgs);
+template __global__ void k_gate_up_tiles<FMT_Q4, 2, 3, 8>(ExpArgs);
+template __global__ void k_down_tiles<FMT_Q4, 1, 3, 8>(ExpArgs);
+template __global__ void k_down_tiles<FMT_Q4, 2, 3, 8>(ExpArgs);
 
 }  // namespace moeb
