@@ -98,7 +98,7 @@ Layout layout(long Tc, int d, int f, int E, int k) {
     L.logits = o; o = align256(o + 4 * (size_t)Tc * E);
     L.idx = o; o = align256(o + 4 * (size_t)TK);
     L.wts = o; o = align256(o + 4 * (size_t)TK);
-    L.xsum = o; o = align256(o + 4 * (size_t)Tc * (d / 64));
+    L.xsum = o; o = align256(o + 4 * (size_t)Tc * xsum_stride(d));
     L.ntiles = o; o += 256;
     L.tiles = o; o = align256(o + 16 * (size_t)(TK + E + 1));
     L.sorted = o; o = align256(o + 4 * (size_t)TK);
@@ -150,6 +150,7 @@ struct ExpLaunch {
     int gu_threads, dn_threads;
     size_t gu_smem, dn_smem;
     bool per_warp;  // tiles kernels: one unit per warp (4 warps per CTA); slots kernels: one unit per CTA
+    int rows_per_cta = 1;  // warp-specialized kernels: 16-row blocks per CTA work item
 };
 
 ExpLaunch pick_kernels(int fmt, int policy, int d, int f) {
@@ -158,11 +159,11 @@ ExpLaunch pick_kernels(int fmt, int policy, int d, int f) {
         return {k_gate_up_slots<FMT_Q4, 8, 4>, k_down_slots<FMT_Q4, 4, 4>, 256, 128, (size_t)d * 2,
                 (size_t)f * 2 + (size_t)f / 16 * 4, false};
     if (policy == MOEB_POLICY_TILES16_RING)
-        return {k_gate_up_tiles<FMT_Q4, 2, 3, 8>, k_down_tiles<FMT_Q4, 2, 3, 8>, 128, 128, gate_up_tiles_smem(2, 3, 8),
-                down_tiles_smem(2, 3, 8), true};
+        return {k_experts_ws<FMT_Q4, 2, 8, 4, 4, false>, k_experts_ws<FMT_Q4, 2, 8, 4, 4, true>, 288, 288,
+                experts_ws_smem(2, 8, 4, 4, false), experts_ws_smem(2, 8, 4, 4, true), false, 8};
     if (policy == MOEB_POLICY_TILES8_RING)
-        return {k_gate_up_tiles<FMT_Q4, 1, 3, 8>, k_down_tiles<FMT_Q4, 1, 3, 8>, 128, 128, gate_up_tiles_smem(1, 3, 8),
-                down_tiles_smem(1, 3, 8), true};
+        return {k_experts_ws<FMT_Q4, 1, 8, 4, 4, false>, k_experts_ws<FMT_Q4, 1, 8, 4, 4, true>, 288, 288,
+                experts_ws_smem(1, 8, 4, 4, false), experts_ws_smem(1, 8, 4, 4, true), false, 8};
     if (policy == MOEB_POLICY_TILES16)
         return {k_gate_up_tiles_reg<FMT_Q4, 2, 1>, k_down_tiles_reg<FMT_Q4, 2, 1>, 128, 128, 0, 0, true};
     return {k_gate_up_tiles_reg<FMT_Q4, 1, 2>, k_down_tiles_reg<FMT_Q4, 1, 2>, 128, 128, 0, 0, true};
@@ -181,8 +182,8 @@ bool allow_smem(const void *fn, size_t bytes) {
     return true;
 }
 
-int grid_for(void (*kern)(ExpArgs), int threads, size_t smem, long units, bool per_warp) {
-    const long ctas = per_warp ? (units + threads / 32 - 1) / (threads / 32) : units;
+int grid_for(void (*kern)(ExpArgs), int threads, size_t smem, long units, bool per_warp, int rows_per_cta) {
+    const long ctas = per_warp ? (units + threads / 32 - 1) / (threads / 32) : (units + rows_per_cta - 1) / rows_per_cta;
     const long cap = (long)occupancy((const void *)kern, threads, smem) * sm_count();
     return (int)std::max<long>(1, std::min(ctas, cap));
 }
@@ -199,13 +200,15 @@ int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaS
     if (!allow_smem((const void *)K.gu, K.gu_smem) || !allow_smem((const void *)K.dn, K.dn_smem))
         return check_launch("cudaFuncSetAttribute");
     {
-        const int grid = grid_for(K.gu, K.gu_threads, K.gu_smem, max_tiles * (a.f / 16), K.per_warp);
+        const long rbs = (a.f / 16 + K.rows_per_cta - 1) / K.rows_per_cta * K.rows_per_cta;
+        const int grid = grid_for(K.gu, K.gu_threads, K.gu_smem, max_tiles * rbs, K.per_warp, K.rows_per_cta);
         if (launch(K.gu, dim3(grid), dim3(K.gu_threads), K.gu_smem, st, a) != cudaSuccess)
             return check_launch("gate_up");
     }
     if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[2]), st);
     {
-        const int grid = grid_for(K.dn, K.dn_threads, K.dn_smem, max_tiles * (a.d / 16), K.per_warp);
+        const long rbs = (a.d / 16 + K.rows_per_cta - 1) / K.rows_per_cta * K.rows_per_cta;
+        const int grid = grid_for(K.dn, K.dn_threads, K.dn_smem, max_tiles * rbs, K.per_warp, K.rows_per_cta);
         if (launch(K.dn, dim3(grid), dim3(K.dn_threads), K.dn_smem, st, a) != cudaSuccess)
             return check_launch("down");
     }

@@ -14,6 +14,9 @@ enum : uint32_t {
     ERR_TIMEOUT = 2u,    // a bounded wait gave up
 };
 
+// Row stride (floats) of the per-64-group activation sums: padded to 4 so rows stay 16-byte aligned for TMA.
+__host__ __device__ __forceinline__ int xsum_stride(int d) { return ((d / 64 + 3) / 4) * 4; }
+
 MOEB_DEV float bf16lo(uint32_t v) { return __uint_as_float(v << 16); }
 MOEB_DEV float bf16hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
 MOEB_DEV float bf2f(uint16_t h) { return __uint_as_float(((uint32_t)h) << 16); }
@@ -117,6 +120,13 @@ MOEB_DEV void tma_load_1d(void *dst, const void *src, unsigned bytes, uint64_t *
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
             "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
+}
+
+MOEB_DEV void tma_load_1d(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
 }
 
 MOEB_DEV float warp_sum(float v) {

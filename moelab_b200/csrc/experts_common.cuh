@@ -1,0 +1,184 @@
+// Device helpers shared by the expert kernels (experts.cu, experts_ws.cu).
+#pragma once
+#include "common.cuh"
+#include "kernels.h"
+
+namespace moeb {
+
+struct TileInfo {
+    int e, start, n;
+};
+
+__device__ __forceinline__ TileInfo tile_info(const ExpArgs &a, int tile) {
+    TileInfo ti;
+    if (a.tile_mode) {
+        const int4 t = a.tiles[tile];
+        ti.e = t.x;
+        ti.start = t.y;
+        ti.n = t.z;
+    } else {
+        ti.e = a.idx[tile];
+        ti.start = tile;
+        ti.n = 1;
+    }
+    if (ti.e < 0 || ti.e >= a.E) ti.e = 0;  // invalid id: computed on expert 0, weighted 0 in the down epilogue
+    return ti;
+}
+
+__device__ __forceinline__ int tile_slot(const ExpArgs &a, const TileInfo &ti, int col) {
+    if (col >= ti.n) return -1;
+    return a.tile_mode ? a.sorted[ti.start + col] : ti.start;
+}
+
+// One 64-group of one projection: 4 k-steps x NT8 column tiles into P, then promotion into C.
+// w: {row gq: word 2c, 2c+1; row gq+8: word 2c, 2c+1}; sb: {row gq, row gq+8} scale|bias.
+template <int NT8>
+__device__ __forceinline__ void q4_group(const uint4 w, const uint2 sb, const uint32_t (&xb)[NT8][8],
+                                         const float (&sx)[NT8][2], float (&C)[NT8][4]) {
+    float P[NT8][4];
+#pragma unroll
+    for (int j = 0; j < NT8; ++j) P[j][0] = P[j][1] = P[j][2] = P[j][3] = 0.f;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const uint32_t wa0 = (s < 2) ? w.x : w.y, wa1 = (s < 2) ? w.z : w.w;
+        const int p0 = (2 * s) & 3, p1 = (2 * s + 1) & 3;
+        const uint32_t A[4] = {q4pair(wa0, p0), q4pair(wa1, p0), q4pair(wa0, p1), q4pair(wa1, p1)};
+#pragma unroll
+        for (int j = 0; j < NT8; ++j) mma_bf16(P[j], A, xb[j][2 * s], xb[j][2 * s + 1]);
+    }
+    const float s0 = bf16lo(sb.x), s1 = bf16lo(sb.y);
+    const float b0 = __fmaf_rn(-128.f, s0, bf16hi(sb.x)), b1 = __fmaf_rn(-128.f, s1, bf16hi(sb.y));
+#pragma unroll
+    for (int j = 0; j < NT8; ++j) {
+        C[j][0] = __fmaf_rn(s0, P[j][0], __fmaf_rn(b0, sx[j][0], C[j][0]));
+        C[j][1] = __fmaf_rn(s0, P[j][1], __fmaf_rn(b0, sx[j][1], C[j][1]));
+        C[j][2] = __fmaf_rn(s1, P[j][2], __fmaf_rn(b1, sx[j][0], C[j][2]));
+        C[j][3] = __fmaf_rn(s1, P[j][3], __fmaf_rn(b1, sx[j][1], C[j][3]));
+    }
+}
+
+__device__ __forceinline__ void load_b16(const uint16_t *p, uint32_t (&o)[8]) {
+    if (p) {
+        const uint4 u0 = *reinterpret_cast<const uint4 *>(p), u1 = *reinterpret_cast<const uint4 *>(p + 8);
+        o[0] = u0.x; o[1] = u0.y; o[2] = u0.z; o[3] = u0.w;
+        o[4] = u1.x; o[5] = u1.y; o[6] = u1.z; o[7] = u1.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = 0u;
+    }
+}
+
+// L2 prefetch of the 16-byte-aligned part of [p, p + bytes), in 4 KB pieces spread over a warp's lanes. The
+// range is shrunk inward to 16-byte boundaries, so nothing outside it is touched.
+__device__ __forceinline__ void prefetch_l2(const void *p, size_t bytes, int lane, int nlanes = 32) {
+    const uintptr_t b = ((uintptr_t)p + 15) & ~(uintptr_t)15, e = ((uintptr_t)p + bytes) & ~(uintptr_t)15;
+    for (uintptr_t q = b + (uintptr_t)lane * 4096; q < e; q += (uintptr_t)nlanes * 4096) {
+        const uint32_t n = (uint32_t)(e - q < 4096 ? e - q : 4096);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(q), "r"(n) : "memory");
+    }
+}
+
+// Pull the share [rb/RB, (rb+1)/RB) of expert e's down projection into L2 (it streams right after gate/up).
+// Called by `nlanes` lanes of a warp (lane in [0, nlanes)).
+__device__ __forceinline__ void prefetch_down(const ExpArgs &a, int e, int rb, int RB, int lane, int nlanes = 32) {
+    const int rb0 = (int)((long)rb * (a.d / 16) / RB), rb1 = (int)((long)(rb + 1) * (a.d / 16) / RB);
+    if (rb1 <= rb0) return;
+    const size_t blk = (size_t)e * (a.d / 16) + rb0;
+    prefetch_l2(a.dn.q + blk * (size_t)(a.f / 64) * 128, (size_t)(rb1 - rb0) * (a.f / 64) * 512, lane, nlanes);
+    prefetch_l2(a.dn.sb + blk * (size_t)(a.f / 64) * 16, (size_t)(rb1 - rb0) * (a.f / 64) * 64, lane, nlanes);
+}
+
+// Weights of one (16-row block, 64-group) for this lane.
+__device__ __forceinline__ uint4 ld_w(const QProj &P, size_t blk, int G, int g, int lane) {
+    return ld_stream_u4(P.q + ((blk * G + g) * 32 + lane) * 4);
+}
+__device__ __forceinline__ uint2 ld_sb(const QProj &P, size_t blk, int G, int g, int gq) {
+    return ld_stream_u2(P.sb + ((blk * G + g) * 8 + gq) * 2);
+}
+
+// gate/up epilogue for one column tile j of a unit: bias, activation, bf16 h, block sums.
+template <int NT8>
+__device__ __forceinline__ void gate_up_store(const ExpArgs &a, const TileInfo &ti, int rb, int j,
+                                              const float (&gs)[4], const float (&us)[4], int lane) {
+    const int gq = lane >> 2, c = lane & 3, f = a.f;
+    const int r0 = rb * 16 + gq, r1 = r0 + 8;
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+        const int slot = tile_slot(a, ti, j * 8 + 2 * c + hf);
+        float g0v = gs[hf], g1v = gs[2 + hf], u0v = us[hf], u1v = us[2 + hf];
+        if (a.bg) {
+            g0v += a.bg[(size_t)ti.e * f + r0];
+            g1v += a.bg[(size_t)ti.e * f + r1];
+            u0v += a.bu[(size_t)ti.e * f + r0];
+            u1v += a.bu[(size_t)ti.e * f + r1];
+        }
+        const uint16_t h0 = f2bf(act_glu(a.act, g0v, u0v)), h1 = f2bf(act_glu(a.act, g1v, u1v));
+        float part = slot >= 0 ? bf2f(h0) + bf2f(h1) : 0.f;
+        part += __shfl_xor_sync(0xffffffffu, part, 4);
+        part += __shfl_xor_sync(0xffffffffu, part, 8);
+        part += __shfl_xor_sync(0xffffffffu, part, 16);
+        if (slot >= 0) {
+            a.h[(size_t)slot * f + r0] = h0;
+            a.h[(size_t)slot * f + r1] = h1;
+            if (gq == 0) a.hsum[(size_t)slot * (f / 16) + rb] = part;
+        }
+    }
+}
+
+// down epilogue of one warp: write the weighted per-slot rows, arrive on the (token, row block) counters and
+// combine every token this arrival completed. Warp-synchronous; no CTA barrier.
+template <int NT8>
+__device__ __forceinline__ void down_store_combine(const ExpArgs &a, const TileInfo &ti, int rb,
+                                                   const float (&C)[NT8][4], int lane) {
+    const int gq = lane >> 2, c = lane & 3, d = a.d, k = a.k, RB = d >> 4;
+    const int r0 = rb * 16 + gq, r1 = r0 + 8;
+#pragma unroll
+    for (int j = 0; j < NT8; ++j)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+            const int slot = tile_slot(a, ti, j * 8 + 2 * c + hf);
+            if (slot >= 0) {
+                const int e_raw = a.idx[slot];
+                const float wsl = (e_raw >= 0 && e_raw < a.E) ? a.wts[slot] : 0.f;
+                float v0 = C[j][hf], v1 = C[j][2 + hf];
+                if (a.bd) {
+                    v0 += a.bd[(size_t)ti.e * d + r0];
+                    v1 += a.bd[(size_t)ti.e * d + r1];
+                }
+                a.yp[(size_t)slot * d + r0] = wsl * v0;
+                a.yp[(size_t)slot * d + r1] = wsl * v1;
+            }
+        }
+    __syncwarp();
+    if (lane == 0) __threadfence();  // cumulative over the warp's writes ordered by the __syncwarp
+    __syncwarp();
+    int tok = -1;
+    bool done = false;
+    if (lane < 8 * NT8) {
+        const int slot = tile_slot(a, ti, lane);
+        if (slot >= 0) {
+            tok = slot / k;
+            done = atomicAdd(a.ycnt + (size_t)tok * RB + rb, 1u) == (unsigned)(k - 1);
+        }
+    }
+    unsigned m = __ballot_sync(0xffffffffu, done);
+    if (m) {
+        if (lane == 0) __threadfence();
+        __syncwarp();
+    }
+    while (m) {
+        const int src = __ffs(m) - 1;
+        m &= m - 1;
+        const int t = __shfl_sync(0xffffffffu, tok, src);
+        if (lane < 16) {
+            const int r = rb * 16 + lane;
+            float acc = 0.f;
+            for (int jj = 0; jj < k; ++jj) acc += __ldcg(a.yp + ((size_t)t * k + jj) * d + r);
+            if (a.residual) acc += bf2f(a.residual[(size_t)t * d + r]);
+            a.y[(size_t)t * d + r] = f2bf(acc);
+        }
+        if (lane == 0) a.ycnt[(size_t)t * RB + rb] = 0u;
+    }
+}
+
+}  // namespace moeb

@@ -1,0 +1,207 @@
+// Grouped expert kernels, warp-specialized TMA pipeline (tile mode: slots grouped by expert).
+//
+// CTA = 1 producer warp + RBC consumer warps. A CTA work item ("super-unit") is one tile (<= 8*NT8 slots of one
+// expert) and RBC consecutive 16-row blocks of the projection. K is streamed in stages of SG 64-groups through
+// an NS-deep shared-memory ring:
+//   producer: per stage, its lanes issue 1-D TMA bulk copies (cp.async.bulk, no multicast, evict-first in L2)
+//     of the RBC row blocks' codes and scale|bias words (contiguous in the fragment-major layout), of the
+//     tile's activation row chunks (x for gate/up, h for down; one copy per slot, rows padded by 16 bytes in
+//     shared memory to spread banks) and of their group sums, all completing on the stage's "full" mbarrier;
+//   consumers: each warp owns one row block, waits on "full", runs the m16n8k16 raw-code MMAs and fp32 scale
+//     promotion of experts_common.cuh on the stage, and arrives on the stage's "empty" mbarrier.
+// The activation tile is fetched once per CTA and shared by all row blocks; consumers never touch global
+// memory until their epilogue (gate/up: bias, activation, h, hsum; down: weighted rows + deterministic combine).
+// Every mbarrier wait is bounded; a timeout records MOEB_DEVERR_TIMEOUT and the CTA stops.
+#include "experts_common.cuh"
+
+namespace moeb {
+
+template <int NT8, int RBC, int SG, bool DOWN>
+struct WSL {
+    static constexpr int NP = DOWN ? 1 : 2;
+    static constexpr int COLS = 8 * NT8;
+    static constexpr int W_BYTES = NP * RBC * SG * 512;
+    static constexpr int SB_BYTES = NP * RBC * SG * 64;
+    static constexpr int X_ROW = SG * 128 + 16;
+    static constexpr int X_BYTES = COLS * X_ROW;
+    static constexpr int S_ROW = ((DOWN ? SG * 16 : SG * 4) + 15) / 16 * 16;
+    static constexpr int S_BYTES = COLS * S_ROW;
+    static constexpr int STAGE = W_BYTES + SB_BYTES + X_BYTES + S_BYTES;
+};
+
+MOEB_DEV void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+template <int FMT, int NT8, int RBC, int SG, int NS, bool DOWN>
+__global__ void __launch_bounds__(32 * (RBC + 1), 1) k_experts_ws(ExpArgs a) {
+    using L = WSL<NT8, RBC, SG, DOWN>;
+    pdl_launch();
+    pdl_wait();
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem_raw + NS * L::STAGE);
+    uint64_t *empty = full + NS;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int RB = DOWN ? (a.d >> 4) : (a.f >> 4);
+    const int G = DOWN ? (a.f >> 6) : (a.d >> 6);
+    const int RBS = (RB + RBC - 1) / RBC;  // super-units per tile
+    const int SPU = (G + SG - 1) / SG;     // stages per super-unit
+    const int n_tiles = a.tile_mode ? *a.ntiles : a.T * a.k;
+    const int n_su = n_tiles * RBS;
+    const int my_su = (int)blockIdx.x < n_su ? (n_su - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+    const int total = my_su * SPU;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(full + i, 1);
+            mbar_init(empty + i, RBC);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    if (warp == RBC) {
+        // ------------------------------------------------------------ producer warp
+        const uint64_t pol = l2_evict_first_policy();
+        const QProj P0 = DOWN ? a.dn : a.g, P1 = a.u;
+        for (int k = 0; k < total; ++k) {
+            const int slot = k % NS;
+            if (k >= NS && !mbar_wait_bounded(empty + slot, (unsigned)(((k / NS) - 1) & 1))) {
+                if (lane == 0) atomicOr(a.err, ERR_TIMEOUT);
+                return;
+            }
+            const int su = (int)blockIdx.x + (k / SPU) * (int)gridDim.x;
+            const int tile = su / RBS, rb0 = (su - tile * RBS) * RBC;
+            const int g0 = (k % SPU) * SG, ng = min(SG, G - g0);
+            const TileInfo ti = tile_info(a, tile);
+            const int nrb = min(RBC, RB - rb0), ncol = min(L::COLS, ti.n);
+            const int sum_bytes = DOWN ? ng * 16 : ((ng + 3) / 4) * 16;
+            if (lane == 0) {
+                if (!DOWN && g0 == 0 && a.dn_prefetch)
+                    for (int r = 0; r < nrb; ++r) prefetch_down(a, ti.e, rb0 + r, RB, 0, 1);
+                mbar_expect_tx(full + slot, (unsigned)(L::NP * nrb * ng * (512 + 64) + ncol * (ng * 128 + sum_bytes)));
+            }
+            __syncwarp();
+            unsigned char *st = smem_raw + (size_t)slot * L::STAGE;
+            const int n_w = L::NP * nrb;  // weight copies (each: codes + scale|bias)
+            for (int ci = lane; ci < n_w + ncol; ci += 32) {
+                if (ci < n_w) {
+                    const int p = ci / nrb, r = ci - p * nrb;
+                    const QProj &PP = p == 0 ? P0 : P1;
+                    const size_t blk = (size_t)ti.e * RB + rb0 + r;
+                    tma_load_1d(st + (p * RBC + r) * SG * 512, PP.q + (blk * G + g0) * 128, ng * 512, full + slot, pol);
+                    tma_load_1d(st + L::W_BYTES + (p * RBC + r) * SG * 64, PP.sb + (blk * G + g0) * 16, ng * 64,
+                                full + slot, pol);
+                } else {
+                    const int col = ci - n_w;
+                    const int s_ = tile_slot(a, ti, col);
+                    const uint16_t *row = DOWN ? a.h + (size_t)s_ * a.f : a.x + (size_t)(s_ / a.k) * a.d;
+                    tma_load_1d(st + L::W_BYTES + L::SB_BYTES + col * L::X_ROW, row + g0 * 64, ng * 128, full + slot);
+                    const float *srow = DOWN ? a.hsum + (size_t)s_ * (a.f / 16) + 4 * g0
+                                             : a.xsum + (size_t)(s_ / a.k) * xsum_stride(a.d) + g0;
+                    tma_load_1d(st + L::W_BYTES + L::SB_BYTES + L::X_BYTES + col * L::S_ROW, srow, sum_bytes,
+                                full + slot);
+                }
+            }
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------- consumer warps (one row block each)
+    const int gq = lane >> 2, c = lane & 3;
+    float C0[NT8][4], C1[NT8][4];
+    TileInfo ti;
+    int rb = 0;
+    for (int k = 0; k < total; ++k) {
+        const int slot = k % NS;
+        const int su = (int)blockIdx.x + (k / SPU) * (int)gridDim.x;
+        const int tile = su / RBS;
+        const int g0 = (k % SPU) * SG, ng = min(SG, G - g0);
+        if (g0 == 0) {
+            ti = tile_info(a, tile);
+            rb = (su - tile * RBS) * RBC + warp;
+#pragma unroll
+            for (int j = 0; j < NT8; ++j)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) C0[j][i] = C1[j][i] = 0.f;
+        }
+        if (!mbar_wait_bounded(full + slot, (unsigned)((k / NS) & 1))) {
+            if (lane == 0) atomicOr(a.err, ERR_TIMEOUT);
+            // give the copies that may still be in flight into this CTA's ring a bounded chance to land
+            for (int q = 1; q < NS && k + q < total; ++q)
+                mbar_wait_bounded(full + (k + q) % NS, (unsigned)(((k + q) / NS) & 1), 1u << 12);
+            return;
+        }
+        const unsigned char *st = smem_raw + (size_t)slot * L::STAGE;
+        if (rb < RB) {
+            const unsigned char *xs = st + L::W_BYTES + L::SB_BYTES;
+            const unsigned char *ss = xs + L::X_BYTES;
+#pragma unroll
+            for (int i = 0; i < SG; ++i) {
+                if (i < ng) {
+                    uint32_t xb[NT8][8];
+                    float sx[NT8][2];
+#pragma unroll
+                    for (int j = 0; j < NT8; ++j) {
+                        const int col = j * 8 + gq;
+                        if (col < ti.n) {
+                            const uint4 *xp = reinterpret_cast<const uint4 *>(xs + col * L::X_ROW + i * 128 + 32 * c);
+                            const uint4 u0 = xp[0], u1 = xp[1];
+                            xb[j][0] = u0.x; xb[j][1] = u0.y; xb[j][2] = u0.z; xb[j][3] = u0.w;
+                            xb[j][4] = u1.x; xb[j][5] = u1.y; xb[j][6] = u1.z; xb[j][7] = u1.w;
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) xb[j][q] = 0u;
+                        }
+#pragma unroll
+                        for (int hf = 0; hf < 2; ++hf) {
+                            const int cc = j * 8 + 2 * c + hf;
+                            if (cc < ti.n) {
+                                if (DOWN) {
+                                    const float4 v = *reinterpret_cast<const float4 *>(ss + cc * L::S_ROW + i * 16);
+                                    sx[j][hf] = (v.x + v.y) + (v.z + v.w);
+                                } else {
+                                    sx[j][hf] = reinterpret_cast<const float *>(ss + cc * L::S_ROW)[i];
+                                }
+                            } else {
+                                sx[j][hf] = 0.f;
+                            }
+                        }
+                    }
+                    const uint4 w0 = reinterpret_cast<const uint4 *>(st + (warp * SG + i) * 512)[lane];
+                    const uint2 b0 = reinterpret_cast<const uint2 *>(st + L::W_BYTES + (warp * SG + i) * 64)[gq];
+                    q4_group<NT8>(w0, b0, xb, sx, C0);
+                    if (!DOWN) {
+                        const uint4 w1 = reinterpret_cast<const uint4 *>(st + ((RBC + warp) * SG + i) * 512)[lane];
+                        const uint2 b1 =
+                            reinterpret_cast<const uint2 *>(st + L::W_BYTES + ((RBC + warp) * SG + i) * 64)[gq];
+                        q4_group<NT8>(w1, b1, xb, sx, C1);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + slot);
+        if (k % SPU == SPU - 1 && rb < RB) {
+            if (DOWN) {
+                down_store_combine<NT8>(a, ti, rb, C0, lane);
+            } else {
+#pragma unroll
+                for (int j = 0; j < NT8; ++j) gate_up_store<NT8>(a, ti, rb, j, C0[j], C1[j], lane);
+            }
+        }
+    }
+}
+
+size_t experts_ws_smem(int nt8, int rbc, int sg, int ns, bool down) {
+    const int np = down ? 1 : 2, cols = 8 * nt8;
+    const size_t stage = (size_t)np * rbc * sg * (512 + 64) + (size_t)cols * (sg * 128 + 16) +
+                         (size_t)cols * (((down ? sg * 16 : sg * 4) + 15) / 16 * 16);
+    return ns * stage + 2 * ns * 8;
+}
+
+template __global__ void k_experts_ws<FMT_Q4, 1, 8, 4, 4, false>(ExpArgs);
+template __global__ void k_experts_ws<FMT_Q4, 2, 8, 4, 4, false>(ExpArgs);
+template __global__ void k_experts_ws<FMT_Q4, 1, 8, 4, 4, true>(ExpArgs);
+template __global__ void k_experts_ws<FMT_Q4, 2, 8, 4, 4, true>(ExpArgs);
+
+}  // namespace moeb

@@ -90,6 +90,9 @@ template <int FMT, int NT8, int GPW>
 __global__ void k_gate_up_tiles_reg(ExpArgs a);
 template <int FMT, int NT8, int GPW>
 __global__ void k_down_tiles_reg(ExpArgs a);
+template <int FMT, int NT8, int RBC, int SG, int NS, bool DOWN>
+__global__ void k_experts_ws(ExpArgs a);
+size_t experts_ws_smem(int nt8, int rbc, int sg, int ns, bool down);
 size_t gate_up_tiles_smem(int nt8, int ns, int gps);
 size_t down_tiles_smem(int nt8, int ns, int gps);
 

@@ -228,7 +228,7 @@ __global__ void __launch_bounds__(128) k_router(RouterArgs a) {
                         p += __shfl_xor_sync(0xffffffffu, p, 1);
                         p += __shfl_xor_sync(0xffffffffu, p, 2);
                         p += __shfl_xor_sync(0xffffffffu, p, 4);
-                        if (i < nt && c < nch && (lane & 7) == 0) a.xsum[(size_t)(t0 + i) * (a.d / 64) + c / 8] = p;
+                        if (i < nt && c < nch && (lane & 7) == 0) a.xsum[(size_t)(t0 + i) * xsum_stride(a.d) + c / 8] = p;
                     }
                 }
             }
@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(256) k_prep(PrepArgs a) {
     pdl_wait();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int t = blockIdx.x * 8 + warp;
-    if (t < a.T) row_group_sums(a.x + (size_t)t * a.d, a.d, a.xsum + (size_t)t * (a.d / 64), lane);
+    if (t < a.T) row_group_sums(a.x + (size_t)t * a.d, a.d, a.xsum + (size_t)t * xsum_stride(a.d), lane);
     if (a.tiles == nullptr) {
         // slot mode: only validate ids
         for (int s = blockIdx.x * 256 + threadIdx.x; s < a.T * a.k; s += gridDim.x * 256) {
