@@ -195,7 +195,7 @@ int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaS
     const long max_tiles = a.tile_mode ? std::min<long>(TK, (long)a.E + TK / nt) : TK;
     ExpLaunch K = pick_kernels(fmt, policy, a.d, a.f);
     if (!K.gu) return fail(MOEB_EUNSUP, "format not supported%s");
-    if (!K.per_warp && (K.gu_smem > 48 * 1024 || K.dn_smem > 48 * 1024))
+    if (policy == MOEB_POLICY_SLOTS && (K.gu_smem > 48 * 1024 || K.dn_smem > 48 * 1024))
         return fail(MOEB_EINVAL, "d or f too large for the decode kernels%s");
     if (!allow_smem((const void *)K.gu, K.gu_smem) || !allow_smem((const void *)K.dn, K.dn_smem))
         return check_launch("cudaFuncSetAttribute");
