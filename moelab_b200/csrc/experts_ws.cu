@@ -61,45 +61,83 @@ __global__ void __launch_bounds__(32 * (RBC + 1), 1) k_experts_ws(ExpArgs a) {
 
     if (warp == RBC) {
         // ------------------------------------------------------------ producer warp
+        // Lane roles are fixed: lanes [0, NP*RBC) copy one (projection, row block) each, lanes [16, 16 + COLS)
+        // copy one activation column each. Per work item every lane computes its source bases once; the item's
+        // tile record and slot ids are fetched one item ahead so no global load sits on the issue path.
+        static_assert(L::NP * RBC <= 16 && L::COLS <= 16, "producer lane roles");
         const uint64_t pol = l2_evict_first_policy();
-        const QProj P0 = DOWN ? a.dn : a.g, P1 = a.u;
+        const QProj PP = (DOWN || lane < RBC) ? (DOWN ? a.dn : a.g) : a.u;
+        const int wr = lane % RBC;        // weight lane: row block offset
+        const int col = lane - 16;        // column lane: column index
+        const bool wlane = lane < L::NP * RBC, clane = col >= 0 && col < L::COLS;
+        auto fetch_tile = [&](int su) {  // tile record (expert, start, n)
+            const int tile = su / RBS;
+            return a.tile_mode ? a.tiles[tile] : make_int4(a.idx[tile], tile, 1, 0);
+        };
+        auto fetch_slot = [&](const int4 &tr) {  // this lane's slot id, or -1
+            return (clane && col < tr.z) ? (a.tile_mode ? a.sorted[tr.y + col] : tr.y) : -1;
+        };
+        int4 tr_n = make_int4(0, 0, 0, 0);
+        int sl_n = -1;
+        if (my_su > 0) {
+            tr_n = fetch_tile(blockIdx.x);
+            sl_n = fetch_slot(tr_n);
+        }
+        const unsigned char *src0 = nullptr, *src1 = nullptr;
+        int nrb = 0, ncol = 0, e = 0;
         for (int k = 0; k < total; ++k) {
             const int slot = k % NS;
+            const int g0 = (k % SPU) * SG, ng = min(SG, G - g0);
+            if (g0 == 0) {  // new work item: take the prefetched metadata, prefetch the next item's
+                const int su = (int)blockIdx.x + (k / SPU) * (int)gridDim.x;
+                const int rb0 = (su - (su / RBS) * RBS) * RBC;
+                e = (tr_n.x < 0 || tr_n.x >= a.E) ? 0 : tr_n.x;
+                ncol = min(L::COLS, tr_n.z);
+                nrb = min(RBC, RB - rb0);
+                const int s_ = sl_n;
+                if (wlane && wr < nrb) {
+                    const size_t blk = (size_t)e * RB + rb0 + wr;
+                    src0 = reinterpret_cast<const unsigned char *>(PP.q + blk * G * 128);
+                    src1 = reinterpret_cast<const unsigned char *>(PP.sb + blk * G * 16);
+                } else if (clane && s_ >= 0) {
+                    src0 = reinterpret_cast<const unsigned char *>(DOWN ? a.h + (size_t)s_ * a.f
+                                                                        : a.x + (size_t)(s_ / a.k) * a.d);
+                    src1 = reinterpret_cast<const unsigned char *>(DOWN ? a.hsum + (size_t)s_ * (a.f / 16)
+                                                                        : a.xsum + (size_t)(s_ / a.k) * xsum_stride(a.d));
+                } else {
+                    src0 = src1 = nullptr;
+                }
+                if (!DOWN && lane == 0 && a.dn_prefetch)
+                    for (int r = 0; r < nrb; ++r) prefetch_down(a, e, rb0 + r, RB, 0, 1);
+                const int nsu = su + (int)gridDim.x;
+                if (nsu < n_su) {
+                    tr_n = fetch_tile(nsu);                 // in flight during this item's stages
+                    if (SPU == 1) sl_n = fetch_slot(tr_n);  // no later stage to hide it behind
+                }
+            } else if (g0 == SG) {
+                const int nsu = (int)blockIdx.x + (k / SPU + 1) * (int)gridDim.x;
+                if (nsu < n_su) sl_n = fetch_slot(tr_n);
+            }
             if (k >= NS && !mbar_wait_bounded(empty + slot, (unsigned)(((k / NS) - 1) & 1))) {
                 if (lane == 0) atomicOr(a.err, ERR_TIMEOUT);
                 return;
             }
-            const int su = (int)blockIdx.x + (k / SPU) * (int)gridDim.x;
-            const int tile = su / RBS, rb0 = (su - tile * RBS) * RBC;
-            const int g0 = (k % SPU) * SG, ng = min(SG, G - g0);
-            const TileInfo ti = tile_info(a, tile);
-            const int nrb = min(RBC, RB - rb0), ncol = min(L::COLS, ti.n);
             const int sum_bytes = DOWN ? ng * 16 : ((ng + 3) / 4) * 16;
-            if (lane == 0) {
-                if (!DOWN && g0 == 0 && a.dn_prefetch)
-                    for (int r = 0; r < nrb; ++r) prefetch_down(a, ti.e, rb0 + r, RB, 0, 1);
+            if (lane == 0)
                 mbar_expect_tx(full + slot, (unsigned)(L::NP * nrb * ng * (512 + 64) + ncol * (ng * 128 + sum_bytes)));
-            }
             __syncwarp();
             unsigned char *st = smem_raw + (size_t)slot * L::STAGE;
-            const int n_w = L::NP * nrb;  // weight copies (each: codes + scale|bias)
-            for (int ci = lane; ci < n_w + ncol; ci += 32) {
-                if (ci < n_w) {
-                    const int p = ci / nrb, r = ci - p * nrb;
-                    const QProj &PP = p == 0 ? P0 : P1;
-                    const size_t blk = (size_t)ti.e * RB + rb0 + r;
-                    tma_load_1d(st + (p * RBC + r) * SG * 512, PP.q + (blk * G + g0) * 128, ng * 512, full + slot, pol);
-                    tma_load_1d(st + L::W_BYTES + (p * RBC + r) * SG * 64, PP.sb + (blk * G + g0) * 16, ng * 64,
+            if (src0 != nullptr) {
+                if (wlane) {
+                    const int p = lane / RBC;
+                    tma_load_1d(st + (p * RBC + wr) * SG * 512, src0 + (size_t)g0 * 512, ng * 512, full + slot, pol);
+                    tma_load_1d(st + L::W_BYTES + (p * RBC + wr) * SG * 64, src1 + (size_t)g0 * 64, ng * 64,
                                 full + slot, pol);
                 } else {
-                    const int col = ci - n_w;
-                    const int s_ = tile_slot(a, ti, col);
-                    const uint16_t *row = DOWN ? a.h + (size_t)s_ * a.f : a.x + (size_t)(s_ / a.k) * a.d;
-                    tma_load_1d(st + L::W_BYTES + L::SB_BYTES + col * L::X_ROW, row + g0 * 64, ng * 128, full + slot);
-                    const float *srow = DOWN ? a.hsum + (size_t)s_ * (a.f / 16) + 4 * g0
-                                             : a.xsum + (size_t)(s_ / a.k) * xsum_stride(a.d) + g0;
-                    tma_load_1d(st + L::W_BYTES + L::SB_BYTES + L::X_BYTES + col * L::S_ROW, srow, sum_bytes,
+                    tma_load_1d(st + L::W_BYTES + L::SB_BYTES + col * L::X_ROW, src0 + (size_t)g0 * 128, ng * 128,
                                 full + slot);
+                    tma_load_1d(st + L::W_BYTES + L::SB_BYTES + L::X_BYTES + col * L::S_ROW,
+                                src1 + (size_t)g0 * (DOWN ? 16 : 4), sum_bytes, full + slot);
                 }
             }
         }
