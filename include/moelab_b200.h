@@ -107,6 +107,19 @@ int moeb_layer_q4(const void *x, const void *gate_w, const void *gate_b, int nor
                   int policy, const void *residual, void *y, int *idx_out, float *wts_out,
                   void *const *stage_events, void *ws, size_t ws_bytes, cudaStream_t stream);
 
+/* --- moeb_experts_q4 for callers that cannot allocate device memory. No counterpart in the reference (moe-lab
+ * always lets the variant allocate its scratch). The scratch lives in a static 16 MiB device array inside the
+ * library (held by every GPU that loads it until exit), so the caller passes only inputs and the output. T is
+ * limited to what fits: moeb_workspace_bytes(T, d, f, E, k) <= MOEB_STATIC_SCRATCH_BYTES, else MOEB_EINVAL.
+ * The first call on a device looks up the array's device address; make it before any stream capture. All
+ * calls share the array: calls that overlap on the GPU (two streams, two threads) race. Device error bits are
+ * cleared on entry and not readable afterwards. Nothing is allocated. */
+#define MOEB_STATIC_SCRATCH_BYTES (16u << 20)
+int moeb_experts_q4_static(const void *x, const void *qg, const void *sbg, const void *qu, const void *sbu,
+                           const void *qd, const void *sbd, const float *bg, const float *bu, const float *bd,
+                           const int *idx, const float *wts, int T, int d, int f, int E, int k, int act, int policy,
+                           const void *residual, void *y, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

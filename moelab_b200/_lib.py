@@ -35,6 +35,7 @@ SIGNATURES = {
     "moeb_mxfp4_from_mlx": (_I, [_P, _P, _L, _L, _P, _P, _P]),
     "moeb_router": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _S, _P]),
     "moeb_experts_q4": (_I, [_P] * 12 + [_I] * 7 + [_P, _P, _P, _S, _P]),
+    "moeb_experts_q4_static": (_I, [_P] * 12 + [_I] * 7 + [_P, _P, _P]),
     "moeb_layer_q4": (_I, [_P, _P, _P, _I, _F] + [_P] * 9 + [_I] * 7 + [_P, _P, _P, _P, _P, _P, _S, _P]),
 }
 

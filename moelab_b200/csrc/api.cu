@@ -260,6 +260,17 @@ int launch_router(const void *x, const void *wg, const void *bias, int T, int d,
 
 }  // namespace
 
+namespace moeb {
+void set_error(const char *msg) { snprintf(g_err, sizeof g_err, "%s", msg); }
+
+// Bytes at the start of a workspace of `ws_bytes` that hold counters and the error word (must read zero before
+// a call); 0 if the workspace cannot hold a single token.
+size_t zero_region_bytes(size_t ws_bytes, int d, int f, int E, int k) {
+    const long cap = capacity(ws_bytes, d, f, E, k);
+    return cap < 1 ? 0 : layout(cap, d, f, E, k).zero_end;
+}
+}  // namespace moeb
+
 extern "C" {
 
 int moeb_version(void) { return MOEB_VERSION; }

@@ -98,4 +98,7 @@ size_t down_tiles_smem(int nt8, int ns, int gps);
 
 enum { FMT_Q4 = 0, FMT_FP4 = 1 };
 
+size_t zero_region_bytes(size_t ws_bytes, int d, int f, int E, int k);
+void set_error(const char *msg);  // message returned by moeb_last_error()
+
 }  // namespace moeb
