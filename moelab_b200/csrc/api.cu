@@ -133,12 +133,14 @@ int check_shape(int T, int d, int f, int E, int k) {
 
 // ------------------------------------------------------------------ dispatcher
 // Load = T*k/E (average slots per expert; the reference's policy variable, metal_q4_moe.py:42-46).
-// Few slots: one tile per slot (no routing step). Otherwise group slots by expert into tiles of 8 or 16.
+// Measured on B200 (Qwen3-30B shape, 16 layers cycled): the split-K decode kernels win up to 16 slots
+// (T <= 2 at k = 8); above that the register-pipelined tiles of 8 slots are fastest at every load measured
+// (T = 4 .. 256, load 0.25 .. 16); tiles of 16 and the TMA variants stay selectable for other shapes.
 int choose_policy(int T, int E, int k) {
     const long TK = (long)T * k;
-    const double load = (double)TK / E;
-    if (TK <= 64 || load < 1.0) return MOEB_POLICY_SLOTS;
-    return load <= 6.0 ? MOEB_POLICY_TILES8 : MOEB_POLICY_TILES16;
+    (void)E;
+    if (TK <= 16) return MOEB_POLICY_SLOTS;
+    return MOEB_POLICY_TILES8;
 }
 
 int nt_of(int policy) { return (policy == MOEB_POLICY_TILES16 || policy == MOEB_POLICY_TILES16_RING) ? 16 : 8; }

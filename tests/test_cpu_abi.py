@@ -39,9 +39,9 @@ def test_host_only_calls():
     assert b >= 256 * 8 * (768 * 2 + 2048 * 4)
     # dispatcher: decode -> per-slot tiles; high load -> grouped tiles
     assert lib.moeb_policy(1, 128, 8) == _lib.POLICY_SLOTS
-    assert lib.moeb_policy(4, 128, 8) == _lib.POLICY_SLOTS
+    assert lib.moeb_policy(2, 128, 8) == _lib.POLICY_SLOTS
+    assert lib.moeb_policy(4, 128, 8) == _lib.POLICY_TILES8
     assert lib.moeb_policy(256, 128, 8) in (_lib.POLICY_TILES8, _lib.POLICY_TILES16)
-    assert lib.moeb_policy(4096, 8, 2) == _lib.POLICY_TILES16
 
 
 def test_bad_shape_is_rejected_before_any_device_work():
