@@ -344,7 +344,7 @@ def main():
     tp = os.path.join(ROOT, "profiles", "traffic_gate_up.json")
     if os.path.exists(tp):
         try:
-            traffic = json.load(open(tp)).get(str(T))
+            traffic = json.load(open(tp)).get(str(T))  # ncu dram bytes of one launch, committed summary
         except (OSError, ValueError):
             traffic = None
     sweep = []
@@ -397,7 +397,8 @@ def main():
         "kernels_us": {"router": round(statistics.mean(r_us), 3), "gate_up": round(statistics.mean(gu_us), 3),
                        "down": round(statistics.mean(dn_us), 3),
                        "note": "CUDA events between stages (serialised, eager)"},
-        "roofline": {"bound": "hbm", "kernel": "k_gate_up", "achieved": round(gu_ach, 1), "peak": peaks["hbm_gbs"],
+        "roofline": {"bound": "hbm", "kernel": "k_gate_up_slots" if T * K_TOP <= 16 else "k_gate_up_tiles_reg",
+                     "achieved": round(gu_ach, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(gu_ach / peaks["hbm_gbs"], 3), "traffic": traffic,
                      "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)" if peaks["source"] == "measured"
                      else "fallback 6650 GB/s",
