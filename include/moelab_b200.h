@@ -96,6 +96,13 @@ int moeb_experts_q4(const void *x, const void *qg, const void *sbg, const void *
                     const int *idx, const float *wts, int T, int d, int f, int E, int k, int act, int policy,
                     const void *residual, void *y, void *ws, size_t ws_bytes, cudaStream_t stream);
 
+/* --- the same for MXFP4 experts (E2M1 codes + E8M0 scales; replaces metal_mxfp4_moe.py:474-512 run and, with
+ * act = 2 and biases, metal_mxfp4_gptoss.py:128-167 run). The E8M0 scale is folded exactly into bf16 operands. */
+int moeb_experts_mxfp4(const void *x, const void *qg, const void *scg, const void *qu, const void *scu,
+                       const void *qd, const void *scd, const float *bg, const float *bu, const float *bd,
+                       const int *idx, const float *wts, int T, int d, int f, int E, int k, int act, int policy,
+                       const void *residual, void *y, void *ws, size_t ws_bytes, cudaStream_t stream);
+
 /* --- full layer call (x, gate weights, packed expert weights + scales + biases, k) -> y: router, routing
  * step, grouped experts and the weighted combine in one stream-ordered sequence (3 launches).
  * Replaces the patched MoE block call of moelab/e2e.py:51-69 (router + mod.run). idx_out / wts_out may be
@@ -106,6 +113,12 @@ int moeb_layer_q4(const void *x, const void *gate_w, const void *gate_b, int nor
                   const float *bg, const float *bu, const float *bd, int T, int d, int f, int E, int k, int act,
                   int policy, const void *residual, void *y, int *idx_out, float *wts_out,
                   void *const *stage_events, void *ws, size_t ws_bytes, cudaStream_t stream);
+/* MXFP4 layer (gpt-oss: gate_b = router bias, act = 2, expert biases bg/bu/bd). */
+int moeb_layer_mxfp4(const void *x, const void *gate_w, const void *gate_b, int norm, float rscale, const void *qg,
+                     const void *scg, const void *qu, const void *scu, const void *qd, const void *scd,
+                     const float *bg, const float *bu, const float *bd, int T, int d, int f, int E, int k, int act,
+                     int policy, const void *residual, void *y, int *idx_out, float *wts_out,
+                     void *const *stage_events, void *ws, size_t ws_bytes, cudaStream_t stream);
 
 /* --- moeb_experts_q4 for callers that cannot allocate device memory. No counterpart in the reference (moe-lab
  * always lets the variant allocate its scratch). The scratch lives in a static 16 MiB device array inside the

@@ -37,6 +37,8 @@ SIGNATURES = {
     "moeb_experts_q4": (_I, [_P] * 12 + [_I] * 7 + [_P, _P, _P, _S, _P]),
     "moeb_experts_q4_static": (_I, [_P] * 12 + [_I] * 7 + [_P, _P, _P]),
     "moeb_layer_q4": (_I, [_P, _P, _P, _I, _F] + [_P] * 9 + [_I] * 7 + [_P, _P, _P, _P, _P, _P, _S, _P]),
+    "moeb_experts_mxfp4": (_I, [_P] * 12 + [_I] * 7 + [_P, _P, _P, _S, _P]),
+    "moeb_layer_mxfp4": (_I, [_P, _P, _P, _I, _F] + [_P] * 9 + [_I] * 7 + [_P, _P, _P, _P, _P, _P, _S, _P]),
 }
 
 _lib = None

@@ -156,6 +156,14 @@ struct ExpLaunch {
 };
 
 ExpLaunch pick_kernels(int fmt, int policy, int d, int f) {
+    if (fmt == FMT_FP4) {  // MXFP4: decode and register-tile kernels (the TMA variant is int4 only)
+        if (policy == MOEB_POLICY_SLOTS)
+            return {k_gate_up_slots<FMT_FP4, 8, 4>, k_down_slots<FMT_FP4, 4, 4>, 256, 128, (size_t)d * 2,
+                    (size_t)f * 2 + (size_t)f / 16 * 4, false};
+        if (policy == MOEB_POLICY_TILES16 || policy == MOEB_POLICY_TILES16_RING)
+            return {k_gate_up_tiles_reg<FMT_FP4, 2, 1>, k_down_tiles_reg<FMT_FP4, 2, 1>, 128, 128, 0, 0, true};
+        return {k_gate_up_tiles_reg<FMT_FP4, 1, 2>, k_down_tiles_reg<FMT_FP4, 1, 2>, 128, 128, 0, 0, true};
+    }
     if (fmt != FMT_Q4) return {nullptr, nullptr, 0, 0, 0, 0, false};
     if (policy == MOEB_POLICY_SLOTS)
         return {k_gate_up_slots<FMT_Q4, 8, 4>, k_down_slots<FMT_Q4, 4, 4>, 256, 128, (size_t)d * 2,
@@ -439,11 +447,12 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
     a.y = static_cast<uint16_t *>(y);
     a.err = at<unsigned>(ws, L.err);
     a.T = T; a.d = d; a.f = f; a.E = E; a.k = k; a.act = act; a.tile_mode = tiles ? 1 : 0;
+    a.fmt = fmt;
     // the down weights of the routed experts are prefetched into L2 while gate/up runs only when gate/up,
     // down and the prefetch all fit comfortably in L2 (otherwise the gate/up stream evicts them again)
     {
         const double U = std::min<double>(E, (double)T * k);
-        const double layer_bytes = U * 3.0 * d * f * 4.5 / 8.0;
+        const double layer_bytes = U * 3.0 * d * f * (fmt == FMT_FP4 ? 4.25 : 4.5) / 8.0;
         a.dn_prefetch = layer_bytes < 48.0 * (1 << 20) ? 1 : 0;
     }
     return run_experts(fmt, a, policy, L, ws, st, ev);
@@ -456,6 +465,26 @@ int moeb_experts_q4(const void *x, const void *qg, const void *sbg, const void *
     if (!idx || !wts) return fail(MOEB_EINVAL, "idx and wts are required%s");
     return experts_common(FMT_Q4, x, qg, sbg, qu, sbu, qd, sbd, bg, bu, bd, idx, wts, T, d, f, E, k, act, policy,
                           residual, y, ws, ws_bytes, st, nullptr, nullptr, 0, 1.f, nullptr, nullptr, nullptr);
+}
+
+int moeb_experts_mxfp4(const void *x, const void *qg, const void *scg, const void *qu, const void *scu,
+                       const void *qd, const void *scd, const float *bg, const float *bu, const float *bd,
+                       const int *idx, const float *wts, int T, int d, int f, int E, int k, int act, int policy,
+                       const void *residual, void *y, void *ws, size_t ws_bytes, cudaStream_t st) {
+    if (!idx || !wts) return fail(MOEB_EINVAL, "idx and wts are required%s");
+    return experts_common(FMT_FP4, x, qg, scg, qu, scu, qd, scd, bg, bu, bd, idx, wts, T, d, f, E, k, act, policy,
+                          residual, y, ws, ws_bytes, st, nullptr, nullptr, 0, 1.f, nullptr, nullptr, nullptr);
+}
+
+int moeb_layer_mxfp4(const void *x, const void *gate_w, const void *gate_b, int norm, float rscale, const void *qg,
+                     const void *scg, const void *qu, const void *scu, const void *qd, const void *scd,
+                     const float *bg, const float *bu, const float *bd, int T, int d, int f, int E, int k, int act,
+                     int policy, const void *residual, void *y, int *idx_out, float *wts_out,
+                     void *const *stage_events, void *ws, size_t ws_bytes, cudaStream_t st) {
+    if (!gate_w) return fail(MOEB_EINVAL, "gate weights are required%s");
+    return experts_common(FMT_FP4, x, qg, scg, qu, scu, qd, scd, bg, bu, bd, nullptr, nullptr, T, d, f, E, k, act,
+                          policy, residual, y, ws, ws_bytes, st, gate_w, gate_b, norm, rscale, idx_out, wts_out,
+                          stage_events);
 }
 
 int moeb_layer_q4(const void *x, const void *gate_w, const void *gate_b, int norm, float rscale, const void *qg,

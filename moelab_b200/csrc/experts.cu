@@ -13,8 +13,11 @@
 // Two launch shapes over work units (tile, 16-row block):
 //   *_slots (decode, one slot per tile): one CTA per unit, the KS warps split K with every load issued up
 //     front, the token's activation row staged in shared memory, fixed-order split-K reduction.
-//   *_tiles (slots grouped by expert into tiles of 8*NT8): one warp per unit over the whole K, a register
-//     double-buffered load pipeline, and a per-warp epilogue (no CTA barriers).
+//   *_tiles_reg (slots grouped by expert into tiles of 8*NT8): one warp per unit over the whole K, a register
+//     double-buffered load pipeline, and a per-warp epilogue (no CTA barriers). The warp-specialized TMA
+//     variant of the tile kernels is in experts_ws.cu.
+// Both weight formats share these kernels (FMT): int4 promotes per 64-group in fp32; MXFP4 folds its E8M0 scale
+// into exact bf16 A fragments (experts_common.cuh).
 // gate/up (reference GATE_UP_SRC metal_q4_decode_v4.py:67-93, GATE_UP_E_SRC metal_q4_tiles_v2.py:179-275):
 //   h[slot][r] = bf16(act(g + bg, u + bu)); hsum[slot][r/16] = sum of the block's 16 bf16 h values.
 // down + combine (DOWN_SRC metal_q4_decode_v4.py:95-144, DOWN_E_SRC + COMBINE_SRC metal_q4_tiles_v2.py):
@@ -56,8 +59,8 @@ __global__ void __launch_bounds__(32 * KS, 3) k_gate_up_slots(ExpArgs a) {
                 const int g = min(g0 + i, g_end - 1);  // clamped: a repeated load, never used
                 wg[i] = ld_w(a.g, blk, G, g, lane);
                 wu[i] = ld_w(a.u, blk, G, g, lane);
-                bg[i] = ld_sb(a.g, blk, G, g, gq);
-                bu[i] = ld_sb(a.u, blk, G, g, gq);
+                bg[i] = ld_scales<FMT>(a.g, blk, G, g, gq);
+                bu[i] = ld_scales<FMT>(a.u, blk, G, g, gq);
             }
             if (!synced) {
                 __syncthreads();  // x row staged (weights already in flight)
@@ -70,8 +73,8 @@ __global__ void __launch_bounds__(32 * KS, 3) k_gate_up_slots(ExpArgs a) {
                     uint32_t xb[1][8];
                     load_b16(gq == 0 ? xs + g * 64 + 16 * c : nullptr, xb[0]);
                     const float sx[1][2] = {{c == 0 ? sxr[g] : 0.f, 0.f}};
-                    q4_group<1>(wg[i], bg[i], xb, sx, Cg);
-                    q4_group<1>(wu[i], bu[i], xb, sx, Cu);
+                    wgroup<FMT, 1>(wg[i], bg[i], c, xb, sx, Cg);
+                    wgroup<FMT, 1>(wu[i], bu[i], c, xb, sx, Cu);
                 }
             }
         }
@@ -130,7 +133,7 @@ __global__ void __launch_bounds__(32 * KS, 8) k_down_slots(ExpArgs a) {
             for (int i = 0; i < GPW; ++i) {
                 const int g = min(g0 + i, g_end - 1);
                 w[i] = ld_w(a.dn, blk, G, g, lane);
-                b[i] = ld_sb(a.dn, blk, G, g, gq);
+                b[i] = ld_scales<FMT>(a.dn, blk, G, g, gq);
             }
             if (!synced) {
                 __syncthreads();
@@ -144,7 +147,7 @@ __global__ void __launch_bounds__(32 * KS, 8) k_down_slots(ExpArgs a) {
                     load_b16(gq == 0 ? hs + g * 64 + 16 * c : nullptr, hb[0]);
                     const float4 v = *reinterpret_cast<const float4 *>(hsum_s + 4 * g);
                     const float sx[1][2] = {{c == 0 ? (v.x + v.y) + (v.z + v.w) : 0.f, 0.f}};
-                    q4_group<1>(w[i], b[i], hb, sx, C);
+                    wgroup<FMT, 1>(w[i], b[i], c, hb, sx, C);
                 }
             }
         }
@@ -177,7 +180,7 @@ struct GUBatch {
     float sx[GPW][NT8][2];
 };
 
-template <int NT8, int GPW>
+template <int FMT, int NT8, int GPW>
 __device__ __forceinline__ void gu_load(GUBatch<NT8, GPW> &B, const ExpArgs &a, size_t blk, int G, int g0,
                                         const uint16_t *const (&xrow)[NT8], const float *const (&sxrow)[NT8][2],
                                         int lane) {
@@ -187,8 +190,8 @@ __device__ __forceinline__ void gu_load(GUBatch<NT8, GPW> &B, const ExpArgs &a, 
         const int g = min(g0 + i, G - 1);
         B.wg[i] = ld_w(a.g, blk, G, g, lane);
         B.wu[i] = ld_w(a.u, blk, G, g, lane);
-        B.bg[i] = ld_sb(a.g, blk, G, g, gq);
-        B.bu[i] = ld_sb(a.u, blk, G, g, gq);
+        B.bg[i] = ld_scales<FMT>(a.g, blk, G, g, gq);
+        B.bu[i] = ld_scales<FMT>(a.u, blk, G, g, gq);
 #pragma unroll
         for (int j = 0; j < NT8; ++j) {
             load_b16(xrow[j] ? xrow[j] + g * 64 : nullptr, B.xb[i][j]);
@@ -198,14 +201,14 @@ __device__ __forceinline__ void gu_load(GUBatch<NT8, GPW> &B, const ExpArgs &a, 
     }
 }
 
-template <int NT8, int GPW>
-__device__ __forceinline__ void gu_compute(const GUBatch<NT8, GPW> &B, int g0, int G, float (&Cg)[NT8][4],
+template <int FMT, int NT8, int GPW>
+__device__ __forceinline__ void gu_compute(const GUBatch<NT8, GPW> &B, int g0, int G, int c, float (&Cg)[NT8][4],
                                            float (&Cu)[NT8][4]) {
 #pragma unroll
     for (int i = 0; i < GPW; ++i) {
         if (g0 + i < G) {
-            q4_group<NT8>(B.wg[i], B.bg[i], B.xb[i], B.sx[i], Cg);
-            q4_group<NT8>(B.wu[i], B.bu[i], B.xb[i], B.sx[i], Cu);
+            wgroup<FMT, NT8>(B.wg[i], B.bg[i], c, B.xb[i], B.sx[i], Cg);
+            wgroup<FMT, NT8>(B.wu[i], B.bu[i], c, B.xb[i], B.sx[i], Cu);
         }
     }
 }
@@ -243,13 +246,13 @@ __global__ void __launch_bounds__(128) k_gate_up_tiles_reg(ExpArgs a) {
 #pragma unroll
             for (int i = 0; i < 4; ++i) Cg[j][i] = Cu[j][i] = 0.f;
         GUBatch<NT8, GPW> A, B;
-        gu_load(A, a, blk, G, 0, xrow, sxrow, lane);
+        gu_load<FMT>(A, a, blk, G, 0, xrow, sxrow, lane);
         for (int g0 = 0; g0 < G; g0 += 2 * GPW) {
-            if (g0 + GPW < G) gu_load(B, a, blk, G, g0 + GPW, xrow, sxrow, lane);
-            gu_compute(A, g0, G, Cg, Cu);
+            if (g0 + GPW < G) gu_load<FMT>(B, a, blk, G, g0 + GPW, xrow, sxrow, lane);
+            gu_compute<FMT>(A, g0, G, c, Cg, Cu);
             if (g0 + GPW < G) {
-                if (g0 + 2 * GPW < G) gu_load(A, a, blk, G, g0 + 2 * GPW, xrow, sxrow, lane);
-                gu_compute(B, g0 + GPW, G, Cg, Cu);
+                if (g0 + 2 * GPW < G) gu_load<FMT>(A, a, blk, G, g0 + 2 * GPW, xrow, sxrow, lane);
+                gu_compute<FMT>(B, g0 + GPW, G, c, Cg, Cu);
             }
         }
 #pragma unroll
@@ -265,7 +268,7 @@ struct DNBatch {
     float4 hs[GPW][NT8][2];
 };
 
-template <int NT8, int GPW>
+template <int FMT, int NT8, int GPW>
 __device__ __forceinline__ void dn_load(DNBatch<NT8, GPW> &B, const ExpArgs &a, size_t blk, int G, int g0,
                                         const uint16_t *const (&hrow)[NT8], const float *const (&hsrow)[NT8][2],
                                         int lane) {
@@ -274,7 +277,7 @@ __device__ __forceinline__ void dn_load(DNBatch<NT8, GPW> &B, const ExpArgs &a, 
     for (int i = 0; i < GPW; ++i) {
         const int g = min(g0 + i, G - 1);
         B.w[i] = ld_w(a.dn, blk, G, g, lane);
-        B.b[i] = ld_sb(a.dn, blk, G, g, gq);
+        B.b[i] = ld_scales<FMT>(a.dn, blk, G, g, gq);
 #pragma unroll
         for (int j = 0; j < NT8; ++j) {
             load_b16(hrow[j] ? hrow[j] + g * 64 : nullptr, B.hb[i][j]);
@@ -286,8 +289,8 @@ __device__ __forceinline__ void dn_load(DNBatch<NT8, GPW> &B, const ExpArgs &a, 
     }
 }
 
-template <int NT8, int GPW>
-__device__ __forceinline__ void dn_compute(const DNBatch<NT8, GPW> &B, int g0, int G, float (&C)[NT8][4]) {
+template <int FMT, int NT8, int GPW>
+__device__ __forceinline__ void dn_compute(const DNBatch<NT8, GPW> &B, int g0, int G, int c, float (&C)[NT8][4]) {
 #pragma unroll
     for (int i = 0; i < GPW; ++i) {
         if (g0 + i < G) {
@@ -299,7 +302,7 @@ __device__ __forceinline__ void dn_compute(const DNBatch<NT8, GPW> &B, int g0, i
                     const float4 v = B.hs[i][j][hf];
                     sx[j][hf] = (v.x + v.y) + (v.z + v.w);
                 }
-            q4_group<NT8>(B.w[i], B.b[i], B.hb[i], sx, C);
+            wgroup<FMT, NT8>(B.w[i], B.b[i], c, B.hb[i], sx, C);
         }
     }
 }
@@ -336,231 +339,30 @@ __global__ void __launch_bounds__(128) k_down_tiles_reg(ExpArgs a) {
 #pragma unroll
             for (int i = 0; i < 4; ++i) C[j][i] = 0.f;
         DNBatch<NT8, GPW> A, B;
-        dn_load(A, a, blk, G, 0, hrow, hsrow, lane);
+        dn_load<FMT>(A, a, blk, G, 0, hrow, hsrow, lane);
         for (int g0 = 0; g0 < G; g0 += 2 * GPW) {
-            if (g0 + GPW < G) dn_load(B, a, blk, G, g0 + GPW, hrow, hsrow, lane);
-            dn_compute(A, g0, G, C);
+            if (g0 + GPW < G) dn_load<FMT>(B, a, blk, G, g0 + GPW, hrow, hsrow, lane);
+            dn_compute<FMT>(A, g0, G, c, C);
             if (g0 + GPW < G) {
-                if (g0 + 2 * GPW < G) dn_load(A, a, blk, G, g0 + 2 * GPW, hrow, hsrow, lane);
-                dn_compute(B, g0 + GPW, G, C);
+                if (g0 + 2 * GPW < G) dn_load<FMT>(A, a, blk, G, g0 + 2 * GPW, hrow, hsrow, lane);
+                dn_compute<FMT>(B, g0 + GPW, G, c, C);
             }
         }
         down_store_combine<NT8>(a, ti, rb, C, lane);
     }
 }
 
-// ================================================================== tile mode, TMA ring
-// One warp per (tile, 16-row block) over the whole K. In the fragment-major layout a unit's codes for groups
-// [g0, g0 + SG) are one contiguous block per projection (and likewise the scale|bias words), so lane 0 of each
-// warp streams whole stages with 1-D TMA bulk copies (evict-first in L2) into a ring of NS shared-memory stages
-// completing on per-stage mbarriers; the warp's MMAs read the ring. Activations and group sums (L2-resident,
-// reused by every row block of a tile) come through plain loads one group ahead. Every wait is bounded: on a
-// timeout the warp records MOEB_DEVERR_TIMEOUT and stops issuing.
-template <int NT8>
-struct UnitSrc {
-    int unit = -1;
-    TileInfo ti;
-    size_t blk;
-    const uint16_t *row[NT8];   // activation row of B column gq of each n8 tile (x or h), or null
-    const float *srow[NT8][2];  // group-sum rows of C columns 2c, 2c+1 (xsum or hsum), or null
-};
-
-template <int NT8, bool DOWN>
-__device__ __forceinline__ void unit_src(UnitSrc<NT8> &u, const ExpArgs &a, int unit, int RB, int lane) {
-    const int gq = lane >> 2, c = lane & 3;
-    u.unit = unit;
-    const int tile = unit / RB, rb = unit - tile * RB;
-    u.ti = tile_info(a, tile);
-    u.blk = (size_t)u.ti.e * RB + rb;
-#pragma unroll
-    for (int j = 0; j < NT8; ++j) {
-        const int sb_ = tile_slot(a, u.ti, j * 8 + gq);
-        if (DOWN) u.row[j] = sb_ >= 0 ? a.h + (size_t)sb_ * a.f + 16 * c : nullptr;
-        else u.row[j] = sb_ >= 0 ? a.x + (size_t)(sb_ / a.k) * a.d + 16 * c : nullptr;
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-            const int sc_ = tile_slot(a, u.ti, j * 8 + 2 * c + hf);
-            if (DOWN) u.srow[j][hf] = sc_ >= 0 ? a.hsum + (size_t)sc_ * (a.f / 16) : nullptr;
-            else u.srow[j][hf] = sc_ >= 0 ? a.xsum + (size_t)(sc_ / a.k) * xsum_stride(a.d) : nullptr;
-        }
-    }
-}
-
-// B operand (16 activations per lane) and the two group sums of one group.
-template <int NT8, bool DOWN>
-__device__ __forceinline__ void load_act(const UnitSrc<NT8> &u, int g, uint32_t (&xb)[NT8][8], float (&sx)[NT8][2]) {
-#pragma unroll
-    for (int j = 0; j < NT8; ++j) {
-        load_b16(u.row[j] ? u.row[j] + g * 64 : nullptr, xb[j]);
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-            const float *p = u.srow[j][hf];
-            if (DOWN) {
-                if (p) {
-                    const float4 v = *reinterpret_cast<const float4 *>(p + 4 * g);
-                    sx[j][hf] = (v.x + v.y) + (v.z + v.w);
-                } else {
-                    sx[j][hf] = 0.f;
-                }
-            } else {
-                sx[j][hf] = p ? p[g] : 0.f;
-            }
-        }
-    }
-}
-
-// NP projections (2 for gate/up, 1 for down) of SG groups per stage
-template <int NP, int SG>
-struct RingStage {
-    static constexpr int Q_BYTES = SG * 512, SB_BYTES = SG * 64;
-    static constexpr int BYTES = NP * (Q_BYTES + SB_BYTES);
-};
-
-template <int FMT, int NT8, int NS, int SG, bool DOWN>
-__device__ __forceinline__ void tiles_tma_body(const ExpArgs &a) {
-    constexpr int NP = DOWN ? 1 : 2;
-    using RS = RingStage<NP, SG>;
-    extern __shared__ __align__(128) unsigned char smem_raw[];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int RB = DOWN ? (a.d >> 4) : (a.f >> 4);
-    const int G = DOWN ? (a.f >> 6) : (a.d >> 6);
-    const int SPU = (G + SG - 1) / SG;  // stages per unit
-    const int n_units = *a.ntiles * RB;
-    const int w0 = blockIdx.x * 4 + warp, nw = gridDim.x * 4;
-    const int my_units = w0 < n_units ? (n_units - w0 + nw - 1) / nw : 0;
-    const int total = my_units * SPU;
-    unsigned char *ring = smem_raw + (size_t)warp * NS * RS::BYTES;
-    uint64_t *bar = reinterpret_cast<uint64_t *>(smem_raw + 4 * NS * RS::BYTES) + warp * NS;
-    const QProj P0 = DOWN ? a.dn : a.g, P1 = a.u;
-    const uint64_t pol = l2_evict_first_policy();
-    if (lane == 0) {
-        for (int i = 0; i < NS; ++i) mbar_init(bar + i, 1);
-        mbar_fence_init();
-    }
-    __syncwarp();
-    int p_unit = -1;
-    size_t p_blk = 0;
-    auto issue = [&](int k) {  // lane 0 only
-        if (k >= total) return;
-        const int unit = w0 + (k / SPU) * nw, g0 = (k % SPU) * SG;
-        if (unit != p_unit) {
-            p_unit = unit;
-            const int tile = unit / RB;
-            int e = a.tile_mode ? a.tiles[tile].x : a.idx[tile];
-            if (e < 0 || e >= a.E) e = 0;
-            p_blk = (size_t)e * RB + (unit - tile * RB);
-            if (!DOWN && g0 == 0 && a.dn_prefetch) prefetch_down(a, e, unit - tile * RB, RB, 0, 1);
-        }
-        const int ng = min(SG, G - g0);
-        uint64_t *b = bar + (k % NS);
-        unsigned char *st = ring + (size_t)(k % NS) * RS::BYTES;
-        mbar_expect_tx(b, (unsigned)(NP * ng * (512 + 64)));
-#pragma unroll
-        for (int p = 0; p < NP; ++p) {
-            const QProj &PP = p == 0 ? P0 : P1;
-            tma_load_1d(st + p * RS::Q_BYTES, PP.q + (p_blk * G + g0) * 128, ng * 512, b, pol);
-            tma_load_1d(st + NP * RS::Q_BYTES + p * RS::SB_BYTES, PP.sb + (p_blk * G + g0) * 16, ng * 64, b, pol);
-        }
-    };
-    if (lane == 0)
-        for (int k = 0; k < NS - 1; ++k) issue(k);
-    UnitSrc<NT8> U;
-    float C0[NT8][4], C1[NT8][4];
-#pragma unroll
-    for (int j = 0; j < NT8; ++j)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) C0[j][i] = C1[j][i] = 0.f;
-    uint32_t xb[NT8][8];
-    float sx[NT8][2];
-    bool ok = true;
-    for (int k = 0; k < total && ok; ++k) {
-        if (lane == 0) issue(k + NS - 1);
-        const int unit = w0 + (k / SPU) * nw, g0 = (k % SPU) * SG;
-        if (g0 == 0) {
-            unit_src<NT8, DOWN>(U, a, unit, RB, lane);
-            load_act<NT8, DOWN>(U, 0, xb, sx);
-        }
-        ok = mbar_wait_bounded(bar + (k % NS), (unsigned)((k / NS) & 1));
-        if (!ok) {
-            if (lane == 0) atomicOr(a.err, ERR_TIMEOUT);
-            break;
-        }
-        const unsigned char *st = ring + (size_t)(k % NS) * RS::BYTES;
-        const int ng = min(SG, G - g0);
-#pragma unroll 1
-        for (int i = 0; i < ng; ++i) {
-            uint32_t xn[NT8][8];
-            float sn[NT8][2];
-            if (g0 + i + 1 < G) load_act<NT8, DOWN>(U, g0 + i + 1, xn, sn);  // next group's activations
-            const uint4 w0v = reinterpret_cast<const uint4 *>(st)[i * 32 + lane];
-            const uint2 s0v = reinterpret_cast<const uint2 *>(st + NP * RS::Q_BYTES)[i * 8 + (lane >> 2)];
-            q4_group<NT8>(w0v, s0v, xb, sx, C0);
-            if (!DOWN) {
-                const uint4 w1v = reinterpret_cast<const uint4 *>(st + RS::Q_BYTES)[i * 32 + lane];
-                const uint2 s1v = reinterpret_cast<const uint2 *>(st + NP * RS::Q_BYTES + RS::SB_BYTES)[i * 8 + (lane >> 2)];
-                q4_group<NT8>(w1v, s1v, xb, sx, C1);
-            }
-#pragma unroll
-            for (int j = 0; j < NT8; ++j) {
-#pragma unroll
-                for (int q = 0; q < 8; ++q) xb[j][q] = xn[j][q];
-                sx[j][0] = sn[j][0];
-                sx[j][1] = sn[j][1];
-            }
-        }
-        __syncwarp();  // every lane is done with this stage before lane 0 refills it
-        if (k % SPU == SPU - 1) {
-            const int rb = unit - (unit / RB) * RB;
-            if (DOWN) {
-                down_store_combine<NT8>(a, U.ti, rb, C0, lane);
-            } else {
-#pragma unroll
-                for (int j = 0; j < NT8; ++j) gate_up_store<NT8>(a, U.ti, rb, j, C0[j], C1[j], lane);
-            }
-#pragma unroll
-            for (int j = 0; j < NT8; ++j)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) C0[j][i] = C1[j][i] = 0.f;
-        }
-    }
-    if (!ok) {  // drain: give every issued stage a bounded chance to land before the CTA exits
-        for (int k = 0; k < NS; ++k) mbar_wait_bounded(bar + k, 0u, 1u << 12), mbar_wait_bounded(bar + k, 1u, 1u << 12);
-    }
-}
-
-template <int FMT, int NT8, int NS, int SG>
-__global__ void __launch_bounds__(128) k_gate_up_tiles(ExpArgs a) {
-    pdl_launch();
-    pdl_wait();
-    tiles_tma_body<FMT, NT8, NS, SG, false>(a);
-}
-
-template <int FMT, int NT8, int NS, int SG>
-__global__ void __launch_bounds__(128) k_down_tiles(ExpArgs a) {
-    pdl_launch();
-    pdl_wait();
-    tiles_tma_body<FMT, NT8, NS, SG, true>(a);
-}
-
-// shared-memory bytes of the TMA-ring tile kernels (4 warps per CTA, plus one mbarrier per stage and warp)
-size_t gate_up_tiles_smem(int nt8, int ns, int sg) {
-    (void)nt8;
-    return (size_t)4 * ns * 2 * sg * (512 + 64) + 4 * ns * 8;
-}
-size_t down_tiles_smem(int nt8, int ns, int sg) {
-    (void)nt8;
-    return (size_t)4 * ns * sg * (512 + 64) + 4 * ns * 8;
-}
-
 template __global__ void k_gate_up_slots<FMT_Q4, 8, 4>(ExpArgs);
 template __global__ void k_down_slots<FMT_Q4, 4, 4>(ExpArgs);
+template __global__ void k_gate_up_slots<FMT_FP4, 8, 4>(ExpArgs);
+template __global__ void k_down_slots<FMT_FP4, 4, 4>(ExpArgs);
+template __global__ void k_gate_up_tiles_reg<FMT_FP4, 1, 2>(ExpArgs);
+template __global__ void k_down_tiles_reg<FMT_FP4, 1, 2>(ExpArgs);
+template __global__ void k_gate_up_tiles_reg<FMT_FP4, 2, 1>(ExpArgs);
+template __global__ void k_down_tiles_reg<FMT_FP4, 2, 1>(ExpArgs);
 template __global__ void k_gate_up_tiles_reg<FMT_Q4, 1, 2>(ExpArgs);
 template __global__ void k_gate_up_tiles_reg<FMT_Q4, 2, 1>(ExpArgs);
 template __global__ void k_down_tiles_reg<FMT_Q4, 1, 2>(ExpArgs);
 template __global__ void k_down_tiles_reg<FMT_Q4, 2, 1>(ExpArgs);
-template __global__ void k_gate_up_tiles<FMT_Q4, 1, 3, 8>(ExpArgs);
-template __global__ void k_gate_up_tiles<FMT_Q4, 2, 3, 8>(ExpArgs);
-template __global__ void k_down_tiles<FMT_Q4, 1, 3, 8>(ExpArgs);
-template __global__ void k_down_tiles<FMT_Q4, 2, 3, 8>(ExpArgs);
 
 }  // namespace moeb

@@ -57,6 +57,60 @@ __device__ __forceinline__ void q4_group(const uint4 w, const uint2 sb, const ui
     }
 }
 
+// ---- MXFP4 (E2M1 codes, E8M0 scale per 32 inputs)
+// Each lane's 16 elements of a 64-group (16c .. 16c+15) lie in one 32-element scale block (c / 2), so the scale
+// is folded into the A fragment exactly: e2m1 * 2^(S-127) is representable in bf16 for S in 1..254. The MMA
+// then accumulates straight into C (no per-group promotion).
+// bf16 bytes of the 8 E2M1 magnitudes {0, .5, 1, 1.5, 2, 3, 4, 6}: high bytes and low bytes, 4 per register.
+constexpr uint32_t FP4_HI0 = 0x3F3F3F00u, FP4_HI1 = 0x40404040u, FP4_LO0 = 0xC0800000u, FP4_LO1 = 0xC0804000u;
+
+// bf16x2 (2^(S-127), 2^(S-127)); S = 0 gives the bf16 subnormal 2^-127.
+__device__ __forceinline__ uint32_t fp4_scale2(uint32_t S) {
+    const uint32_t b = S ? (S << 7) : 0x40u;
+    return b | (b << 16);
+}
+
+// The 4 bf16x2 pairs (elements 2p, 2p+1) of one interleaved code word, scaled by scale2.
+__device__ __forceinline__ void fp4_word(uint32_t w, uint32_t scale2, uint32_t (&pr)[4]) {
+    const uint32_t mag = w & 0x77777777u;
+    const uint32_t LA = __byte_perm(FP4_LO0, FP4_LO1, mag), HA = __byte_perm(FP4_HI0, FP4_HI1, mag);
+    const uint32_t LB = __byte_perm(FP4_LO0, FP4_LO1, mag >> 16), HB = __byte_perm(FP4_HI0, FP4_HI1, mag >> 16);
+    const uint32_t L01 = __byte_perm(LA, LB, 0x5140), H01 = __byte_perm(HA, HB, 0x5140);
+    const uint32_t L23 = __byte_perm(LA, LB, 0x7362), H23 = __byte_perm(HA, HB, 0x7362);
+    pr[0] = __byte_perm(L01, H01, 0x5140) | ((w << 12) & 0x80008000u);
+    pr[1] = __byte_perm(L01, H01, 0x7362) | ((w << 8) & 0x80008000u);
+    pr[2] = __byte_perm(L23, H23, 0x5140) | ((w << 4) & 0x80008000u);
+    pr[3] = __byte_perm(L23, H23, 0x7362) | (w & 0x80008000u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162 *>(&pr[i]);
+        const __nv_bfloat162 s2 = *reinterpret_cast<const __nv_bfloat162 *>(&scale2);
+        v = __hmul2(v, s2);
+        pr[i] = *reinterpret_cast<uint32_t *>(&v);
+    }
+}
+
+// One 64-group of an MXFP4 projection: sc4 = E8M0 bytes {row gq half 0, half 1, row gq+8 half 0, half 1}.
+template <int NT8>
+__device__ __forceinline__ void fp4_group(const uint4 w, const uint32_t sc4, int c, const uint32_t (&xb)[NT8][8],
+                                          float (&C)[NT8][4]) {
+    const uint32_t s0 = fp4_scale2((sc4 >> (8 * (c >> 1))) & 0xFFu);
+    const uint32_t s1 = fp4_scale2((sc4 >> (8 * (2 + (c >> 1)))) & 0xFFu);
+    uint32_t r0a[4], r0b[4], r1a[4], r1b[4];
+    fp4_word(w.x, s0, r0a);
+    fp4_word(w.y, s0, r0b);
+    fp4_word(w.z, s1, r1a);
+    fp4_word(w.w, s1, r1b);
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const int p0 = (2 * s) & 3, p1 = (2 * s + 1) & 3;
+        const uint32_t A[4] = {s < 2 ? r0a[p0] : r0b[p0], s < 2 ? r1a[p0] : r1b[p0], s < 2 ? r0a[p1] : r0b[p1],
+                               s < 2 ? r1a[p1] : r1b[p1]};
+#pragma unroll
+        for (int j = 0; j < NT8; ++j) mma_bf16(C[j], A, xb[j][2 * s], xb[j][2 * s + 1]);
+    }
+}
+
 __device__ __forceinline__ void load_b16(const uint16_t *p, uint32_t (&o)[8]) {
     if (p) {
         const uint4 u0 = *reinterpret_cast<const uint4 *>(p), u1 = *reinterpret_cast<const uint4 *>(p + 8);
@@ -85,7 +139,9 @@ __device__ __forceinline__ void prefetch_down(const ExpArgs &a, int e, int rb, i
     if (rb1 <= rb0) return;
     const size_t blk = (size_t)e * (a.d / 16) + rb0;
     prefetch_l2(a.dn.q + blk * (size_t)(a.f / 64) * 128, (size_t)(rb1 - rb0) * (a.f / 64) * 512, lane, nlanes);
-    prefetch_l2(a.dn.sb + blk * (size_t)(a.f / 64) * 16, (size_t)(rb1 - rb0) * (a.f / 64) * 64, lane, nlanes);
+    // scale words: int4 16 uint32 per (row block, group), MXFP4 8 (32 bytes of E8M0)
+    const int spg = a.fmt == FMT_FP4 ? 8 : 16;
+    prefetch_l2(a.dn.sb + blk * (size_t)(a.f / 64) * spg, (size_t)(rb1 - rb0) * (a.f / 64) * spg * 4, lane, nlanes);
 }
 
 // Weights of one (16-row block, 64-group) for this lane.
@@ -94,6 +150,20 @@ __device__ __forceinline__ uint4 ld_w(const QProj &P, size_t blk, int G, int g, 
 }
 __device__ __forceinline__ uint2 ld_sb(const QProj &P, size_t blk, int G, int g, int gq) {
     return ld_stream_u2(P.sb + ((blk * G + g) * 8 + gq) * 2);
+}
+// Per-lane scale words of one (row block, group): int4 -> {scale|bias row gq, row gq+8}; MXFP4 -> the 4 E8M0
+// bytes of rows gq, gq+8 in .x (.y unused).
+template <int FMT>
+__device__ __forceinline__ uint2 ld_scales(const QProj &P, size_t blk, int G, int g, int gq) {
+    if (FMT == FMT_FP4) return make_uint2(ld_stream_u32(P.sb + (blk * G + g) * 8 + gq), 0u);
+    return ld_sb(P, blk, G, g, gq);
+}
+// One group of either format into C (int4 uses the group sums sx; MXFP4 ignores them).
+template <int FMT, int NT8>
+__device__ __forceinline__ void wgroup(const uint4 w, const uint2 sc, int c, const uint32_t (&xb)[NT8][8],
+                                       const float (&sx)[NT8][2], float (&C)[NT8][4]) {
+    if (FMT == FMT_FP4) fp4_group<NT8>(w, sc.x, c, xb, C);
+    else q4_group<NT8>(w, sc, xb, sx, C);
 }
 
 // gate/up epilogue for one column tile j of a unit: bias, activation, bf16 h, block sums.

@@ -5,6 +5,8 @@
 
 namespace moeb {
 
+enum { FMT_Q4 = 0, FMT_FP4 = 1 };
+
 struct RouterArgs {
     const uint16_t *x;     // [T][d] bf16
     const uint16_t *wg;    // [E][d] bf16 gate
@@ -63,6 +65,7 @@ struct ExpArgs {
     unsigned *err;
     int T, d, f, E, k, act, tile_mode;
     int dn_prefetch;  // gate/up pulls the down weights of its expert into L2
+    int fmt;          // FMT_Q4 or FMT_FP4
 };
 
 template <int TPB, int JMAX, int U>
@@ -82,10 +85,6 @@ template <int FMT, int KS, int GPW>
 __global__ void k_gate_up_slots(ExpArgs a);
 template <int FMT, int KS, int GPW>
 __global__ void k_down_slots(ExpArgs a);
-template <int FMT, int NT8, int NS, int GPS>
-__global__ void k_gate_up_tiles(ExpArgs a);
-template <int FMT, int NT8, int NS, int GPS>
-__global__ void k_down_tiles(ExpArgs a);
 template <int FMT, int NT8, int GPW>
 __global__ void k_gate_up_tiles_reg(ExpArgs a);
 template <int FMT, int NT8, int GPW>
@@ -93,10 +92,7 @@ __global__ void k_down_tiles_reg(ExpArgs a);
 template <int FMT, int NT8, int RBC, int SG, int NS, bool DOWN>
 __global__ void k_experts_ws(ExpArgs a);
 size_t experts_ws_smem(int nt8, int rbc, int sg, int ns, bool down);
-size_t gate_up_tiles_smem(int nt8, int ns, int gps);
-size_t down_tiles_smem(int nt8, int ns, int gps);
 
-enum { FMT_Q4 = 0, FMT_FP4 = 1 };
 
 size_t zero_region_bytes(size_t ws_bytes, int d, int f, int E, int k);
 void set_error(const char *msg);  // message returned by moeb_last_error()

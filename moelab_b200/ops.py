@@ -160,8 +160,12 @@ def _expert_ptrs(state):
             _p(state.get("bd"))]
 
 
+def _fmt(state):
+    return state.get("fmt", "q4")
+
+
 def experts_q4(state, x, idx, wts, act=0, policy=POLICY_AUTO, residual=None):
-    """y = sum_j wts * expert(x) (+ residual), bf16 [T, d]."""
+    """y = sum_j wts * expert(x) (+ residual), bf16 [T, d]. The state's format picks the int4 or MXFP4 entry."""
     _need(x, torch.bfloat16, "x")
     _need(idx, torch.int32, "idx")
     _need(wts, torch.float32, "wts")
@@ -172,9 +176,13 @@ def experts_q4(state, x, idx, wts, act=0, policy=POLICY_AUTO, residual=None):
     ws = state["ws"]
     buf = ws.get(max(T, 1))
     y = torch.empty_like(x)
-    _lib.call("moeb_experts_q4", _p(x), *_expert_ptrs(state), _p(idx), _p(wts), T, d, f, E, k, int(act),
+    fn = "moeb_experts_mxfp4" if _fmt(state) == "mxfp4" else "moeb_experts_q4"
+    _lib.call(fn, _p(x), *_expert_ptrs(state), _p(idx), _p(wts), T, d, f, E, k, int(act),
               int(policy), _p(residual), _p(y), _p(buf), buf.numel(), _stream())
     return y
+
+
+experts = experts_q4
 
 
 def layer_q4(state, x, gate_w, k, gate_b=None, norm=True, rscale=1.0, act=0, policy=POLICY_AUTO, residual=None,
@@ -197,10 +205,14 @@ def layer_q4(state, x, gate_w, k, gate_b=None, norm=True, rscale=1.0, act=0, pol
             if ev.cuda_event == 0:
                 ev.record()  # creates the underlying cudaEvent_t
         evp = (ctypes.c_void_p * 4)(*[ctypes.c_void_p(ev.cuda_event) for ev in stage_events])
-    _lib.call("moeb_layer_q4", _p(x), _p(gate_w), _p(gate_b), int(bool(norm)), float(rscale), *_expert_ptrs(state),
+    fn = "moeb_layer_mxfp4" if _fmt(state) == "mxfp4" else "moeb_layer_q4"
+    _lib.call(fn, _p(x), _p(gate_w), _p(gate_b), int(bool(norm)), float(rscale), *_expert_ptrs(state),
               T, d, f, E, k, int(act), int(policy), _p(residual), _p(y), _p(idx), _p(wts), evp, _p(buf),
               buf.numel(), _stream())
     return (y, idx, wts) if return_routing else y
+
+
+layer = layer_q4
 
 
 def policy(T, E, k):
