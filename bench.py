@@ -282,6 +282,141 @@ def cpu_baseline(T, seconds, warmup=1, steps=None):
     return T * n / el, n, el
 
 
+# ------------------------------------------------------------------ expert parallel (N > 1)
+def make_ep_layers(n_layers, rank, world, d=D, f=F, e=E):
+    """This rank's E/world experts of n_layers layers (seeded per layer and rank) and each layer's gate (seeded
+    per layer, the same on every rank)."""
+    from moelab_b200 import ep
+    from moelab_b200.variants.cuda import b200_q4_moe as v
+    El = e // world
+    layers = []
+    for li in range(n_layers):
+        g = torch.Generator(device="cuda").manual_seed(1000 + 7919 * li + 104729 * rank)
+        mk = lambda *s_: (torch.randn(*s_, generator=g, device="cuda") * 0.02).to(torch.bfloat16)  # noqa: E731
+        st = v.prepare(mk(El, f, d), mk(El, f, d), mk(El, d, f))
+        ep.attach(st, rank, world, e)
+        gg = torch.Generator(device="cuda").manual_seed(555 + li)
+        layers.append((st, (torch.randn(e, d, generator=gg, device="cuda") * 0.02).to(torch.bfloat16)))
+    torch.cuda.synchronize()
+    return layers
+
+
+def ep_steps(layers, xs, n, k=K_TOP, k0=0, timings=None):
+    from moelab_b200 import ep
+    y = None
+    for i in range(n):
+        st, gate = layers[(k0 + i) % len(layers)]
+        x = xs[(k0 + i) % len(xs)]
+        y = ep.layer(st, x, gate, k, residual=x, timings=timings)
+    return y
+
+
+def time_ep(layers, xs, n, ws, k=K_TOP):
+    barrier(ws)
+    torch.cuda.synchronize()
+    a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a_.record()
+    ep_steps(layers, xs, n, k)
+    b_.record()
+    b_.synchronize()
+    torch.cuda.synchronize()
+    barrier(ws)
+    return max_over_ranks(ws, a_.elapsed_time(b_) / 1e3)
+
+
+def ep_expert_roofline(layers, xs, n, d=D, f=F, k=K_TOP):
+    """Expert kernels on the received rows, timed with events inside ep.layer: algorithmic bytes (unique local
+    experts' weights + rows in + h out and back in + fp32 slot outputs) / time, and FLOPs / time."""
+    byts, flops, secs = 0.0, 0.0, 0.0
+    for i in range(n):
+        ev = [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+        tm = {"events": ev}
+        ep_steps(layers, xs, 1, k, k0=i, timings=tm)
+        torch.cuda.synchronize()
+        R = tm["rows_received"]
+        rows = tm["recv_rows"]
+        U = int(torch.unique(rows[:, d:d + 2].contiguous().view(torch.int32)).numel()) if R else 0
+        byts += U * 3 * d * f * W_BITS / 8 + R * (d + 8) * 2 + 2 * R * f * 2 + R * d * 4
+        flops += 6.0 * d * f * R
+        secs += ev[0].elapsed_time(ev[1]) / 1e3
+    return byts / secs / 1e9, flops / secs / 1e12, byts / n, secs / n * 1e6
+
+
+def run_ep(a, ws, rank, local, peaks):
+    from moelab_b200 import ep
+    T = a.tokens
+    layers = make_ep_layers(a.layers, rank, ws)
+    xs = make_inputs(T, a.layers, seed=5 + rank)
+    ep_steps(layers, xs, max(a.warmup, 3))
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    t_soak = time.perf_counter()
+    while time.perf_counter() - t_soak < a.soak_seconds:
+        ep_steps(layers, xs, len(layers))
+        torch.cuda.synchronize()
+    t = time_ep(layers, xs, a.steps, ws)
+    ck = clocks.stop()
+    value = ws * T * a.steps / t
+    ach, tfs, b_per, us_exp = ep_expert_roofline(layers, xs, min(2 * a.layers, a.steps))
+    sweep = []
+    for Ts in [int(s_) for s_ in a.sweep.split(",") if s_.strip()]:
+        xs_s = make_inputs(Ts, a.layers, seed=77 + Ts + rank)
+        ep_steps(layers, xs_s, 3)
+        n_s = 2 * a.layers
+        ts = time_ep(layers, xs_s, n_s, ws)
+        sweep.append({"T": Ts, "us_per_call": round(ts / n_s * 1e6, 3),
+                      "tokens_per_s": round(ws * Ts * n_s / ts, 1)})
+    # end to end through the public API with host buffers
+    xh = torch.randn(T, D, generator=torch.Generator().manual_seed(9 + rank)).to(torch.bfloat16).pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+    for i in range(4):
+        xd = xh.to("cuda", non_blocking=True)
+        st, gate = layers[i % len(layers)]
+        yh.copy_(ep.layer(st, xd, gate, K_TOP, residual=xd), non_blocking=True)
+    torch.cuda.synchronize()
+    barrier(ws)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(a.e2e_steps):
+        xd = xh.to("cuda", non_blocking=True)
+        st, gate = layers[i % len(layers)]
+        yh.copy_(ep.layer(st, xd, gate, K_TOP, residual=xd), non_blocking=True)
+    e1.record()
+    e1.synchronize()
+    torch.cuda.synchronize()
+    te = max_over_ranks(ws, e0.elapsed_time(e1) / 1e3)
+    if rank != 0:
+        return
+    line = {
+        "metric": "MoE-layer tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": ws,
+        "steps": a.steps, "warmup": max(a.warmup, 3), "ms_per_step": round(t / a.steps * 1e3, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) tokens)",
+        "config": {"workload": WORKLOAD + ", experts split over the GPUs", "tokens_per_gpu": T, "d": D, "f": F,
+                   "E": E, "k": K_TOP, "layers": a.layers, "experts_per_gpu": E // ws,
+                   "weights_gb_per_gpu": round(a.layers * 3 * (E // ws) * D * F * W_BITS / 8 / 1e9, 2),
+                   "l2": "inputs larger than L2: 16 independent layers cycled",
+                   "parallelism": f"ep{ws}", "exchange": "NCCL all-to-all-v (counts, rows, slot outputs)",
+                   "graph": "eager (the count exchange is read on the host every layer)"},
+        "us_per_call": round(t / a.steps * 1e6, 3),
+        "sweep": sweep,
+        "roofline": {"bound": "hbm", "kernel": "expert kernels on received rows (prep + gate_up + down)",
+                     "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(ach / peaks["hbm_gbs"], 3), "traffic": None,
+                     "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)",
+                     "algorithmic_bytes_per_launch": round(b_per), "us_per_launch": round(us_exp, 2),
+                     "tflops": round(tfs, 2)},
+        "cpu_baseline": None,
+        "e2e": {"value": round(ws * T * a.e2e_steps / te, 1), "unit": "tokens/s", "h2d_bytes_per_step": T * D * 2,
+                "d2h_bytes_per_step": T * D * 2, "us_per_call": round(te / a.e2e_steps * 1e6, 3),
+                "note": "public API ep.layer(); pinned host x in and y out every step"},
+        "clocks": ck,
+        "gpu_launches": 7 * a.steps,
+    }
+    print(json.dumps(line), flush=True)
+
+
 # ------------------------------------------------------------------ main
 def run_reference(a, ws, rank):
     if rank != 0:
@@ -309,6 +444,9 @@ def main():
         return
     from moelab_b200 import roofline
     peaks = roofline.b200_peaks()
+    if ws > 1:
+        run_ep(a, ws, rank, local, peaks)
+        return
     T = a.tokens
     v, layers = make_layers(a.layers, seed=1000 + 7919 * rank, device="cuda")
     xs = make_inputs(T, a.layers, seed=5 + rank)

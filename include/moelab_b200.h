@@ -120,6 +120,35 @@ int moeb_layer_mxfp4(const void *x, const void *gate_w, const void *gate_b, int 
                      int policy, const void *residual, void *y, int *idx_out, float *wts_out,
                      void *const *stage_events, void *ws, size_t ws_bytes, cudaStream_t stream);
 
+/* --- expert parallelism over P ranks (one process per GPU; rank r owns experts [r*E/P, (r+1)*E/P)).
+ * No counterpart in the reference (moe-lab runs one device); the exchange follows the usual two all-to-all-v
+ * steps, done by the caller with NCCL between these calls:
+ *   1. moeb_ep_dispatch: stable counting sort of the T*k slots (ids from the router) by owning rank. Writes
+ *      send_counts[P], slot_pos[T*k] (send row of each slot, -1 for an invalid id, which also sets
+ *      MOEB_DEVERR_EXPERT_ID in ws) and send_rows[T*k][d + 8] bf16: the slot's token row followed by a 16-byte
+ *      tail {int32 local expert id, fp32 weight, 0, 0}. Rows for rank p are rows [sum(counts[<p]), +counts[p]).
+ *   2. caller: all-to-all of the counts, then all-to-all-v of the rows (row size (d + 8) * 2 bytes).
+ *   3. moeb_ep_experts_q4 / _mxfp4 on the R received rows: yp[R][d] fp32 = weight * (W_down h + b_down), the
+ *      same per-slot value the single-GPU down kernel produces (workspace: moeb_ep_workspace_bytes).
+ *   4. caller: all-to-all-v of yp back to the owners (reverse counts), into back[sum(send_counts)][d].
+ *   5. moeb_ep_combine: y[t] = sum over j of back[slot_pos[t*k + j]] in j order, + residual, rounded to bf16
+ *      (the single-GPU combine's order and rounding).
+ * P <= 32, E % P == 0. */
+int moeb_ep_dispatch(const void *x, const int *idx, const float *wts, int T, int d, int k, int E, int P,
+                     void *send_rows, int *send_counts, int *slot_pos, void *ws, size_t ws_bytes,
+                     cudaStream_t stream);
+size_t moeb_ep_workspace_bytes(int R, int d, int f, int E_local);
+int moeb_ep_experts_q4(const void *rows, int R, int d, int f, int E_local, const void *qg, const void *sbg,
+                       const void *qu, const void *sbu, const void *qd, const void *sbd, const float *bg,
+                       const float *bu, const float *bd, int act, int policy, float *yp, void *ws, size_t ws_bytes,
+                       cudaStream_t stream);
+int moeb_ep_experts_mxfp4(const void *rows, int R, int d, int f, int E_local, const void *qg, const void *scg,
+                          const void *qu, const void *scu, const void *qd, const void *scd, const float *bg,
+                          const float *bu, const float *bd, int act, int policy, float *yp, void *ws,
+                          size_t ws_bytes, cudaStream_t stream);
+int moeb_ep_combine(const float *back, const int *slot_pos, int T, int d, int k, const void *residual, void *y,
+                    cudaStream_t stream);
+
 /* --- moeb_experts_q4 for callers that cannot allocate device memory. No counterpart in the reference (moe-lab
  * always lets the variant allocate its scratch). The scratch lives in a static 16 MiB device array inside the
  * library (held by every GPU that loads it until exit), so the caller passes only inputs and the output. T is

@@ -86,7 +86,8 @@ struct Layout {
     size_t logits, idx, wts, xsum, ntiles, tiles, sorted, h, hsum, yp, total;
 };
 
-Layout layout(long Tc, int d, int f, int E, int k) {
+// with_yp = false: no per-slot output region (expert-parallel calls write the slot outputs to the caller's buffer).
+Layout layout(long Tc, int d, int f, int E, int k, bool with_yp = true) {
     Layout L;
     const long TK = Tc * k;
     size_t o = 0;
@@ -104,18 +105,18 @@ Layout layout(long Tc, int d, int f, int E, int k) {
     L.sorted = o; o = align256(o + 4 * (size_t)TK);
     L.h = o; o = align256(o + 2 * (size_t)TK * f);
     L.hsum = o; o = align256(o + 4 * (size_t)TK * (f / 16));
-    L.yp = o; o = align256(o + 4 * (size_t)TK * d);
+    L.yp = o; o = align256(o + (with_yp ? 4 * (size_t)TK * d : 0));
     L.total = o;
     return L;
 }
 
 // Largest token capacity whose layout fits in `bytes` (layout size is monotone in T).
-long capacity(size_t bytes, int d, int f, int E, int k) {
+long capacity(size_t bytes, int d, int f, int E, int k, bool with_yp = true) {
     long lo = 0, hi = 1;
-    while (layout(hi, d, f, E, k).total <= bytes && hi < (1L << 24)) hi *= 2;
+    while (layout(hi, d, f, E, k, with_yp).total <= bytes && hi < (1L << 24)) hi *= 2;
     while (lo < hi) {
         long mid = (lo + hi + 1) / 2;
-        if (layout(mid, d, f, E, k).total <= bytes) lo = mid; else hi = mid - 1;
+        if (layout(mid, d, f, E, k, with_yp).total <= bytes) lo = mid; else hi = mid - 1;
     }
     return lo;
 }
@@ -391,14 +392,18 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
                           const int *idx, const float *wts, int T, int d, int f, int E, int k, int act, int policy,
                           const void *residual, void *y, void *ws, size_t ws_bytes, cudaStream_t st,
                           const void *gate_w, const void *gate_b, int norm, float rscale, int *idx_out,
-                          float *wts_out, void *const *ev) {
+                          float *wts_out, void *const *ev, float *yp_out = nullptr) {
+    // yp_out != null: expert-parallel rows (k = 1, each x row of d + 8 values ends in its {expert, weight}
+    // tail); down writes the weighted fp32 slot outputs to yp_out and nothing is combined here.
+    const bool ep = yp_out != nullptr;
     int rc = check_shape(T, d, f, E, k);
     if (rc) return rc;
     if (act < 0 || act > 2) return fail(MOEB_EINVAL, "act must be 0, 1 or 2%s");
     if (T == 0) return MOEB_OK;
-    const long cap = capacity(ws_bytes, d, f, E, k);
+    const long cap = capacity(ws_bytes, d, f, E, k, !ep);
     if (cap < T) return fail(MOEB_EINVAL, "workspace too small for T tokens%s");
-    const Layout L = layout(cap, d, f, E, k);
+    const Layout L = layout(cap, d, f, E, k, !ep);
+    const int xs = ep ? d + 8 : d;
     if (policy == MOEB_POLICY_AUTO) policy = choose_policy(T, E, k);
     if (policy != MOEB_POLICY_SLOTS && !is_tiles(policy)) return fail(MOEB_EINVAL, "unknown policy%s");
     const bool tiles = policy != MOEB_POLICY_SLOTS;
@@ -415,6 +420,11 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
         p.x = static_cast<const uint16_t *>(x);
         p.idx = idx;
         p.T = T; p.d = d; p.E = E; p.k = k;
+        p.xs = xs;
+        if (ep) {
+            idx = p.idx = p.idx_w = at<int>(ws, L.idx);
+            wts = p.wts_w = at<float>(ws, L.wts);
+        }
         p.xsum = at<float>(ws, L.xsum);
         p.cnt_all = at<unsigned>(ws, L.cnt_all);
         p.NT = nt_of(policy);
@@ -428,6 +438,7 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
     if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[1]), st);
     ExpArgs a = {};
     a.x = static_cast<const uint16_t *>(x);
+    a.xs = xs;
     a.xsum = at<float>(ws, L.xsum);
     a.g = {static_cast<const uint32_t *>(qg), static_cast<const uint32_t *>(sbg)};
     a.u = {static_cast<const uint32_t *>(qu), static_cast<const uint32_t *>(sbu)};
@@ -441,7 +452,8 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
     a.sorted = at<int>(ws, L.sorted);
     a.h = at<uint16_t>(ws, L.h);
     a.hsum = at<float>(ws, L.hsum);
-    a.yp = at<float>(ws, L.yp);
+    a.yp = ep ? yp_out : at<float>(ws, L.yp);
+    a.slot_out = ep ? 1 : 0;
     a.ycnt = at<unsigned>(ws, L.ycnt);
     a.residual = static_cast<const uint16_t *>(residual);
     a.y = static_cast<uint16_t *>(y);
@@ -496,6 +508,71 @@ int moeb_layer_q4(const void *x, const void *gate_w, const void *gate_b, int nor
     return experts_common(FMT_Q4, x, qg, sbg, qu, sbu, qd, sbd, bg, bu, bd, nullptr, nullptr, T, d, f, E, k, act,
                           policy, residual, y, ws, ws_bytes, st, gate_w, gate_b, norm, rscale, idx_out, wts_out,
                           stage_events);
+}
+
+// ------------------------------------------------------------------ expert parallelism
+static int check_ep(int T, int d, int k, int E, int P) {
+    if (T < 0 || d <= 0 || d % 64 || k <= 0 || k > 32 || k > E) return fail(MOEB_EINVAL, "bad T, d or k%s");
+    if (P < 1 || P > 32 || E % P) return fail(MOEB_EINVAL, "need 1 <= P <= 32 ranks and E a multiple of P%s");
+    return MOEB_OK;
+}
+
+int moeb_ep_dispatch(const void *x, const int *idx, const float *wts, int T, int d, int k, int E, int P,
+                     void *send_rows, int *send_counts, int *slot_pos, void *ws, size_t ws_bytes, cudaStream_t st) {
+    if (int rc = check_ep(T, d, k, E, P)) return rc;
+    if (!ws || ws_bytes < 256) return fail(MOEB_EINVAL, "workspace required (its error word is used)%s");
+    if (T == 0) {
+        if (cudaMemsetAsync(send_counts, 0, sizeof(int) * P, st) != cudaSuccess) return check_launch("ep_dispatch");
+        return MOEB_OK;
+    }
+    EPArgs a = {};
+    a.x = static_cast<const uint16_t *>(x);
+    a.idx = idx;
+    a.wts = wts;
+    a.T = T; a.d = d; a.k = k; a.E = E; a.P = P;
+    a.send_counts = send_counts;
+    a.slot_pos = slot_pos;
+    a.rows = static_cast<uint16_t *>(send_rows);
+    a.err = static_cast<unsigned *>(ws);
+    if (launch(k_ep_plan, dim3(1), dim3(1024), 0, st, a) != cudaSuccess) return check_launch("ep_plan");
+    if (launch(k_ep_pack, dim3((unsigned)(((long)T * k + 7) / 8)), dim3(256), 0, st, a) != cudaSuccess)
+        return check_launch("ep_pack");
+    return MOEB_OK;
+}
+
+size_t moeb_ep_workspace_bytes(int R, int d, int f, int E_local) {
+    if (R < 1) R = 1;
+    return layout(R, d, f, E_local, 1, false).total;
+}
+
+int moeb_ep_experts_q4(const void *rows, int R, int d, int f, int E_local, const void *qg, const void *sbg,
+                       const void *qu, const void *sbu, const void *qd, const void *sbd, const float *bg,
+                       const float *bu, const float *bd, int act, int policy, float *yp, void *ws, size_t ws_bytes,
+                       cudaStream_t st) {
+    if (!yp) return fail(MOEB_EINVAL, "yp is required%s");
+    return experts_common(FMT_Q4, rows, qg, sbg, qu, sbu, qd, sbd, bg, bu, bd, nullptr, nullptr, R, d, f, E_local,
+                          1, act, policy, nullptr, nullptr, ws, ws_bytes, st, nullptr, nullptr, 0, 1.f, nullptr,
+                          nullptr, nullptr, yp);
+}
+
+int moeb_ep_experts_mxfp4(const void *rows, int R, int d, int f, int E_local, const void *qg, const void *scg,
+                          const void *qu, const void *scu, const void *qd, const void *scd, const float *bg,
+                          const float *bu, const float *bd, int act, int policy, float *yp, void *ws,
+                          size_t ws_bytes, cudaStream_t st) {
+    if (!yp) return fail(MOEB_EINVAL, "yp is required%s");
+    return experts_common(FMT_FP4, rows, qg, scg, qu, scu, qd, scd, bg, bu, bd, nullptr, nullptr, R, d, f, E_local,
+                          1, act, policy, nullptr, nullptr, ws, ws_bytes, st, nullptr, nullptr, 0, 1.f, nullptr,
+                          nullptr, nullptr, yp);
+}
+
+int moeb_ep_combine(const float *back, const int *slot_pos, int T, int d, int k, const void *residual, void *y,
+                    cudaStream_t st) {
+    if (T < 0 || d <= 0 || d % 64 || k <= 0 || k > 32) return fail(MOEB_EINVAL, "bad T, d or k%s");
+    if (T == 0) return MOEB_OK;
+    if (launch(k_ep_combine, dim3(T), dim3(256), 0, st, back, slot_pos, T, d, k,
+               static_cast<const uint16_t *>(residual), static_cast<uint16_t *>(y)) != cudaSuccess)
+        return check_launch("ep_combine");
+    return MOEB_OK;
 }
 
 }  // extern "C"

@@ -46,7 +46,7 @@ __global__ void __launch_bounds__(32 * KS, 3) k_gate_up_slots(ExpArgs a) {
         const TileInfo ti = tile_info(a, slot);
         const size_t blk = (size_t)ti.e * RB + rb;
         if (warp == KS - 1 && a.dn_prefetch) prefetch_down(a, ti.e, rb, RB, lane);
-        const uint4 *xsrc = reinterpret_cast<const uint4 *>(a.x + (size_t)(slot / a.k) * d);
+        const uint4 *xsrc = reinterpret_cast<const uint4 *>(a.x + (size_t)(slot / a.k) * a.xs);
         for (int i = threadIdx.x; i < d / 8; i += 32 * KS) xs4[i] = xsrc[i];
         const float *sxr = a.xsum + (size_t)(slot / a.k) * xsum_stride(d);
         float Cg[1][4] = {{0.f, 0.f, 0.f, 0.f}}, Cu[1][4] = {{0.f, 0.f, 0.f, 0.f}};
@@ -233,7 +233,7 @@ __global__ void __launch_bounds__(128) k_gate_up_tiles_reg(ExpArgs a) {
 #pragma unroll
         for (int j = 0; j < NT8; ++j) {
             const int sb_ = tile_slot(a, ti, j * 8 + gq);
-            xrow[j] = sb_ >= 0 ? a.x + (size_t)(sb_ / a.k) * d + 16 * c : nullptr;
+            xrow[j] = sb_ >= 0 ? a.x + (size_t)(sb_ / a.k) * a.xs + 16 * c : nullptr;
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
                 const int sc_ = tile_slot(a, ti, j * 8 + 2 * c + hf);

@@ -219,6 +219,7 @@ __device__ __forceinline__ void down_store_combine(const ExpArgs &a, const TileI
                 a.yp[(size_t)slot * d + r1] = wsl * v1;
             }
         }
+    if (a.slot_out) return;  // expert-parallel: the token's owner combines
     __syncwarp();
     if (lane == 0) __threadfence();  // cumulative over the warp's writes ordered by the __syncwarp
     __syncwarp();

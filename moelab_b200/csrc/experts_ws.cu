@@ -101,7 +101,7 @@ __global__ void __launch_bounds__(32 * (RBC + 1), 1) k_experts_ws(ExpArgs a) {
                     src1 = reinterpret_cast<const unsigned char *>(PP.sb + blk * G * 16);
                 } else if (clane && s_ >= 0) {
                     src0 = reinterpret_cast<const unsigned char *>(DOWN ? a.h + (size_t)s_ * a.f
-                                                                        : a.x + (size_t)(s_ / a.k) * a.d);
+                                                                        : a.x + (size_t)(s_ / a.k) * a.xs);
                     src1 = reinterpret_cast<const unsigned char *>(DOWN ? a.hsum + (size_t)s_ * (a.f / 16)
                                                                         : a.xsum + (size_t)(s_ / a.k) * xsum_stride(a.d));
                 } else {

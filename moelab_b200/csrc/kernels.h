@@ -31,6 +31,10 @@ struct PrepArgs {
     const uint16_t *x;
     const int *idx;
     int T, d, E, k;
+    int xs;  // x row stride in bf16 elements (d, or d + 8 for expert-parallel rows with their tail)
+    // expert-parallel rows (k == 1): each row's tail {local expert, weight bits} is unpacked into these
+    int *idx_w;
+    float *wts_w;
     float *xsum;
     unsigned *cnt_all;
     int NT;
@@ -47,7 +51,8 @@ struct QProj {
 };
 
 struct ExpArgs {
-    const uint16_t *x;  // [T][d] bf16
+    const uint16_t *x;  // [T][xs] bf16 (the first d values of each row are the activations)
+    int xs;             // x row stride in bf16 elements
     const float *xsum;  // [T][d/64]
     QProj g, u, dn;
     const float *bg, *bu, *bd;  // optional expert biases [E][f], [E][f], [E][d]
@@ -66,7 +71,24 @@ struct ExpArgs {
     int T, d, f, E, k, act, tile_mode;
     int dn_prefetch;  // gate/up pulls the down weights of its expert into L2
     int fmt;          // FMT_Q4 or FMT_FP4
+    int slot_out;     // 1: down stops after writing the weighted per-slot outputs yp (caller's buffer), no combine
 };
+
+// Expert-parallel dispatch plan / pack / combine (csrc/ep.cu).
+struct EPArgs {
+    const uint16_t *x;    // [T][d] bf16
+    const int *idx;       // [T*k] global expert ids
+    const float *wts;     // [T*k]
+    int T, d, k, E, P;    // P ranks own E/P consecutive experts each
+    int *send_counts;     // [P]
+    int *slot_pos;        // [T*k] row of each slot in the send buffer, -1 = dropped (invalid id)
+    uint16_t *rows;       // [T*k][d + 8] send rows: x of the slot's token, then {local expert, weight, 0, 0}
+    unsigned *err;
+};
+__global__ void k_ep_plan(EPArgs a);
+__global__ void k_ep_pack(EPArgs a);
+__global__ void k_ep_combine(const float *back, const int *slot_pos, int T, int d, int k, const uint16_t *residual,
+                             uint16_t *y);
 
 template <int TPB, int JMAX, int U>
 __global__ void k_router(RouterArgs a);

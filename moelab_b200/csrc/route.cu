@@ -279,8 +279,19 @@ __global__ void __launch_bounds__(256) k_prep(PrepArgs a) {
     pdl_wait();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int t = blockIdx.x * 8 + warp;
-    if (t < a.T) row_group_sums(a.x + (size_t)t * a.d, a.d, a.xsum + (size_t)t * xsum_stride(a.d), lane);
+    if (t < a.T) {
+        const uint16_t *xr = a.x + (size_t)t * a.xs;
+        row_group_sums(xr, a.d, a.xsum + (size_t)t * xsum_stride(a.d), lane);
+        if (a.idx_w && lane == 0) {  // expert-parallel row (k = 1): unpack and validate its tail
+            const int2 m = *reinterpret_cast<const int2 *>(xr + a.d);
+            if (m.x < 0 || m.x >= a.E) atomicOr(a.err, ERR_EXPERT_ID);
+            a.idx_w[t] = m.x;
+            a.wts_w[t] = __int_as_float(m.y);
+            __threadfence();  // the tile builder (last CTA) reads the ids
+        }
+    }
     if (a.tiles == nullptr) {
+        if (a.idx_w) return;  // ids validated with their rows
         // slot mode: only validate ids
         for (int s = blockIdx.x * 256 + threadIdx.x; s < a.T * a.k; s += gridDim.x * 256) {
             const int e = a.idx[s];

@@ -38,16 +38,20 @@ class Workspace:
     """Caller-owned scratch for the layer kernels, grown on demand (allocation happens here, in Python,
     never inside the library). Zeroed once at allocation; the kernels keep its counters zero."""
 
-    def __init__(self, d, f, E, k, device=None):
+    def __init__(self, d, f, E, k, device=None, ep=False):
         self.d, self.f, self.E, self.k = d, f, E, k
         self.device = device
+        self.ep = ep  # expert-parallel rows (k = 1, no per-slot output region): sized by moeb_ep_workspace_bytes
         self.T = 0
         self.buf = None
 
     def get(self, T):
         if T > self.T:
             Tn = max(T, 2 * self.T, 16)
-            nbytes = _lib.load().moeb_workspace_bytes(Tn, self.d, self.f, self.E, self.k)
+            if self.ep:
+                nbytes = _lib.load().moeb_ep_workspace_bytes(Tn, self.d, self.f, self.E)
+            else:
+                nbytes = _lib.load().moeb_workspace_bytes(Tn, self.d, self.f, self.E, self.k)
             self.buf = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
             _lib.call("moeb_workspace_init", _p(self.buf), nbytes, _stream())
             self.T = Tn
@@ -217,3 +221,47 @@ layer = layer_q4
 
 def policy(T, E, k):
     return _lib.load().moeb_policy(T, E, k)
+
+
+# ------------------------------------------------------------------ expert parallelism (device steps)
+def ep_dispatch(x, idx, wts, E, P, ws):
+    """Sort the T*k slots by owning rank and pack their send rows (x row + {local expert, weight} tail).
+    Returns rows bf16 [T*k, d + 8] (the first sum(send_counts) are valid), send_counts int32 [P] and
+    slot_pos int32 [T*k]. ws: any Workspace (its error word records invalid ids)."""
+    _need(x, torch.bfloat16, "x")
+    _need(idx, torch.int32, "idx")
+    _need(wts, torch.float32, "wts")
+    T, d = x.shape
+    k = idx.shape[1]
+    rows = torch.empty(T * k, d + 8, dtype=torch.bfloat16, device=x.device)
+    send_counts = torch.empty(P, dtype=torch.int32, device=x.device)
+    slot_pos = torch.empty(T * k, dtype=torch.int32, device=x.device)
+    buf = ws.get(1)
+    _lib.call("moeb_ep_dispatch", _p(x), _p(idx), _p(wts), T, d, k, E, P, _p(rows), _p(send_counts),
+              _p(slot_pos), _p(buf), buf.numel(), _stream())
+    return rows, send_counts, slot_pos
+
+
+def ep_experts(state, rows, act=0, policy=POLICY_AUTO):
+    """The local experts on received rows (bf16 [R, d + 8]) -> yp fp32 [R, d], weight * (W_down h + b_down)."""
+    _need(rows, torch.bfloat16, "rows")
+    R, d = rows.shape[0], rows.shape[1] - 8
+    yp = torch.empty(R, d, dtype=torch.float32, device=rows.device)
+    if R == 0:
+        return yp
+    buf = state["ep_ws"].get(R)
+    fn = "moeb_ep_experts_mxfp4" if _fmt(state) == "mxfp4" else "moeb_ep_experts_q4"
+    _lib.call(fn, _p(rows), R, d, state["f"], state["E"], *_expert_ptrs(state), int(act), int(policy), _p(yp),
+              _p(buf), buf.numel(), _stream())
+    return yp
+
+
+def ep_combine(back, slot_pos, T, k, residual=None):
+    """y bf16 [T, d] = sum_j back[slot_pos[t*k + j]] (fixed j order) + residual."""
+    _need(back, torch.float32, "back")
+    _need(slot_pos, torch.int32, "slot_pos")
+    _need(residual, torch.bfloat16, "residual")
+    d = back.shape[1]
+    y = torch.empty(T, d, dtype=torch.bfloat16, device=back.device)
+    _lib.call("moeb_ep_combine", _p(back), _p(slot_pos), T, d, k, _p(residual), _p(y), _stream())
+    return y

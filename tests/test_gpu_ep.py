@@ -1,0 +1,157 @@
+"""Expert parallelism on one B200: the dispatch / combine kernels bit-exact against the oracle's restatement, the
+expert kernels on received rows against the fp64 oracle, and the whole expert-parallel layer (P ranks emulated
+by threads sharing the GPU, exchanging through ThreadGroup) bit-exact against the single-GPU layer when both
+run the same expert kernels."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from ep_workers import ThreadGroup
+from helpers import assert_close, load_variant
+from moelab_b200 import ep, ops
+from moelab_b200.variants.cuda import b200_mxfp4_moe, b200_q4_moe
+from oracle import ep as oep
+
+pytestmark = pytest.mark.gpu
+
+
+def _ids(T, E, k, seed, invalid=False):
+    rng = np.random.default_rng(seed)
+    idx = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+    if invalid and T:
+        idx[0, 0] = E + 3
+        idx[T - 1, k - 1] = -1
+    w = rng.random((T, k)).astype(np.float32)
+    return idx, w
+
+
+@pytest.mark.parametrize("P", [1, 2, 4, 8])
+@pytest.mark.parametrize("T", [1, 5, 64, 300])
+@pytest.mark.parametrize("invalid", [False, True])
+def test_dispatch_bit_exact(P, T, invalid):
+    E, k, d = 64, 8, 256
+    idx, w = _ids(T, E, k, seed=T + P, invalid=invalid)
+    x = torch.randn(T, d, device="cuda").to(torch.bfloat16)
+    ws = ops.Workspace(d, 64, E, k, "cuda")
+    rows, counts, pos = ops.ep_dispatch(x, torch.from_numpy(idx).cuda(), torch.from_numpy(w).cuda(), E, P, ws)
+    rc, rp = oep.ep_plan(idx, E, P)
+    np.testing.assert_array_equal(counts.cpu().numpy(), rc)
+    np.testing.assert_array_equal(pos.cpu().numpy(), rp)
+    ref_rows = oep.ep_pack(x, idx, w, rp, E, P)
+    got = rows[:ref_rows.shape[0]].view(torch.int16).cpu().numpy().view(np.uint16)
+    np.testing.assert_array_equal(got, ref_rows)
+    assert (ws.read_error() == ops._lib.DEVERR_EXPERT_ID) == invalid
+
+
+@pytest.mark.parametrize("T,k", [(1, 1), (3, 8), (40, 4), (257, 6)])
+@pytest.mark.parametrize("residual", [False, True])
+def test_combine_bit_exact(T, k, residual):
+    d = 192
+    n = T * k
+    rng = np.random.default_rng(T * k)
+    perm = rng.permutation(n + 5)[:n].astype(np.int32)  # rows of back in any order, some unused
+    perm[rng.random(n) < 0.1] = -1  # dropped slots
+    back = rng.standard_normal((n + 5, d)).astype(np.float32)
+    res = torch.randn(T, d).to(torch.bfloat16) if residual else None
+    y = ops.ep_combine(torch.from_numpy(back).cuda(), torch.from_numpy(perm).cuda(), T, k,
+                       None if res is None else res.cuda())
+    ref = oep.ep_combine(back, perm, T, k, res)
+    np.testing.assert_array_equal(oracle.bf16_bits(y), ref)
+
+
+def _layer(E, d, f, seed, fmt="q4"):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    mk = lambda *s: (torch.randn(*s, generator=g, device="cuda") * 0.02).to(torch.bfloat16)  # noqa: E731
+    return [mk(E, f, d), mk(E, f, d), mk(E, d, f)], mk(E, d)
+
+
+@pytest.mark.parametrize("fmt", ["q4", "mxfp4"])
+@pytest.mark.parametrize("R", [1, 9, 100])
+def test_expert_rows_vs_oracle(fmt, R):
+    E, d, f, P = 16, 256, 320, 4
+    v = b200_mxfp4_moe if fmt == "mxfp4" else b200_q4_moe
+    w, _ = _layer(E, d, f, seed=R)
+    st = ep.shard(v, *w, rank=1, world=P)
+    El = E // P
+    rng = np.random.default_rng(R)
+    x = torch.randn(R, d).to(torch.bfloat16)
+    e = rng.integers(0, El, R).astype(np.int32)
+    wt = rng.random(R).astype(np.float32)
+    rows = np.zeros((R, d + 8), np.uint16)
+    rows[:, :d] = oracle.bf16_bits(x)
+    rows[:, d:d + 2] = e[:, None].view(np.uint16).reshape(R, 2)
+    rows[:, d + 2:d + 4] = wt[:, None].view(np.uint16).reshape(R, 2)
+    rt = torch.from_numpy(rows.view(np.int16)).view(torch.bfloat16).cuda()
+    yp = ops.ep_experts(st, rt)
+    wg, wu, wd = (t.cpu().numpy() for t in v.dequant(st))
+    ref = oep.ep_expert_rows(rows, wg, wu, wd)
+    assert_close(yp, ref, what=(fmt, R))
+
+
+def _emulated(P, v, w, gate, tokens, k, policy, seed, act=0, biases=None, gate_b=None):
+    """P threads run ep.layer on their own tokens; returns per-rank (y, idx, wts, x)."""
+    grp = ThreadGroup(P)
+    states = [ep.shard(v, *w, r, P, *(biases or (None, None, None)), act=act) for r in range(P)]
+    xs = [torch.randn(T, w[0].shape[2], generator=torch.Generator(device="cuda").manual_seed(seed + r),
+                      device="cuda").to(torch.bfloat16) for r, T in enumerate(tokens)]
+    torch.cuda.synchronize()
+
+    def body(r, comm):
+        return ep.layer(states[r], xs[r], gate, k, gate_b=gate_b, residual=xs[r], policy=policy, comm=comm,
+                        return_routing=True)
+
+    out = grp.run(body)
+    torch.cuda.synchronize()
+    return [(y, i, wt, x) for (y, i, wt), x in zip(out, xs)]
+
+
+POL = {"slots": ops.POLICY_SLOTS, "tiles8": ops.POLICY_TILES8, "tiles16": ops.POLICY_TILES16}
+
+
+@pytest.mark.parametrize("P,tokens", [(2, [4, 7]), (4, [1, 0, 33, 16]), (8, [2, 9, 1, 1, 40, 0, 3, 17])])
+@pytest.mark.parametrize("pol", list(POL))
+def test_emulated_ep_bit_exact_vs_single_gpu(P, tokens, pol):
+    E, d, f, k = 32, 256, 384, 4
+    w, gate = _layer(E, d, f, seed=P)
+    full = b200_q4_moe.prepare(*w)
+    b200_q4_moe._ws(full, k)
+    for y, idx, wts, x in _emulated(P, b200_q4_moe, w, gate, tokens, k, POL[pol], seed=10 * P):
+        if x.shape[0] == 0:
+            assert y.shape == (0, d)
+            continue
+        ri, _ = oracle.router(x, gate, k)
+        np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+        ys = ops.experts(full, x, idx, wts, policy=POL[pol], residual=x)
+        assert torch.equal(y, ys), (pol, (y.float() - ys.float()).abs().max())
+
+
+@pytest.mark.parametrize("P", [2, 4])
+def test_emulated_ep_auto_policy_vs_oracle(P):
+    E, d, f, k = 64, 512, 256, 8
+    w, gate = _layer(E, d, f, seed=7)
+    full = b200_q4_moe.prepare(*w)
+    wg, wu, wd = (t.cpu().numpy() for t in b200_q4_moe.dequant(full))
+    for y, idx, wts, x in _emulated(P, b200_q4_moe, w, gate, [1, 64, 2, 3][:P], k, None, seed=3):
+        ref = oracle.moe_forward(x.float().cpu().numpy(), wg, wu, wd, idx.cpu().numpy(), wts.cpu().numpy())
+        assert_close(y, ref + x.float().cpu().numpy())
+
+
+@pytest.mark.parametrize("pol", ["slots", "tiles8"])
+def test_emulated_ep_gptoss_mxfp4_bit_exact(pol):
+    """gpt-oss: MXFP4 experts, biases, clamped SwiGLU, router bias, over 4 ranks."""
+    E, d, f, k, P = 16, 576, 576, 4, 4
+    w, gate = _layer(E, d, f, seed=11)
+    g = torch.Generator(device="cuda").manual_seed(12)
+    b = (4 * torch.randn(E, f, generator=g, device="cuda"), 4 * torch.randn(E, f, generator=g, device="cuda"),
+         0.1 * torch.randn(E, d, generator=g, device="cuda"))
+    gb = (torch.randn(E, generator=g, device="cuda")).to(torch.bfloat16)
+    full = b200_mxfp4_moe.prepare(*w)
+    full.update(bg=b[0], bu=b[1], bd=b[2])
+    b200_mxfp4_moe._ws(full, k)
+    for y, idx, wts, x in _emulated(P, b200_mxfp4_moe, w, gate, [3, 8, 0, 21], k, POL[pol], seed=5, act=2,
+                                    biases=b, gate_b=gb):
+        if x.shape[0] == 0:
+            continue
+        ys = ops.experts(full, x, idx, wts, act=2, policy=POL[pol], residual=x)
+        assert torch.equal(y, ys)
