@@ -113,6 +113,17 @@ int moeb_layer_q4(const void *x, const void *gate_w, const void *gate_b, int nor
                   const float *bg, const float *bu, const float *bd, int T, int d, int f, int E, int k, int act,
                   int policy, const void *residual, void *y, int *idx_out, float *wts_out,
                   void *const *stage_events, void *ws, size_t ws_bytes, cudaStream_t stream);
+/* DeepSeek layer with always-on shared experts (replaces the MoE block of moelab/e2e.py:130-148: routed experts
+ * + shared_experts(x), :146-147). The weight arrays hold E routed experts followed by n_shared shared experts of
+ * the same width f (a shared MLP of width n*f split along f into n experts). The router picks k of the E routed
+ * experts (DeepSeek-V2 greedy: norm = 0, rscale = routed_scaling_factor) and appends the shared ones with weight
+ * 1, so the grouped kernels run them with the routed slots and the combine adds them last. idx_out / wts_out
+ * are [T][k + n_shared]. k + n_shared <= 32. Workspace: moeb_workspace_bytes(T, d, f, E + n_shared, k + n_shared). */
+int moeb_layer_q4_shared(const void *x, const void *gate_w, const void *gate_b, int norm, float rscale, int n_shared,
+                         const void *qg, const void *sbg, const void *qu, const void *sbu, const void *qd,
+                         const void *sbd, const float *bg, const float *bu, const float *bd, int T, int d, int f, int E,
+                         int k, int act, int policy, const void *residual, void *y, int *idx_out, float *wts_out,
+                         void *const *stage_events, void *ws, size_t ws_bytes, cudaStream_t stream);
 /* MXFP4 layer (gpt-oss: gate_b = router bias, act = 2, expert biases bg/bu/bd). */
 int moeb_layer_mxfp4(const void *x, const void *gate_w, const void *gate_b, int norm, float rscale, const void *qg,
                      const void *scg, const void *qu, const void *scu, const void *qd, const void *scd,

@@ -39,6 +39,7 @@ SIGNATURES = {
     "moeb_layer_q4": (_I, [_P, _P, _P, _I, _F] + [_P] * 9 + [_I] * 7 + [_P, _P, _P, _P, _P, _P, _S, _P]),
     "moeb_experts_mxfp4": (_I, [_P] * 12 + [_I] * 7 + [_P, _P, _P, _S, _P]),
     "moeb_layer_mxfp4": (_I, [_P, _P, _P, _I, _F] + [_P] * 9 + [_I] * 7 + [_P, _P, _P, _P, _P, _P, _S, _P]),
+    "moeb_layer_q4_shared": (_I, [_P, _P, _P, _I, _F, _I] + [_P] * 9 + [_I] * 7 + [_P] * 6 + [_S, _P]),
     "moeb_ep_dispatch": (_I, [_P, _P, _P] + [_I] * 5 + [_P, _P, _P, _P, _S, _P]),
     "moeb_ep_workspace_bytes": (_S, [_I, _I, _I, _I]),
     "moeb_ep_experts_q4": (_I, [_P] + [_I] * 4 + [_P] * 9 + [_I, _I, _P, _P, _S, _P]),

@@ -240,10 +240,12 @@ void (*router_kernel(int E))(RouterArgs) {
     return k_router<TPB, 32, U>;
 }
 
+// E, k: routed experts / slots; ns shared experts follow as ids E .. E + ns - 1 (slots per token k + ns).
 int launch_router(const void *x, const void *wg, const void *bias, int T, int d, int E, int k, int norm,
                   float scale, int *idx, float *wts, float *logits, bool want_xsum, int policy, const Layout &L,
-                  void *ws, cudaStream_t st) {
+                  void *ws, cudaStream_t st, int ns = 0) {
     RouterArgs r = {};
+    r.ns = ns;
     r.x = static_cast<const uint16_t *>(x);
     r.wg = static_cast<const uint16_t *>(wg);
     r.bias = static_cast<const uint16_t *>(bias);
@@ -260,7 +262,7 @@ int launch_router(const void *x, const void *wg, const void *bias, int T, int d,
     r.tiles = tiles ? at<int4>(ws, L.tiles) : nullptr;
     r.ntiles = at<int>(ws, L.ntiles);
     r.sorted = at<int>(ws, L.sorted);
-    const size_t smem = tiles ? 8 * (size_t)E : 0;
+    const size_t smem = tiles ? 8 * (size_t)(E + ns) : 0;
     // tokens per CTA: 1 up to T = 64 (more CTAs in flight, the gate row re-read from L2), 4 above
     const int tpb = T <= 64 ? 1 : 4;
     void (*kern)(RouterArgs) = tpb == 1 ? router_kernel<1, 8>(E) : router_kernel<4, 4>(E);
@@ -392,7 +394,7 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
                           const int *idx, const float *wts, int T, int d, int f, int E, int k, int act, int policy,
                           const void *residual, void *y, void *ws, size_t ws_bytes, cudaStream_t st,
                           const void *gate_w, const void *gate_b, int norm, float rscale, int *idx_out,
-                          float *wts_out, void *const *ev, float *yp_out = nullptr) {
+                          float *wts_out, void *const *ev, float *yp_out = nullptr, int ns = 0) {
     // yp_out != null: expert-parallel rows (k = 1, each x row of d + 8 values ends in its {expert, weight}
     // tail); down writes the weighted fp32 slot outputs to yp_out and nothing is combined here.
     const bool ep = yp_out != nullptr;
@@ -411,7 +413,9 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
     if (gate_w) {  // layer call: router produces ids, weights, x group sums and (tile mode) the tiles
         int *ri = idx_out ? idx_out : at<int>(ws, L.idx);
         float *rw = wts_out ? wts_out : at<float>(ws, L.wts);
-        rc = launch_router(x, gate_w, gate_b, T, d, E, k, norm, rscale, ri, rw, nullptr, true, policy, L, ws, st);
+        // E, k count the ns shared experts / slots; the router picks among the E - ns routed experts
+        rc = launch_router(x, gate_w, gate_b, T, d, E - ns, k - ns, norm, rscale, ri, rw, nullptr, true, policy, L,
+                           ws, st, ns);
         if (rc) return rc;
         idx = ri;
         wts = rw;
@@ -497,6 +501,19 @@ int moeb_layer_mxfp4(const void *x, const void *gate_w, const void *gate_b, int 
     return experts_common(FMT_FP4, x, qg, scg, qu, scu, qd, scd, bg, bu, bd, nullptr, nullptr, T, d, f, E, k, act,
                           policy, residual, y, ws, ws_bytes, st, gate_w, gate_b, norm, rscale, idx_out, wts_out,
                           stage_events);
+}
+
+int moeb_layer_q4_shared(const void *x, const void *gate_w, const void *gate_b, int norm, float rscale, int n_shared,
+                         const void *qg, const void *sbg, const void *qu, const void *sbu, const void *qd,
+                         const void *sbd, const float *bg, const float *bu, const float *bd, int T, int d, int f, int E,
+                         int k, int act, int policy, const void *residual, void *y, int *idx_out, float *wts_out,
+                         void *const *stage_events, void *ws, size_t ws_bytes, cudaStream_t st) {
+    if (!gate_w) return fail(MOEB_EINVAL, "gate weights are required%s");
+    if (n_shared < 0 || k <= 0 || k + n_shared > 32 || k > E)
+        return fail(MOEB_EINVAL, "need n_shared >= 0, 0 < k <= E and k + n_shared <= 32%s");
+    return experts_common(FMT_Q4, x, qg, sbg, qu, sbu, qd, sbd, bg, bu, bd, nullptr, nullptr, T, d, f, E + n_shared,
+                          k + n_shared, act, policy, residual, y, ws, ws_bytes, st, gate_w, gate_b, norm, rscale,
+                          idx_out, wts_out, stage_events, nullptr, n_shared);
 }
 
 int moeb_layer_q4(const void *x, const void *gate_w, const void *gate_b, int norm, float rscale, const void *qg,

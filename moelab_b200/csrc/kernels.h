@@ -12,6 +12,7 @@ struct RouterArgs {
     const uint16_t *wg;    // [E][d] bf16 gate
     const uint16_t *bias;  // [E] bf16 or null
     int T, d, E, k, norm;
+    int ns;  // shared experts: ids E .. E + ns - 1 appended to every token with weight 1 (slots per token k + ns)
     float scale;
     float *logits;  // [T][E] fp32 (workspace or caller buffer)
     int *idx;       // [T][k]

@@ -165,9 +165,13 @@ __device__ void topk_token(const RouterArgs &a, int t, int lane) {
         s = den;
     }
     const float off = a.norm ? top0 : m0;
+    const int ks = k + a.ns;
     if (lane < k) {
-        a.idx[(size_t)t * k + lane] = myi;
-        a.wts[(size_t)t * k + lane] = expf(myv - off) / s * a.scale;
+        a.idx[(size_t)t * ks + lane] = myi;
+        a.wts[(size_t)t * ks + lane] = expf(myv - off) / s * a.scale;
+    } else if (lane < ks) {  // always-on shared experts after the routed ones (summed last, weight 1)
+        a.idx[(size_t)t * ks + lane] = E + (lane - k);
+        a.wts[(size_t)t * ks + lane] = 1.f;
     }
 }
 
@@ -268,7 +272,7 @@ __global__ void __launch_bounds__(128) k_router(RouterArgs a) {
     }
     __syncthreads();
     if (!s_last) return;
-    build_tiles(a.idx, a.T * a.k, a.E, a.NT, a.tiles, a.ntiles, a.sorted, a.err);
+    build_tiles(a.idx, a.T * (a.k + a.ns), a.E + a.ns, a.NT, a.tiles, a.ntiles, a.sorted, a.err);
     if (threadIdx.x == 0) *a.cnt_all = 0;
 }
 

@@ -190,9 +190,11 @@ experts = experts_q4
 
 
 def layer_q4(state, x, gate_w, k, gate_b=None, norm=True, rscale=1.0, act=0, policy=POLICY_AUTO, residual=None,
-             return_routing=False, stage_events=None):
+             return_routing=False, stage_events=None, n_shared=0):
     """The layer call (x, gate weights, packed experts, k) -> y: router + routing + experts + combine.
-    stage_events: optional 4 torch.cuda.Event (before router, after router, after gate/up, after down)."""
+    stage_events: optional 4 torch.cuda.Event (before router, after router, after gate/up, after down).
+    n_shared: the state's last n_shared experts are always-on shared experts (int4 only); the routing returned
+    then has k + n_shared slots per token."""
     _need(x, torch.bfloat16, "x")
     _need(gate_w, torch.bfloat16, "gate_w")
     _need(gate_b, torch.bfloat16, "gate_b")
@@ -201,18 +203,26 @@ def layer_q4(state, x, gate_w, k, gate_b=None, norm=True, rscale=1.0, act=0, pol
     E, f = state["E"], state["f"]
     buf = state["ws"].get(max(T, 1))
     y = torch.empty_like(x)
-    idx = torch.empty(T, k, dtype=torch.int32, device=x.device) if return_routing else None
-    wts = torch.empty(T, k, dtype=torch.float32, device=x.device) if return_routing else None
+    ks = k + n_shared
+    idx = torch.empty(T, ks, dtype=torch.int32, device=x.device) if return_routing else None
+    wts = torch.empty(T, ks, dtype=torch.float32, device=x.device) if return_routing else None
     evp = None
     if stage_events is not None:
         for ev in stage_events:
             if ev.cuda_event == 0:
                 ev.record()  # creates the underlying cudaEvent_t
         evp = (ctypes.c_void_p * 4)(*[ctypes.c_void_p(ev.cuda_event) for ev in stage_events])
-    fn = "moeb_layer_mxfp4" if _fmt(state) == "mxfp4" else "moeb_layer_q4"
-    _lib.call(fn, _p(x), _p(gate_w), _p(gate_b), int(bool(norm)), float(rscale), *_expert_ptrs(state),
-              T, d, f, E, k, int(act), int(policy), _p(residual), _p(y), _p(idx), _p(wts), evp, _p(buf),
-              buf.numel(), _stream())
+    if n_shared:
+        if _fmt(state) != "q4":
+            raise ValueError("shared experts are supported for int4 states")
+        _lib.call("moeb_layer_q4_shared", _p(x), _p(gate_w), _p(gate_b), int(bool(norm)), float(rscale),
+                  int(n_shared), *_expert_ptrs(state), T, d, f, E - n_shared, k, int(act), int(policy),
+                  _p(residual), _p(y), _p(idx), _p(wts), evp, _p(buf), buf.numel(), _stream())
+    else:
+        fn = "moeb_layer_mxfp4" if _fmt(state) == "mxfp4" else "moeb_layer_q4"
+        _lib.call(fn, _p(x), _p(gate_w), _p(gate_b), int(bool(norm)), float(rscale), *_expert_ptrs(state),
+                  T, d, f, E, k, int(act), int(policy), _p(residual), _p(y), _p(idx), _p(wts), evp, _p(buf),
+                  buf.numel(), _stream())
     return (y, idx, wts) if return_routing else y
 
 

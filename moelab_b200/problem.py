@@ -33,6 +33,15 @@ def make_routing(T, E, k, mode="uniform", rng=None, zipf_a=1.2):
     return idx, w
 
 
+def zipf_bias(E, s=1.1, seed=0, gain=2.0):
+    """Per-expert router bias for the skewed DeepSeek-V2-Lite config: gain * log(Zipf(s) popularity), the
+    popularity ranks assigned over a seeded expert permutation (the "zipf" routing mode above with s = 1.1), so
+    a few experts are hot. float32 [E]."""
+    rng = np.random.default_rng(seed)
+    pop = 1.0 / np.arange(1, E + 1) ** s
+    return (np.log(pop)[rng.permutation(E)] * gain).astype(np.float32)
+
+
 def make_problem(shape, T, routing="uniform", seed=0):
     rng = np.random.default_rng(seed)
     d, f, E, k = shape.d, shape.f, shape.E, shape.k

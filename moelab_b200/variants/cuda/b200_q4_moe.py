@@ -83,12 +83,31 @@ def run_slots(s, x, idx, act=None):
     return y if x.dtype == torch.bfloat16 else y.to(x.dtype)
 
 
+def prepare_shared(w_gate, w_up, w_down, sw_gate, sw_up, sw_down):
+    """DeepSeek layer: routed experts [E, f, d], [E, f, d], [E, d, f] plus the always-on shared MLP
+    (gate/up [fs, d], down [d, fs]; moelab/e2e.py:146-147). The shared MLP is split along its width into
+    fs / f experts of width f appended after the routed ones: SwiGLU acts per row of h and down sums over the
+    width, so the split changes nothing but the fp32 summation grouping."""
+    E, f, d = w_gate.shape
+    fs = sw_gate.shape[0]
+    assert fs % f == 0, "shared width must be a multiple of the expert width"
+    n = fs // f
+    sg = sw_gate.reshape(n, f, d)
+    su = sw_up.reshape(n, f, d)
+    sd = sw_down.reshape(d, n, f).permute(1, 0, 2)
+    s = prepare(torch.cat([w_gate, sg]), torch.cat([w_up, su]), torch.cat([w_down, sd]))
+    s["n_shared"] = n
+    return s
+
+
 def layer(s, x, gate_w, k, gate_b=None, norm=True, rscale=1.0, act=None, residual=None, return_routing=False,
           stage_events=None):
+    """Router + experts (+ the state's shared experts, if any) -> y; routing has k + n_shared slots per token."""
     act = s.get("act", 0) if act is None else act
-    _ws(s, k)
+    ns = s.get("n_shared", 0)
+    _ws(s, k + ns)
     return ops.layer_q4(s, x, gate_w, k, gate_b=gate_b, norm=norm, rscale=rscale, act=act, policy=_policy(),
-                        residual=residual, return_routing=return_routing, stage_events=stage_events)
+                        residual=residual, return_routing=return_routing, stage_events=stage_events, n_shared=ns)
 
 
 def custom_wins(T, k, E, D, F):
