@@ -5,8 +5,12 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <cudaTypedefs.h>
+
 #include <algorithm>
+#include <map>
 #include <mutex>
+#include <tuple>
 #include <unordered_map>
 
 #include "../../include/moelab_b200.h"
@@ -134,50 +138,119 @@ int check_shape(int T, int d, int f, int E, int k) {
 
 // ------------------------------------------------------------------ dispatcher
 // Load = T*k/E (average slots per expert; the reference's policy variable, metal_q4_moe.py:42-46).
-// Measured on B200 (Qwen3-30B shape, 16 layers cycled): the split-K decode kernels win up to 16 slots
-// (T <= 2 at k = 8); above that the register-pipelined tiles of 8 slots are fastest at every load measured
-// (T = 4 .. 256, load 0.25 .. 16); tiles of 16 and the TMA variants stay selectable for other shapes.
+// Measured on B200 (Qwen3-30B shape, 16 layers cycled, CUDA graph): the split-K decode kernels win up to 16
+// slots (T <= 2 at k = 8); above that the warp-specialized tensor-map pipeline beats the register tiles at
+// every load (T = 4: 50.8 vs 55.6 us, T = 32: 126 vs 145 us), with tiles of 8 slots up to load ~4 and tiles of
+// 16 at high load (T = 256, load 16: 291 vs 329 us).
 int choose_policy(int T, int E, int k) {
     const long TK = (long)T * k;
-    (void)E;
     if (TK <= 16) return MOEB_POLICY_SLOTS;
-    return MOEB_POLICY_TILES8;
+    return TK >= 8L * E ? MOEB_POLICY_TILES16_RING : MOEB_POLICY_TILES8_RING;
 }
 
 int nt_of(int policy) { return (policy == MOEB_POLICY_TILES16 || policy == MOEB_POLICY_TILES16_RING) ? 16 : 8; }
 bool is_tiles(int policy) { return policy >= MOEB_POLICY_TILES8 && policy <= MOEB_POLICY_TILES16_RING; }
 
+// One expert kernel launch: per_warp kernels run one (tile, 16-row block) unit per warp; the others one unit
+// per CTA, where a warp-specialized kernel's unit is `rows` consecutive row blocks (rows > 1 also means it
+// reads the weights through tensor maps whose box is rows x sg).
+struct KLaunch {
+    void (*fn)(ExpArgs);
+    int threads;
+    size_t smem;
+    bool per_warp;
+    int rows, sg;
+};
 struct ExpLaunch {
-    void (*gu)(ExpArgs);
-    void (*dn)(ExpArgs);
-    int gu_threads, dn_threads;
-    size_t gu_smem, dn_smem;
-    bool per_warp;  // tiles kernels: one unit per warp (4 warps per CTA); slots kernels: one unit per CTA
-    int rows_per_cta = 1;  // warp-specialized kernels: 16-row blocks per CTA work item
+    KLaunch gu, dn;
 };
 
+constexpr int WS_RBC = 8, WS_SG = 4, WS_NS_GU = 2, WS_NS_DN = 4;
+
+KLaunch ws_kernel(int nt8, bool down) {
+    void (*fn)(ExpArgs) = nullptr;
+    if (nt8 == 1) fn = down ? k_experts_ws<FMT_Q4, 1, WS_RBC, WS_SG, WS_NS_DN, true, 2>
+                            : k_experts_ws<FMT_Q4, 1, WS_RBC, WS_SG, WS_NS_GU, false, 2>;
+    else fn = down ? k_experts_ws<FMT_Q4, 2, WS_RBC, WS_SG, WS_NS_DN, true, 2>
+                   : k_experts_ws<FMT_Q4, 2, WS_RBC, WS_SG, WS_NS_GU, false, 2>;
+    return {fn, 32 * (WS_RBC + 1), experts_ws_smem(nt8, WS_RBC, WS_SG, down ? WS_NS_DN : WS_NS_GU, down), false,
+            WS_RBC, WS_SG};
+}
+
+// Kernels per policy: TILES8 / TILES16 run the register-pipelined tile kernels, the *_RING policies the
+// warp-specialized tensor-map pipeline (faster on B200 for both projections, so the dispatcher picks it).
 ExpLaunch pick_kernels(int fmt, int policy, int d, int f) {
+    const KLaunch none = {nullptr, 0, 0, false, 1, 0};
     if (fmt == FMT_FP4) {  // MXFP4: decode and register-tile kernels (the TMA variant is int4 only)
         if (policy == MOEB_POLICY_SLOTS)
-            return {k_gate_up_slots<FMT_FP4, 8, 4>, k_down_slots<FMT_FP4, 4, 4>, 256, 128, (size_t)d * 2,
-                    (size_t)f * 2 + (size_t)f / 16 * 4, false};
+            return {{k_gate_up_slots<FMT_FP4, 8, 4>, 256, (size_t)d * 2, false, 1, 0},
+                    {k_down_slots<FMT_FP4, 4, 4>, 128, (size_t)f * 2 + (size_t)f / 16 * 4, false, 1, 0}};
         if (policy == MOEB_POLICY_TILES16 || policy == MOEB_POLICY_TILES16_RING)
-            return {k_gate_up_tiles_reg<FMT_FP4, 2, 1>, k_down_tiles_reg<FMT_FP4, 2, 1>, 128, 128, 0, 0, true};
-        return {k_gate_up_tiles_reg<FMT_FP4, 1, 2>, k_down_tiles_reg<FMT_FP4, 1, 2>, 128, 128, 0, 0, true};
+            return {{k_gate_up_tiles_reg<FMT_FP4, 2, 1>, 128, 0, true, 1, 0},
+                    {k_down_tiles_reg<FMT_FP4, 2, 1>, 128, 0, true, 1, 0}};
+        return {{k_gate_up_tiles_reg<FMT_FP4, 1, 2>, 128, 0, true, 1, 0},
+                {k_down_tiles_reg<FMT_FP4, 1, 2>, 128, 0, true, 1, 0}};
     }
-    if (fmt != FMT_Q4) return {nullptr, nullptr, 0, 0, 0, 0, false};
+    if (fmt != FMT_Q4) return {none, none};
     if (policy == MOEB_POLICY_SLOTS)
-        return {k_gate_up_slots<FMT_Q4, 8, 4>, k_down_slots<FMT_Q4, 4, 4>, 256, 128, (size_t)d * 2,
-                (size_t)f * 2 + (size_t)f / 16 * 4, false};
-    if (policy == MOEB_POLICY_TILES16_RING)
-        return {k_experts_ws<FMT_Q4, 2, 8, 4, 4, false>, k_experts_ws<FMT_Q4, 2, 8, 4, 4, true>, 288, 288,
-                experts_ws_smem(2, 8, 4, 4, false), experts_ws_smem(2, 8, 4, 4, true), false, 8};
-    if (policy == MOEB_POLICY_TILES8_RING)
-        return {k_experts_ws<FMT_Q4, 1, 8, 4, 4, false>, k_experts_ws<FMT_Q4, 1, 8, 4, 4, true>, 288, 288,
-                experts_ws_smem(1, 8, 4, 4, false), experts_ws_smem(1, 8, 4, 4, true), false, 8};
+        return {{k_gate_up_slots<FMT_Q4, 8, 4>, 256, (size_t)d * 2, false, 1, 0},
+                {k_down_slots<FMT_Q4, 4, 4>, 128, (size_t)f * 2 + (size_t)f / 16 * 4, false, 1, 0}};
+    if (policy == MOEB_POLICY_TILES16_RING) return {ws_kernel(2, false), ws_kernel(2, true)};
+    if (policy == MOEB_POLICY_TILES8_RING) return {ws_kernel(1, false), ws_kernel(1, true)};
     if (policy == MOEB_POLICY_TILES16)
-        return {k_gate_up_tiles_reg<FMT_Q4, 2, 1>, k_down_tiles_reg<FMT_Q4, 2, 1>, 128, 128, 0, 0, true};
-    return {k_gate_up_tiles_reg<FMT_Q4, 1, 2>, k_down_tiles_reg<FMT_Q4, 1, 2>, 128, 128, 0, 0, true};
+        return {{k_gate_up_tiles_reg<FMT_Q4, 2, 1>, 128, 0, true, 1, 0},
+                {k_down_tiles_reg<FMT_Q4, 2, 1>, 128, 0, true, 1, 0}};
+    return {{k_gate_up_tiles_reg<FMT_Q4, 1, 2>, 128, 0, true, 1, 0}, {k_down_tiles_reg<FMT_Q4, 1, 2>, 128, 0, true, 1, 0}};
+}
+
+// ---- tensor maps for the warp-specialized kernels (driver entry point, cached per weight array and shape)
+PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 2-D view of a fragment-major projection: rows = row blocks of all experts, each row the K/64 groups' bytes
+// (codes: 512 B per group as uint64 elements; scale|bias: 64 B per group as uint32); box = brows rows x
+// bgroups groups. words = 32-bit words per group (128 or 16).
+bool encode_weights_map(CUtensorMap *out, const void *base, int words, long groups, long rows, int bgroups,
+                        int brows) {
+    using Key = std::tuple<const void *, int, long, long, int, int>;
+    static std::mutex mu;
+    static std::map<Key, CUtensorMap> cache;
+    const Key key{base, words, groups, rows, bgroups, brows};
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        *out = it->second;
+        return true;
+    }
+    auto fn = tmap_encoder();
+    if (!fn) return false;
+    const bool wide = words == 128;  // codes: 8-byte elements keep the box row (SG * 512 B) within 256 elements
+    const int esz = wide ? 8 : 4, per_group = words * 4 / esz;
+    const cuuint64_t dims[2] = {(cuuint64_t)groups * per_group, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)groups * words * 4};
+    const cuuint32_t box[2] = {(cuuint32_t)(bgroups * per_group), (cuuint32_t)brows};
+    const cuuint32_t es[2] = {1, 1};
+    if (box[0] > 256 || box[1] > 256) return false;
+    CUtensorMap m;
+    if (fn(&m, wide ? CU_TENSOR_MAP_DATA_TYPE_UINT64 : CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void *>(base),
+           dims, strides, box, es,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    if (cache.size() > 4096) cache.clear();  // bounded: a long-lived process cycling through many weight sets
+    cache[key] = m;
+    *out = m;
+    return true;
 }
 
 // Opt a kernel in to more than 48 KB of dynamic shared memory (once per kernel).
@@ -193,9 +266,9 @@ bool allow_smem(const void *fn, size_t bytes) {
     return true;
 }
 
-int grid_for(void (*kern)(ExpArgs), int threads, size_t smem, long units, bool per_warp, int rows_per_cta) {
-    const long ctas = per_warp ? (units + threads / 32 - 1) / (threads / 32) : (units + rows_per_cta - 1) / rows_per_cta;
-    const long cap = (long)occupancy((const void *)kern, threads, smem) * sm_count();
+int grid_for(const KLaunch &k, long units) {
+    const long ctas = k.per_warp ? (units + k.threads / 32 - 1) / (k.threads / 32) : units;
+    const long cap = (long)occupancy((const void *)k.fn, k.threads, k.smem) * sm_count();
     return (int)std::max<long>(1, std::min(ctas, cap));
 }
 
@@ -205,22 +278,33 @@ int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaS
     const int nt = nt_of(policy);
     const long max_tiles = a.tile_mode ? std::min<long>(TK, (long)a.E + TK / nt) : TK;
     ExpLaunch K = pick_kernels(fmt, policy, a.d, a.f);
-    if (!K.gu) return fail(MOEB_EUNSUP, "format not supported%s");
-    if (policy == MOEB_POLICY_SLOTS && (K.gu_smem > 48 * 1024 || K.dn_smem > 48 * 1024))
+    if (!K.gu.fn) return fail(MOEB_EUNSUP, "format not supported%s");
+    if (policy == MOEB_POLICY_SLOTS && (K.gu.smem > 48 * 1024 || K.dn.smem > 48 * 1024))
         return fail(MOEB_EINVAL, "d or f too large for the decode kernels%s");
-    if (!allow_smem((const void *)K.gu, K.gu_smem) || !allow_smem((const void *)K.dn, K.dn_smem))
+    if (!allow_smem((const void *)K.gu.fn, K.gu.smem) || !allow_smem((const void *)K.dn.fn, K.dn.smem))
         return check_launch("cudaFuncSetAttribute");
+    const int RBf = a.f / 16, RBd = a.d / 16;
+    if (K.gu.sg) {
+        if (!encode_weights_map(&a.tmq[0], a.g.q, 128, a.d / 64, (long)a.E * RBf, K.gu.sg, K.gu.rows) ||
+            !encode_weights_map(&a.tmsb[0], a.g.sb, 16, a.d / 64, (long)a.E * RBf, K.gu.sg, K.gu.rows) ||
+            !encode_weights_map(&a.tmq[1], a.u.q, 128, a.d / 64, (long)a.E * RBf, K.gu.sg, K.gu.rows) ||
+            !encode_weights_map(&a.tmsb[1], a.u.sb, 16, a.d / 64, (long)a.E * RBf, K.gu.sg, K.gu.rows))
+            return fail(MOEB_ELAUNCH, "tensor map encoding failed (gate/up)%s");
+    }
+    if (K.dn.sg) {
+        if (!encode_weights_map(&a.tmq[2], a.dn.q, 128, a.f / 64, (long)a.E * RBd, K.dn.sg, K.dn.rows) ||
+            !encode_weights_map(&a.tmsb[2], a.dn.sb, 16, a.f / 64, (long)a.E * RBd, K.dn.sg, K.dn.rows))
+            return fail(MOEB_ELAUNCH, "tensor map encoding failed (down)%s");
+    }
     {
-        const long rbs = (a.f / 16 + K.rows_per_cta - 1) / K.rows_per_cta * K.rows_per_cta;
-        const int grid = grid_for(K.gu, K.gu_threads, K.gu_smem, max_tiles * rbs, K.per_warp, K.rows_per_cta);
-        if (launch(K.gu, dim3(grid), dim3(K.gu_threads), K.gu_smem, st, a) != cudaSuccess)
+        const long units = max_tiles * ((RBf + K.gu.rows - 1) / K.gu.rows);
+        if (launch(K.gu.fn, dim3(grid_for(K.gu, units)), dim3(K.gu.threads), K.gu.smem, st, a) != cudaSuccess)
             return check_launch("gate_up");
     }
     if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[2]), st);
     {
-        const long rbs = (a.d / 16 + K.rows_per_cta - 1) / K.rows_per_cta * K.rows_per_cta;
-        const int grid = grid_for(K.dn, K.dn_threads, K.dn_smem, max_tiles * rbs, K.per_warp, K.rows_per_cta);
-        if (launch(K.dn, dim3(grid), dim3(K.dn_threads), K.dn_smem, st, a) != cudaSuccess)
+        const long units = max_tiles * ((RBd + K.dn.rows - 1) / K.dn.rows);
+        if (launch(K.dn.fn, dim3(grid_for(K.dn, units)), dim3(K.dn.threads), K.dn.smem, st, a) != cudaSuccess)
             return check_launch("down");
     }
     if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[3]), st);

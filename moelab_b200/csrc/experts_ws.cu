@@ -3,10 +3,12 @@
 // CTA = 1 producer warp + RBC consumer warps. A CTA work item ("super-unit") is one tile (<= 8*NT8 slots of one
 // expert) and RBC consecutive 16-row blocks of the projection. K is streamed in stages of SG 64-groups through
 // an NS-deep shared-memory ring:
-//   producer: per stage, its lanes issue 1-D TMA bulk copies (cp.async.bulk, no multicast, evict-first in L2)
-//     of the RBC row blocks' codes and scale|bias words (contiguous in the fragment-major layout), of the
-//     tile's activation row chunks (x for gate/up, h for down; one copy per slot, rows padded by 16 bytes in
-//     shared memory to spread banks) and of their group sums, all completing on the stage's "full" mbarrier;
+//   producer: per stage, lane 0 issues one 2-D tensor copy per projection for the codes (RBC row blocks x SG
+//     groups x 512 B) and one for the scale|bias words (x 64 B), evict-first in L2, no multicast; the lanes
+//     of the tile's columns each issue a 1-D bulk copy of their activation row chunk (x for gate/up, h for
+//     down; rows padded by 16 bytes in shared memory to spread banks) and of its group sums. Everything
+//     completes on the stage's "full" mbarrier. (A bulk copy has a fixed issue cost, so few large copies per
+//     stage matter: the tensor copies replace 2*NP*RBC row-block copies.)
 //   consumers: each warp owns one row block, waits on "full", runs the m16n8k16 raw-code MMAs and fp32 scale
 //     promotion of experts_common.cuh on the stage, and arrives on the stage's "empty" mbarrier.
 // The activation tile is fetched once per CTA and shared by all row blocks; consumers never touch global
@@ -24,17 +26,21 @@ struct WSL {
     static constexpr int SB_BYTES = NP * RBC * SG * 64;
     static constexpr int X_ROW = SG * 128 + 16;
     static constexpr int X_BYTES = COLS * X_ROW;
-    static constexpr int S_ROW = ((DOWN ? SG * 16 : SG * 4) + 15) / 16 * 16;
+    // group sums: down 16 bytes per group; gate/up 4 bytes per group, copied from the 16-byte boundary at or
+    // below the stage's first group (a bulk copy must start 16-byte aligned), so up to 3 extra leading floats
+    static constexpr int S_ROW = DOWN ? SG * 16 : (SG % 4 == 0 ? SG * 4 : ((SG + 3) * 4 + 15) / 16 * 16);
     static constexpr int S_BYTES = COLS * S_ROW;
     static constexpr int STAGE = W_BYTES + SB_BYTES + X_BYTES + S_BYTES;
+    static_assert(STAGE % 128 == 0 && W_BYTES % 128 == 0 && SB_BYTES % 128 == 0 && (RBC * SG * 64) % 128 == 0,
+                  "tensor-copy destinations must stay 128-byte aligned");
 };
 
 MOEB_DEV void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-template <int FMT, int NT8, int RBC, int SG, int NS, bool DOWN>
-__global__ void __launch_bounds__(32 * (RBC + 1), 1) k_experts_ws(ExpArgs a) {
+template <int FMT, int NT8, int RBC, int SG, int NS, bool DOWN, int MB>
+__global__ void __launch_bounds__(32 * (RBC + 1), MB) k_experts_ws(const __grid_constant__ ExpArgs a) {
     using L = WSL<NT8, RBC, SG, DOWN>;
     pdl_launch();
     pdl_wait();
@@ -61,15 +67,19 @@ __global__ void __launch_bounds__(32 * (RBC + 1), 1) k_experts_ws(ExpArgs a) {
 
     if (warp == RBC) {
         // ------------------------------------------------------------ producer warp
-        // Lane roles are fixed: lanes [0, NP*RBC) copy one (projection, row block) each, lanes [16, 16 + COLS)
-        // copy one activation column each. Per work item every lane computes its source bases once; the item's
-        // tile record and slot ids are fetched one item ahead so no global load sits on the issue path.
-        static_assert(L::NP * RBC <= 16 && L::COLS <= 16, "producer lane roles");
+        // Lane 0 issues the weight tensor copies; lanes [16, 16 + COLS) copy one activation column each. Per work
+        // item every lane computes its source bases once; the item's tile record and slot ids are fetched one
+        // item ahead so no global load sits on the issue path.
+        static_assert(L::COLS <= 16, "producer lane roles");
         const uint64_t pol = l2_evict_first_policy();
-        const QProj PP = (DOWN || lane < RBC) ? (DOWN ? a.dn : a.g) : a.u;
-        const int wr = lane % RBC;        // weight lane: row block offset
-        const int col = lane - 16;        // column lane: column index
-        const bool wlane = lane < L::NP * RBC, clane = col >= 0 && col < L::COLS;
+        const int col = lane - 16;  // column lane: column index
+        const bool clane = col >= 0 && col < L::COLS;
+        const int m0 = DOWN ? 2 : 0;  // tensor maps of this kernel's projections
+        if (lane == 0)
+            for (int p = 0; p < L::NP; ++p) {
+                tmap_prefetch(&a.tmq[m0 + p]);
+                tmap_prefetch(&a.tmsb[m0 + p]);
+            }
         auto fetch_tile = [&](int su) {  // tile record (expert, start, n)
             const int tile = su / RBS;
             return a.tile_mode ? a.tiles[tile] : make_int4(a.idx[tile], tile, 1, 0);
@@ -84,22 +94,18 @@ __global__ void __launch_bounds__(32 * (RBC + 1), 1) k_experts_ws(ExpArgs a) {
             sl_n = fetch_slot(tr_n);
         }
         const unsigned char *src0 = nullptr, *src1 = nullptr;
-        int nrb = 0, ncol = 0, e = 0;
+        int ncol = 0, row0 = 0;
         for (int k = 0; k < total; ++k) {
             const int slot = k % NS;
             const int g0 = (k % SPU) * SG, ng = min(SG, G - g0);
             if (g0 == 0) {  // new work item: take the prefetched metadata, prefetch the next item's
                 const int su = (int)blockIdx.x + (k / SPU) * (int)gridDim.x;
                 const int rb0 = (su - (su / RBS) * RBS) * RBC;
-                e = (tr_n.x < 0 || tr_n.x >= a.E) ? 0 : tr_n.x;
+                const int e = (tr_n.x < 0 || tr_n.x >= a.E) ? 0 : tr_n.x;
                 ncol = min(L::COLS, tr_n.z);
-                nrb = min(RBC, RB - rb0);
+                row0 = e * RB + rb0;
                 const int s_ = sl_n;
-                if (wlane && wr < nrb) {
-                    const size_t blk = (size_t)e * RB + rb0 + wr;
-                    src0 = reinterpret_cast<const unsigned char *>(PP.q + blk * G * 128);
-                    src1 = reinterpret_cast<const unsigned char *>(PP.sb + blk * G * 16);
-                } else if (clane && s_ >= 0) {
+                if (clane && s_ >= 0) {
                     src0 = reinterpret_cast<const unsigned char *>(DOWN ? a.h + (size_t)s_ * a.f
                                                                         : a.x + (size_t)(s_ / a.k) * a.xs);
                     src1 = reinterpret_cast<const unsigned char *>(DOWN ? a.hsum + (size_t)s_ * (a.f / 16)
@@ -108,7 +114,7 @@ __global__ void __launch_bounds__(32 * (RBC + 1), 1) k_experts_ws(ExpArgs a) {
                     src0 = src1 = nullptr;
                 }
                 if (!DOWN && lane == 0 && a.dn_prefetch)
-                    for (int r = 0; r < nrb; ++r) prefetch_down(a, e, rb0 + r, RB, 0, 1);
+                    for (int r = 0; r < min(RBC, RB - rb0); ++r) prefetch_down(a, e, rb0 + r, RB, 0, 1);
                 const int nsu = su + (int)gridDim.x;
                 if (nsu < n_su) {
                     tr_n = fetch_tile(nsu);                 // in flight during this item's stages
@@ -122,23 +128,23 @@ __global__ void __launch_bounds__(32 * (RBC + 1), 1) k_experts_ws(ExpArgs a) {
                 if (lane == 0) atomicOr(a.err, ERR_TIMEOUT);
                 return;
             }
-            const int sum_bytes = DOWN ? ng * 16 : ((ng + 3) / 4) * 16;
+            const int ga = DOWN ? g0 : (g0 & ~3);  // first group of the sums copy (16-byte aligned source)
+            const int sum_bytes = DOWN ? ng * 16 : ((g0 + ng - ga + 3) / 4) * 16;
+            // a tensor copy always delivers its whole box (rows or groups past the end arrive as zeros)
             if (lane == 0)
-                mbar_expect_tx(full + slot, (unsigned)(L::NP * nrb * ng * (512 + 64) + ncol * (ng * 128 + sum_bytes)));
+                mbar_expect_tx(full + slot, (unsigned)(L::NP * RBC * SG * (512 + 64) + ncol * (ng * 128 + sum_bytes)));
             __syncwarp();
             unsigned char *st = smem_raw + (size_t)slot * L::STAGE;
-            if (src0 != nullptr) {
-                if (wlane) {
-                    const int p = lane / RBC;
-                    tma_load_1d(st + (p * RBC + wr) * SG * 512, src0 + (size_t)g0 * 512, ng * 512, full + slot, pol);
-                    tma_load_1d(st + L::W_BYTES + (p * RBC + wr) * SG * 64, src1 + (size_t)g0 * 64, ng * 64,
-                                full + slot, pol);
-                } else {
-                    tma_load_1d(st + L::W_BYTES + L::SB_BYTES + col * L::X_ROW, src0 + (size_t)g0 * 128, ng * 128,
-                                full + slot);
-                    tma_load_1d(st + L::W_BYTES + L::SB_BYTES + L::X_BYTES + col * L::S_ROW,
-                                src1 + (size_t)g0 * (DOWN ? 16 : 4), sum_bytes, full + slot);
+            if (lane == 0) {
+                for (int p = 0; p < L::NP; ++p) {
+                    tma_load_2d(st + p * RBC * SG * 512, &a.tmq[m0 + p], g0 * 64, row0, full + slot, pol);
+                    tma_load_2d(st + L::W_BYTES + p * RBC * SG * 64, &a.tmsb[m0 + p], g0 * 16, row0, full + slot, pol);
                 }
+            } else if (src0 != nullptr) {
+                tma_load_1d(st + L::W_BYTES + L::SB_BYTES + col * L::X_ROW, src0 + (size_t)g0 * 128, ng * 128,
+                            full + slot);
+                tma_load_1d(st + L::W_BYTES + L::SB_BYTES + L::X_BYTES + col * L::S_ROW,
+                            src1 + (size_t)ga * (DOWN ? 16 : 4), sum_bytes, full + slot);
             }
         }
         return;
@@ -198,7 +204,7 @@ __global__ void __launch_bounds__(32 * (RBC + 1), 1) k_experts_ws(ExpArgs a) {
                                     const float4 v = *reinterpret_cast<const float4 *>(ss + cc * L::S_ROW + i * 16);
                                     sx[j][hf] = (v.x + v.y) + (v.z + v.w);
                                 } else {
-                                    sx[j][hf] = reinterpret_cast<const float *>(ss + cc * L::S_ROW)[i];
+                                    sx[j][hf] = reinterpret_cast<const float *>(ss + cc * L::S_ROW)[(g0 & 3) + i];
                                 }
                             } else {
                                 sx[j][hf] = 0.f;
@@ -232,14 +238,16 @@ __global__ void __launch_bounds__(32 * (RBC + 1), 1) k_experts_ws(ExpArgs a) {
 
 size_t experts_ws_smem(int nt8, int rbc, int sg, int ns, bool down) {
     const int np = down ? 1 : 2, cols = 8 * nt8;
-    const size_t stage = (size_t)np * rbc * sg * (512 + 64) + (size_t)cols * (sg * 128 + 16) +
-                         (size_t)cols * (((down ? sg * 16 : sg * 4) + 15) / 16 * 16);
+    const int s_row = down ? sg * 16 : (sg % 4 == 0 ? sg * 4 : ((sg + 3) * 4 + 15) / 16 * 16);
+    const size_t stage = (size_t)np * rbc * sg * (512 + 64) + (size_t)cols * (sg * 128 + 16) + (size_t)cols * s_row;
     return ns * stage + 2 * ns * 8;
 }
 
-template __global__ void k_experts_ws<FMT_Q4, 1, 8, 4, 4, false>(ExpArgs);
-template __global__ void k_experts_ws<FMT_Q4, 2, 8, 4, 4, false>(ExpArgs);
-template __global__ void k_experts_ws<FMT_Q4, 1, 8, 4, 4, true>(ExpArgs);
-template __global__ void k_experts_ws<FMT_Q4, 2, 8, 4, 4, true>(ExpArgs);
+// gate/up: 4 groups per stage, 2 stages, 2 CTAs per SM; down: 4 groups per stage, 4 stages, 2 CTAs per SM
+// (measured best of the (SG, NS, CTAs/SM) sweep on the Qwen3-30B shape at T = 4, 32, 256)
+template __global__ void k_experts_ws<FMT_Q4, 1, 8, 4, 2, false, 2>(const __grid_constant__ ExpArgs);
+template __global__ void k_experts_ws<FMT_Q4, 2, 8, 4, 2, false, 2>(const __grid_constant__ ExpArgs);
+template __global__ void k_experts_ws<FMT_Q4, 1, 8, 4, 4, true, 2>(const __grid_constant__ ExpArgs);
+template __global__ void k_experts_ws<FMT_Q4, 2, 8, 4, 4, true, 2>(const __grid_constant__ ExpArgs);
 
 }  // namespace moeb

@@ -1,5 +1,6 @@
 // Internal kernel argument blocks and declarations (not part of the C ABI).
 #pragma once
+#include <cuda.h>  // CUtensorMap
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -73,6 +74,11 @@ struct ExpArgs {
     int dn_prefetch;  // gate/up pulls the down weights of its expert into L2
     int fmt;          // FMT_Q4 or FMT_FP4
     int slot_out;     // 1: down stops after writing the weighted per-slot outputs yp (caller's buffer), no combine
+    // warp-specialized kernels: 2-D tensor maps over each projection's codes (uint64 elements) and scale|bias
+    // words (uint32), viewed as [row blocks of all experts][K/64 groups x 512 B | 64 B] ([0] gate, [1] up,
+    // [2] down); a box is RBC row blocks x SG groups (RBC rows of SG*512 | SG*64 contiguous bytes), so one
+    // copy per array and projection fills a pipeline stage
+    CUtensorMap tmq[3], tmsb[3];
 };
 
 // Expert-parallel dispatch plan / pack / combine (csrc/ep.cu).
@@ -112,8 +118,8 @@ template <int FMT, int NT8, int GPW>
 __global__ void k_gate_up_tiles_reg(ExpArgs a);
 template <int FMT, int NT8, int GPW>
 __global__ void k_down_tiles_reg(ExpArgs a);
-template <int FMT, int NT8, int RBC, int SG, int NS, bool DOWN>
-__global__ void k_experts_ws(ExpArgs a);
+template <int FMT, int NT8, int RBC, int SG, int NS, bool DOWN, int MB>
+__global__ void k_experts_ws(const __grid_constant__ ExpArgs a);
 size_t experts_ws_smem(int nt8, int rbc, int sg, int ns, bool down);
 
 

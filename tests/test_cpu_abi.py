@@ -40,8 +40,8 @@ def test_host_only_calls():
     # dispatcher: decode -> per-slot tiles; high load -> grouped tiles
     assert lib.moeb_policy(1, 128, 8) == _lib.POLICY_SLOTS
     assert lib.moeb_policy(2, 128, 8) == _lib.POLICY_SLOTS
-    assert lib.moeb_policy(4, 128, 8) == _lib.POLICY_TILES8
-    assert lib.moeb_policy(256, 128, 8) in (_lib.POLICY_TILES8, _lib.POLICY_TILES16)
+    assert lib.moeb_policy(4, 128, 8) == _lib.POLICY_TILES8_RING
+    assert lib.moeb_policy(256, 128, 8) in (_lib.POLICY_TILES8_RING, _lib.POLICY_TILES16_RING)
 
 
 def test_bad_shape_is_rejected_before_any_device_work():
