@@ -266,6 +266,8 @@ bool allow_smem(const void *fn, size_t bytes) {
     return true;
 }
 
+bool separate_combine(const KLaunch &dn) { return dn.sg > 0; }
+
 int grid_for(const KLaunch &k, long units) {
     const long ctas = k.per_warp ? (units + k.threads / 32 - 1) / (k.threads / 32) : units;
     const long cap = (long)occupancy((const void *)k.fn, k.threads, k.smem) * sm_count();
@@ -302,11 +304,18 @@ int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaS
             return check_launch("gate_up");
     }
     if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[2]), st);
+    // combine: fused into down (last arrival per (token, row block) sums the k slot rows), or a separate pass
+    // over the weighted slot rows when down is the warp-specialized kernel (no fences / counters in its epilogue)
+    const bool sep = !a.slot_out && separate_combine(K.dn);
+    if (sep) a.slot_out = 1;
     {
         const long units = max_tiles * ((RBd + K.dn.rows - 1) / K.dn.rows);
         if (launch(K.dn.fn, dim3(grid_for(K.dn, units)), dim3(K.dn.threads), K.dn.smem, st, a) != cudaSuccess)
             return check_launch("down");
     }
+    if (sep && launch(k_combine, dim3(a.T), dim3(256), 0, st, (const float *)a.yp, a.T, a.d, a.k, a.residual, a.y) !=
+                   cudaSuccess)
+        return check_launch("combine");
     if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[3]), st);
     (void)L;
     (void)ws;

@@ -94,6 +94,7 @@ struct EPArgs {
 };
 __global__ void k_ep_plan(EPArgs a);
 __global__ void k_ep_pack(EPArgs a);
+__global__ void k_combine(const float *yp, int T, int d, int k, const uint16_t *residual, uint16_t *y);
 __global__ void k_ep_combine(const float *back, const int *slot_pos, int T, int d, int k, const uint16_t *residual,
                              uint16_t *y);
 
