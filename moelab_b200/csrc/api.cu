@@ -313,8 +313,8 @@ int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaS
         if (launch(K.dn.fn, dim3(grid_for(K.dn, units)), dim3(K.dn.threads), K.dn.smem, st, a) != cudaSuccess)
             return check_launch("down");
     }
-    if (sep && launch(k_combine, dim3(a.T), dim3(256), 0, st, (const float *)a.yp, a.T, a.d, a.k, a.residual, a.y) !=
-                   cudaSuccess)
+    if (sep && launch(k_combine, dim3((unsigned)(((long)a.T * (a.d / 4) + 127) / 128)), dim3(128), 0, st,
+                      (const float *)a.yp, a.T, a.d, a.k, a.residual, a.y) != cudaSuccess)
         return check_launch("combine");
     if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[3]), st);
     (void)L;

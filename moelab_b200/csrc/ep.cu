@@ -123,31 +123,33 @@ __global__ void __launch_bounds__(256) k_ep_combine(const float *__restrict__ ba
     }
 }
 
-// grid T, block 256: y[t] = sum_j yp[t*k + j] (fixed j order) + residual, rounded once to bf16: the combine of
-// the grouped kernels when down writes only the weighted slot rows (same order and rounding as the fused one).
-__global__ void __launch_bounds__(256) k_combine(const float *__restrict__ yp, int T, int d, int k,
+// grid ceil(T * d / 4 / 128), block 128: one thread per (token, 4 columns) so every slot row is loaded by many
+// CTAs at once. y[t] = sum_j yp[t*k + j] (fixed j order) + residual, rounded once to bf16: the combine of the
+// grouped kernels when down writes only the weighted slot rows (same order and rounding as the fused one).
+__global__ void __launch_bounds__(128) k_combine(const float *__restrict__ yp, int T, int d, int k,
                                                  const uint16_t *__restrict__ residual, uint16_t *__restrict__ y) {
     pdl_launch();
     pdl_wait();
-    const int t = blockIdx.x;
-    for (int c = threadIdx.x; c < d / 4; c += blockDim.x) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int j = 0; j < k; ++j) {
-            const float4 v = __ldcs(reinterpret_cast<const float4 *>(yp + ((size_t)t * k + j) * d) + c);
-            acc.x += v.x;
-            acc.y += v.y;
-            acc.z += v.z;
-            acc.w += v.w;
-        }
-        if (residual) {
-            const uint2 r = *reinterpret_cast<const uint2 *>(residual + (size_t)t * d + 4 * c);
-            acc.x += bf16lo(r.x);
-            acc.y += bf16hi(r.x);
-            acc.z += bf16lo(r.y);
-            acc.w += bf16hi(r.y);
-        }
-        *reinterpret_cast<uint2 *>(y + (size_t)t * d + 4 * c) = make_uint2(pack_bf2(acc.x, acc.y), pack_bf2(acc.z, acc.w));
+    const int q = d / 4;
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long)T * q) return;
+    const int t = (int)(i / q), c = (int)(i - (long)t * q);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < k; ++j) {
+        const float4 v = __ldcs(reinterpret_cast<const float4 *>(yp + ((size_t)t * k + j) * d) + c);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
     }
+    if (residual) {
+        const uint2 r = *reinterpret_cast<const uint2 *>(residual + (size_t)t * d + 4 * c);
+        acc.x += bf16lo(r.x);
+        acc.y += bf16hi(r.x);
+        acc.z += bf16lo(r.y);
+        acc.w += bf16hi(r.y);
+    }
+    *reinterpret_cast<uint2 *>(y + (size_t)t * d + 4 * c) = make_uint2(pack_bf2(acc.x, acc.y), pack_bf2(acc.z, acc.w));
 }
 
 }  // namespace moeb

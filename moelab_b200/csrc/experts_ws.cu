@@ -28,7 +28,8 @@ struct WSL {
     static constexpr int X_BYTES = COLS * X_ROW;
     // group sums: down 16 bytes per group; gate/up 4 bytes per group, copied from the 16-byte boundary at or
     // below the stage's first group (a bulk copy must start 16-byte aligned), so up to 3 extra leading floats
-    static constexpr int S_ROW = DOWN ? SG * 16 : (SG % 4 == 0 ? SG * 4 : ((SG + 3) * 4 + 15) / 16 * 16);
+    // (down rows get 16 bytes of padding: lanes 2c + hf then read float4s from distinct bank groups)
+    static constexpr int S_ROW = DOWN ? SG * 16 + 16 : (SG % 4 == 0 ? SG * 4 : ((SG + 3) * 4 + 15) / 16 * 16);
     static constexpr int S_BYTES = COLS * S_ROW;
     static constexpr int STAGE = W_BYTES + SB_BYTES + X_BYTES + S_BYTES;
     static_assert(STAGE % 128 == 0 && W_BYTES % 128 == 0 && SB_BYTES % 128 == 0 && (RBC * SG * 64) % 128 == 0,
@@ -238,7 +239,7 @@ __global__ void __launch_bounds__(32 * (RBC + 1), MB) k_experts_ws(const __grid_
 
 size_t experts_ws_smem(int nt8, int rbc, int sg, int ns, bool down) {
     const int np = down ? 1 : 2, cols = 8 * nt8;
-    const int s_row = down ? sg * 16 : (sg % 4 == 0 ? sg * 4 : ((sg + 3) * 4 + 15) / 16 * 16);
+    const int s_row = down ? sg * 16 + 16 : (sg % 4 == 0 ? sg * 4 : ((sg + 3) * 4 + 15) / 16 * 16);
     const size_t stage = (size_t)np * rbc * sg * (512 + 64) + (size_t)cols * (sg * 128 + 16) + (size_t)cols * s_row;
     return ns * stage + 2 * ns * 8;
 }
