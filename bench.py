@@ -535,7 +535,7 @@ def main():
         "kernels_us": {"router": round(statistics.mean(r_us), 3), "gate_up": round(statistics.mean(gu_us), 3),
                        "down": round(statistics.mean(dn_us), 3),
                        "note": "CUDA events between stages (serialised, eager)"},
-        "roofline": {"bound": "hbm", "kernel": "k_gate_up_slots" if T * K_TOP <= 16 else "k_gate_up_tiles_reg",
+        "roofline": {"bound": "hbm", "kernel": "k_gate_up_slots" if T * K_TOP <= 16 else "k_experts_ws (gate/up)",
                      "achieved": round(gu_ach, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(gu_ach / peaks["hbm_gbs"], 3), "traffic": traffic,
                      "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)" if peaks["source"] == "measured"
@@ -543,7 +543,7 @@ def main():
                      "algorithmic_bytes_per_launch": round(statistics.mean(gu_b)),
                      "down_achieved_gbs": round(dn_ach, 1)},
         "cpu_baseline": cpu, "e2e": e2e, "clocks": ck,
-        "gpu_launches": 3 * a.steps,
+        "gpu_launches": (3 if T * K_TOP <= 16 else 4) * a.steps,  # router, gate/up, down (+ combine in tile mode)
     }
     print(json.dumps(line), flush=True)
 
