@@ -301,91 +301,115 @@ def make_ep_layers(n_layers, rank, world, d=D, f=F, e=E):
     return layers
 
 
-def ep_steps(layers, xs, n, k=K_TOP, k0=0, timings=None):
+def ep_steps(layers, xs, n, xch, k=K_TOP, k0=0):
+    """n expert-parallel layer calls over the peer-memory exchange (layer and input i mod L)."""
     from moelab_b200 import ep
     y = None
     for i in range(n):
         st, gate = layers[(k0 + i) % len(layers)]
         x = xs[(k0 + i) % len(xs)]
-        y = ep.layer(st, x, gate, k, residual=x, timings=timings)
+        y = ep.layer_p2p(st, x, gate, k, xch, residual=x)
     return y
 
 
-def time_ep(layers, xs, n, ws, k=K_TOP):
+def ep_graph(layers, xs, n, xch, ws):
+    """CUDA graph of n expert-parallel layer calls (every rank captures and replays the same sequence)."""
     barrier(ws)
-    torch.cuda.synchronize()
-    a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a_.record()
-    ep_steps(layers, xs, n, k)
-    b_.record()
-    b_.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(gr, stream=s):
+            ep_steps(layers, xs, n, xch)
+    torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
     barrier(ws)
-    return max_over_ranks(ws, a_.elapsed_time(b_) / 1e3)
+    gr.replay()  # warm replay (every rank)
+    torch.cuda.synchronize()
+    return gr
 
 
-def ep_expert_roofline(layers, xs, n, d=D, f=F, k=K_TOP):
-    """Expert kernels on the received rows, timed with events inside ep.layer: algorithmic bytes (unique local
-    experts' weights + rows in + h out and back in + fp32 slot outputs) / time, and FLOPs / time."""
-    byts, flops, secs = 0.0, 0.0, 0.0
+def ep_layer_bytes(layers, xs, n, xch, ws, d=D, f=F, k=K_TOP):
+    """Algorithmic bytes one GPU moves per layer call: the weights of its experts that received rows, the rows
+    in, h out and back in, and the weighted rows out (measured on n eager calls)."""
+    from moelab_b200 import ep, ops
+    total = 0.0
     for i in range(n):
-        ev = [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
-        tm = {"events": ev}
-        ep_steps(layers, xs, 1, k, k0=i, timings=tm)
-        torch.cuda.synchronize()
-        R = tm["rows_received"]
-        rows = tm["recv_rows"]
-        U = int(torch.unique(rows[:, d:d + 2].contiguous().view(torch.int32)).numel()) if R else 0
-        byts += U * 3 * d * f * W_BITS / 8 + R * (d + 8) * 2 + 2 * R * f * 2 + R * d * 4
-        flops += 6.0 * d * f * R
-        secs += ev[0].elapsed_time(ev[1]) / 1e3
-    return byts / secs / 1e9, flops / secs / 1e12, byts / n, secs / n * 1e6
+        st, gate = layers[i % len(layers)]
+        x = xs[i % len(xs)]
+        idx, _ = ops.router(x, gate, k)
+        allidx = [torch.empty_like(idx) for _ in range(ws)]
+        import torch.distributed as dist
+        dist.all_gather(allidx, idx)
+        ids = torch.cat(allidx).reshape(-1)
+        El = E // ws
+        mine = ids[(ids // El) == xch.me]
+        U = int(torch.unique(mine).numel())
+        R = int(mine.numel())
+        total += U * 3 * d * f * W_BITS / 8 + R * (d + 8) * 2 + 2 * R * f * 2 + R * d * 4
+        ep.layer_p2p(st, x, gate, k, xch, residual=x)
+    return total / n
 
 
 def run_ep(a, ws, rank, local, peaks):
     from moelab_b200 import ep
     T = a.tokens
+    sweep_T = [int(s_) for s_ in a.sweep.split(",") if s_.strip()]
     layers = make_ep_layers(a.layers, rank, ws)
-    xs = make_inputs(T, a.layers, seed=5 + rank)
-    ep_steps(layers, xs, max(a.warmup, 3))
-    torch.cuda.synchronize()
-    clocks = ClockSampler(local)
-    clocks.start()
-    t_soak = time.perf_counter()
-    while time.perf_counter() - t_soak < a.soak_seconds:
-        ep_steps(layers, xs, len(layers))
+    xch = ep.PeerExchange.create(max([T] + sweep_T) * K_TOP, D)
+    try:
+        xs = make_inputs(T, a.layers, seed=5 + rank)
+        ep_steps(layers, xs, max(a.warmup, 3), xch)  # eager warm-up (also sizes the workspaces)
         torch.cuda.synchronize()
-    t = time_ep(layers, xs, a.steps, ws)
-    ck = clocks.stop()
-    value = ws * T * a.steps / t
-    ach, tfs, b_per, us_exp = ep_expert_roofline(layers, xs, min(2 * a.layers, a.steps))
-    sweep = []
-    for Ts in [int(s_) for s_ in a.sweep.split(",") if s_.strip()]:
-        xs_s = make_inputs(Ts, a.layers, seed=77 + Ts + rank)
-        ep_steps(layers, xs_s, 3)
-        n_s = 2 * a.layers
-        ts = time_ep(layers, xs_s, n_s, ws)
-        sweep.append({"T": Ts, "us_per_call": round(ts / n_s * 1e6, 3),
-                      "tokens_per_s": round(ws * Ts * n_s / ts, 1)})
-    # end to end through the public API with host buffers
-    xh = torch.randn(T, D, generator=torch.Generator().manual_seed(9 + rank)).to(torch.bfloat16).pin_memory()
-    yh = torch.empty_like(xh).pin_memory()
-    for i in range(4):
-        xd = xh.to("cuda", non_blocking=True)
-        st, gate = layers[i % len(layers)]
-        yh.copy_(ep.layer(st, xd, gate, K_TOP, residual=xd), non_blocking=True)
-    torch.cuda.synchronize()
-    barrier(ws)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(a.e2e_steps):
-        xd = xh.to("cuda", non_blocking=True)
-        st, gate = layers[i % len(layers)]
-        yh.copy_(ep.layer(st, xd, gate, K_TOP, residual=xd), non_blocking=True)
-    e1.record()
-    e1.synchronize()
-    torch.cuda.synchronize()
-    te = max_over_ranks(ws, e0.elapsed_time(e1) / 1e3)
+        gr = ep_graph(layers, xs, a.steps, xch, ws)
+        clocks = ClockSampler(local)
+        clocks.start()
+        t_soak = time.perf_counter()
+        while time.perf_counter() - t_soak < a.soak_seconds:
+            barrier(ws)
+            gr.replay()
+            torch.cuda.synchronize()
+        t = max_over_ranks(ws, time_graph(gr, ws))
+        ck = clocks.stop()
+        value = ws * T * a.steps / t
+        lay_b = ep_layer_bytes(layers, xs, len(layers), xch, ws)
+        lay_ach = lay_b / (t / a.steps) / 1e9
+        del gr
+        sweep = []
+        for Ts in sweep_T:
+            xs_s = make_inputs(Ts, a.layers, seed=77 + Ts + rank)
+            ep_steps(layers, xs_s, 3, xch)
+            n_s = 2 * a.layers
+            gs = ep_graph(layers, xs_s, n_s, xch, ws)
+            ts = max_over_ranks(ws, time_graph(gs, ws))
+            del gs
+            sweep.append({"T": Ts, "us_per_call": round(ts / n_s * 1e6, 3), "tokens_per_s": round(ws * Ts * n_s / ts, 1)})
+        # end to end through the public API with host buffers (eager)
+        xh = torch.randn(T, D, generator=torch.Generator().manual_seed(9 + rank)).to(torch.bfloat16).pin_memory()
+        yh = torch.empty_like(xh).pin_memory()
+        for i in range(4):
+            xd = xh.to("cuda", non_blocking=True)
+            st, gate = layers[i % len(layers)]
+            yh.copy_(ep.layer_p2p(st, xd, gate, K_TOP, xch, residual=xd), non_blocking=True)
+        torch.cuda.synchronize()
+        barrier(ws)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(a.e2e_steps):
+            xd = xh.to("cuda", non_blocking=True)
+            st, gate = layers[i % len(layers)]
+            yh.copy_(ep.layer_p2p(st, xd, gate, K_TOP, xch, residual=xd), non_blocking=True)
+        e1.record()
+        e1.synchronize()
+        torch.cuda.synchronize()
+        te = max_over_ranks(ws, e0.elapsed_time(e1) / 1e3)
+        errs = xch.read_error()
+        torch.cuda.synchronize()
+        barrier(ws)
+    finally:
+        torch.cuda.synchronize()
+        barrier(ws)
+        xch.close()
     if rank != 0:
         return
     line = {
@@ -397,22 +421,26 @@ def run_ep(a, ws, rank, local, peaks):
                    "E": E, "k": K_TOP, "layers": a.layers, "experts_per_gpu": E // ws,
                    "weights_gb_per_gpu": round(a.layers * 3 * (E // ws) * D * F * W_BITS / 8 / 1e9, 2),
                    "l2": "inputs larger than L2: 16 independent layers cycled",
-                   "parallelism": f"ep{ws}", "exchange": "NCCL all-to-all-v (counts, rows, slot outputs)",
-                   "graph": "eager (the count exchange is read on the host every layer)"},
+                   "parallelism": f"ep{ws}",
+                   "exchange": "NVLink peer memory (CUDA IPC buffers): dispatch and return stored by the kernels, "
+                               "epoch flags, no host synchronisation",
+                   "graph": "one CUDA graph of K steps per rank"},
         "us_per_call": round(t / a.steps * 1e6, 3),
+        "layer_gbs_per_gpu": round(lay_ach, 1), "layer_frac_of_hbm_peak": round(lay_ach / peaks["hbm_gbs"], 3),
         "sweep": sweep,
-        "roofline": {"bound": "hbm", "kernel": "expert kernels on received rows (prep + gate_up + down)",
-                     "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(ach / peaks["hbm_gbs"], 3), "traffic": None,
+        "roofline": {"bound": "hbm", "kernel": "whole expert-parallel layer per GPU (router, dispatch, experts, "
+                                               "return, combine)",
+                     "achieved": round(lay_ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(lay_ach / peaks["hbm_gbs"], 3), "traffic": None,
                      "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)",
-                     "algorithmic_bytes_per_launch": round(b_per), "us_per_launch": round(us_exp, 2),
-                     "tflops": round(tfs, 2)},
+                     "algorithmic_bytes_per_launch": round(lay_b)},
         "cpu_baseline": None,
         "e2e": {"value": round(ws * T * a.e2e_steps / te, 1), "unit": "tokens/s", "h2d_bytes_per_step": T * D * 2,
                 "d2h_bytes_per_step": T * D * 2, "us_per_call": round(te / a.e2e_steps * 1e6, 3),
-                "note": "public API ep.layer(); pinned host x in and y out every step"},
+                "note": "public API ep.layer_p2p(); pinned host x in and y out every step, eager"},
+        "device_errors": errs,
         "clocks": ck,
-        "gpu_launches": 7 * a.steps,
+        "gpu_launches": 8 * a.steps,  # router, plan, send, prep, gate/up, down, signal, combine
     }
     print(json.dumps(line), flush=True)
 

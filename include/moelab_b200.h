@@ -160,6 +160,40 @@ int moeb_ep_experts_mxfp4(const void *rows, int R, int d, int f, int E_local, co
 int moeb_ep_combine(const float *back, const int *slot_pos, int T, int d, int k, const void *residual, void *y,
                     cudaStream_t stream);
 
+/* --- expert parallelism over NVLink peer memory (no host synchronisation, CUDA-graph capturable).
+ * Every rank owns one exchange buffer of moeb_ep_p2p_bytes(P, C, d) bytes (C = rows per (source, owner) block,
+ * at least the largest T*k of a call), allocated with moeb_ep_ipc_alloc and mapped into every other rank with
+ * moeb_ep_ipc_handle / moeb_ep_ipc_open (CUDA IPC, plain peer mappings, no multicast). `peers` is a DEVICE array
+ * of the P buffer addresses as seen by this rank (its own included), `self` its own buffer. Per layer call,
+ * every rank issues, in this order on one stream:
+ *   1. moeb_ep_p2p_dispatch: plan as moeb_ep_dispatch, then each slot's row + tail is stored straight into its
+ *      owner's buffer (block `me`, row slot_pos % C); the owner's flag for this source is released with the
+ *      call's epoch (a per-buffer counter every rank advances once per call). slot_pos [T*k] is in capacity
+ *      layout (owner * C + row).
+ *   2. moeb_ep_p2p_experts_q4: waits (bounded, ~2 s, then MOEB_DEVERR_TIMEOUT) for each source's flag, runs the
+ *      grouped kernels on the valid rows (tile mode; padding rows are skipped) and stores each weighted fp32 row
+ *      straight into its owner's return block, then releases the owners' return flags.
+ *      Workspace: moeb_ep_workspace_bytes(P * C, d, f, E_local).
+ *   3. moeb_ep_p2p_combine: waits for the return flags of all P ranks, then y as moeb_ep_combine.
+ * The buffers are reused every call without extra synchronisation: a rank sends call n + 1 only after its
+ * combine of call n saw every rank's return flag, i.e. after every rank finished reading call n's rows. */
+size_t moeb_ep_p2p_bytes(int P, int C, int d);
+int moeb_ep_ipc_alloc(size_t bytes, void **ptr);
+int moeb_ep_ipc_free(void *ptr);
+int moeb_ep_ipc_handle(void *ptr, void *handle /* 64 bytes */);
+int moeb_ep_ipc_open(const void *handle, void **ptr);
+int moeb_ep_ipc_close(void *ptr);
+int moeb_ep_p2p_dispatch(const void *x, const int *idx, const float *wts, int T, int d, int k, int E, int P, int me,
+                         int C, void *const *peers, void *self, int *send_counts, int *slot_pos, cudaStream_t stream);
+int moeb_ep_p2p_experts_q4(void *const *peers, void *self, int P, int me, int C, int d, int f, int E_local,
+                           const void *qg, const void *sbg, const void *qu, const void *sbu, const void *qd,
+                           const void *sbd, const float *bg, const float *bu, const float *bd, int act, int policy,
+                           void *ws, size_t ws_bytes, cudaStream_t stream);
+int moeb_ep_p2p_combine(void *self, const int *slot_pos, int P, int C, int T, int d, int k, const void *residual,
+                        void *y, cudaStream_t stream);
+/* Sticky error bits of the exchange buffer (a wait that gave up); synchronises the stream, clears them. */
+int moeb_ep_p2p_read_error(void *self, int P, int C, int d, unsigned *out, cudaStream_t stream);
+
 /* --- moeb_experts_q4 for callers that cannot allocate device memory. No counterpart in the reference (moe-lab
  * always lets the variant allocate its scratch). The scratch lives in a static 16 MiB device array inside the
  * library (held by every GPU that loads it until exit), so the caller passes only inputs and the output. T is

@@ -482,15 +482,26 @@ int moeb_router(const void *x, const void *wg, const void *bias, int T, int d, i
 }
 
 // ------------------------------------------------------------------ experts (ids given) and full layer
+struct P2PParams {
+    const unsigned *rflag;
+    const int *rcnt;
+    const unsigned *epoch;
+    int C, me;
+    unsigned char *const *peers;
+    size_t yoff;
+};
+
 static int experts_common(int fmt, const void *x, const void *qg, const void *sbg, const void *qu, const void *sbu,
                           const void *qd, const void *sbd, const float *bg, const float *bu, const float *bd,
                           const int *idx, const float *wts, int T, int d, int f, int E, int k, int act, int policy,
                           const void *residual, void *y, void *ws, size_t ws_bytes, cudaStream_t st,
                           const void *gate_w, const void *gate_b, int norm, float rscale, int *idx_out,
-                          float *wts_out, void *const *ev, float *yp_out = nullptr, int ns = 0) {
-    // yp_out != null: expert-parallel rows (k = 1, each x row of d + 8 values ends in its {expert, weight}
-    // tail); down writes the weighted fp32 slot outputs to yp_out and nothing is combined here.
-    const bool ep = yp_out != nullptr;
+                          float *wts_out, void *const *ev, float *yp_out = nullptr, int ns = 0,
+                          const P2PParams *pp = nullptr) {
+    // yp_out != null or pp != null: expert-parallel rows (k = 1, each x row of d + 8 values ends in its
+    // {expert, weight} tail); down writes the weighted fp32 slot outputs to yp_out (or straight into the owners'
+    // return blocks, pp) and nothing is combined here.
+    const bool ep = yp_out != nullptr || pp != nullptr;
     int rc = check_shape(T, d, f, E, k);
     if (rc) return rc;
     if (act < 0 || act > 2) return fail(MOEB_EINVAL, "act must be 0, 1 or 2%s");
@@ -522,6 +533,12 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
             idx = p.idx = p.idx_w = at<int>(ws, L.idx);
             wts = p.wts_w = at<float>(ws, L.wts);
         }
+        if (pp) {
+            p.rflag = pp->rflag;
+            p.rcnt = pp->rcnt;
+            p.epoch = pp->epoch;
+            p.C = pp->C;
+        }
         p.xsum = at<float>(ws, L.xsum);
         p.cnt_all = at<unsigned>(ws, L.cnt_all);
         p.NT = nt_of(policy);
@@ -549,8 +566,14 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
     a.sorted = at<int>(ws, L.sorted);
     a.h = at<uint16_t>(ws, L.h);
     a.hsum = at<float>(ws, L.hsum);
-    a.yp = ep ? yp_out : at<float>(ws, L.yp);
+    a.yp = yp_out ? yp_out : at<float>(ws, L.yp);
     a.slot_out = ep ? 1 : 0;
+    if (pp) {
+        a.ypeers = pp->peers;
+        a.yoff = pp->yoff;
+        a.C = pp->C;
+        a.me = pp->me;
+    }
     a.ycnt = at<unsigned>(ws, L.ycnt);
     a.residual = static_cast<const uint16_t *>(residual);
     a.y = static_cast<uint16_t *>(y);
@@ -673,6 +696,114 @@ int moeb_ep_experts_mxfp4(const void *rows, int R, int d, int f, int E_local, co
     return experts_common(FMT_FP4, rows, qg, scg, qu, scu, qd, scd, bg, bu, bd, nullptr, nullptr, R, d, f, E_local,
                           1, act, policy, nullptr, nullptr, ws, ws_bytes, st, nullptr, nullptr, 0, 1.f, nullptr,
                           nullptr, nullptr, yp);
+}
+
+// ---- peer-memory exchange (CUDA IPC mappings of plain device allocations; no multicast objects)
+size_t moeb_ep_p2p_bytes(int P, int C, int d) { return p2p_layout(P, C, d).total; }
+
+int moeb_ep_ipc_alloc(size_t bytes, void **ptr) {
+    if (!ptr || bytes == 0) return fail(MOEB_EINVAL, "bad allocation request%s");
+    if (cudaMalloc(ptr, bytes) != cudaSuccess) return check_launch("ipc_alloc");
+    if (cudaMemset(*ptr, 0, bytes) != cudaSuccess) return check_launch("ipc_alloc memset");
+    if (cudaDeviceSynchronize() != cudaSuccess) return check_launch("ipc_alloc sync");
+    return MOEB_OK;
+}
+int moeb_ep_ipc_free(void *ptr) {
+    if (ptr && cudaFree(ptr) != cudaSuccess) return check_launch("ipc_free");
+    return MOEB_OK;
+}
+int moeb_ep_ipc_handle(void *ptr, void *handle) {
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, ptr) != cudaSuccess) return check_launch("ipc_handle");
+    memcpy(handle, &h, sizeof h);
+    return MOEB_OK;
+}
+int moeb_ep_ipc_open(const void *handle, void **ptr) {
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof h);
+    if (cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return check_launch("ipc_open");
+    return MOEB_OK;
+}
+int moeb_ep_ipc_close(void *ptr) {
+    if (ptr && cudaIpcCloseMemHandle(ptr) != cudaSuccess) return check_launch("ipc_close");
+    return MOEB_OK;
+}
+
+int moeb_ep_p2p_dispatch(const void *x, const int *idx, const float *wts, int T, int d, int k, int E, int P, int me,
+                         int C, void *const *peers, void *self, int *send_counts, int *slot_pos, cudaStream_t st) {
+    if (int rc = check_ep(T, d, k, E, P)) return rc;
+    if (me < 0 || me >= P || !peers || !self) return fail(MOEB_EINVAL, "bad rank or exchange buffers%s");
+    if ((long)T * k > C) return fail(MOEB_EINVAL, "T*k exceeds the exchange capacity C%s");
+    EPArgs a = {};
+    a.x = static_cast<const uint16_t *>(x);
+    a.idx = idx;
+    a.wts = wts;
+    a.T = T; a.d = d; a.k = k; a.E = E; a.P = P;
+    a.send_counts = send_counts;
+    a.slot_pos = slot_pos;
+    a.err = reinterpret_cast<unsigned *>(static_cast<unsigned char *>(self) + p2p_layout(P, C, d).err);
+    a.C = C;
+    a.me = me;
+    a.peers = reinterpret_cast<unsigned char *const *>(peers);
+    a.self = static_cast<unsigned char *>(self);
+    if (launch(k_ep_plan, dim3(1), dim3(1024), 0, st, a) != cudaSuccess) return check_launch("ep_plan");
+    // the sending kernel runs even for T = 0: it still publishes the (zero) counts and the epoch flags
+    if (launch(k_ep_send, dim3((unsigned)std::max<long>(1, ((long)T * k + 7) / 8)), dim3(256), 0, st, a) != cudaSuccess)
+        return check_launch("ep_send");
+    return MOEB_OK;
+}
+
+static int p2p_experts(int fmt, void *const *peers, void *self, int P, int me, int C, int d, int f, int E_local,
+                       const void *qg, const void *sg, const void *qu, const void *su, const void *qd, const void *sd,
+                       const float *bg, const float *bu, const float *bd, int act, int policy, void *ws,
+                       size_t ws_bytes, cudaStream_t st) {
+    if (P < 1 || P > 32 || me < 0 || me >= P || C < 1 || !peers || !self)
+        return fail(MOEB_EINVAL, "bad exchange parameters%s");
+    const P2PLayout L = p2p_layout(P, C, d);
+    unsigned char *b = static_cast<unsigned char *>(self);
+    P2PParams pp;
+    pp.rflag = reinterpret_cast<const unsigned *>(b + L.rflag);
+    pp.rcnt = reinterpret_cast<const int *>(b + L.rcnt);
+    pp.epoch = reinterpret_cast<const unsigned *>(b + L.epoch);
+    pp.C = C;
+    pp.me = me;
+    pp.peers = reinterpret_cast<unsigned char *const *>(peers);
+    pp.yoff = L.back;
+    // the warp-specialized kernels (tile mode) are the ones that skip padding rows and fence their peer stores
+    if (policy != MOEB_POLICY_TILES16_RING) policy = MOEB_POLICY_TILES8_RING;
+    int rc = experts_common(fmt, b + L.rows, qg, sg, qu, su, qd, sd, bg, bu, bd, nullptr, nullptr, P * C, d, f,
+                            E_local, 1, act, policy, nullptr, nullptr, ws, ws_bytes, st, nullptr, nullptr, 0, 1.f,
+                            nullptr, nullptr, nullptr, nullptr, 0, &pp);
+    if (rc) return rc;
+    if (launch(k_ep_signal, dim3(1), dim3(32), 0, st, reinterpret_cast<unsigned char *const *>(peers), b, P, C, d, me) !=
+        cudaSuccess)
+        return check_launch("ep_signal");
+    return MOEB_OK;
+}
+
+int moeb_ep_p2p_experts_q4(void *const *peers, void *self, int P, int me, int C, int d, int f, int E_local,
+                           const void *qg, const void *sbg, const void *qu, const void *sbu, const void *qd,
+                           const void *sbd, const float *bg, const float *bu, const float *bd, int act, int policy,
+                           void *ws, size_t ws_bytes, cudaStream_t st) {
+    return p2p_experts(FMT_Q4, peers, self, P, me, C, d, f, E_local, qg, sbg, qu, sbu, qd, sbd, bg, bu, bd, act,
+                       policy, ws, ws_bytes, st);
+}
+
+int moeb_ep_p2p_combine(void *self, const int *slot_pos, int P, int C, int T, int d, int k, const void *residual,
+                        void *y, cudaStream_t st) {
+    if (T < 0 || d <= 0 || d % 64 || k <= 0 || k > 32 || P < 1 || P > 32) return fail(MOEB_EINVAL, "bad shape%s");
+    if (T == 0) return MOEB_OK;
+    unsigned char *b = static_cast<unsigned char *>(self);
+    if (launch(k_ep_combine_p2p, dim3((unsigned)(((long)T * (d / 4) + 127) / 128)), dim3(128), 0, st,
+               (const unsigned char *)b, slot_pos, P, C, T, d, k, static_cast<const uint16_t *>(residual),
+               static_cast<uint16_t *>(y), reinterpret_cast<unsigned *>(b + p2p_layout(P, C, d).err)) != cudaSuccess)
+        return check_launch("ep_combine_p2p");
+    return MOEB_OK;
+}
+
+int moeb_ep_p2p_read_error(void *self, int P, int C, int d, unsigned *out, cudaStream_t st) {
+    unsigned char *b = static_cast<unsigned char *>(self) + p2p_layout(P, C, d).err;
+    return moeb_read_error(b, out, st);
 }
 
 int moeb_ep_combine(const float *back, const int *slot_pos, int T, int d, int k, const void *residual, void *y,

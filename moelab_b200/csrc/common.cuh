@@ -151,6 +151,38 @@ MOEB_DEV void tmap_prefetch(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// ---- cross-GPU signalling (expert-parallel exchange over peer memory)
+// Slot id meaning "no work here" (padding of a capacity block): skipped by the tile builder, not an error.
+constexpr int SLOT_SKIP = -2147483647 - 1;
+
+MOEB_DEV uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+MOEB_DEV unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+MOEB_DEV void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded wait until *flag == want (acquire, system scope). Gives up after ~2 s of wall time (a peer that never
+// signals), records ERR_TIMEOUT and returns false; the caller then carries on with whatever data is there.
+MOEB_DEV bool wait_flag_sys(const unsigned *flag, unsigned want, unsigned *err) {
+    if (ld_acquire_sys(flag) == want) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_sys(flag) != want) {
+        if (globaltimer_ns() - t0 > 2000000000ull) {
+            atomicOr(err, ERR_TIMEOUT);
+            return false;
+        }
+        __nanosleep(128);
+    }
+    return true;
+}
+
 MOEB_DEV float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

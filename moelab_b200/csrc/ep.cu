@@ -28,6 +28,10 @@ __global__ void __launch_bounds__(PLAN_THREADS) k_ep_plan(EPArgs a) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int TK = a.T * a.k, P = a.P, El = a.E / a.P;
     if (tid < P) base[tid] = 0;
+    if (a.C > 0 && tid == 0) {  // peer-memory exchange: a new layer call (every rank counts the same calls)
+        unsigned *ep = reinterpret_cast<unsigned *>(a.self + p2p_layout(P, a.C, a.d).epoch);
+        *ep = *ep + 1u;
+    }
     for (int c0 = 0; c0 < TK; c0 += PLAN_THREADS) {
         if (lane < P) wcnt[warp][lane] = 0;
         __syncthreads();  // zeroed counts (and, first time, base) visible
@@ -58,10 +62,10 @@ __global__ void __launch_bounds__(PLAN_THREADS) k_ep_plan(EPArgs a) {
     __syncthreads();
     // base[] now holds the totals: exclusive scan over the owners, then shift every slot by its owner's offset
     __shared__ int off[PLAN_MAXP];
-    if (tid == 0) {
+    if (tid == 0) {  // packed send buffer: owner blocks back to back; peer exchange: fixed blocks of C rows
         int run = 0;
         for (int p = 0; p < P; ++p) {
-            off[p] = run;
+            off[p] = a.C > 0 ? p * a.C : run;
             run += base[p];
         }
     }
@@ -90,6 +94,104 @@ __global__ void __launch_bounds__(256) k_ep_pack(EPArgs a) {
         const int e = a.idx[s];
         dst[d / 8] = make_uint4((unsigned)(e % El), __float_as_uint(a.wts[s]), 0u, 0u);
     }
+}
+
+// Peer-memory dispatch: grid ceil(T*k / 8), block 256, warp per slot. The slot's row goes straight into the
+// owner's exchange buffer (source block `me`, row slot_pos % C); the last CTA to finish then publishes, per
+// owner, the row count and the epoch flag (system-scope release after a system-scope fence).
+__global__ void __launch_bounds__(256) k_ep_send(EPArgs a) {
+    pdl_launch();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int s = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int d = a.d, El = a.E / a.P, C = a.C;
+    const P2PLayout L = p2p_layout(a.P, C, d);
+    if (s < a.T * a.k) {
+        const int pos = a.slot_pos[s];
+        if (pos >= 0) {
+            const int dst = pos / C, row = pos - dst * C;
+            const uint4 *src = reinterpret_cast<const uint4 *>(a.x + (size_t)(s / a.k) * d);
+            uint4 *out = reinterpret_cast<uint4 *>(a.peers[dst] + L.rows + ((size_t)a.me * C + row) * (d + 8) * 2);
+            for (int i = lane; i < d / 8; i += 32) out[i] = src[i];
+            if (lane == 0) out[d / 8] = make_uint4((unsigned)(a.idx[s] % El), __float_as_uint(a.wts[s]), 0u, 0u);
+        }
+    }
+    __shared__ int s_last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();  // this CTA's row stores (ordered by the barrier) before the counter
+        unsigned *ctr = reinterpret_cast<unsigned *>(a.self + L.ctr);
+        s_last = atomicAdd(ctr, 1u) == gridDim.x - 1;
+        if (s_last) {
+            *ctr = 0u;
+            __threadfence_system();
+        }
+    }
+    __syncthreads();
+    if (!s_last) return;
+    const unsigned ep = *reinterpret_cast<const unsigned *>(a.self + L.epoch);
+    for (int dst = threadIdx.x; dst < a.P; dst += blockDim.x) {
+        reinterpret_cast<int *>(a.peers[dst] + L.rcnt)[a.me] = a.send_counts[dst];
+        __threadfence_system();
+        st_release_sys(reinterpret_cast<unsigned *>(a.peers[dst] + L.rflag) + a.me, ep);
+    }
+}
+
+// Peer-memory return: one warp after the expert kernels wrote their rows into the owners' return blocks (each
+// writing warp fenced at system scope): tell every owner that this rank's block is complete.
+__global__ void k_ep_signal(unsigned char *const *peers, unsigned char *self, int P, int C, int d, int me) {
+    pdl_launch();
+    pdl_wait();
+    const P2PLayout L = p2p_layout(P, C, d);
+    const unsigned ep = *reinterpret_cast<const unsigned *>(self + L.epoch);
+    __threadfence_system();
+    for (int dst = threadIdx.x; dst < P; dst += blockDim.x)
+        st_release_sys(reinterpret_cast<unsigned *>(peers[dst] + L.bflag) + me, ep);
+}
+
+// Peer-memory combine: grid ceil(T * d / 4 / 128), block 128. Waits until every expert rank holding one of the
+// token's slots has signalled, then y[t] = sum_j back[slot_pos[t*k + j]] (fixed j order) + residual.
+__global__ void __launch_bounds__(128) k_ep_combine_p2p(const unsigned char *self, const int *__restrict__ slot_pos,
+                                                        int P, int C, int T, int d, int k,
+                                                        const uint16_t *__restrict__ residual,
+                                                        uint16_t *__restrict__ y, unsigned *err) {
+    pdl_launch();
+    pdl_wait();
+    const P2PLayout L = p2p_layout(P, C, d);
+    const unsigned ep = *reinterpret_cast<const unsigned *>(self + L.epoch);
+    const unsigned *bflag = reinterpret_cast<const unsigned *>(self + L.bflag);
+    __shared__ int ok;
+    if (threadIdx.x < 32) {  // one warp waits for all P expert ranks (P <= 32)
+        const bool done = threadIdx.x >= P || wait_flag_sys(bflag + threadIdx.x, ep, err);
+        (void)done;
+        __syncwarp();
+        if (threadIdx.x == 0) ok = 1;
+    }
+    __syncthreads();
+    (void)ok;
+    const float *back = reinterpret_cast<const float *>(self + L.back);
+    const int q = d / 4;
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long)T * q) return;
+    const int t = (int)(i / q), c = (int)(i - (long)t * q);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < k; ++j) {
+        const int pos = slot_pos[(size_t)t * k + j];
+        if (pos < 0) continue;
+        const float4 v = __ldcs(reinterpret_cast<const float4 *>(back + (size_t)pos * d) + c);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+    }
+    if (residual) {
+        const uint2 r = *reinterpret_cast<const uint2 *>(residual + (size_t)t * d + 4 * c);
+        acc.x += bf16lo(r.x);
+        acc.y += bf16hi(r.x);
+        acc.z += bf16lo(r.y);
+        acc.w += bf16hi(r.y);
+    }
+    *reinterpret_cast<uint2 *>(y + (size_t)t * d + 4 * c) = make_uint2(pack_bf2(acc.x, acc.y), pack_bf2(acc.z, acc.w));
 }
 
 // grid T, block 256: one CTA per token, 4 columns per thread per step

@@ -215,11 +215,14 @@ __device__ __forceinline__ void down_store_combine(const ExpArgs &a, const TileI
                     v0 += a.bd[(size_t)ti.e * d + r0];
                     v1 += a.bd[(size_t)ti.e * d + r1];
                 }
-                a.yp[(size_t)slot * d + r0] = wsl * v0;
-                a.yp[(size_t)slot * d + r1] = wsl * v1;
+                float *yrow = a.ypeers ? reinterpret_cast<float *>(a.ypeers[slot / a.C] + a.yoff) +
+                                             ((size_t)a.me * a.C + slot % a.C) * d
+                                       : a.yp + (size_t)slot * d;
+                yrow[r0] = wsl * v0;
+                yrow[r1] = wsl * v1;
             }
         }
-    if (a.slot_out) return;  // expert-parallel: the token's owner combines
+    if (a.slot_out) return;  // expert-parallel or separate combine pass: the rows are combined later
     __syncwarp();
     if (lane == 0) __threadfence();  // cumulative over the warp's writes ordered by the __syncwarp
     __syncwarp();

@@ -235,6 +235,10 @@ __global__ void __launch_bounds__(32 * (RBC + 1), MB) k_experts_ws(const __grid_
             }
         }
     }
+    if (DOWN && a.ypeers) {  // rows stored into peers' memory: make them visible system-wide before exiting
+        __syncwarp();
+        if (lane == 0) __threadfence_system();
+    }
 }
 
 size_t experts_ws_smem(int nt8, int rbc, int sg, int ns, bool down) {

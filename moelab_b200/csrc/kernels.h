@@ -37,6 +37,12 @@ struct PrepArgs {
     // expert-parallel rows (k == 1): each row's tail {local expert, weight bits} is unpacked into these
     int *idx_w;
     float *wts_w;
+    // peer-memory exchange: rows arrive in capacity blocks of C rows per source; rflag[src] == *epoch once
+    // source src has written its rcnt[src] rows (null: rows are all valid)
+    const unsigned *rflag;
+    const int *rcnt;
+    const unsigned *epoch;
+    int C;
     float *xsum;
     unsigned *cnt_all;
     int NT;
@@ -74,12 +80,38 @@ struct ExpArgs {
     int dn_prefetch;  // gate/up pulls the down weights of its expert into L2
     int fmt;          // FMT_Q4 or FMT_FP4
     int slot_out;     // 1: down stops after writing the weighted per-slot outputs yp (caller's buffer), no combine
+    // peer-memory exchange: slot s's weighted row goes to (float *)(ypeers[s / C] + yoff) + (me * C + s % C) * d,
+    // this rank's return block in the owner's buffer, instead of yp; the writing warps fence at system scope
+    unsigned char *const *ypeers;
+    size_t yoff;
+    int C, me;
     // warp-specialized kernels: 2-D tensor maps over each projection's codes (uint64 elements) and scale|bias
     // words (uint32), viewed as [row blocks of all experts][K/64 groups x 512 B | 64 B] ([0] gate, [1] up,
     // [2] down); a box is RBC row blocks x SG groups (RBC rows of SG*512 | SG*64 contiguous bytes), so one
     // copy per array and projection fills a pipeline stage
     CUtensorMap tmq[3], tmsb[3];
 };
+
+// Per-rank buffer of the peer-memory exchange (one allocation, mapped by every rank of the group):
+//   epoch counter and a grid counter, rflag[P] / rcnt[P] (written by the sources), bflag[P] (written by the
+//   expert ranks), rows [P][C][d + 8] bf16 (source blocks), back [P][C][d] fp32 (return blocks).
+struct P2PLayout {
+    size_t epoch, err, ctr, rflag, rcnt, bflag, rows, back, total;
+};
+__host__ __device__ inline P2PLayout p2p_layout(int P, int C, int d) {
+    P2PLayout L;
+    auto up = [](size_t v) { return (v + 255) & ~(size_t)255; };
+    L.epoch = 0;
+    L.err = 64;
+    L.ctr = 128;
+    L.rflag = 256;
+    L.rcnt = L.rflag + up(4 * (size_t)P);
+    L.bflag = L.rcnt + up(4 * (size_t)P);
+    L.rows = L.bflag + up(4 * (size_t)P);
+    L.back = L.rows + up((size_t)P * C * (d + 8) * 2);
+    L.total = L.back + up((size_t)P * C * d * 4);
+    return L;
+}
 
 // Expert-parallel dispatch plan / pack / combine (csrc/ep.cu).
 struct EPArgs {
@@ -91,10 +123,19 @@ struct EPArgs {
     int *slot_pos;        // [T*k] row of each slot in the send buffer, -1 = dropped (invalid id)
     uint16_t *rows;       // [T*k][d + 8] send rows: x of the slot's token, then {local expert, weight, 0, 0}
     unsigned *err;
+    // peer-memory exchange (C > 0): slot_pos in capacity layout (dst * C + rank inside dst), rows written into
+    // peers[dst]'s source block `me`; self = this rank's exchange buffer (epoch, counters)
+    int C, me;
+    unsigned char *const *peers;
+    unsigned char *self;
 };
 __global__ void k_ep_plan(EPArgs a);
 __global__ void k_ep_pack(EPArgs a);
 __global__ void k_combine(const float *yp, int T, int d, int k, const uint16_t *residual, uint16_t *y);
+__global__ void k_ep_send(EPArgs a);
+__global__ void k_ep_signal(unsigned char *const *peers, unsigned char *self, int P, int C, int d, int me);
+__global__ void k_ep_combine_p2p(const unsigned char *self, const int *slot_pos, int P, int C, int T, int d, int k,
+                                 const uint16_t *residual, uint16_t *y, unsigned *err);
 __global__ void k_ep_combine(const float *back, const int *slot_pos, int T, int d, int k, const uint16_t *residual,
                              uint16_t *y);
 

@@ -62,6 +62,7 @@ __device__ void build_tiles(const int *__restrict__ idx, int TK, int E, int NT, 
     bool bad = false;
     for (int s = tid; s < TK; s += nth) {
         int e = __ldcg(idx + s);
+        if (e == SLOT_SKIP) continue;  // capacity padding: no work, not an error
         if (e < 0 || e >= E) { bad = true; e = 0; }
         atomicAdd(&cnt[e], 1);
     }
@@ -92,6 +93,7 @@ __device__ void build_tiles(const int *__restrict__ idx, int TK, int E, int NT, 
     __syncthreads();
     for (int s = tid; s < TK; s += nth) {
         int e = __ldcg(idx + s);
+        if (e == SLOT_SKIP) continue;
         if (e < 0 || e >= E) e = 0;
         const int pos = atomicAdd(&cnt[e], 1);
         sorted[off[e] + pos] = s;
@@ -285,12 +287,24 @@ __global__ void __launch_bounds__(256) k_prep(PrepArgs a) {
     const int t = blockIdx.x * 8 + warp;
     if (t < a.T) {
         const uint16_t *xr = a.x + (size_t)t * a.xs;
-        row_group_sums(xr, a.d, a.xsum + (size_t)t * xsum_stride(a.d), lane);
+        bool valid = true;
+        if (a.rflag) {  // peer-memory exchange: row t is slot t % C of source t / C; wait for that source
+            const int src = t / a.C;
+            if (lane == 0) wait_flag_sys(a.rflag + src, *a.epoch, a.err);
+            __syncwarp();
+            valid = (t % a.C) < *reinterpret_cast<const volatile int *>(a.rcnt + src);
+        }
+        if (valid) row_group_sums(xr, a.d, a.xsum + (size_t)t * xsum_stride(a.d), lane);
         if (a.idx_w && lane == 0) {  // expert-parallel row (k = 1): unpack and validate its tail
-            const int2 m = *reinterpret_cast<const int2 *>(xr + a.d);
-            if (m.x < 0 || m.x >= a.E) atomicOr(a.err, ERR_EXPERT_ID);
-            a.idx_w[t] = m.x;
-            a.wts_w[t] = __int_as_float(m.y);
+            if (valid) {
+                const int2 m = *reinterpret_cast<const int2 *>(xr + a.d);
+                if (m.x < 0 || m.x >= a.E) atomicOr(a.err, ERR_EXPERT_ID);
+                a.idx_w[t] = m.x;
+                a.wts_w[t] = __int_as_float(m.y);
+            } else {
+                a.idx_w[t] = SLOT_SKIP;
+                a.wts_w[t] = 0.f;
+            }
             __threadfence();  // the tile builder (last CTA) reads the ids
         }
     }

@@ -16,10 +16,12 @@ Steps 4 and 6 move bytes only (rows travel as uint8 so any backend carries them)
 choreography is the same code in both. Every rank takes the same collective steps in the same order, including
 for T = 0 tokens.
 """
+import ctypes
+
 import torch
 import torch.distributed as dist
 
-from . import ops
+from . import _lib, ops
 
 
 class CudaKernels:
@@ -118,4 +120,91 @@ def layer(state, x, gate_w, k, gate_b=None, norm=True, rscale=1.0, act=None, res
     y = kernels.combine(back, slot_pos, T, k, residual)
     if timings is not None:
         timings.update(rows_sent=ns, rows_received=nr, recv_rows=recv_rows)
+    return (y, idx, wts) if return_routing else y
+
+
+# ------------------------------------------------------------------ exchange over NVLink peer memory
+class PeerExchange:
+    """The exchange buffers of an expert-parallel group: one device allocation per rank (rows in, weighted
+    rows back, flags), mapped into every rank of the group with CUDA IPC (plain peer mappings, no multicast).
+    C = rows per (source, owner) block: at least the largest T*k of any call. `peers` is a device array of the
+    P buffer addresses as this rank sees them."""
+
+    def __init__(self, P, me, C, d, device, base, ptrs, opened=(), owns=True):
+        self.P, self.me, self.C, self.d, self.device = P, me, C, d, device
+        self.base = base
+        self.ptrs = list(ptrs)
+        self.peers = torch.tensor(self.ptrs, dtype=torch.int64, device=device)
+        self._opened = list(opened)
+        self._owns = owns
+
+    @staticmethod
+    def nbytes(P, C, d):
+        return _lib.load().moeb_ep_p2p_bytes(P, C, d)
+
+    @staticmethod
+    def _alloc(nbytes):
+        p = ctypes.c_void_p()
+        _lib.call("moeb_ep_ipc_alloc", nbytes, ctypes.byref(p))
+        return p.value
+
+    @classmethod
+    def create(cls, C, d, group=None, device=None):
+        """Collective over `group` (every rank calls it): allocate, exchange IPC handles, map the peers."""
+        P, me = dist.get_world_size(group), dist.get_rank(group)
+        device = device or torch.device("cuda", torch.cuda.current_device())
+        base = cls._alloc(cls.nbytes(P, C, d))
+        h = (ctypes.c_ubyte * 64)()
+        _lib.call("moeb_ep_ipc_handle", ctypes.c_void_p(base), h)
+        mine = torch.tensor(list(bytes(h)), dtype=torch.uint8, device=device)
+        allh = [torch.empty_like(mine) for _ in range(P)]
+        dist.all_gather(allh, mine, group=group)
+        ptrs, opened = [], []
+        for r in range(P):
+            if r == me:
+                ptrs.append(base)
+                continue
+            hr = (ctypes.c_ubyte * 64)(*allh[r].cpu().tolist())
+            p = ctypes.c_void_p()
+            _lib.call("moeb_ep_ipc_open", hr, ctypes.byref(p))
+            ptrs.append(p.value)
+            opened.append(p.value)
+        dist.barrier(group=group)
+        return cls(P, me, C, d, device, base, ptrs, opened)
+
+    @classmethod
+    def local_group(cls, P, C, d, device):
+        """P exchanges for P ranks emulated in one process on one device (tests): plain buffers, no IPC."""
+        bases = [cls._alloc(cls.nbytes(P, C, d)) for _ in range(P)]
+        return [cls(P, r, C, d, device, bases[r], bases, owns=True) for r in range(P)]
+
+    def read_error(self):
+        out = ctypes.c_uint(0)
+        _lib.call("moeb_ep_p2p_read_error", ctypes.c_void_p(self.base), self.P, self.C, self.d, ctypes.byref(out),
+                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        return out.value
+
+    def close(self):
+        for p in self._opened:
+            _lib.call("moeb_ep_ipc_close", ctypes.c_void_p(p))
+        self._opened = []
+        if self._owns and self.base:
+            _lib.call("moeb_ep_ipc_free", ctypes.c_void_p(self.base))
+        self.base = 0
+
+
+def layer_p2p(state, x, gate_w, k, xch, gate_b=None, norm=True, rscale=1.0, act=None, residual=None, policy=None,
+              return_routing=False):
+    """The expert-parallel layer call over peer memory: router, dispatch (rows stored into the owners'
+    buffers), this rank's experts on what it received (rows stored back), combine. No host synchronisation:
+    the sequence can be captured in a CUDA graph. Every rank of the group must make the same calls."""
+    act = state.get("act", 0) if act is None else act
+    if policy is None:
+        T_all = x.shape[0] * xch.P  # the group's tokens per call, if every rank has as many as this one
+        policy = ops.POLICY_TILES16_RING if T_all * k >= 8 * state["E_global"] else ops.POLICY_TILES8_RING
+    T, d = x.shape
+    idx, wts = ops.router(x, gate_w, k, gate_b=gate_b, norm=norm, scale=rscale)
+    slot_pos = ops.ep_p2p_dispatch(x, idx, wts, state["E_global"], xch)
+    ops.ep_p2p_experts(state, xch, act=act, policy=policy)
+    y = ops.ep_p2p_combine(xch, slot_pos, T, k, d, residual=residual, device=x.device)
     return (y, idx, wts) if return_routing else y

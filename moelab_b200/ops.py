@@ -275,3 +275,37 @@ def ep_combine(back, slot_pos, T, k, residual=None):
     y = torch.empty(T, d, dtype=torch.bfloat16, device=back.device)
     _lib.call("moeb_ep_combine", _p(back), _p(slot_pos), T, d, k, _p(residual), _p(y), _stream())
     return y
+
+
+# ------------------------------------------------------------------ expert parallelism over peer memory
+def ep_p2p_dispatch(x, idx, wts, E, xch):
+    """Route this rank's slots straight into the owners' exchange buffers. Returns slot_pos int32 [T*k] in
+    capacity layout (owner * C + row) for the combine."""
+    _need(x, torch.bfloat16, "x")
+    _need(idx, torch.int32, "idx")
+    _need(wts, torch.float32, "wts")
+    T, d = x.shape
+    k = idx.shape[1]
+    send_counts = torch.empty(xch.P, dtype=torch.int32, device=x.device)
+    slot_pos = torch.empty(T * k, dtype=torch.int32, device=x.device)
+    _lib.call("moeb_ep_p2p_dispatch", _p(x), _p(idx), _p(wts), T, d, k, E, xch.P, xch.me, xch.C, _p(xch.peers),
+              ctypes.c_void_p(xch.base), _p(send_counts), _p(slot_pos), _stream())
+    return slot_pos
+
+
+def ep_p2p_experts(state, xch, act=0, policy=POLICY_AUTO):
+    """This rank's experts on the rows every source sent it; outputs go straight back to the owners."""
+    if _fmt(state) != "q4":
+        raise ValueError("the peer-memory exchange runs int4 states")
+    buf = state["ep_ws"].get(xch.P * xch.C)
+    _lib.call("moeb_ep_p2p_experts_q4", _p(xch.peers), ctypes.c_void_p(xch.base), xch.P, xch.me, xch.C,
+              state["dm"], state["f"], state["E"], *_expert_ptrs(state), int(act), int(policy), _p(buf),
+              buf.numel(), _stream())
+
+
+def ep_p2p_combine(xch, slot_pos, T, k, d, residual=None, device=None):
+    _need(residual, torch.bfloat16, "residual")
+    y = torch.empty(T, d, dtype=torch.bfloat16, device=device or slot_pos.device)
+    _lib.call("moeb_ep_p2p_combine", ctypes.c_void_p(xch.base), _p(slot_pos), xch.P, xch.C, T, d, k,
+              _p(residual), _p(y), _stream())
+    return y

@@ -145,3 +145,71 @@ class ThreadGroup:
         if err:
             raise err[0]
         return res
+
+
+def p2p_rank(rank, P, port, tokens, d, f, E, k, seed, policy, calls, q):
+    """Rank on GPU `rank`: the peer-memory expert-parallel layer (CUDA IPC buffers, eager and in a CUDA graph)
+    against the single-GPU layer on the full weights, bit-exact."""
+    xch = None
+    try:
+        torch.cuda.set_device(rank)
+        _init(rank, P, port, "nccl")
+        from moelab_b200 import ep, ops
+        from moelab_b200.variants.cuda import b200_q4_moe as v
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        mk = lambda *s: (torch.randn(*s, generator=g, device="cuda") * 0.02).to(torch.bfloat16)  # noqa: E731
+        w = [mk(E, f, d), mk(E, f, d), mk(E, d, f)]
+        gate = mk(E, d)
+        full = v.prepare(*w)
+        v._ws(full, k)
+        st = ep.shard(v, *w, rank, P)
+        xch = ep.PeerExchange.create(max(tokens) * k, d)
+        T = tokens[rank]
+        bad = []
+        xs = []
+        for c in range(calls):
+            x = torch.randn(T, d, generator=torch.Generator(device="cuda").manual_seed(seed + 10 * c + rank),
+                            device="cuda").to(torch.bfloat16)
+            xs.append(x)
+            y, idx, wts = ep.layer_p2p(st, x, gate, k, xch, residual=x, policy=policy, return_routing=True)
+            if T:
+                ys = ops.experts(full, x, idx, wts, policy=policy, residual=x)
+                if not torch.equal(y, ys):
+                    bad.append(("eager", c, float((y.float() - ys.float()).abs().max())))
+        # the same sequence captured in a CUDA graph and replayed (every rank replays it)
+        torch.cuda.synchronize()
+        dist.barrier()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(gr, stream=s):
+                ys_g = [ep.layer_p2p(st, x, gate, k, xch, residual=x, policy=policy) for x in xs]
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        dist.barrier()
+        gr.replay()
+        torch.cuda.synchronize()
+        for c, x in enumerate(xs):
+            if T:
+                idx, wts = ops.router(x, gate, k)
+                ys = ops.experts(full, x, idx, wts, policy=policy, residual=x)
+                if not torch.equal(ys_g[c], ys):
+                    bad.append(("graph", c, float((ys_g[c].float() - ys.float()).abs().max())))
+        dist.barrier()
+        err = xch.read_error() | st["ep_ws"].read_error()
+        del gr
+        q.put((rank, "ok", {"bad": bad, "err": err}))
+    except Exception:
+        q.put((rank, "error", traceback.format_exc()))
+    finally:
+        if xch is not None:
+            try:
+                torch.cuda.synchronize()
+                if dist.is_initialized():
+                    dist.barrier()
+                xch.close()
+            except Exception:  # noqa: BLE001
+                pass
+        if dist.is_initialized():
+            dist.destroy_process_group()

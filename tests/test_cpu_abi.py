@@ -19,8 +19,26 @@ def declared_functions():
     return names
 
 
+def declared_arity():
+    """Parameter count of every declared function (comments stripped; `void` alone counts as none)."""
+    out = {}
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        src = re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S)
+        for name, params in re.findall(r"\b(moeb_\w+)\s*\(([^)]*)\)\s*;", src):
+            params = params.strip()
+            out[name] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
 def test_header_matches_binding_table():
     assert declared_functions() == set(_lib.SIGNATURES), declared_functions() ^ set(_lib.SIGNATURES)
+
+
+def test_binding_arity_matches_header():
+    ar = declared_arity()
+    assert set(ar) == set(_lib.SIGNATURES)
+    bad = {n: (ar[n], len(_lib.SIGNATURES[n][1])) for n in ar if ar[n] != len(_lib.SIGNATURES[n][1])}
+    assert not bad, bad
 
 
 def test_library_exports_every_symbol():

@@ -155,3 +155,45 @@ def test_emulated_ep_gptoss_mxfp4_bit_exact(pol):
             continue
         ys = ops.experts(full, x, idx, wts, act=2, policy=POL[pol], residual=x)
         assert torch.equal(y, ys)
+
+
+# ------------------------------------------------------------------ exchange over peer memory, emulated
+P2P_POL = {"tiles8ring": ops.POLICY_TILES8_RING, "tiles16ring": ops.POLICY_TILES16_RING}
+
+
+@pytest.mark.parametrize("P,tokens", [(2, [4, 7]), (4, [1, 0, 33, 16]), (8, [2, 9, 1, 1, 40, 0, 3, 17])])
+@pytest.mark.parametrize("pol", list(P2P_POL))
+def test_p2p_emulated_bit_exact_vs_single_gpu(P, tokens, pol):
+    """P ranks emulated phase by phase on one GPU (all dispatches, then all experts, then all combines), so
+    every flag a kernel waits for was released by an earlier kernel on the stream. Three calls in a row reuse
+    the buffers with advancing epochs; every output must equal the single-GPU layer bit for bit."""
+    E, d, f, k = 32, 256, 384, 4
+    w, gate = _layer(E, d, f, seed=100 + P)
+    full = b200_q4_moe.prepare(*w)
+    b200_q4_moe._ws(full, k)
+    C = max(tokens) * k
+    xchs = ep.PeerExchange.local_group(P, C, d, "cuda")
+    states = [ep.shard(b200_q4_moe, *w, r, P) for r in range(P)]
+    try:
+        for call in range(3):
+            xs = [torch.randn(T, d, generator=torch.Generator(device="cuda").manual_seed(call * 100 + r),
+                              device="cuda").to(torch.bfloat16) for r, T in enumerate(tokens)]
+            routing = []
+            for r in range(P):
+                idx, wts = ops.router(xs[r], gate, k)
+                routing.append((idx, wts, ops.ep_p2p_dispatch(xs[r], idx, wts, E, xchs[r])))
+            for r in range(P):
+                ops.ep_p2p_experts(states[r], xchs[r], policy=P2P_POL[pol])
+            for r in range(P):
+                idx, wts, sp = routing[r]
+                y = ops.ep_p2p_combine(xchs[r], sp, tokens[r], k, d, residual=xs[r], device="cuda")
+                if tokens[r] == 0:
+                    continue
+                ys = ops.experts(full, xs[r], idx, wts, policy=P2P_POL[pol], residual=xs[r])
+                assert torch.equal(y, ys), (call, r, (y.float() - ys.float()).abs().max())
+        torch.cuda.synchronize()
+        assert all(x.read_error() == 0 for x in xchs)
+        assert all(s["ep_ws"].read_error() == 0 for s in states)
+    finally:
+        for x in xchs:
+            x.close()
