@@ -142,14 +142,21 @@ int check_shape(int T, int d, int f, int E, int k) {
 // slots (T <= 2 at k = 8); above that the warp-specialized tensor-map pipeline beats the register tiles at
 // every load (T = 4: 50.8 vs 55.6 us, T = 32: 126 vs 145 us), with tiles of 8 slots up to load ~4 and tiles of
 // 16 at high load (T = 256, load 16: 291 vs 329 us).
-int choose_policy(int T, int E, int k) {
+// From 64 slots per expert the tcgen05 kernels (tiles of 128, weights dequantized once per tile) win: Mixtral
+// T = 256 / 1024 / 4096: 0.58 / 1.36 / 4.39 ms vs 1.26 / 4.61 / 17.6 ms, Qwen3-235B T = 2048: 2.80 vs 4.12 ms
+// (they lose at 16 slots per expert: Qwen3-235B T = 256, 0.90 vs 0.71 ms).
+int choose_policy(int T, int E, int k, int d, int f) {
     const long TK = (long)T * k;
     if (TK <= 16) return MOEB_POLICY_SLOTS;
+    if (TK >= 64L * E && d % 128 == 0 && f % 128 == 0) return MOEB_POLICY_TC;
     return TK >= 8L * E ? MOEB_POLICY_TILES16_RING : MOEB_POLICY_TILES8_RING;
 }
 
-int nt_of(int policy) { return (policy == MOEB_POLICY_TILES16 || policy == MOEB_POLICY_TILES16_RING) ? 16 : 8; }
-bool is_tiles(int policy) { return policy >= MOEB_POLICY_TILES8 && policy <= MOEB_POLICY_TILES16_RING; }
+int nt_of(int policy) {
+    if (policy == MOEB_POLICY_TC) return 128;
+    return (policy == MOEB_POLICY_TILES16 || policy == MOEB_POLICY_TILES16_RING) ? 16 : 8;
+}
+bool is_tiles(int policy) { return policy >= MOEB_POLICY_TILES8 && policy <= MOEB_POLICY_TC; }
 
 // One expert kernel launch: per_warp kernels run one (tile, 16-row block) unit per warp; the others one unit
 // per CTA, where a warp-specialized kernel's unit is `rows` consecutive row blocks (rows > 1 also means it
@@ -160,6 +167,7 @@ struct KLaunch {
     size_t smem;
     bool per_warp;
     int rows, sg;
+    bool tc = false;  // tensor-core kernel: reads the activations through the expert-sorted row map
 };
 struct ExpLaunch {
     KLaunch gu, dn;
@@ -175,6 +183,12 @@ KLaunch ws_kernel(int nt8, bool down) {
                    : k_experts_ws<FMT_Q4, 2, WS_RBC, WS_SG, WS_NS_GU, false, 2>;
     return {fn, 32 * (WS_RBC + 1), experts_ws_smem(nt8, WS_RBC, WS_SG, down ? WS_NS_DN : WS_NS_GU, down), false,
             WS_RBC, WS_SG};
+}
+
+constexpr int TC_NT = 128, TC_NS_GU = 3, TC_NS_DN = 4;
+KLaunch tc_kernel(bool down) {
+    void (*fn)(ExpArgs) = down ? k_experts_tc<TC_NT, TC_NS_DN, true> : k_experts_tc<TC_NT, TC_NS_GU, false>;
+    return {fn, 320, experts_tc_smem(TC_NT, down ? TC_NS_DN : TC_NS_GU, down), false, 8, 1, true};
 }
 
 // Kernels per policy: TILES8 / TILES16 run the register-pipelined tile kernels, the *_RING policies the
@@ -195,6 +209,10 @@ ExpLaunch pick_kernels(int fmt, int policy, int d, int f) {
     if (policy == MOEB_POLICY_SLOTS)
         return {{k_gate_up_slots<FMT_Q4, 8, 4>, 256, (size_t)d * 2, false, 1, 0},
                 {k_down_slots<FMT_Q4, 4, 4>, 128, (size_t)f * 2 + (size_t)f / 16 * 4, false, 1, 0}};
+    if (policy == MOEB_POLICY_TC) {
+        if (d % 128 || f % 128) return {none, none};
+        return {tc_kernel(false), tc_kernel(true)};
+    }
     if (policy == MOEB_POLICY_TILES16_RING) return {ws_kernel(2, false), ws_kernel(2, true)};
     if (policy == MOEB_POLICY_TILES8_RING) return {ws_kernel(1, false), ws_kernel(1, true)};
     if (policy == MOEB_POLICY_TILES16)
@@ -268,6 +286,19 @@ bool allow_smem(const void *fn, size_t bytes) {
 
 bool separate_combine(const KLaunch &dn) { return dn.sg > 0; }
 
+// 2-D map over rows x d bf16 activations (row stride d * 2 bytes), box 64 x brows, 128-byte swizzle.
+bool encode_rows_map(CUtensorMap *out, const void *base, long rows, int d, int brows) {
+    auto fn = tmap_encoder();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)d, (cuuint64_t)std::max<long>(rows, 1)};
+    const cuuint64_t strides[1] = {(cuuint64_t)d * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)brows};
+    const cuuint32_t es[2] = {1, 1};
+    return fn(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int grid_for(const KLaunch &k, long units) {
     const long ctas = k.per_warp ? (units + k.threads / 32 - 1) / (k.threads / 32) : units;
     const long cap = (long)occupancy((const void *)k.fn, k.threads, k.smem) * sm_count();
@@ -298,11 +329,20 @@ int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaS
             !encode_weights_map(&a.tmsb[2], a.dn.sb, 16, a.f / 64, (long)a.E * RBd, K.dn.sg, K.dn.rows))
             return fail(MOEB_ELAUNCH, "tensor map encoding failed (down)%s");
     }
+    if (K.gu.tc) {  // activations in expert-sorted order (in the slot-row region, free until down writes it)
+        uint16_t *xs = reinterpret_cast<uint16_t *>(a.yp);
+        if (launch(k_gather_rows, dim3((unsigned)((TK + 7) / 8)), dim3(256), 0, st, a.x, (const int *)a.sorted, (int)TK,
+                   a.k, a.d, xs) != cudaSuccess)
+            return check_launch("gather");
+        if (!encode_rows_map(&a.tmx, xs, TK, a.d, TC_NT)) return fail(MOEB_ELAUNCH, "tensor map encoding failed (x)%s");
+    }
     {
         const long units = max_tiles * ((RBf + K.gu.rows - 1) / K.gu.rows);
         if (launch(K.gu.fn, dim3(grid_for(K.gu, units)), dim3(K.gu.threads), K.gu.smem, st, a) != cudaSuccess)
             return check_launch("gate_up");
     }
+    if (K.dn.tc && !encode_rows_map(&a.tmx, a.h, TK, a.f, TC_NT))
+        return fail(MOEB_ELAUNCH, "tensor map encoding failed (h)%s");
     if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[2]), st);
     // combine: fused into down (last arrival per (token, row block) sums the k slot rows), or a separate pass
     // over the weighted slot rows when down is the warp-specialized kernel (no fences / counters in its epilogue)
@@ -403,7 +443,7 @@ int moeb_read_error(void *ws, unsigned *out, cudaStream_t st) {
     return MOEB_OK;
 }
 
-int moeb_policy(int T, int E, int k) { return choose_policy(T, E, k); }
+int moeb_policy(int T, int E, int k) { return choose_policy(T, E, k, 128, 128); }
 
 // ------------------------------------------------------------------ quantizers
 static int check_rows(long rows, long K) {
@@ -510,8 +550,13 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
     if (cap < T) return fail(MOEB_EINVAL, "workspace too small for T tokens%s");
     const Layout L = layout(cap, d, f, E, k, !ep);
     const int xs = ep ? d + 8 : d;
-    if (policy == MOEB_POLICY_AUTO) policy = choose_policy(T, E, k);
+    if (policy == MOEB_POLICY_AUTO) {
+        policy = choose_policy(T, E, k, d, f);
+        if (policy == MOEB_POLICY_TC && (fmt != FMT_Q4 || ep)) policy = MOEB_POLICY_TILES16_RING;
+    }
     if (policy != MOEB_POLICY_SLOTS && !is_tiles(policy)) return fail(MOEB_EINVAL, "unknown policy%s");
+    if (policy == MOEB_POLICY_TC && (fmt != FMT_Q4 || d % 128 || f % 128 || ep))
+        return fail(MOEB_EINVAL, "the tensor-core policy needs int4 weights and d, f multiples of 128%s");
     const bool tiles = policy != MOEB_POLICY_SLOTS;
     if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[0]), st);
     if (gate_w) {  // layer call: router produces ids, weights, x group sums and (tile mode) the tiles

@@ -110,6 +110,11 @@ MOEB_DEV bool mbar_wait_bounded(uint64_t *bar, unsigned parity, unsigned limit =
         if (mbar_try_wait(bar, parity)) return true;
     return false;
 }
+MOEB_DEV uint64_t l2_evict_last_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
 MOEB_DEV uint64_t l2_evict_first_policy() {
     uint64_t pol;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));

@@ -90,6 +90,9 @@ struct ExpArgs {
     // [2] down); a box is RBC row blocks x SG groups (RBC rows of SG*512 | SG*64 contiguous bytes), so one
     // copy per array and projection fills a pipeline stage
     CUtensorMap tmq[3], tmsb[3];
+    // tensor-core kernels: 2-D map over the expert-sorted activation rows of the launch (x gathered for gate/up,
+    // h for down), box 64 k x NT rows, 128-byte swizzle
+    CUtensorMap tmx;
 };
 
 // Per-rank buffer of the peer-memory exchange (one allocation, mapped by every rank of the group):
@@ -162,6 +165,10 @@ template <int FMT, int NT8, int GPW>
 __global__ void k_down_tiles_reg(ExpArgs a);
 template <int FMT, int NT8, int RBC, int SG, int NS, bool DOWN, int MB>
 __global__ void k_experts_ws(const __grid_constant__ ExpArgs a);
+template <int NT, int NS, bool DOWN>
+__global__ void k_experts_tc(const __grid_constant__ ExpArgs a);
+size_t experts_tc_smem(int nt, int ns, bool down);
+__global__ void k_gather_rows(const uint16_t *x, const int *sorted, int TK, int k, int d, uint16_t *xs);
 size_t experts_ws_smem(int nt8, int rbc, int sg, int ns, bool down);
 
 

@@ -130,3 +130,64 @@ def test_mixtral(mixtral, fmt, routing, T):
     else:
         ref = torch_ref(v, st, x, it, wt, deq)
     assert_close(y, ref, what=(fmt, routing, T))
+
+
+# ------------------------------------------------------------------ tensor-core policy (tcgen05, tiles of 128)
+@pytest.mark.parametrize("T,routing", [(1, "uniform"), (3, "uniform"), (64, "uniform"), (300, "uniform"),
+                                       (300, "one_hot"), (513, "zipf")])
+def test_tc_small_vs_oracle(T, routing):
+    """Tiles of up to 128 slots on the tensor cores: partial tiles, several tiles per expert, empty experts."""
+    from helpers import problem_tensors
+    from moelab_b200.shapes import MoEShape
+    sh = MoEShape("tc", d=256, f=384, E=8, k=2)
+    p, w, x, idx, wts = problem_tensors(sh, T, routing, seed=T)
+    st = b200_q4_moe.prepare(*w)
+    b200_q4_moe._ws(st, sh.k)
+    y = ops.experts(st, x, idx, wts, policy=ops.POLICY_TC)
+    assert_close(y, ref_from_state(b200_q4_moe, st, x, idx, wts), what=(T, routing))
+    assert st["ws"].read_error() == 0
+    # the same through the layer call with a fused residual
+    gate = (torch.randn(sh.E, sh.d, device="cuda") * 0.02).to(torch.bfloat16)
+    b200_q4_moe.POLICY = ops.POLICY_TC
+    try:
+        y2, i2, w2 = b200_q4_moe.layer(st, x, gate, sh.k, residual=x, return_routing=True)
+    finally:
+        b200_q4_moe.POLICY = None
+    assert_close(y2, ref_from_state(b200_q4_moe, st, x, i2, w2) + x.float().cpu().numpy())
+
+
+@pytest.mark.parametrize("T", [256, 2048])
+def test_tc_qwen3_235b(T):
+    d, f, E, k = 4096, 1536, 128, 8
+    w, mk = _w(E, f, d, seed=900 + T)
+    st = b200_q4_moe.prepare(*w)
+    del w
+    b200_q4_moe._ws(st, k)
+    x = torch.randn(T, d, generator=torch.Generator(device="cuda").manual_seed(T), device="cuda").to(torch.bfloat16)
+    idx, wts = make_routing(T, E, k, "uniform", np.random.default_rng(T))
+    it, wt = torch.from_numpy(idx).cuda(), torch.from_numpy(wts).cuda()
+    y = ops.experts(st, x, it, wt, policy=ops.POLICY_TC)
+    assert_close(y, torch_ref(b200_q4_moe, st, x, it, wt), what=T)
+
+
+@pytest.mark.parametrize("routing", ["uniform", "one_hot", "round_robin"])
+@pytest.mark.parametrize("T", [256, 1024, 4096])
+def test_tc_mixtral(mixtral, routing, T):
+    st, deq = mixtral[0]["q4"], mixtral[1]["q4"]
+    idx, wts = make_routing(T, 8, 2, routing, np.random.default_rng(T))
+    x = torch.randn(T, 4096, generator=torch.Generator(device="cuda").manual_seed(T), device="cuda").to(torch.bfloat16)
+    it, wt = torch.from_numpy(idx).cuda(), torch.from_numpy(wts).cuda()
+    b200_q4_moe._ws(st, 2)
+    y = ops.experts(st, x, it, wt, policy=ops.POLICY_TC)
+    assert_close(y, torch_ref(b200_q4_moe, st, x, it, wt, deq), what=(routing, T))
+
+
+def test_tc_rejects_unsupported_shapes():
+    from moelab_b200.shapes import MoEShape
+    from helpers import problem_tensors
+    sh = MoEShape("odd", d=192, f=256, E=4, k=2)
+    p, w, x, idx, wts = problem_tensors(sh, 8)
+    st = b200_q4_moe.prepare(*w)
+    b200_q4_moe._ws(st, 2)
+    with pytest.raises(ops._lib.MoebError, match="multiples of 128"):
+        ops.experts(st, x, idx, wts, policy=ops.POLICY_TC)
