@@ -44,6 +44,7 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=256)
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bound on the CPU baseline sample")
     ap.add_argument("--soak-seconds", type=float, default=1.5, help="replays before the timed region (clocks)")
+    ap.add_argument("--configs", type=int, default=1, help="1: also time the other BASELINE configurations (1 GPU)")
     return ap.parse_args()
 
 
@@ -244,6 +245,102 @@ def measure_T(v, layers, T, ws, rank, n_steps, seed):
             "unique_experts": round(float(np.mean([torch.unique(i).numel() for i in idxs])), 2),
             "tokens_per_s": round(T * n_steps / t, 1),
             "stage_us": [round(statistics.mean(x), 2) for x in (r_us, gu_us, dn_us)]}
+
+
+# ------------------------------------------------------------------ the other BASELINE configurations (1 GPU)
+CONFIGS = [
+    # name, shape, format/options, T values
+    ("gpt-oss-20b mxfp4 (biases, clamped SwiGLU, gate bias)", dict(d=2880, f=2880, E=32, k=4), "gptoss", [1, 8, 32, 128]),
+    ("deepseek-v2-lite int4 + 2 shared experts (Zipf-biased greedy router)", dict(d=2048, f=1408, E=64, k=6),
+     "deepseek", [1, 16, 64, 256]),
+    ("qwen3-235b-a22b int4", dict(d=4096, f=1536, E=128, k=8), "q4", [1, 32, 256, 2048]),
+    ("mixtral-8x7b int4", dict(d=4096, f=14336, E=8, k=2), "q4", [1, 16, 256, 1024, 4096]),
+    ("mixtral-8x7b mxfp4", dict(d=4096, f=14336, E=8, k=2), "mxfp4", [1, 16, 256, 1024]),
+]
+
+
+def config_layers(d, f, E, k, kind, n_layers=2, seed=11):
+    """n_layers seeded layers of one configuration and a layer-call closure (router included)."""
+    from moelab_b200.problem import zipf_bias
+    from moelab_b200.variants.cuda import b200_mxfp4_gptoss as vg, b200_mxfp4_moe as vm, b200_q4_moe as vq
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    mk = lambda *s_, sc=0.02: (torch.randn(*s_, generator=g, device="cuda") * sc).to(torch.bfloat16)  # noqa: E731
+    layers = []
+    for _ in range(n_layers):
+        w = [mk(E, f, d), mk(E, f, d), mk(E, d, f)]
+        gate = mk(E, d)
+        if kind == "gptoss":
+            b = [mk(E, f, sc=0.01).float(), mk(E, f, sc=0.01).float(), mk(E, d, sc=0.01).float()]
+            st = vg.state(*w, *b)
+            gb = mk(E, sc=0.01)
+            call = (lambda st, x, gate, gb=gb: vg.layer(st, x, gate, k, gate_b=gb, residual=x))
+            bits = 4.25
+        elif kind == "deepseek":
+            sw = [mk(2 * f, d), mk(2 * f, d), mk(d, 2 * f)]
+            st = vq.prepare_shared(*w, *sw)
+            gb = torch.from_numpy(zipf_bias(E, 1.1, seed=7)).to("cuda", torch.bfloat16)
+            call = (lambda st, x, gate, gb=gb: vq.layer(st, x, gate, k, gate_b=gb, norm=False, residual=x))
+            bits = 4.5
+        elif kind == "mxfp4":
+            st = vm.prepare(*w)
+            call = (lambda st, x, gate: vm.layer(st, x, gate, k, residual=x))
+            bits = 4.25
+        else:
+            st = vq.prepare(*w)
+            call = (lambda st, x, gate: vq.layer(st, x, gate, k, residual=x))
+            bits = 4.5
+        del w
+        layers.append((st, gate, call))
+    torch.cuda.synchronize()
+    return layers, bits
+
+
+def measure_config(name, shp, kind, Ts, peaks, n_calls=8):
+    d, f, E, k = shp["d"], shp["f"], shp["E"], shp["k"]
+    layers, bits = config_layers(d, f, E, k, kind)
+    ns = 2 if kind == "deepseek" else 0
+    out = []
+    for T in Ts:
+        g = torch.Generator(device="cuda").manual_seed(1000 + T)
+        xs = [torch.randn(T, d, generator=g, device="cuda").to(torch.bfloat16) for _ in layers]
+        for i, (st, gate, call) in enumerate(layers):  # warm-up (sizes the workspaces)
+            call(st, xs[i], gate)
+        torch.cuda.synchronize()
+        s_ = torch.cuda.Stream()
+        s_.wait_stream(torch.cuda.current_stream())
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s_):
+            with torch.cuda.graph(gr, stream=s_):
+                for i in range(n_calls):
+                    st, gate, call = layers[i % len(layers)]
+                    call(st, xs[i % len(layers)], gate)
+        torch.cuda.current_stream().wait_stream(s_)
+        gr.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(3):
+            gr.replay()
+        e1.record()
+        e1.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (3 * n_calls)
+        del gr
+        # algorithmic bytes / flops of one call (unique routed experts of layer 0's routing, + shared experts)
+        from moelab_b200 import ops
+        idx, _ = ops.router(xs[0], layers[0][1], k)
+        U = int(torch.unique(idx).numel()) + ns
+        ks = k + ns
+        byts = U * 3 * d * f * bits / 8 + 2 * T * d * 2 + 2 * T * ks * f * 2 + E * d * 2
+        flops = 6.0 * d * f * T * ks
+        t_roof = max(byts / (peaks["hbm_gbs"] * 1e9), flops / (peaks["bf16_tflops"] * 1e12))
+        out.append({"config": name, "T": T, "us_per_call": round(us, 2), "tokens_per_s": round(T / us * 1e6, 1),
+                    "gbs": round(byts / us / 1e3, 1), "tflops": round(flops / us / 1e6, 1),
+                    "roofline_frac": round(t_roof / (us * 1e-6), 3),
+                    "bound": "hbm" if byts / (peaks["hbm_gbs"] * 1e9) >= flops / (peaks["bf16_tflops"] * 1e12)
+                    else "tensor"})
+    del layers
+    torch.cuda.empty_cache()
+    return out
 
 
 # ------------------------------------------------------------------ CPU baseline (reference's CPU torch path)
@@ -540,6 +637,10 @@ def main():
     e2e = {"value": round(ws * T * a.e2e_steps / te, 1), "unit": "tokens/s", "h2d_bytes_per_step": T * D * 2,
            "d2h_bytes_per_step": T * D * 2, "us_per_call": round(te / a.e2e_steps * 1e6, 3),
            "note": "public API v.layer(); pinned host x copied in and y copied out every step, no graph"}
+    configs = []
+    if a.configs:
+        for name, shp, kind, Ts in CONFIGS:
+            configs += measure_config(name, shp, kind, Ts, peaks)
     cpu = None
     if rank == 0 and ws == 1:
         val, n, el = cpu_baseline(T, a.cpu_seconds)
@@ -570,6 +671,7 @@ def main():
                      else "fallback 6650 GB/s",
                      "algorithmic_bytes_per_launch": round(statistics.mean(gu_b)),
                      "down_achieved_gbs": round(dn_ach, 1)},
+        "configs": configs,
         "cpu_baseline": cpu, "e2e": e2e, "clocks": ck,
         "gpu_launches": (3 if T * K_TOP <= 16 else 4) * a.steps,  # router, gate/up, down (+ combine in tile mode)
     }

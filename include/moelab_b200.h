@@ -45,7 +45,7 @@ typedef struct CUstream_st *cudaStream_t;
 #define MOEB_POLICY_TILES16 3 /* tiles of <= 16 slots */
 #define MOEB_POLICY_TILES8_RING 4  /* tiles of <= 8 slots, weights streamed by TMA into a per-warp ring */
 #define MOEB_POLICY_TILES16_RING 5 /* tiles of <= 16 slots, TMA ring */
-#define MOEB_POLICY_TC 6 /* tiles of <= 128 slots on tcgen05 tensor cores (int4; d and f multiples of 128) */
+#define MOEB_POLICY_TC 6 /* tiles of <= 128 slots on tcgen05 tensor cores (d and f multiples of 128) */
 
 /* device error bits readable with moeb_read_error */
 #define MOEB_DEVERR_EXPERT_ID 1u /* an expert id outside [0, E) was given; that slot contributed nothing */
@@ -62,8 +62,8 @@ size_t moeb_workspace_bytes(int T, int d, int f, int E, int k);
 int moeb_workspace_init(void *ws, size_t ws_bytes, cudaStream_t stream);
 /* Copies the sticky device error word to *out (host) and clears it. Synchronises `stream`. */
 int moeb_read_error(void *ws, unsigned *out, cudaStream_t stream);
-/* Policy the dispatcher picks for AUTO (host-only, no device work) for an int4 layer whose d and f are multiples
- * of 128 (other shapes and MXFP4 replace MOEB_POLICY_TC by MOEB_POLICY_TILES16_RING). */
+/* Policy the dispatcher picks for AUTO (host-only, no device work) for a layer whose d and f are multiples of 128
+ * (other shapes get MOEB_POLICY_TILES16_RING where this returns MOEB_POLICY_TC). */
 int moeb_policy(int T, int E, int k);
 
 /* --- quantizers: w bf16 [rows][K] -> B200 layout. Replace mx.quantize(w, group_size=64, bits=4) and

@@ -175,46 +175,54 @@ struct ExpLaunch {
 
 constexpr int WS_RBC = 8, WS_SG = 4, WS_NS_GU = 2, WS_NS_DN = 4;
 
-KLaunch ws_kernel(int nt8, bool down) {
+template <int FMT>
+KLaunch ws_kernel_fmt(int nt8, bool down) {
     void (*fn)(ExpArgs) = nullptr;
-    if (nt8 == 1) fn = down ? k_experts_ws<FMT_Q4, 1, WS_RBC, WS_SG, WS_NS_DN, true, 2>
-                            : k_experts_ws<FMT_Q4, 1, WS_RBC, WS_SG, WS_NS_GU, false, 2>;
-    else fn = down ? k_experts_ws<FMT_Q4, 2, WS_RBC, WS_SG, WS_NS_DN, true, 2>
-                   : k_experts_ws<FMT_Q4, 2, WS_RBC, WS_SG, WS_NS_GU, false, 2>;
-    return {fn, 32 * (WS_RBC + 1), experts_ws_smem(nt8, WS_RBC, WS_SG, down ? WS_NS_DN : WS_NS_GU, down), false,
+    if (nt8 == 1) fn = down ? k_experts_ws<FMT, 1, WS_RBC, WS_SG, WS_NS_DN, true, 2>
+                            : k_experts_ws<FMT, 1, WS_RBC, WS_SG, WS_NS_GU, false, 2>;
+    else fn = down ? k_experts_ws<FMT, 2, WS_RBC, WS_SG, WS_NS_DN, true, 2>
+                   : k_experts_ws<FMT, 2, WS_RBC, WS_SG, WS_NS_GU, false, 2>;
+    return {fn, 32 * (WS_RBC + 1), experts_ws_smem(nt8, WS_RBC, WS_SG, down ? WS_NS_DN : WS_NS_GU, down, FMT), false,
             WS_RBC, WS_SG};
+}
+KLaunch ws_kernel(int fmt, int nt8, bool down) {
+    return fmt == FMT_FP4 ? ws_kernel_fmt<FMT_FP4>(nt8, down) : ws_kernel_fmt<FMT_Q4>(nt8, down);
 }
 
 constexpr int TC_NT = 128, TC_NS_GU = 3, TC_NS_DN = 4;
-KLaunch tc_kernel(bool down) {
-    void (*fn)(ExpArgs) = down ? k_experts_tc<TC_NT, TC_NS_DN, true> : k_experts_tc<TC_NT, TC_NS_GU, false>;
-    return {fn, 320, experts_tc_smem(TC_NT, down ? TC_NS_DN : TC_NS_GU, down), false, 8, 1, true};
+KLaunch tc_kernel(int fmt, bool down) {
+    void (*fn)(ExpArgs) = fmt == FMT_FP4 ? (down ? k_experts_tc<FMT_FP4, TC_NT, TC_NS_DN, true>
+                                                 : k_experts_tc<FMT_FP4, TC_NT, TC_NS_GU, false>)
+                                         : (down ? k_experts_tc<FMT_Q4, TC_NT, TC_NS_DN, true>
+                                                 : k_experts_tc<FMT_Q4, TC_NT, TC_NS_GU, false>);
+    return {fn, 448, experts_tc_smem(TC_NT, down ? TC_NS_DN : TC_NS_GU, down, fmt), false, 8, 1, true};
 }
 
 // Kernels per policy: TILES8 / TILES16 run the register-pipelined tile kernels, the *_RING policies the
 // warp-specialized tensor-map pipeline (faster on B200 for both projections, so the dispatcher picks it).
 ExpLaunch pick_kernels(int fmt, int policy, int d, int f) {
     const KLaunch none = {nullptr, 0, 0, false, 1, 0};
-    if (fmt == FMT_FP4) {  // MXFP4: decode and register-tile kernels (the TMA variant is int4 only)
-        if (policy == MOEB_POLICY_SLOTS)
+    if (fmt != FMT_Q4 && fmt != FMT_FP4) return {none, none};
+    if (policy == MOEB_POLICY_SLOTS) {
+        if (fmt == FMT_FP4)
             return {{k_gate_up_slots<FMT_FP4, 8, 4>, 256, (size_t)d * 2, false, 1, 0},
                     {k_down_slots<FMT_FP4, 4, 4>, 128, (size_t)f * 2 + (size_t)f / 16 * 4, false, 1, 0}};
-        if (policy == MOEB_POLICY_TILES16 || policy == MOEB_POLICY_TILES16_RING)
+        return {{k_gate_up_slots<FMT_Q4, 8, 4>, 256, (size_t)d * 2, false, 1, 0},
+                {k_down_slots<FMT_Q4, 4, 4>, 128, (size_t)f * 2 + (size_t)f / 16 * 4, false, 1, 0}};
+    }
+    if (policy == MOEB_POLICY_TC) {
+        if (d % 128 || f % 128) return {none, none};
+        return {tc_kernel(fmt, false), tc_kernel(fmt, true)};
+    }
+    if (policy == MOEB_POLICY_TILES16_RING) return {ws_kernel(fmt, 2, false), ws_kernel(fmt, 2, true)};
+    if (policy == MOEB_POLICY_TILES8_RING) return {ws_kernel(fmt, 1, false), ws_kernel(fmt, 1, true)};
+    if (fmt == FMT_FP4) {
+        if (policy == MOEB_POLICY_TILES16)
             return {{k_gate_up_tiles_reg<FMT_FP4, 2, 1>, 128, 0, true, 1, 0},
                     {k_down_tiles_reg<FMT_FP4, 2, 1>, 128, 0, true, 1, 0}};
         return {{k_gate_up_tiles_reg<FMT_FP4, 1, 2>, 128, 0, true, 1, 0},
                 {k_down_tiles_reg<FMT_FP4, 1, 2>, 128, 0, true, 1, 0}};
     }
-    if (fmt != FMT_Q4) return {none, none};
-    if (policy == MOEB_POLICY_SLOTS)
-        return {{k_gate_up_slots<FMT_Q4, 8, 4>, 256, (size_t)d * 2, false, 1, 0},
-                {k_down_slots<FMT_Q4, 4, 4>, 128, (size_t)f * 2 + (size_t)f / 16 * 4, false, 1, 0}};
-    if (policy == MOEB_POLICY_TC) {
-        if (d % 128 || f % 128) return {none, none};
-        return {tc_kernel(false), tc_kernel(true)};
-    }
-    if (policy == MOEB_POLICY_TILES16_RING) return {ws_kernel(2, false), ws_kernel(2, true)};
-    if (policy == MOEB_POLICY_TILES8_RING) return {ws_kernel(1, false), ws_kernel(1, true)};
     if (policy == MOEB_POLICY_TILES16)
         return {{k_gate_up_tiles_reg<FMT_Q4, 2, 1>, 128, 0, true, 1, 0},
                 {k_down_tiles_reg<FMT_Q4, 2, 1>, 128, 0, true, 1, 0}};
@@ -317,16 +325,17 @@ int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaS
     if (!allow_smem((const void *)K.gu.fn, K.gu.smem) || !allow_smem((const void *)K.dn.fn, K.dn.smem))
         return check_launch("cudaFuncSetAttribute");
     const int RBf = a.f / 16, RBd = a.d / 16;
+    const int sw = fmt == FMT_FP4 ? 8 : 16;  // scale words per (row block, group)
     if (K.gu.sg) {
         if (!encode_weights_map(&a.tmq[0], a.g.q, 128, a.d / 64, (long)a.E * RBf, K.gu.sg, K.gu.rows) ||
-            !encode_weights_map(&a.tmsb[0], a.g.sb, 16, a.d / 64, (long)a.E * RBf, K.gu.sg, K.gu.rows) ||
+            !encode_weights_map(&a.tmsb[0], a.g.sb, sw, a.d / 64, (long)a.E * RBf, K.gu.sg, K.gu.rows) ||
             !encode_weights_map(&a.tmq[1], a.u.q, 128, a.d / 64, (long)a.E * RBf, K.gu.sg, K.gu.rows) ||
-            !encode_weights_map(&a.tmsb[1], a.u.sb, 16, a.d / 64, (long)a.E * RBf, K.gu.sg, K.gu.rows))
+            !encode_weights_map(&a.tmsb[1], a.u.sb, sw, a.d / 64, (long)a.E * RBf, K.gu.sg, K.gu.rows))
             return fail(MOEB_ELAUNCH, "tensor map encoding failed (gate/up)%s");
     }
     if (K.dn.sg) {
         if (!encode_weights_map(&a.tmq[2], a.dn.q, 128, a.f / 64, (long)a.E * RBd, K.dn.sg, K.dn.rows) ||
-            !encode_weights_map(&a.tmsb[2], a.dn.sb, 16, a.f / 64, (long)a.E * RBd, K.dn.sg, K.dn.rows))
+            !encode_weights_map(&a.tmsb[2], a.dn.sb, sw, a.f / 64, (long)a.E * RBd, K.dn.sg, K.dn.rows))
             return fail(MOEB_ELAUNCH, "tensor map encoding failed (down)%s");
     }
     if (K.gu.tc) {  // activations in expert-sorted order (in the slot-row region, free until down writes it)
@@ -552,11 +561,11 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
     const int xs = ep ? d + 8 : d;
     if (policy == MOEB_POLICY_AUTO) {
         policy = choose_policy(T, E, k, d, f);
-        if (policy == MOEB_POLICY_TC && (fmt != FMT_Q4 || ep)) policy = MOEB_POLICY_TILES16_RING;
+        if (policy == MOEB_POLICY_TC && ep) policy = MOEB_POLICY_TILES16_RING;
     }
     if (policy != MOEB_POLICY_SLOTS && !is_tiles(policy)) return fail(MOEB_EINVAL, "unknown policy%s");
-    if (policy == MOEB_POLICY_TC && (fmt != FMT_Q4 || d % 128 || f % 128 || ep))
-        return fail(MOEB_EINVAL, "the tensor-core policy needs int4 weights and d, f multiples of 128%s");
+    if (policy == MOEB_POLICY_TC && (d % 128 || f % 128 || ep))
+        return fail(MOEB_EINVAL, "the tensor-core policy needs d, f multiples of 128%s");
     const bool tiles = policy != MOEB_POLICY_SLOTS;
     if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[0]), st);
     if (gate_w) {  // layer call: router produces ids, weights, x group sums and (tile mode) the tiles

@@ -6,14 +6,14 @@
 //   warp 0 (producer, one lane): per stage, 2-D tensor copies of the packed int4 codes and scale|bias words of
 //     the 8 row blocks (one group; per projection) and of the tile's activation rows (64 k, NT rows, 128-byte
 //     swizzle: the UMMA K-major layout); "full" mbarrier with transaction bytes. No multicast.
-//   warps 2..5 (dequant): int4 -> bf16 w = s*q + b (q|0x4300 = 128+q exactly; one HSUB2 and one HFMA2, a single
+//   warps 2..9 (dequant): int4 -> bf16 w = s*q + b (q|0x4300 = 128+q exactly; one HSUB2 and one HFMA2, a single
 //     bf16 rounding), written into the stage's A tile in the same swizzled K-major layout; then a proxy fence
 //     (generic writes -> tensor-core reads) and one arrival per warp on the stage's "deq" mbarrier.
-//   warp 1 (MMA, one lane): waits "deq", issues 4 k-steps of tcgen05.mma (M = 128, N = NT, K = 16, bf16 x bf16
-//     -> fp32) per projection, and tcgen05.commit frees the stage ("empty"); after the last group it commits the
+//   warp 1 (MMA, one lane): waits "deq", issues 4 k-steps of tcgen05.mma (M = 128, N = the tile's slot count
+//     rounded up to 16, K = 16, bf16 x bf16 -> fp32) per projection, and tcgen05.commit frees the stage ("empty"); after the last group it commits the
 //     item's accumulator ("accf"). Two accumulator sets alternate between items, so the next item's MMAs run
 //     while the epilogue drains the previous one.
-//   warps 6..9 (epilogue): tcgen05.ld 16 columns at a time (warp w reads TMEM lanes 32*(w%4)..+31 = its rows);
+//   warps 10..13 (epilogue): tcgen05.ld 16 columns at a time (warp w reads TMEM lanes 32*(w%4)..+31 = its rows);
 //     gate/up: bias + activation -> h in slot-sorted order; down: weight * (acc + bias) -> the slot's fp32 row
 //     for the separate combine pass. Then "acce" frees the accumulator set.
 // The activations arrive in expert-sorted order (x gathered by k_gather_rows; gate/up writes h sorted), so each
@@ -28,7 +28,8 @@ namespace moeb {
 namespace {
 
 constexpr int TC_M = 128;
-constexpr int TC_THREADS = 320;  // 10 warps
+constexpr int TC_DQW = 8;                       // dequant warps
+constexpr int TC_THREADS = 32 * (2 + TC_DQW + 4);  // producer, MMA, dequant, 4 epilogue warps
 
 // K-major operand descriptor, 128-byte swizzle: 8-row groups 1024 B apart (SBO), rows of 128 B.
 MOEB_DEV uint64_t sdesc_sw128(uint32_t saddr) {
@@ -72,13 +73,14 @@ MOEB_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-template <int NT, bool DOWN>
+template <int FMT, int NT, bool DOWN>
 struct TCL {
     static constexpr int NP = DOWN ? 1 : 2;
+    static constexpr int SBG = FMT == FMT_FP4 ? 32 : 64;  // scale bytes per (row block, group)
     static constexpr int A_BYTES = TC_M * 128;         // one projection's 128 rows x 64 k, bf16, swizzled
     static constexpr int X_BYTES = NT * 128;           // NT rows x 64 k
     static constexpr int Q_BYTES = 8 * 512;            // packed codes, 8 row blocks x one group
-    static constexpr int S_BYTES = 8 * 64;             // scale|bias words
+    static constexpr int S_BYTES = 8 * SBG;            // int4 scale|bias words / MXFP4 E8M0 bytes
     static constexpr int STAGE_RAW = NP * A_BYTES + X_BYTES + NP * (Q_BYTES + S_BYTES);
     static constexpr int STAGE = (STAGE_RAW + 1023) / 1024 * 1024;
     static constexpr int TMEM_COLS = 2 * NP * NT;      // two accumulator sets
@@ -87,9 +89,9 @@ struct TCL {
 
 }  // namespace
 
-template <int NT, int NS, bool DOWN>
+template <int FMT, int NT, int NS, bool DOWN>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_constant__ ExpArgs a) {
-    using L = TCL<NT, DOWN>;
+    using L = TCL<FMT, NT, DOWN>;
     pdl_launch();
     pdl_wait();
     extern __shared__ __align__(1024) unsigned char tsm_raw[];
@@ -109,7 +111,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_const
     if (threadIdx.x == 0) {
         for (int i = 0; i < NS; ++i) {
             mbar_init(full + i, 1);
-            mbar_init(deq + i, 4);
+            mbar_init(deq + i, TC_DQW);
             mbar_init(empty + i, 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -163,7 +165,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_const
                     tma_load_2d(st + L::NP * L::A_BYTES, &a.tmx, g * 64, tr.y, full + s, pol_x);
                     for (int p = 0; p < L::NP; ++p) {
                         tma_load_2d(q + p * L::Q_BYTES, &a.tmq[m0 + p], g * 64, row0, full + s, pol);
-                        tma_load_2d(q + L::NP * L::Q_BYTES + p * L::S_BYTES, &a.tmsb[m0 + p], g * 16, row0, full + s, pol);
+                        tma_load_2d(q + L::NP * L::Q_BYTES + p * L::S_BYTES, &a.tmsb[m0 + p], g * (L::SBG / 4), row0,
+                                    full + s, pol);
                     }
                 }
             }
@@ -174,11 +177,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_const
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            const uint32_t idesc = idesc_bf16(TC_M, NT);
             int k = 0;
             bool ok = true;
             for (int it = 0; it < my_items && ok; ++it) {
                 const int b = it & 1;
+                const int item = (int)blockIdx.x + it * (int)gridDim.x;
+                const int nslot = a.tiles[item / MT].z;
+                // MMA width: the tile's slots rounded up to 16 (columns past them are never read)
+                const uint32_t idesc = idesc_bf16(TC_M, min(NT, max(16, (nslot + 15) & ~15)));
                 if (it >= 2 && !mbar_wait_bounded(acce + b, (unsigned)(((it >> 1) - 1) & 1))) {
                     atomicOr(a.err, timeout_err);
                     s_fail = 1;
@@ -211,8 +217,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_const
             // MMAs still in flight finish before TMEM is released (bounded)
             if (k > 0) mbar_wait_bounded(empty + (k - 1) % NS, (unsigned)(((k - 1) / NS) & 1), 1u << 16);
         }
-    } else if (warp < 6) {
-        // ------------------------------------------------------------ dequant (4 warps, 4 of the 8 * NP blocks each)
+    } else if (warp < 2 + TC_DQW) {
+        // ------------------------------------------------------------ dequant (8 warps, NP of the 8 * NP blocks each)
         const int dw = warp - 2;
         const int gq = lane >> 2, c = lane & 3;
         const uint32_t k128 = 0x43004300u;
@@ -229,27 +235,40 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_const
                 unsigned char *st = tsm + (size_t)s * L::STAGE;
                 const unsigned char *q = st + L::NP * L::A_BYTES + L::X_BYTES;
 #pragma unroll
-                for (int j = 0; j < 2 * L::NP; ++j) {
-                    const int blk = dw + 4 * j;  // (projection, row block)
+                for (int j = 0; j < L::NP; ++j) {
+                    const int blk = dw + TC_DQW * j;  // (projection, row block)
                     const int p = blk >> 3, rb = blk & 7;
                     const uint4 w = reinterpret_cast<const uint4 *>(q + p * L::Q_BYTES + rb * 512)[lane];
-                    const uint32_t *sbw = reinterpret_cast<const uint32_t *>(q + L::NP * L::Q_BYTES + p * L::S_BYTES + rb * 64);
+                    const uint32_t *sbw = reinterpret_cast<const uint32_t *>(q + L::NP * L::Q_BYTES + p * L::S_BYTES + rb * L::SBG);
                     unsigned char *A = st + p * L::A_BYTES;
 #pragma unroll
                     for (int hf = 0; hf < 2; ++hf) {  // rows gq (words .x .y) and gq + 8 (words .z .w)
-                        const uint32_t sbv = sbw[gq * 2 + hf];
-                        const uint32_t s2 = (sbv & 0xFFFFu) | (sbv << 16), b2 = (sbv >> 16) | (sbv & 0xFFFF0000u);
                         const int r = rb * 16 + gq + 8 * hf;
                         const uint32_t wa = hf ? w.z : w.x, wb = hf ? w.w : w.y;
                         uint32_t out[8];
+                        if (FMT == FMT_FP4) {
+                            // E2M1 * 2^(S-127) is exact in bf16; elements 16c .. 16c+15 share the scale of half c / 2
+                            const uint32_t S = (sbw[gq] >> (8 * (hf * 2 + (c >> 1)))) & 0xFFu;
+                            uint32_t lo[4], hi[4];
+                            fp4_word(wa, fp4_scale2(S), lo);
+                            fp4_word(wb, fp4_scale2(S), hi);
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const uint32_t v = q4pair(i < 4 ? wa : wb, i & 3);  // (128 + q_2p, 128 + q_2p+1)
-                            __nv_bfloat162 qv = *reinterpret_cast<const __nv_bfloat162 *>(&v);
-                            qv = __hsub2(qv, *reinterpret_cast<const __nv_bfloat162 *>(&k128));
-                            const __nv_bfloat162 r2 = __hfma2(qv, *reinterpret_cast<const __nv_bfloat162 *>(&s2),
-                                                              *reinterpret_cast<const __nv_bfloat162 *>(&b2));
-                            out[i] = *reinterpret_cast<const uint32_t *>(&r2);
+                            for (int i = 0; i < 4; ++i) {
+                                out[i] = lo[i];
+                                out[4 + i] = hi[i];
+                            }
+                        } else {
+                            const uint32_t sbv = sbw[gq * 2 + hf];
+                            const uint32_t s2 = (sbv & 0xFFFFu) | (sbv << 16), b2 = (sbv >> 16) | (sbv & 0xFFFF0000u);
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                const uint32_t v = q4pair(i < 4 ? wa : wb, i & 3);  // (128 + q_2p, 128 + q_2p+1)
+                                __nv_bfloat162 qv = *reinterpret_cast<const __nv_bfloat162 *>(&v);
+                                qv = __hsub2(qv, *reinterpret_cast<const __nv_bfloat162 *>(&k128));
+                                const __nv_bfloat162 r2 = __hfma2(qv, *reinterpret_cast<const __nv_bfloat162 *>(&s2),
+                                                                  *reinterpret_cast<const __nv_bfloat162 *>(&b2));
+                                out[i] = *reinterpret_cast<const uint32_t *>(&r2);
+                            }
                         }
                         // elements 16c .. 16c+15 of row r = chunks 2c, 2c+1 (16 B each), swizzled by r % 8
                         uint4 *row = reinterpret_cast<uint4 *>(A + r * 128);
@@ -264,7 +283,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_const
             if (!ok) break;
         }
     } else {
-        // ------------------------------------------------------------ epilogue (warps 6..9: rows 32 * (warp % 4) + lane)
+        // ------------------------------------------------------------ epilogue (warps 10..13: rows 32 * (warp % 4) + lane)
         const int quarter = warp & 3;
         for (int it = 0; it < my_items && !*reinterpret_cast<volatile int *>(&s_fail); ++it) {
             const int item = (int)blockIdx.x + it * (int)gridDim.x;
@@ -281,7 +300,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_const
             const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16);
             if (!DOWN) {
                 const float bgr = a.bg ? a.bg[(size_t)e * a.f + row] : 0.f, bur = a.bu ? a.bu[(size_t)e * a.f + row] : 0.f;
-                for (int c0 = 0; c0 < NT; c0 += 16) {
+                for (int c0 = 0; c0 < tr.z; c0 += 16) {
                     float gv[16], uv[16];
                     tmem_ld16(tl + (uint32_t)((b * 2 + 0) * NT + c0), gv);
                     tmem_ld16(tl + (uint32_t)((b * 2 + 1) * NT + c0), uv);
@@ -293,7 +312,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_const
                 }
             } else {
                 const float bdr = a.bd ? a.bd[(size_t)e * a.d + row] : 0.f;
-                for (int c0 = 0; c0 < NT; c0 += 16) {
+                for (int c0 = 0; c0 < tr.z; c0 += 16) {
                     float dv[16];
                     tmem_ld16(tl + (uint32_t)(b * NT + c0), dv);
 #pragma unroll
@@ -322,9 +341,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_const
     }
 }
 
-size_t experts_tc_smem(int nt, int ns, bool down) {
-    const int np = down ? 1 : 2;
-    const size_t raw = (size_t)np * TC_M * 128 + (size_t)nt * 128 + (size_t)np * (8 * 512 + 8 * 64);
+size_t experts_tc_smem(int nt, int ns, bool down, int fmt) {
+    const int np = down ? 1 : 2, sbg = fmt == FMT_FP4 ? 32 : 64;
+    const size_t raw = (size_t)np * TC_M * 128 + (size_t)nt * 128 + (size_t)np * (8 * 512 + 8 * sbg);
     const size_t stage = (raw + 1023) / 1024 * 1024;
     return 1024 /* alignment slack */ + ns * stage + (3 * ns + 4) * 8;
 }
@@ -341,7 +360,9 @@ __global__ void __launch_bounds__(256) k_gather_rows(const uint16_t *__restrict_
     for (int c = lane; c < d / 8; c += 32) dst[c] = src[c];
 }
 
-template __global__ void k_experts_tc<128, 3, false>(const __grid_constant__ ExpArgs);
-template __global__ void k_experts_tc<128, 4, true>(const __grid_constant__ ExpArgs);
+template __global__ void k_experts_tc<FMT_Q4, 128, 3, false>(const __grid_constant__ ExpArgs);
+template __global__ void k_experts_tc<FMT_Q4, 128, 4, true>(const __grid_constant__ ExpArgs);
+template __global__ void k_experts_tc<FMT_FP4, 128, 3, false>(const __grid_constant__ ExpArgs);
+template __global__ void k_experts_tc<FMT_FP4, 128, 4, true>(const __grid_constant__ ExpArgs);
 
 }  // namespace moeb

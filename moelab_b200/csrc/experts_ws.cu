@@ -18,12 +18,13 @@
 
 namespace moeb {
 
-template <int NT8, int RBC, int SG, bool DOWN>
+template <int FMT, int NT8, int RBC, int SG, bool DOWN>
 struct WSL {
     static constexpr int NP = DOWN ? 1 : 2;
     static constexpr int COLS = 8 * NT8;
+    static constexpr int SBG = FMT == FMT_FP4 ? 32 : 64;  // scale bytes per (row block, group)
     static constexpr int W_BYTES = NP * RBC * SG * 512;
-    static constexpr int SB_BYTES = NP * RBC * SG * 64;
+    static constexpr int SB_BYTES = NP * RBC * SG * SBG;
     static constexpr int X_ROW = SG * 128 + 16;
     static constexpr int X_BYTES = COLS * X_ROW;
     // group sums: down 16 bytes per group; gate/up 4 bytes per group, copied from the 16-byte boundary at or
@@ -32,9 +33,17 @@ struct WSL {
     static constexpr int S_ROW = DOWN ? SG * 16 + 16 : (SG % 4 == 0 ? SG * 4 : ((SG + 3) * 4 + 15) / 16 * 16);
     static constexpr int S_BYTES = COLS * S_ROW;
     static constexpr int STAGE = W_BYTES + SB_BYTES + X_BYTES + S_BYTES;
-    static_assert(STAGE % 128 == 0 && W_BYTES % 128 == 0 && SB_BYTES % 128 == 0 && (RBC * SG * 64) % 128 == 0,
+    static_assert(STAGE % 128 == 0 && W_BYTES % 128 == 0 && SB_BYTES % 128 == 0 && (RBC * SG * SBG) % 128 == 0,
                   "tensor-copy destinations must stay 128-byte aligned");
 };
+
+// This lane's scale words of one (row block, group) in a stage: int4 {scale|bias row gq, row gq+8}; MXFP4 the
+// 4 E8M0 bytes of rows gq, gq+8 in .x
+template <int FMT>
+MOEB_DEV uint2 stage_scales(const unsigned char *p, int gq) {
+    if (FMT == FMT_FP4) return make_uint2(reinterpret_cast<const uint32_t *>(p)[gq], 0u);
+    return reinterpret_cast<const uint2 *>(p)[gq];
+}
 
 MOEB_DEV void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -42,7 +51,7 @@ MOEB_DEV void mbar_arrive(uint64_t *bar) {
 
 template <int FMT, int NT8, int RBC, int SG, int NS, bool DOWN, int MB>
 __global__ void __launch_bounds__(32 * (RBC + 1), MB) k_experts_ws(const __grid_constant__ ExpArgs a) {
-    using L = WSL<NT8, RBC, SG, DOWN>;
+    using L = WSL<FMT, NT8, RBC, SG, DOWN>;
     pdl_launch();
     pdl_wait();
     extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -133,13 +142,14 @@ __global__ void __launch_bounds__(32 * (RBC + 1), MB) k_experts_ws(const __grid_
             const int sum_bytes = DOWN ? ng * 16 : ((g0 + ng - ga + 3) / 4) * 16;
             // a tensor copy always delivers its whole box (rows or groups past the end arrive as zeros)
             if (lane == 0)
-                mbar_expect_tx(full + slot, (unsigned)(L::NP * RBC * SG * (512 + 64) + ncol * (ng * 128 + sum_bytes)));
+                mbar_expect_tx(full + slot, (unsigned)(L::NP * RBC * SG * (512 + L::SBG) + ncol * (ng * 128 + sum_bytes)));
             __syncwarp();
             unsigned char *st = smem_raw + (size_t)slot * L::STAGE;
             if (lane == 0) {
                 for (int p = 0; p < L::NP; ++p) {
                     tma_load_2d(st + p * RBC * SG * 512, &a.tmq[m0 + p], g0 * 64, row0, full + slot, pol);
-                    tma_load_2d(st + L::W_BYTES + p * RBC * SG * 64, &a.tmsb[m0 + p], g0 * 16, row0, full + slot, pol);
+                    tma_load_2d(st + L::W_BYTES + p * RBC * SG * L::SBG, &a.tmsb[m0 + p], g0 * (L::SBG / 4), row0,
+                                full + slot, pol);
                 }
             } else if (src0 != nullptr) {
                 tma_load_1d(st + L::W_BYTES + L::SB_BYTES + col * L::X_ROW, src0 + (size_t)g0 * 128, ng * 128,
@@ -200,7 +210,7 @@ __global__ void __launch_bounds__(32 * (RBC + 1), MB) k_experts_ws(const __grid_
 #pragma unroll
                         for (int hf = 0; hf < 2; ++hf) {
                             const int cc = j * 8 + 2 * c + hf;
-                            if (cc < ti.n) {
+                            if (FMT == FMT_Q4 && cc < ti.n) {  // group sums: int4 promotion only
                                 if (DOWN) {
                                     const float4 v = *reinterpret_cast<const float4 *>(ss + cc * L::S_ROW + i * 16);
                                     sx[j][hf] = (v.x + v.y) + (v.z + v.w);
@@ -213,13 +223,11 @@ __global__ void __launch_bounds__(32 * (RBC + 1), MB) k_experts_ws(const __grid_
                         }
                     }
                     const uint4 w0 = reinterpret_cast<const uint4 *>(st + (warp * SG + i) * 512)[lane];
-                    const uint2 b0 = reinterpret_cast<const uint2 *>(st + L::W_BYTES + (warp * SG + i) * 64)[gq];
-                    q4_group<NT8>(w0, b0, xb, sx, C0);
+                    wgroup<FMT, NT8>(w0, stage_scales<FMT>(st + L::W_BYTES + (warp * SG + i) * L::SBG, gq), c, xb, sx, C0);
                     if (!DOWN) {
                         const uint4 w1 = reinterpret_cast<const uint4 *>(st + ((RBC + warp) * SG + i) * 512)[lane];
-                        const uint2 b1 =
-                            reinterpret_cast<const uint2 *>(st + L::W_BYTES + ((RBC + warp) * SG + i) * 64)[gq];
-                        q4_group<NT8>(w1, b1, xb, sx, C1);
+                        wgroup<FMT, NT8>(w1, stage_scales<FMT>(st + L::W_BYTES + ((RBC + warp) * SG + i) * L::SBG, gq),
+                                         c, xb, sx, C1);
                     }
                 }
             }
@@ -241,18 +249,21 @@ __global__ void __launch_bounds__(32 * (RBC + 1), MB) k_experts_ws(const __grid_
     }
 }
 
-size_t experts_ws_smem(int nt8, int rbc, int sg, int ns, bool down) {
-    const int np = down ? 1 : 2, cols = 8 * nt8;
+size_t experts_ws_smem(int nt8, int rbc, int sg, int ns, bool down, int fmt) {
+    const int np = down ? 1 : 2, cols = 8 * nt8, sbg = fmt == FMT_FP4 ? 32 : 64;
     const int s_row = down ? sg * 16 + 16 : (sg % 4 == 0 ? sg * 4 : ((sg + 3) * 4 + 15) / 16 * 16);
-    const size_t stage = (size_t)np * rbc * sg * (512 + 64) + (size_t)cols * (sg * 128 + 16) + (size_t)cols * s_row;
+    const size_t stage = (size_t)np * rbc * sg * (512 + sbg) + (size_t)cols * (sg * 128 + 16) + (size_t)cols * s_row;
     return ns * stage + 2 * ns * 8;
 }
 
 // gate/up: 4 groups per stage, 2 stages, 2 CTAs per SM; down: 4 groups per stage, 4 stages, 2 CTAs per SM
 // (measured best of the (SG, NS, CTAs/SM) sweep on the Qwen3-30B shape at T = 4, 32, 256)
-template __global__ void k_experts_ws<FMT_Q4, 1, 8, 4, 2, false, 2>(const __grid_constant__ ExpArgs);
-template __global__ void k_experts_ws<FMT_Q4, 2, 8, 4, 2, false, 2>(const __grid_constant__ ExpArgs);
-template __global__ void k_experts_ws<FMT_Q4, 1, 8, 4, 4, true, 2>(const __grid_constant__ ExpArgs);
-template __global__ void k_experts_ws<FMT_Q4, 2, 8, 4, 4, true, 2>(const __grid_constant__ ExpArgs);
+#define MOEB_WS(FMT)                                                                         \
+    template __global__ void k_experts_ws<FMT, 1, 8, 4, 2, false, 2>(const __grid_constant__ ExpArgs); \
+    template __global__ void k_experts_ws<FMT, 2, 8, 4, 2, false, 2>(const __grid_constant__ ExpArgs); \
+    template __global__ void k_experts_ws<FMT, 1, 8, 4, 4, true, 2>(const __grid_constant__ ExpArgs);  \
+    template __global__ void k_experts_ws<FMT, 2, 8, 4, 4, true, 2>(const __grid_constant__ ExpArgs);
+MOEB_WS(FMT_Q4)
+MOEB_WS(FMT_FP4)
 
 }  // namespace moeb

@@ -182,6 +182,17 @@ def test_tc_mixtral(mixtral, routing, T):
     assert_close(y, torch_ref(b200_q4_moe, st, x, it, wt, deq), what=(routing, T))
 
 
+@pytest.mark.parametrize("T", [256, 1024])
+def test_tc_mixtral_mxfp4(mixtral, T):
+    st, deq = mixtral[0]["mxfp4"], mixtral[1]["mxfp4"]
+    idx, wts = make_routing(T, 8, 2, "uniform", np.random.default_rng(T))
+    x = torch.randn(T, 4096, generator=torch.Generator(device="cuda").manual_seed(T), device="cuda").to(torch.bfloat16)
+    it, wt = torch.from_numpy(idx).cuda(), torch.from_numpy(wts).cuda()
+    b200_mxfp4_moe._ws(st, 2)
+    y = ops.experts(st, x, it, wt, policy=ops.POLICY_TC)
+    assert_close(y, torch_ref(b200_mxfp4_moe, st, x, it, wt, deq), what=T)
+
+
 def test_tc_rejects_unsupported_shapes():
     from moelab_b200.shapes import MoEShape
     from helpers import problem_tensors

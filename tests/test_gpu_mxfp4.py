@@ -14,7 +14,8 @@ from moelab_b200.shapes import MoEShape
 pytestmark = pytest.mark.gpu
 FP4 = ROOT + "/moelab_b200/variants/cuda/b200_mxfp4_moe.py"
 GPTOSS = ROOT + "/moelab_b200/variants/cuda/b200_mxfp4_gptoss.py"
-POLICIES = {"auto": None, "slots": ops.POLICY_SLOTS, "tiles8": ops.POLICY_TILES8, "tiles16": ops.POLICY_TILES16}
+POLICIES = {"auto": None, "slots": ops.POLICY_SLOTS, "tiles8": ops.POLICY_TILES8, "tiles16": ops.POLICY_TILES16,
+            "tiles8ring": ops.POLICY_TILES8_RING, "tiles16ring": ops.POLICY_TILES16_RING}
 
 
 @pytest.fixture(scope="module")
@@ -135,3 +136,46 @@ def test_gptoss20b_shape_layer(gmod, T):
     ri, _ = oracle.router(x, gate, sh.k, bias=gb)
     np.testing.assert_array_equal(idx.cpu().numpy(), ri)
     assert_close(y, ref_from_state(gmod, st, x, idx, wts, act=2, bg=b[0], bu=b[1], bd=b[2]), what=T)
+
+
+# ------------------------------------------------------------------ tensor-core policy (tcgen05), MXFP4
+@pytest.mark.parametrize("T,routing", [(1, "uniform"), (9, "uniform"), (200, "uniform"), (300, "one_hot"),
+                                       (513, "zipf")])
+def test_tc_mxfp4_vs_oracle(mod, T, routing):
+    """E2M1 * E8M0 decoded exactly into the swizzled UMMA tiles; tiles of up to 128 slots."""
+    sh = MoEShape("tc", d=256, f=384, E=8, k=2)
+    p, w, x, idx, wts = problem_tensors(sh, T, routing, seed=T)
+    st = mod.prepare(*w)
+    mod._ws(st, sh.k)
+    y = ops.experts(st, x, idx, wts, policy=ops.POLICY_TC)
+    assert_close(y, ref_from_state(mod, st, x, idx, wts), what=(T, routing))
+
+
+@pytest.mark.parametrize("T", [64, 300])
+def test_tc_mxfp4_large_scales(mod, T):
+    sh = MoEShape("big-scales", d=256, f=256, E=8, k=2)
+    p, w, x, idx, wts = problem_tensors(sh, T, seed=T)
+    w = [(t.float() * 256).to(torch.bfloat16) for t in w]
+    x = (x.float() / 256).to(torch.bfloat16)
+    st = mod.prepare(*w)
+    mod._ws(st, sh.k)
+    y = ops.experts(st, x, idx, wts, policy=ops.POLICY_TC)
+    assert_close(y, ref_from_state(mod, st, x, idx, wts))
+
+
+def test_tc_gptoss_epilogue():
+    """Biases + clamped SwiGLU in the tensor-core epilogue (d = f = 1152, multiples of 128)."""
+    g = load_variant(GPTOSS)
+    E, d, f, k, T = 8, 1152, 1152, 4, 256
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    mk = lambda *s, sc=0.02: (torch.randn(*s, generator=gen, device="cuda") * sc).to(torch.bfloat16)  # noqa: E731
+    w = [mk(E, f, d), mk(E, f, d), mk(E, d, f)]
+    b = (4 * torch.randn(E, f, generator=gen, device="cuda"), 4 * torch.randn(E, f, generator=gen, device="cuda"),
+         0.1 * torch.randn(E, d, generator=gen, device="cuda"))
+    st = g.state(*w, *b)
+    g._b._ws(st, k)
+    x = torch.randn(T, d, generator=gen, device="cuda").to(torch.bfloat16)
+    idx = torch.stack([torch.randperm(E, generator=gen, device="cuda")[:k] for _ in range(T)]).to(torch.int32)
+    wts = torch.rand(T, k, generator=gen, device="cuda")
+    y = ops.experts(st, x, idx, wts, act=2, policy=ops.POLICY_TC)
+    assert_close(y, ref_from_state(g, st, x, idx, wts, act=2, bg=b[0], bu=b[1], bd=b[2]))
