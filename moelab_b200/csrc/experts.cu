@@ -30,7 +30,7 @@ namespace moeb {
 // ================================================================== slot mode (decode)
 // One CTA per (slot, 16-row block); KS warps split the K groups; GPW groups per warp are loaded at once.
 template <int FMT, int KS, int GPW>
-__global__ void __launch_bounds__(32 * KS, 3) k_gate_up_slots(ExpArgs a) {
+__global__ void __launch_bounds__(32 * KS, FMT == FMT_FP4 ? 2 : 3) k_gate_up_slots(ExpArgs a) {
     pdl_launch();
     pdl_wait();
     extern __shared__ uint4 xs4[];  // the slot's x row, d bf16
@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(32 * KS, 3) k_gate_up_slots(ExpArgs a) {
 }
 
 template <int FMT, int KS, int GPW>
-__global__ void __launch_bounds__(32 * KS, 8) k_down_slots(ExpArgs a) {
+__global__ void __launch_bounds__(32 * KS, FMT == FMT_FP4 ? 4 : 8) k_down_slots(ExpArgs a) {
     pdl_launch();
     pdl_wait();
     extern __shared__ uint4 hs4[];  // the slot's h row (f bf16) followed by its f/16 block sums
