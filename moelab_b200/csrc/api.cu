@@ -142,7 +142,7 @@ int check_shape(int T, int d, int f, int E, int k) {
 // slots (T <= 2 at k = 8); above that the warp-specialized tensor-map pipeline beats the register tiles at
 // every load (T = 4: 50.8 vs 55.6 us, T = 32: 126 vs 145 us), with tiles of 8 slots up to load ~4 and tiles of
 // 16 at high load (T = 256, load 16: 291 vs 329 us).
-// From 64 slots per expert the tcgen05 kernels (tiles of 128, weights dequantized once per tile) win: Mixtral
+// From 64 slots per expert the tcgen05 kernels (tiles of 256, weights dequantized once per tile) win: Mixtral
 // T = 256 / 1024 / 4096: 0.58 / 1.36 / 4.39 ms vs 1.26 / 4.61 / 17.6 ms, Qwen3-235B T = 2048: 2.80 vs 4.12 ms
 // (they lose at 16 slots per expert: Qwen3-235B T = 256, 0.90 vs 0.71 ms).
 int choose_policy(int T, int E, int k, int d, int f) {
@@ -152,8 +152,13 @@ int choose_policy(int T, int E, int k, int d, int f) {
     return TK >= 8L * E ? MOEB_POLICY_TILES16_RING : MOEB_POLICY_TILES8_RING;
 }
 
-int nt_of(int policy) {
-    if (policy == MOEB_POLICY_TC) return 128;
+// tcgen05 tile size: 256 slots (weights dequantized once for up to 256 slots; gate/up has one accumulator set)
+// from 128 slots per expert on, else 128 (two accumulator sets overlap the epilogue). Measured: Mixtral T=256
+// (64 slots/expert) 467 vs 538 us; Mixtral T=4096 3.26 vs 3.75 ms; Qwen3-235B T=2048 2.43 vs 2.65 ms.
+int tc_nt(long TK, int E) { return TK >= 128L * E ? 256 : 128; }
+
+int nt_of(int policy, long TK, int E) {
+    if (policy == MOEB_POLICY_TC) return tc_nt(TK, E);
     return (policy == MOEB_POLICY_TILES16 || policy == MOEB_POLICY_TILES16_RING) ? 16 : 8;
 }
 bool is_tiles(int policy) { return policy >= MOEB_POLICY_TILES8 && policy <= MOEB_POLICY_TC; }
@@ -189,18 +194,21 @@ KLaunch ws_kernel(int fmt, int nt8, bool down) {
     return fmt == FMT_FP4 ? ws_kernel_fmt<FMT_FP4>(nt8, down) : ws_kernel_fmt<FMT_Q4>(nt8, down);
 }
 
-constexpr int TC_NT = 128, TC_NS_GU = 3, TC_NS_DN = 4;
-KLaunch tc_kernel(int fmt, bool down) {
-    void (*fn)(ExpArgs) = fmt == FMT_FP4 ? (down ? k_experts_tc<FMT_FP4, TC_NT, TC_NS_DN, true>
-                                                 : k_experts_tc<FMT_FP4, TC_NT, TC_NS_GU, false>)
-                                         : (down ? k_experts_tc<FMT_Q4, TC_NT, TC_NS_DN, true>
-                                                 : k_experts_tc<FMT_Q4, TC_NT, TC_NS_GU, false>);
-    return {fn, 448, experts_tc_smem(TC_NT, down ? TC_NS_DN : TC_NS_GU, down, fmt), false, 8, 1, true};
+// (tile, stages, accumulator sets): gate/up 128 -> (3, 2), 256 -> (3, 1); down 128 / 256 -> (4, 2)
+template <int FMT>
+void (*tc_fn(int nt, bool down))(ExpArgs) {
+    if (nt == 256) return down ? k_experts_tc<FMT, 256, 4, 2, true> : k_experts_tc<FMT, 256, 3, 1, false>;
+    return down ? k_experts_tc<FMT, 128, 4, 2, true> : k_experts_tc<FMT, 128, 3, 2, false>;
+}
+KLaunch tc_kernel(int fmt, int nt, bool down) {
+    void (*fn)(ExpArgs) = fmt == FMT_FP4 ? tc_fn<FMT_FP4>(nt, down) : tc_fn<FMT_Q4>(nt, down);
+    const int ns = down ? 4 : 3, acc = (down || nt == 128) ? 2 : 1;
+    return {fn, 448, experts_tc_smem(nt, ns, acc, down, fmt), false, 8, 1, true};
 }
 
 // Kernels per policy: TILES8 / TILES16 run the register-pipelined tile kernels, the *_RING policies the
 // warp-specialized tensor-map pipeline (faster on B200 for both projections, so the dispatcher picks it).
-ExpLaunch pick_kernels(int fmt, int policy, int d, int f) {
+ExpLaunch pick_kernels(int fmt, int policy, int d, int f, int nt) {
     const KLaunch none = {nullptr, 0, 0, false, 1, 0};
     if (fmt != FMT_Q4 && fmt != FMT_FP4) return {none, none};
     if (policy == MOEB_POLICY_SLOTS) {
@@ -212,7 +220,7 @@ ExpLaunch pick_kernels(int fmt, int policy, int d, int f) {
     }
     if (policy == MOEB_POLICY_TC) {
         if (d % 128 || f % 128) return {none, none};
-        return {tc_kernel(fmt, false), tc_kernel(fmt, true)};
+        return {tc_kernel(fmt, nt, false), tc_kernel(fmt, nt, true)};
     }
     if (policy == MOEB_POLICY_TILES16_RING) return {ws_kernel(fmt, 2, false), ws_kernel(fmt, 2, true)};
     if (policy == MOEB_POLICY_TILES8_RING) return {ws_kernel(fmt, 1, false), ws_kernel(fmt, 1, true)};
@@ -316,9 +324,9 @@ int grid_for(const KLaunch &k, long units) {
 int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaStream_t st,
                 void *const *ev) {
     const long TK = (long)a.T * a.k;
-    const int nt = nt_of(policy);
+    const int nt = nt_of(policy, TK, a.E);
     const long max_tiles = a.tile_mode ? std::min<long>(TK, (long)a.E + TK / nt) : TK;
-    ExpLaunch K = pick_kernels(fmt, policy, a.d, a.f);
+    ExpLaunch K = pick_kernels(fmt, policy, a.d, a.f, nt);
     if (!K.gu.fn) return fail(MOEB_EUNSUP, "format not supported%s");
     if (policy == MOEB_POLICY_SLOTS && (K.gu.smem > 48 * 1024 || K.dn.smem > 48 * 1024))
         return fail(MOEB_EINVAL, "d or f too large for the decode kernels%s");
@@ -343,14 +351,14 @@ int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaS
         if (launch(k_gather_rows, dim3((unsigned)((TK + 7) / 8)), dim3(256), 0, st, a.x, (const int *)a.sorted, (int)TK,
                    a.k, a.d, xs) != cudaSuccess)
             return check_launch("gather");
-        if (!encode_rows_map(&a.tmx, xs, TK, a.d, TC_NT)) return fail(MOEB_ELAUNCH, "tensor map encoding failed (x)%s");
+        if (!encode_rows_map(&a.tmx, xs, TK, a.d, nt)) return fail(MOEB_ELAUNCH, "tensor map encoding failed (x)%s");
     }
     {
         const long units = max_tiles * ((RBf + K.gu.rows - 1) / K.gu.rows);
         if (launch(K.gu.fn, dim3(grid_for(K.gu, units)), dim3(K.gu.threads), K.gu.smem, st, a) != cudaSuccess)
             return check_launch("gate_up");
     }
-    if (K.dn.tc && !encode_rows_map(&a.tmx, a.h, TK, a.f, TC_NT))
+    if (K.dn.tc && !encode_rows_map(&a.tmx, a.h, TK, a.f, nt))
         return fail(MOEB_ELAUNCH, "tensor map encoding failed (h)%s");
     if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[2]), st);
     // combine: fused into down (last arrival per (token, row block) sums the k slot rows), or a separate pass
@@ -400,7 +408,7 @@ int launch_router(const void *x, const void *wg, const void *bias, int T, int d,
     r.cnt_all = at<unsigned>(ws, L.cnt_all);
     r.err = at<unsigned>(ws, L.err);
     const bool tiles = is_tiles(policy);
-    r.NT = nt_of(policy);
+    r.NT = nt_of(policy, (long)T * (k + ns), E + ns);
     r.tiles = tiles ? at<int4>(ws, L.tiles) : nullptr;
     r.ntiles = at<int>(ws, L.ntiles);
     r.sorted = at<int>(ws, L.sorted);
@@ -595,7 +603,7 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
         }
         p.xsum = at<float>(ws, L.xsum);
         p.cnt_all = at<unsigned>(ws, L.cnt_all);
-        p.NT = nt_of(policy);
+        p.NT = nt_of(policy, (long)T * k, E);
         p.tiles = tiles ? at<int4>(ws, L.tiles) : nullptr;
         p.ntiles = at<int>(ws, L.ntiles);
         p.sorted = at<int>(ws, L.sorted);

@@ -1,5 +1,5 @@
 // Grouped expert kernels on the 5th-generation tensor cores (tcgen05, accumulators in TMEM), for high loads
-// (tiles of up to NT = 128 slots of one expert).
+// (tiles of up to NT = 256 slots of one expert: the weights are dequantized once per tile).
 //
 // A work item is (tile, 128 output rows). D[128 rows][NT slots] = W[128][K] . X[NT][K]^T accumulates in TMEM
 // (fp32, lane = row, column = slot). K streams through an NS-deep shared-memory ring, one 64-group per stage:
@@ -11,8 +11,9 @@
 //     (generic writes -> tensor-core reads) and one arrival per warp on the stage's "deq" mbarrier.
 //   warp 1 (MMA, one lane): waits "deq", issues 4 k-steps of tcgen05.mma (M = 128, N = the tile's slot count
 //     rounded up to 16, K = 16, bf16 x bf16 -> fp32) per projection, and tcgen05.commit frees the stage ("empty"); after the last group it commits the
-//     item's accumulator ("accf"). Two accumulator sets alternate between items, so the next item's MMAs run
-//     while the epilogue drains the previous one.
+//     item's accumulator ("accf"). With two accumulator sets (down) the next item's MMAs run while the epilogue
+//     drains the previous one; gate/up's two projections of 256 columns fill TMEM, so it has one set (the
+//     epilogue is a few percent of an item's K loop).
 //   warps 10..13 (epilogue): tcgen05.ld 16 columns at a time (warp w reads TMEM lanes 32*(w%4)..+31 = its rows);
 //     gate/up: bias + activation -> h in slot-sorted order; down: weight * (acc + bias) -> the slot's fp32 row
 //     for the separate combine pass. Then "acce" frees the accumulator set.
@@ -73,7 +74,7 @@ MOEB_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-template <int FMT, int NT, bool DOWN>
+template <int FMT, int NT, int ACC, bool DOWN>
 struct TCL {
     static constexpr int NP = DOWN ? 1 : 2;
     static constexpr int SBG = FMT == FMT_FP4 ? 32 : 64;  // scale bytes per (row block, group)
@@ -83,22 +84,22 @@ struct TCL {
     static constexpr int S_BYTES = 8 * SBG;            // int4 scale|bias words / MXFP4 E8M0 bytes
     static constexpr int STAGE_RAW = NP * A_BYTES + X_BYTES + NP * (Q_BYTES + S_BYTES);
     static constexpr int STAGE = (STAGE_RAW + 1023) / 1024 * 1024;
-    static constexpr int TMEM_COLS = 2 * NP * NT;      // two accumulator sets
+    static constexpr int TMEM_COLS = ACC * NP * NT;    // ACC accumulator sets
     static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation");
 };
 
 }  // namespace
 
-template <int FMT, int NT, int NS, bool DOWN>
+template <int FMT, int NT, int NS, int ACC, bool DOWN>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_constant__ ExpArgs a) {
-    using L = TCL<FMT, NT, DOWN>;
+    using L = TCL<FMT, NT, ACC, DOWN>;
     pdl_launch();
     pdl_wait();
     extern __shared__ __align__(1024) unsigned char tsm_raw[];
     // 1024-byte aligned base for the swizzled tiles
     unsigned char *tsm = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(tsm_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t *full = reinterpret_cast<uint64_t *>(tsm + (size_t)NS * L::STAGE);
-    uint64_t *deq = full + NS, *empty = deq + NS, *accf = empty + NS, *acce = accf + 2;
+    uint64_t *deq = full + NS, *empty = deq + NS, *accf = empty + NS, *acce = accf + ACC;
     __shared__ uint32_t s_tmem;
     __shared__ int s_fail;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -114,7 +115,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_const
             mbar_init(deq + i, TC_DQW);
             mbar_init(empty + i, 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < ACC; ++b) {
             mbar_init(accf + b, 1);
             mbar_init(acce + b, 4);
         }
@@ -180,12 +181,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_const
             int k = 0;
             bool ok = true;
             for (int it = 0; it < my_items && ok; ++it) {
-                const int b = it & 1;
+                const int b = it % ACC, use = it / ACC;  // accumulator set and how often it was used before
                 const int item = (int)blockIdx.x + it * (int)gridDim.x;
                 const int nslot = a.tiles[item / MT].z;
                 // MMA width: the tile's slots rounded up to 16 (columns past them are never read)
                 const uint32_t idesc = idesc_bf16(TC_M, min(NT, max(16, (nslot + 15) & ~15)));
-                if (it >= 2 && !mbar_wait_bounded(acce + b, (unsigned)(((it >> 1) - 1) & 1))) {
+                if (use >= 1 && !mbar_wait_bounded(acce + b, (unsigned)((use - 1) & 1))) {
                     atomicOr(a.err, timeout_err);
                     s_fail = 1;
                     break;
@@ -290,8 +291,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_const
             const int tile = item / MT, mt = item - tile * MT;
             const int4 tr = a.tiles[tile];
             const int e = (tr.x < 0 || tr.x >= a.E) ? 0 : tr.x;
-            const int b = it & 1;
-            if (!mbar_wait_bounded(accf + b, (unsigned)((it >> 1) & 1))) {
+            const int b = it % ACC;
+            if (!mbar_wait_bounded(accf + b, (unsigned)((it / ACC) & 1))) {
                 if (lane == 0) atomicOr(a.err, timeout_err);
                 break;
             }
@@ -341,11 +342,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_const
     }
 }
 
-size_t experts_tc_smem(int nt, int ns, bool down, int fmt) {
+size_t experts_tc_smem(int nt, int ns, int acc, bool down, int fmt) {
+    (void)acc;
     const int np = down ? 1 : 2, sbg = fmt == FMT_FP4 ? 32 : 64;
     const size_t raw = (size_t)np * TC_M * 128 + (size_t)nt * 128 + (size_t)np * (8 * 512 + 8 * sbg);
     const size_t stage = (raw + 1023) / 1024 * 1024;
-    return 1024 /* alignment slack */ + ns * stage + (3 * ns + 4) * 8;
+    return 1024 /* alignment slack */ + ns * stage + (3 * ns + 2 * acc) * 8;
 }
 
 // x rows of the slots in expert-sorted order (the activation operand of the tensor-core gate/up)
@@ -360,9 +362,14 @@ __global__ void __launch_bounds__(256) k_gather_rows(const uint16_t *__restrict_
     for (int c = lane; c < d / 8; c += 32) dst[c] = src[c];
 }
 
-template __global__ void k_experts_tc<FMT_Q4, 128, 3, false>(const __grid_constant__ ExpArgs);
-template __global__ void k_experts_tc<FMT_Q4, 128, 4, true>(const __grid_constant__ ExpArgs);
-template __global__ void k_experts_tc<FMT_FP4, 128, 3, false>(const __grid_constant__ ExpArgs);
-template __global__ void k_experts_tc<FMT_FP4, 128, 4, true>(const __grid_constant__ ExpArgs);
+// gate/up: tiles of 256 slots with one accumulator set (2 x 256 TMEM columns) or of 128 with two; down: 4 stages,
+// two sets
+#define MOEB_TC(FMT)                                                                         \
+    template __global__ void k_experts_tc<FMT, 256, 3, 1, false>(const __grid_constant__ ExpArgs); \
+    template __global__ void k_experts_tc<FMT, 256, 4, 2, true>(const __grid_constant__ ExpArgs);  \
+    template __global__ void k_experts_tc<FMT, 128, 3, 2, false>(const __grid_constant__ ExpArgs); \
+    template __global__ void k_experts_tc<FMT, 128, 4, 2, true>(const __grid_constant__ ExpArgs);
+MOEB_TC(FMT_Q4)
+MOEB_TC(FMT_FP4)
 
 }  // namespace moeb

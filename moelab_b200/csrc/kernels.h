@@ -165,9 +165,9 @@ template <int FMT, int NT8, int GPW>
 __global__ void k_down_tiles_reg(ExpArgs a);
 template <int FMT, int NT8, int RBC, int SG, int NS, bool DOWN, int MB>
 __global__ void k_experts_ws(const __grid_constant__ ExpArgs a);
-template <int FMT, int NT, int NS, bool DOWN>
+template <int FMT, int NT, int NS, int ACC, bool DOWN>
 __global__ void k_experts_tc(const __grid_constant__ ExpArgs a);
-size_t experts_tc_smem(int nt, int ns, bool down, int fmt);
+size_t experts_tc_smem(int nt, int ns, int acc, bool down, int fmt);
 __global__ void k_gather_rows(const uint16_t *x, const int *sorted, int TK, int k, int d, uint16_t *xs);
 size_t experts_ws_smem(int nt8, int rbc, int sg, int ns, bool down, int fmt);
 
