@@ -12,6 +12,7 @@ LIB_PATH = os.path.join(HERE, "lib", "libmoelab_b200.so")
 MOEB_OK, MOEB_EINVAL, MOEB_ELAUNCH, MOEB_ETIMEOUT, MOEB_EUNSUP = 0, 1, 2, 3, 4
 POLICY_AUTO, POLICY_SLOTS, POLICY_TILES8, POLICY_TILES16, POLICY_TILES8_RING, POLICY_TILES16_RING = 0, 1, 2, 3, 4, 5
 POLICY_TC = 6
+POLICY_DECODE = 7
 DEVERR_EXPERT_ID, DEVERR_TIMEOUT = 1, 2
 
 _P = ctypes.c_void_p

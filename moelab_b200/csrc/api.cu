@@ -421,6 +421,43 @@ int launch_router(const void *x, const void *wg, const void *bias, int T, int d,
     return MOEB_OK;
 }
 
+// ------------------------------------------------------------------ fused decode (one cooperative kernel)
+template <int FMT>
+void (*decode_kernel(int E))(ExpArgs, RouterArgs, unsigned *) {
+    const int J = (E + 31) / 32;
+    if (J <= 1) return k_decode<FMT, 1>;
+    if (J <= 2) return k_decode<FMT, 2>;
+    if (J <= 4) return k_decode<FMT, 4>;
+    if (J <= 8) return k_decode<FMT, 8>;
+    if (J <= 16) return k_decode<FMT, 16>;
+    return k_decode<FMT, 32>;
+}
+
+int launch_decode(int fmt, const ExpArgs &a, const RouterArgs &r, unsigned *ctr, cudaStream_t st) {
+    void (*kern)(ExpArgs, RouterArgs, unsigned *) =
+        fmt == FMT_FP4 ? decode_kernel<FMT_FP4>(r.wg ? r.E : 1) : decode_kernel<FMT_Q4>(r.wg ? r.E : 1);
+    const size_t smem = decode_smem(a.d, a.f);
+    if (!allow_smem((const void *)kern, smem)) return check_launch("decode smem");
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 256, smem) != cudaSuccess || occ < 1)
+        return fail(MOEB_ELAUNCH, "decode kernel does not fit an SM%s");
+    // every CTA must be resident at once (phases hand over through counters): at most occ per SM
+    const long units = std::max<long>((long)a.T * a.k * std::max(a.f, a.d) / 16, r.wg ? (r.E + 7) / 8 : 1);
+    const int grid = (int)std::max<long>(1, std::min<long>((long)occ * sm_count(), units));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, a, r, ctr) != cudaSuccess) return check_launch("decode");
+    return MOEB_OK;
+}
+
 }  // namespace
 
 namespace moeb {
@@ -571,12 +608,20 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
         policy = choose_policy(T, E, k, d, f);
         if (policy == MOEB_POLICY_TC && ep) policy = MOEB_POLICY_TILES16_RING;
     }
-    if (policy != MOEB_POLICY_SLOTS && !is_tiles(policy)) return fail(MOEB_EINVAL, "unknown policy%s");
+    if (policy == MOEB_POLICY_DECODE && (ep || (long)T * k > 16)) policy = MOEB_POLICY_SLOTS;  // decode only
+    if (policy != MOEB_POLICY_SLOTS && policy != MOEB_POLICY_DECODE && !is_tiles(policy))
+        return fail(MOEB_EINVAL, "unknown policy%s");
     if (policy == MOEB_POLICY_TC && (d % 128 || f % 128 || ep))
         return fail(MOEB_EINVAL, "the tensor-core policy needs d, f multiples of 128%s");
-    const bool tiles = policy != MOEB_POLICY_SLOTS;
+    const bool fused = policy == MOEB_POLICY_DECODE;
+    const bool tiles = policy != MOEB_POLICY_SLOTS && !fused;
     if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[0]), st);
-    if (gate_w) {  // layer call: router produces ids, weights, x group sums and (tile mode) the tiles
+    if (fused) {  // the single decode kernel routes (or checks the given ids) itself
+        if (gate_w) {
+            idx = idx_out ? idx_out : at<int>(ws, L.idx);
+            wts = wts_out ? wts_out : at<float>(ws, L.wts);
+        }
+    } else if (gate_w) {  // layer call: router produces ids, weights, x group sums and (tile mode) the tiles
         int *ri = idx_out ? idx_out : at<int>(ws, L.idx);
         float *rw = wts_out ? wts_out : at<float>(ws, L.wts);
         // E, k count the ns shared experts / slots; the router picks among the E - ns routed experts
@@ -648,6 +693,24 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
         const double U = std::min<double>(E, (double)T * k);
         const double layer_bytes = U * 3.0 * d * f * (fmt == FMT_FP4 ? 4.25 : 4.5) / 8.0;
         a.dn_prefetch = layer_bytes < 48.0 * (1 << 20) ? 1 : 0;
+    }
+    if (fused) {
+        RouterArgs r = {};
+        if (gate_w) {
+            r.x = static_cast<const uint16_t *>(x);
+            r.wg = static_cast<const uint16_t *>(gate_w);
+            r.bias = static_cast<const uint16_t *>(gate_b);
+            r.T = T; r.d = d; r.E = E - ns; r.k = k - ns; r.norm = norm; r.ns = ns; r.scale = rscale;
+            r.logits = at<float>(ws, L.logits);
+            r.idx = const_cast<int *>(idx);
+            r.wts = const_cast<float *>(wts);
+            r.xsum = at<float>(ws, L.xsum);
+            r.err = at<unsigned>(ws, L.err);
+        }
+        rc = launch_decode(fmt, a, r, at<unsigned>(ws, L.cnt_all), st);
+        if (ev)
+            for (int i = 1; i < 4; ++i) cudaEventRecord(static_cast<cudaEvent_t>(ev[i]), st);
+        return rc;
     }
     return run_experts(fmt, a, policy, L, ws, st, ev);
 }

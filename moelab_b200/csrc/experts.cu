@@ -23,84 +23,21 @@
 // down + combine (DOWN_SRC metal_q4_decode_v4.py:95-144, DOWN_E_SRC + COMBINE_SRC metal_q4_tiles_v2.py):
 //   yp[slot][r] = w_slot * (Wd h + bd); the last unit to finish a (token, 16-row block) sums its k slots in
 //   fixed order j = 0..k-1 (deterministic, no float atomics), adds the optional residual and writes y.
-#include "experts_common.cuh"
+#include "slots_common.cuh"
 
 namespace moeb {
 
 // ================================================================== slot mode (decode)
-// One CTA per (slot, 16-row block); KS warps split the K groups; GPW groups per warp are loaded at once.
+// One CTA per (slot, 16-row block); KS warps split the K groups; GPW groups per warp are loaded at once. The unit
+// bodies live in slots_common.cuh (shared with the fused decode kernel).
 template <int FMT, int KS, int GPW>
 __global__ void __launch_bounds__(32 * KS, FMT == FMT_FP4 ? 2 : 3) k_gate_up_slots(ExpArgs a) {
     pdl_launch();
     pdl_wait();
     extern __shared__ uint4 xs4[];  // the slot's x row, d bf16
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int gq = lane >> 2, c = lane & 3;
-    const int d = a.d, f = a.f;
-    const int RB = f >> 4, G = d >> 6;
-    const int g_beg = warp * G / KS, g_end = (warp + 1) * G / KS;
-    __shared__ float red[KS][2][4][32];
-    const uint16_t *xs = reinterpret_cast<const uint16_t *>(xs4);
-    for (int unit = blockIdx.x; unit < a.T * a.k * RB; unit += gridDim.x) {
-        const int slot = unit / RB, rb = unit - slot * RB;
-        const TileInfo ti = tile_info(a, slot);
-        const size_t blk = (size_t)ti.e * RB + rb;
-        if (warp == KS - 1 && a.dn_prefetch) prefetch_down(a, ti.e, rb, RB, lane);
-        const uint4 *xsrc = reinterpret_cast<const uint4 *>(a.x + (size_t)(slot / a.k) * a.xs);
-        for (int i = threadIdx.x; i < d / 8; i += 32 * KS) xs4[i] = xsrc[i];
-        const float *sxr = a.xsum + (size_t)(slot / a.k) * xsum_stride(d);
-        float Cg[1][4] = {{0.f, 0.f, 0.f, 0.f}}, Cu[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-        bool synced = false;
-        for (int g0 = g_beg; g0 < g_end; g0 += GPW) {
-            uint4 wg[GPW], wu[GPW];
-            uint2 bg[GPW], bu[GPW];
-#pragma unroll
-            for (int i = 0; i < GPW; ++i) {
-                const int g = min(g0 + i, g_end - 1);  // clamped: a repeated load, never used
-                wg[i] = ld_w(a.g, blk, G, g, lane);
-                wu[i] = ld_w(a.u, blk, G, g, lane);
-                bg[i] = ld_scales<FMT>(a.g, blk, G, g, gq);
-                bu[i] = ld_scales<FMT>(a.u, blk, G, g, gq);
-            }
-            if (!synced) {
-                __syncthreads();  // x row staged (weights already in flight)
-                synced = true;
-            }
-#pragma unroll
-            for (int i = 0; i < GPW; ++i) {
-                if (g0 + i < g_end) {
-                    const int g = g0 + i;
-                    uint32_t xb[1][8];
-                    load_b16(gq == 0 ? xs + g * 64 + 16 * c : nullptr, xb[0]);
-                    const float sx[1][2] = {{c == 0 ? sxr[g] : 0.f, 0.f}};
-                    wgroup<FMT, 1>(wg[i], bg[i], c, xb, sx, Cg);
-                    wgroup<FMT, 1>(wu[i], bu[i], c, xb, sx, Cu);
-                }
-            }
-        }
-        if (!synced) __syncthreads();
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            red[warp][0][i][lane] = Cg[0][i];
-            red[warp][1][i][lane] = Cu[0][i];
-        }
-        __syncthreads();
-        if (warp == 0) {
-            float gs[4], us[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                gs[i] = red[0][0][i][lane];
-                us[i] = red[0][1][i][lane];
-#pragma unroll
-                for (int w = 1; w < KS; ++w) {
-                    gs[i] += red[w][0][i][lane];
-                    us[i] += red[w][1][i][lane];
-                }
-            }
-            gate_up_store<1>(a, ti, rb, 0, gs, us, lane);
-        }
-        __syncthreads();
-    }
+    __shared__ float red[KS * 2 * 4 * 32];
+    for (int unit = blockIdx.x; unit < a.T * a.k * (a.f >> 4); unit += gridDim.x)
+        gate_up_slot_unit<FMT, KS, GPW>(a, unit, xs4, red);
 }
 
 template <int FMT, int KS, int GPW>
@@ -108,65 +45,9 @@ __global__ void __launch_bounds__(32 * KS, FMT == FMT_FP4 ? 4 : 8) k_down_slots(
     pdl_launch();
     pdl_wait();
     extern __shared__ uint4 hs4[];  // the slot's h row (f bf16) followed by its f/16 block sums
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int gq = lane >> 2, c = lane & 3;
-    const int d = a.d, f = a.f;
-    const int RB = d >> 4, G = f >> 6;
-    const int g_beg = warp * G / KS, g_end = (warp + 1) * G / KS;
-    __shared__ float red[KS][4][32];
-    const uint16_t *hs = reinterpret_cast<const uint16_t *>(hs4);
-    const float *hsum_s = reinterpret_cast<const float *>(hs4 + f / 8);
-    for (int unit = blockIdx.x; unit < a.T * a.k * RB; unit += gridDim.x) {
-        const int slot = unit / RB, rb = unit - slot * RB;
-        const TileInfo ti = tile_info(a, slot);
-        const size_t blk = (size_t)ti.e * RB + rb;
-        const uint4 *hsrc = reinterpret_cast<const uint4 *>(a.h + (size_t)slot * f);
-        for (int i = threadIdx.x; i < f / 8; i += 32 * KS) hs4[i] = hsrc[i];
-        const uint4 *ssrc = reinterpret_cast<const uint4 *>(a.hsum + (size_t)slot * (f / 16));
-        for (int i = threadIdx.x; i < f / 64; i += 32 * KS) hs4[f / 8 + i] = ssrc[i];
-        float C[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-        bool synced = false;
-        for (int g0 = g_beg; g0 < g_end; g0 += GPW) {
-            uint4 w[GPW];
-            uint2 b[GPW];
-#pragma unroll
-            for (int i = 0; i < GPW; ++i) {
-                const int g = min(g0 + i, g_end - 1);
-                w[i] = ld_w(a.dn, blk, G, g, lane);
-                b[i] = ld_scales<FMT>(a.dn, blk, G, g, gq);
-            }
-            if (!synced) {
-                __syncthreads();
-                synced = true;
-            }
-#pragma unroll
-            for (int i = 0; i < GPW; ++i) {
-                if (g0 + i < g_end) {
-                    const int g = g0 + i;
-                    uint32_t hb[1][8];
-                    load_b16(gq == 0 ? hs + g * 64 + 16 * c : nullptr, hb[0]);
-                    const float4 v = *reinterpret_cast<const float4 *>(hsum_s + 4 * g);
-                    const float sx[1][2] = {{c == 0 ? (v.x + v.y) + (v.z + v.w) : 0.f, 0.f}};
-                    wgroup<FMT, 1>(w[i], b[i], c, hb, sx, C);
-                }
-            }
-        }
-        if (!synced) __syncthreads();
-#pragma unroll
-        for (int i = 0; i < 4; ++i) red[warp][i][lane] = C[0][i];
-        __syncthreads();
-        if (warp == 0) {
-            float cs[1][4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                cs[0][i] = red[0][i][lane];
-#pragma unroll
-                for (int w = 1; w < KS; ++w) cs[0][i] += red[w][i][lane];
-            }
-            down_store_combine<1>(a, ti, rb, cs, lane);
-        }
-        __syncthreads();
-    }
+    __shared__ float red[KS * 4 * 32];
+    for (int unit = blockIdx.x; unit < a.T * a.k * (a.d >> 4); unit += gridDim.x)
+        down_slot_unit<FMT, KS, GPW>(a, unit, hs4, red);
 }
 
 // ================================================================== tile mode, register pipeline

@@ -135,6 +135,9 @@ struct EPArgs {
 __global__ void k_ep_plan(EPArgs a);
 __global__ void k_ep_pack(EPArgs a);
 __global__ void k_combine(const float *yp, int T, int d, int k, const uint16_t *residual, uint16_t *y);
+template <int FMT, int JMAX>
+__global__ void k_decode(ExpArgs a, RouterArgs r, unsigned *ctr);
+size_t decode_smem(int d, int f);
 __global__ void k_ep_send(EPArgs a);
 __global__ void k_ep_signal(unsigned char *const *peers, unsigned char *self, int P, int C, int d, int me);
 __global__ void k_ep_combine_p2p(const unsigned char *self, const int *slot_pos, int P, int C, int T, int d, int k,
