@@ -405,7 +405,7 @@ def ep_steps(layers, xs, n, xch, k=K_TOP, k0=0):
     for i in range(n):
         st, gate = layers[(k0 + i) % len(layers)]
         x = xs[(k0 + i) % len(xs)]
-        y = ep.layer_p2p(st, x, gate, k, xch, residual=x)
+        y = ep.layer_p2p(st, x, gate, k, xch, residual=x, max_tokens=x.shape[0])  # every rank has T tokens
     return y
 
 
@@ -444,7 +444,7 @@ def ep_layer_bytes(layers, xs, n, xch, ws, d=D, f=F, k=K_TOP):
         U = int(torch.unique(mine).numel())
         R = int(mine.numel())
         total += U * 3 * d * f * W_BITS / 8 + R * (d + 8) * 2 + 2 * R * f * 2 + R * d * 4
-        ep.layer_p2p(st, x, gate, k, xch, residual=x)
+        ep.layer_p2p(st, x, gate, k, xch, residual=x, max_tokens=x.shape[0])
     return total / n
 
 
@@ -487,7 +487,7 @@ def run_ep(a, ws, rank, local, peaks):
         for i in range(4):
             xd = xh.to("cuda", non_blocking=True)
             st, gate = layers[i % len(layers)]
-            yh.copy_(ep.layer_p2p(st, xd, gate, K_TOP, xch, residual=xd), non_blocking=True)
+            yh.copy_(ep.layer_p2p(st, xd, gate, K_TOP, xch, residual=xd, max_tokens=T), non_blocking=True)
         torch.cuda.synchronize()
         barrier(ws)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -495,7 +495,7 @@ def run_ep(a, ws, rank, local, peaks):
         for i in range(a.e2e_steps):
             xd = xh.to("cuda", non_blocking=True)
             st, gate = layers[i % len(layers)]
-            yh.copy_(ep.layer_p2p(st, xd, gate, K_TOP, xch, residual=xd), non_blocking=True)
+            yh.copy_(ep.layer_p2p(st, xd, gate, K_TOP, xch, residual=xd, max_tokens=T), non_blocking=True)
         e1.record()
         e1.synchronize()
         torch.cuda.synchronize()

@@ -169,7 +169,9 @@ int moeb_ep_combine(const float *back, const int *slot_pos, int T, int d, int k,
  * at least the largest T*k of a call), allocated with moeb_ep_ipc_alloc and mapped into every other rank with
  * moeb_ep_ipc_handle / moeb_ep_ipc_open (CUDA IPC, plain peer mappings, no multicast). `peers` is a DEVICE array
  * of the P buffer addresses as seen by this rank (its own included), `self` its own buffer. Per layer call,
- * every rank issues, in this order on one stream:
+ * every rank issues, in this order on one stream (Cs = this call's rows per source block, 0 < Cs <= C, the same
+ * on every rank and at least every rank's T*k; Cs = 0 means C: a small Cs keeps the owners' scan of the blocks
+ * short for small calls):
  *   1. moeb_ep_p2p_dispatch: plan as moeb_ep_dispatch, then each slot's row + tail is stored straight into its
  *      owner's buffer (block `me`, row slot_pos % C); the owner's flag for this source is released with the
  *      call's epoch (a per-buffer counter every rank advances once per call). slot_pos [T*k] is in capacity
@@ -188,8 +190,9 @@ int moeb_ep_ipc_handle(void *ptr, void *handle /* 64 bytes */);
 int moeb_ep_ipc_open(const void *handle, void **ptr);
 int moeb_ep_ipc_close(void *ptr);
 int moeb_ep_p2p_dispatch(const void *x, const int *idx, const float *wts, int T, int d, int k, int E, int P, int me,
-                         int C, void *const *peers, void *self, int *send_counts, int *slot_pos, cudaStream_t stream);
-int moeb_ep_p2p_experts_q4(void *const *peers, void *self, int P, int me, int C, int d, int f, int E_local,
+                         int C, int Cs, void *const *peers, void *self, int *send_counts, int *slot_pos,
+                         cudaStream_t stream);
+int moeb_ep_p2p_experts_q4(void *const *peers, void *self, int P, int me, int C, int Cs, int d, int f, int E_local,
                            const void *qg, const void *sbg, const void *qu, const void *sbu, const void *qd,
                            const void *sbd, const float *bg, const float *bu, const float *bd, int act, int policy,
                            void *ws, size_t ws_bytes, cudaStream_t stream);

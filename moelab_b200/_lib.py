@@ -53,8 +53,8 @@ SIGNATURES = {
     "moeb_ep_ipc_handle": (_I, [_P, _P]),
     "moeb_ep_ipc_open": (_I, [_P, ctypes.POINTER(ctypes.c_void_p)]),
     "moeb_ep_ipc_close": (_I, [_P]),
-    "moeb_ep_p2p_dispatch": (_I, [_P, _P, _P] + [_I] * 7 + [_P, _P, _P, _P, _P]),
-    "moeb_ep_p2p_experts_q4": (_I, [_P, _P] + [_I] * 6 + [_P] * 9 + [_I, _I, _P, _S, _P]),
+    "moeb_ep_p2p_dispatch": (_I, [_P, _P, _P] + [_I] * 8 + [_P, _P, _P, _P, _P]),
+    "moeb_ep_p2p_experts_q4": (_I, [_P, _P] + [_I] * 7 + [_P] * 9 + [_I, _I, _P, _S, _P]),
     "moeb_ep_p2p_combine": (_I, [_P, _P] + [_I] * 5 + [_P, _P, _P]),
     "moeb_ep_p2p_read_error": (_I, [_P, _I, _I, _I, ctypes.POINTER(ctypes.c_uint), _P]),
 }

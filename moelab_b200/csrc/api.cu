@@ -580,7 +580,7 @@ struct P2PParams {
     const unsigned *rflag;
     const int *rcnt;
     const unsigned *epoch;
-    int C, me;
+    int C, me;  // C: this call's rows per source block
     unsigned char *const *peers;
     size_t yoff;
 };
@@ -855,10 +855,13 @@ int moeb_ep_ipc_close(void *ptr) {
 }
 
 int moeb_ep_p2p_dispatch(const void *x, const int *idx, const float *wts, int T, int d, int k, int E, int P, int me,
-                         int C, void *const *peers, void *self, int *send_counts, int *slot_pos, cudaStream_t st) {
+                         int C, int Cs, void *const *peers, void *self, int *send_counts, int *slot_pos,
+                         cudaStream_t st) {
     if (int rc = check_ep(T, d, k, E, P)) return rc;
     if (me < 0 || me >= P || !peers || !self) return fail(MOEB_EINVAL, "bad rank or exchange buffers%s");
-    if ((long)T * k > C) return fail(MOEB_EINVAL, "T*k exceeds the exchange capacity C%s");
+    if (Cs <= 0) Cs = C;
+    if (Cs > C) return fail(MOEB_EINVAL, "Cs exceeds the exchange capacity C%s");
+    if ((long)T * k > Cs) return fail(MOEB_EINVAL, "T*k exceeds the call's rows per source Cs%s");
     EPArgs a = {};
     a.x = static_cast<const uint16_t *>(x);
     a.idx = idx;
@@ -868,6 +871,7 @@ int moeb_ep_p2p_dispatch(const void *x, const int *idx, const float *wts, int T,
     a.slot_pos = slot_pos;
     a.err = reinterpret_cast<unsigned *>(static_cast<unsigned char *>(self) + p2p_layout(P, C, d).err);
     a.C = C;
+    a.Cs = Cs;
     a.me = me;
     a.peers = reinterpret_cast<unsigned char *const *>(peers);
     a.self = static_cast<unsigned char *>(self);
@@ -878,11 +882,12 @@ int moeb_ep_p2p_dispatch(const void *x, const int *idx, const float *wts, int T,
     return MOEB_OK;
 }
 
-static int p2p_experts(int fmt, void *const *peers, void *self, int P, int me, int C, int d, int f, int E_local,
-                       const void *qg, const void *sg, const void *qu, const void *su, const void *qd, const void *sd,
-                       const float *bg, const float *bu, const float *bd, int act, int policy, void *ws,
-                       size_t ws_bytes, cudaStream_t st) {
-    if (P < 1 || P > 32 || me < 0 || me >= P || C < 1 || !peers || !self)
+static int p2p_experts(int fmt, void *const *peers, void *self, int P, int me, int C, int Cs, int d, int f,
+                       int E_local, const void *qg, const void *sg, const void *qu, const void *su, const void *qd,
+                       const void *sd, const float *bg, const float *bu, const float *bd, int act, int policy,
+                       void *ws, size_t ws_bytes, cudaStream_t st) {
+    if (Cs <= 0) Cs = C;
+    if (P < 1 || P > 32 || me < 0 || me >= P || C < 1 || Cs > C || !peers || !self)
         return fail(MOEB_EINVAL, "bad exchange parameters%s");
     const P2PLayout L = p2p_layout(P, C, d);
     unsigned char *b = static_cast<unsigned char *>(self);
@@ -890,13 +895,19 @@ static int p2p_experts(int fmt, void *const *peers, void *self, int P, int me, i
     pp.rflag = reinterpret_cast<const unsigned *>(b + L.rflag);
     pp.rcnt = reinterpret_cast<const int *>(b + L.rcnt);
     pp.epoch = reinterpret_cast<const unsigned *>(b + L.epoch);
-    pp.C = C;
+    pp.C = Cs;
     pp.me = me;
     pp.peers = reinterpret_cast<unsigned char *const *>(peers);
     pp.yoff = L.back;
-    // the warp-specialized kernels (tile mode) are the ones that skip padding rows and fence their peer stores
-    if (policy != MOEB_POLICY_TILES16_RING) policy = MOEB_POLICY_TILES8_RING;
-    int rc = experts_common(fmt, b + L.rows, qg, sg, qu, su, qd, sd, bg, bu, bd, nullptr, nullptr, P * C, d, f,
+    // kernels that skip padding rows and fence their peer stores: the decode kernels for small calls (each
+    // padding unit exits at once), the warp-specialized tiles otherwise. With every rank sending about Cs slots
+    // spread over the P owners, an owner receives about Cs rows: the load is Cs / E_local rows per expert.
+    if (policy == MOEB_POLICY_AUTO)
+        policy = (Cs <= 16 && (long)P * Cs <= 128) ? MOEB_POLICY_SLOTS
+                 : ((long)Cs >= 8L * E_local ? MOEB_POLICY_TILES16_RING : MOEB_POLICY_TILES8_RING);
+    else if (policy != MOEB_POLICY_SLOTS && policy != MOEB_POLICY_TILES8_RING && policy != MOEB_POLICY_TILES16_RING)
+        policy = MOEB_POLICY_TILES8_RING;
+    int rc = experts_common(fmt, b + L.rows, qg, sg, qu, su, qd, sd, bg, bu, bd, nullptr, nullptr, P * Cs, d, f,
                             E_local, 1, act, policy, nullptr, nullptr, ws, ws_bytes, st, nullptr, nullptr, 0, 1.f,
                             nullptr, nullptr, nullptr, nullptr, 0, &pp);
     if (rc) return rc;
@@ -906,11 +917,11 @@ static int p2p_experts(int fmt, void *const *peers, void *self, int P, int me, i
     return MOEB_OK;
 }
 
-int moeb_ep_p2p_experts_q4(void *const *peers, void *self, int P, int me, int C, int d, int f, int E_local,
+int moeb_ep_p2p_experts_q4(void *const *peers, void *self, int P, int me, int C, int Cs, int d, int f, int E_local,
                            const void *qg, const void *sbg, const void *qu, const void *sbu, const void *qd,
                            const void *sbd, const float *bg, const float *bu, const float *bd, int act, int policy,
                            void *ws, size_t ws_bytes, cudaStream_t st) {
-    return p2p_experts(FMT_Q4, peers, self, P, me, C, d, f, E_local, qg, sbg, qu, sbu, qd, sbd, bg, bu, bd, act,
+    return p2p_experts(FMT_Q4, peers, self, P, me, C, Cs, d, f, E_local, qg, sbg, qu, sbu, qd, sbd, bg, bu, bd, act,
                        policy, ws, ws_bytes, st);
 }
 

@@ -65,7 +65,7 @@ __global__ void __launch_bounds__(PLAN_THREADS) k_ep_plan(EPArgs a) {
     if (tid == 0) {  // packed send buffer: owner blocks back to back; peer exchange: fixed blocks of C rows
         int run = 0;
         for (int p = 0; p < P; ++p) {
-            off[p] = a.C > 0 ? p * a.C : run;
+            off[p] = a.C > 0 ? p * a.Cs : run;
             run += base[p];
         }
     }
@@ -104,14 +104,14 @@ __global__ void __launch_bounds__(256) k_ep_send(EPArgs a) {
     pdl_wait();
     const int lane = threadIdx.x & 31;
     const int s = blockIdx.x * 8 + (threadIdx.x >> 5);
-    const int d = a.d, El = a.E / a.P, C = a.C;
-    const P2PLayout L = p2p_layout(a.P, C, d);
+    const int d = a.d, El = a.E / a.P, Cs = a.Cs;
+    const P2PLayout L = p2p_layout(a.P, a.C, d);
     if (s < a.T * a.k) {
         const int pos = a.slot_pos[s];
         if (pos >= 0) {
-            const int dst = pos / C, row = pos - dst * C;
+            const int dst = pos / Cs, row = pos - dst * Cs;
             const uint4 *src = reinterpret_cast<const uint4 *>(a.x + (size_t)(s / a.k) * d);
-            uint4 *out = reinterpret_cast<uint4 *>(a.peers[dst] + L.rows + ((size_t)a.me * C + row) * (d + 8) * 2);
+            uint4 *out = reinterpret_cast<uint4 *>(a.peers[dst] + L.rows + ((size_t)a.me * Cs + row) * (d + 8) * 2);
             for (int i = lane; i < d / 8; i += 32) out[i] = src[i];
             if (lane == 0) out[d / 8] = make_uint4((unsigned)(a.idx[s] % El), __float_as_uint(a.wts[s]), 0u, 0u);
         }

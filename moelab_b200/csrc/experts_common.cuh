@@ -222,7 +222,13 @@ __device__ __forceinline__ void down_store_combine(const ExpArgs &a, const TileI
                 yrow[r1] = wsl * v1;
             }
         }
-    if (a.slot_out) return;  // expert-parallel or separate combine pass: the rows are combined later
+    if (a.slot_out) {  // expert-parallel or separate combine pass: the rows are combined later
+        if (a.ypeers && NT8 == 1 && !a.tile_mode) {  // decode kernels: peers' rows visible before the kernel ends
+            __syncwarp();
+            if (lane == 0) __threadfence_system();
+        }
+        return;
+    }
     __syncwarp();
     if (lane == 0) __threadfence();  // cumulative over the warp's writes ordered by the __syncwarp
     __syncwarp();

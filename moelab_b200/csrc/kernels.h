@@ -37,8 +37,8 @@ struct PrepArgs {
     // expert-parallel rows (k == 1): each row's tail {local expert, weight bits} is unpacked into these
     int *idx_w;
     float *wts_w;
-    // peer-memory exchange: rows arrive in capacity blocks of C rows per source; rflag[src] == *epoch once
-    // source src has written its rcnt[src] rows (null: rows are all valid)
+    // peer-memory exchange: rows arrive in blocks of C rows per source (this call's block size); rflag[src] ==
+    // *epoch once source src has written its rcnt[src] rows (null: rows are all valid)
     const unsigned *rflag;
     const int *rcnt;
     const unsigned *epoch;
@@ -80,8 +80,9 @@ struct ExpArgs {
     int dn_prefetch;  // gate/up pulls the down weights of its expert into L2
     int fmt;          // FMT_Q4 or FMT_FP4
     int slot_out;     // 1: down stops after writing the weighted per-slot outputs yp (caller's buffer), no combine
-    // peer-memory exchange: slot s's weighted row goes to (float *)(ypeers[s / C] + yoff) + (me * C + s % C) * d,
-    // this rank's return block in the owner's buffer, instead of yp; the writing warps fence at system scope
+    // peer-memory exchange: slot s's weighted row goes to (float *)(ypeers[s / C] + yoff) + (me * C + s % C) * d
+    // (C = this call's block size), this rank's return block in the owner's buffer, instead of yp; the writing
+    // warps fence at system scope
     unsigned char *const *ypeers;
     size_t yoff;
     int C, me;
@@ -126,9 +127,10 @@ struct EPArgs {
     int *slot_pos;        // [T*k] row of each slot in the send buffer, -1 = dropped (invalid id)
     uint16_t *rows;       // [T*k][d + 8] send rows: x of the slot's token, then {local expert, weight, 0, 0}
     unsigned *err;
-    // peer-memory exchange (C > 0): slot_pos in capacity layout (dst * C + rank inside dst), rows written into
-    // peers[dst]'s source block `me`; self = this rank's exchange buffer (epoch, counters)
-    int C, me;
+    // peer-memory exchange (C > 0, the buffers' capacity in rows per source): this call's blocks hold Cs rows
+    // (Cs <= C), slot_pos is in block layout (dst * Cs + rank inside dst), rows are written into peers[dst]'s
+    // source block `me`; self = this rank's exchange buffer (epoch, counters)
+    int C, Cs, me;
     unsigned char *const *peers;
     unsigned char *self;
 };

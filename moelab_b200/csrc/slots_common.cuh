@@ -16,6 +16,7 @@ __device__ __forceinline__ void gate_up_slot_unit(const ExpArgs &a, int unit, ui
     const int g_beg = warp * G / KS, g_end = (warp + 1) * G / KS;
     const uint16_t *xs = reinterpret_cast<const uint16_t *>(xs4);
     const int slot = unit / RB, rb = unit - slot * RB;
+    if (a.idx[slot] == SLOT_SKIP) return;  // padding row of a peer-exchange block (uniform across the CTA)
     const TileInfo ti = tile_info(a, slot);
     const size_t blk = (size_t)ti.e * RB + rb;
     if (warp == KS - 1 && a.dn_prefetch) prefetch_down(a, ti.e, rb, RB, lane);
@@ -86,6 +87,7 @@ __device__ __forceinline__ void down_slot_unit(const ExpArgs &a, int unit, uint4
     const uint16_t *hs = reinterpret_cast<const uint16_t *>(hs4);
     const float *hsum_s = reinterpret_cast<const float *>(hs4 + f / 8);
     const int slot = unit / RB, rb = unit - slot * RB;
+    if (a.idx[slot] == SLOT_SKIP) return;
     const TileInfo ti = tile_info(a, slot);
     const size_t blk = (size_t)ti.e * RB + rb;
     const uint4 *hsrc = reinterpret_cast<const uint4 *>(a.h + (size_t)slot * f);

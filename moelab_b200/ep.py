@@ -194,17 +194,18 @@ class PeerExchange:
 
 
 def layer_p2p(state, x, gate_w, k, xch, gate_b=None, norm=True, rscale=1.0, act=None, residual=None, policy=None,
-              return_routing=False):
+              return_routing=False, max_tokens=None):
     """The expert-parallel layer call over peer memory: router, dispatch (rows stored into the owners'
     buffers), this rank's experts on what it received (rows stored back), combine. No host synchronisation:
-    the sequence can be captured in a CUDA graph. Every rank of the group must make the same calls."""
+    the sequence can be captured in a CUDA graph. Every rank of the group must make the same calls.
+    max_tokens: a bound on every rank's T for this call, the same on all ranks (default: the exchange's
+    capacity); a small bound keeps the owners' scan of the source blocks short."""
     act = state.get("act", 0) if act is None else act
-    if policy is None:
-        T_all = x.shape[0] * xch.P  # the group's tokens per call, if every rank has as many as this one
-        policy = ops.POLICY_TILES16_RING if T_all * k >= 8 * state["E_global"] else ops.POLICY_TILES8_RING
+    policy = ops.POLICY_AUTO if policy is None else policy  # the library picks by the call's block size
     T, d = x.shape
+    Cs = xch.C if max_tokens is None else min(xch.C, max(1, int(max_tokens) * k))
     idx, wts = ops.router(x, gate_w, k, gate_b=gate_b, norm=norm, scale=rscale)
-    slot_pos = ops.ep_p2p_dispatch(x, idx, wts, state["E_global"], xch)
-    ops.ep_p2p_experts(state, xch, act=act, policy=policy)
+    slot_pos = ops.ep_p2p_dispatch(x, idx, wts, state["E_global"], xch, Cs=Cs)
+    ops.ep_p2p_experts(state, xch, act=act, policy=policy, Cs=Cs)
     y = ops.ep_p2p_combine(xch, slot_pos, T, k, d, residual=residual, device=x.device)
     return (y, idx, wts) if return_routing else y

@@ -5,6 +5,7 @@ CUDA, contiguous, with the dtypes documented in include/moelab_b200.h (packed co
 uint8 tensors).
 """
 import ctypes
+import threading
 
 import torch
 
@@ -46,18 +47,20 @@ class Workspace:
         self.ep = ep  # expert-parallel rows (k = 1, no per-slot output region): sized by moeb_ep_workspace_bytes
         self.T = 0
         self.buf = None
+        self._lock = threading.Lock()  # callers on several threads must not see a buffer before it is zeroed
 
     def get(self, T):
-        if T > self.T:
-            Tn = max(T, 2 * self.T, 16)
-            if self.ep:
-                nbytes = _lib.load().moeb_ep_workspace_bytes(Tn, self.d, self.f, self.E)
-            else:
-                nbytes = _lib.load().moeb_workspace_bytes(Tn, self.d, self.f, self.E, self.k)
-            self.buf = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
-            _lib.call("moeb_workspace_init", _p(self.buf), nbytes, _stream())
-            self.T = Tn
-        return self.buf
+        with self._lock:
+            if T > self.T:
+                Tn = max(T, 2 * self.T, 16)
+                if self.ep:
+                    nbytes = _lib.load().moeb_ep_workspace_bytes(Tn, self.d, self.f, self.E)
+                else:
+                    nbytes = _lib.load().moeb_workspace_bytes(Tn, self.d, self.f, self.E, self.k)
+                buf = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+                _lib.call("moeb_workspace_init", _p(buf), nbytes, _stream())
+                self.buf, self.T = buf, Tn
+            return self.buf
 
     def read_error(self):
         """Sticky device error bits (MOEB_DEVERR_*); synchronises the current stream and clears them."""
@@ -137,6 +140,7 @@ def mxfp4_from_mlx(wq, scales):
 
 # ------------------------------------------------------------------ router
 _ROUTER_WS = {}
+_ROUTER_LOCK = threading.Lock()
 
 
 def router(x, gate_w, k, gate_b=None, norm=True, scale=1.0, return_logits=False):
@@ -150,9 +154,10 @@ def router(x, gate_w, k, gate_b=None, norm=True, scale=1.0, return_logits=False)
     wts = torch.empty(T, k, dtype=torch.float32, device=x.device)
     logits = torch.empty(T, E, dtype=torch.float32, device=x.device) if return_logits else None
     key = (x.device, d, E, k)
-    ws = _ROUTER_WS.get(key)
-    if ws is None:
-        ws = _ROUTER_WS[key] = Workspace(d, 64, E, k, x.device)
+    with _ROUTER_LOCK:
+        ws = _ROUTER_WS.get(key)
+        if ws is None:
+            ws = _ROUTER_WS[key] = Workspace(d, 64, E, k, x.device)
     buf = ws.get(max(T, 1))
     _lib.call("moeb_router", _p(x), _p(gate_w), _p(gate_b), T, d, E, k, int(bool(norm)), float(scale), _p(idx),
               _p(wts), _p(logits), _p(buf), buf.numel(), _stream())
@@ -280,9 +285,9 @@ def ep_combine(back, slot_pos, T, k, residual=None):
 
 
 # ------------------------------------------------------------------ expert parallelism over peer memory
-def ep_p2p_dispatch(x, idx, wts, E, xch):
+def ep_p2p_dispatch(x, idx, wts, E, xch, Cs=0):
     """Route this rank's slots straight into the owners' exchange buffers. Returns slot_pos int32 [T*k] in
-    capacity layout (owner * C + row) for the combine."""
+    block layout (owner * Cs + row) for the combine. Cs: this call's rows per source block (0 = capacity)."""
     _need(x, torch.bfloat16, "x")
     _need(idx, torch.int32, "idx")
     _need(wts, torch.float32, "wts")
@@ -290,17 +295,18 @@ def ep_p2p_dispatch(x, idx, wts, E, xch):
     k = idx.shape[1]
     send_counts = torch.empty(xch.P, dtype=torch.int32, device=x.device)
     slot_pos = torch.empty(T * k, dtype=torch.int32, device=x.device)
-    _lib.call("moeb_ep_p2p_dispatch", _p(x), _p(idx), _p(wts), T, d, k, E, xch.P, xch.me, xch.C, _p(xch.peers),
-              ctypes.c_void_p(xch.base), _p(send_counts), _p(slot_pos), _stream())
+    _lib.call("moeb_ep_p2p_dispatch", _p(x), _p(idx), _p(wts), T, d, k, E, xch.P, xch.me, xch.C, int(Cs),
+              _p(xch.peers), ctypes.c_void_p(xch.base), _p(send_counts), _p(slot_pos), _stream())
     return slot_pos
 
 
-def ep_p2p_experts(state, xch, act=0, policy=POLICY_AUTO):
+def ep_p2p_experts(state, xch, act=0, policy=POLICY_AUTO, Cs=0):
     """This rank's experts on the rows every source sent it; outputs go straight back to the owners."""
     if _fmt(state) != "q4":
         raise ValueError("the peer-memory exchange runs int4 states")
-    buf = state["ep_ws"].get(xch.P * xch.C)
-    _lib.call("moeb_ep_p2p_experts_q4", _p(xch.peers), ctypes.c_void_p(xch.base), xch.P, xch.me, xch.C,
+    Cs = Cs or xch.C
+    buf = state["ep_ws"].get(xch.P * Cs)
+    _lib.call("moeb_ep_p2p_experts_q4", _p(xch.peers), ctypes.c_void_p(xch.base), xch.P, xch.me, xch.C, int(Cs),
               state["dm"], state["f"], state["E"], *_expert_ptrs(state), int(act), int(policy), _p(buf),
               buf.numel(), _stream())
 

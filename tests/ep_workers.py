@@ -184,7 +184,8 @@ def p2p_rank(rank, P, port, tokens, d, f, E, k, seed, policy, calls, q):
         gr = torch.cuda.CUDAGraph()
         with torch.cuda.stream(s):
             with torch.cuda.graph(gr, stream=s):
-                ys_g = [ep.layer_p2p(st, x, gate, k, xch, residual=x, policy=policy) for x in xs]
+                ys_g = [ep.layer_p2p(st, x, gate, k, xch, residual=x, policy=policy, max_tokens=max(tokens))
+                        for x in xs]
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
         dist.barrier()

@@ -158,20 +158,23 @@ def test_emulated_ep_gptoss_mxfp4_bit_exact(pol):
 
 
 # ------------------------------------------------------------------ exchange over peer memory, emulated
-P2P_POL = {"tiles8ring": ops.POLICY_TILES8_RING, "tiles16ring": ops.POLICY_TILES16_RING}
+P2P_POL = {"tiles8ring": ops.POLICY_TILES8_RING, "tiles16ring": ops.POLICY_TILES16_RING, "slots": ops.POLICY_SLOTS}
 
 
 @pytest.mark.parametrize("P,tokens", [(2, [4, 7]), (4, [1, 0, 33, 16]), (8, [2, 9, 1, 1, 40, 0, 3, 17])])
 @pytest.mark.parametrize("pol", list(P2P_POL))
-def test_p2p_emulated_bit_exact_vs_single_gpu(P, tokens, pol):
+@pytest.mark.parametrize("blocks", ["capacity", "tight"])
+def test_p2p_emulated_bit_exact_vs_single_gpu(P, tokens, pol, blocks):
     """P ranks emulated phase by phase on one GPU (all dispatches, then all experts, then all combines), so
     every flag a kernel waits for was released by an earlier kernel on the stream. Three calls in a row reuse
-    the buffers with advancing epochs; every output must equal the single-GPU layer bit for bit."""
+    the buffers with advancing epochs; every output must equal the single-GPU layer bit for bit. Blocks of the
+    whole capacity, or of the call's own bound (Cs = max T * k < C)."""
     E, d, f, k = 32, 256, 384, 4
     w, gate = _layer(E, d, f, seed=100 + P)
     full = b200_q4_moe.prepare(*w)
     b200_q4_moe._ws(full, k)
-    C = max(tokens) * k
+    C = 2 * max(tokens) * k + 4
+    Cs = 0 if blocks == "capacity" else max(tokens) * k
     xchs = ep.PeerExchange.local_group(P, C, d, "cuda")
     states = [ep.shard(b200_q4_moe, *w, r, P) for r in range(P)]
     try:
@@ -181,9 +184,9 @@ def test_p2p_emulated_bit_exact_vs_single_gpu(P, tokens, pol):
             routing = []
             for r in range(P):
                 idx, wts = ops.router(xs[r], gate, k)
-                routing.append((idx, wts, ops.ep_p2p_dispatch(xs[r], idx, wts, E, xchs[r])))
+                routing.append((idx, wts, ops.ep_p2p_dispatch(xs[r], idx, wts, E, xchs[r], Cs=Cs)))
             for r in range(P):
-                ops.ep_p2p_experts(states[r], xchs[r], policy=P2P_POL[pol])
+                ops.ep_p2p_experts(states[r], xchs[r], policy=P2P_POL[pol], Cs=Cs)
             for r in range(P):
                 idx, wts, sp = routing[r]
                 y = ops.ep_p2p_combine(xchs[r], sp, tokens[r], k, d, residual=xs[r], device="cuda")

@@ -45,7 +45,7 @@ def test_nccl_ep_bit_exact_vs_single_gpu(fmt, policy):
 
 
 @pytest.mark.skipif(_ngpu() < 2, reason="needs 2 or more GPUs")
-@pytest.mark.parametrize("policy", [ops.POLICY_TILES8_RING, ops.POLICY_TILES16_RING])
+@pytest.mark.parametrize("policy", [ops.POLICY_TILES8_RING, ops.POLICY_TILES16_RING, ops.POLICY_SLOTS])
 def test_p2p_ep_bit_exact_vs_single_gpu(policy):
     """The peer-memory exchange over real GPUs (CUDA IPC mappings over NVLink), eager and as a CUDA graph."""
     from ep_workers import p2p_rank
