@@ -45,6 +45,9 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bound on the CPU baseline sample")
     ap.add_argument("--soak-seconds", type=float, default=1.5, help="replays before the timed region (clocks)")
     ap.add_argument("--configs", type=int, default=1, help="1: also time the other BASELINE configurations (1 GPU)")
+    ap.add_argument("--profile-config", default="", help="run 3 eager layer calls of the CONFIGS entry whose name "
+                    "starts with this (for ncu captures of one kernel) and exit")
+    ap.add_argument("--profile-tokens", type=int, default=1024)
     return ap.parse_args()
 
 
@@ -561,8 +564,24 @@ def run_reference(a, ws, rank):
     print(json.dumps(line), flush=True)
 
 
+def profile_config(a):
+    """A few eager layer calls of one configuration: the small, self-ending workload ncu captures are taken on."""
+    name, shp, kind, _ = next(c for c in CONFIGS if c[0].startswith(a.profile_config))
+    layers, _ = config_layers(shp["d"], shp["f"], shp["E"], shp["k"], kind, n_layers=1)
+    st, gate, call = layers[0]
+    x = torch.randn(a.profile_tokens, shp["d"], generator=torch.Generator(device="cuda").manual_seed(3),
+                    device="cuda").to(torch.bfloat16)
+    for _ in range(3):
+        call(st, x, gate)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_config": name, "T": a.profile_tokens, "ok": True}))
+
+
 def main():
     a = parse()
+    if a.profile_config:
+        profile_config(a)
+        return
     ws, rank, local = dist_init(a)
     if a.impl == "reference":
         run_reference(a, ws, rank)
