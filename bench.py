@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--profile-config", default="", help="run 3 eager layer calls of the CONFIGS entry whose name "
                     "starts with this (for ncu captures of one kernel) and exit")
     ap.add_argument("--profile-tokens", type=int, default=1024)
+    ap.add_argument("--profile-policy", default="", help="pin the expert kernels for --profile-config (slots, "
+                    "tiles8, tiles16, ring8, ring16, tc, decode; default: the load-based dispatcher)")
     return ap.parse_args()
 
 
@@ -567,6 +569,13 @@ def run_reference(a, ws, rank):
 def profile_config(a):
     """A few eager layer calls of one configuration: the small, self-ending workload ncu captures are taken on."""
     name, shp, kind, _ = next(c for c in CONFIGS if c[0].startswith(a.profile_config))
+    if a.profile_policy:
+        from moelab_b200 import ops
+        from moelab_b200.variants.cuda import b200_mxfp4_moe as vm, b200_q4_moe as vq
+        pol = {"slots": ops.POLICY_SLOTS, "tiles8": ops.POLICY_TILES8, "tiles16": ops.POLICY_TILES16,
+               "ring8": ops.POLICY_TILES8_RING, "ring16": ops.POLICY_TILES16_RING, "tc": ops.POLICY_TC,
+               "decode": ops.POLICY_DECODE}[a.profile_policy]
+        vq.POLICY = vm.POLICY = pol  # the gpt-oss variant runs through vm
     layers, _ = config_layers(shp["d"], shp["f"], shp["E"], shp["k"], kind, n_layers=1)
     st, gate, call = layers[0]
     x = torch.randn(a.profile_tokens, shp["d"], generator=torch.Generator(device="cuda").manual_seed(3),

@@ -142,20 +142,23 @@ int check_shape(int T, int d, int f, int E, int k) {
 // slots (T <= 2 at k = 8); above that the warp-specialized tensor-map pipeline beats the register tiles at
 // every load (T = 4: 50.8 vs 55.6 us, T = 32: 126 vs 145 us), with tiles of 8 slots up to load ~4 and tiles of
 // 16 at high load (T = 256, load 16: 291 vs 329 us).
-// From 64 slots per expert the tcgen05 kernels (tiles of 256, weights dequantized once per tile) win: Mixtral
-// T = 256 / 1024 / 4096: 0.58 / 1.36 / 4.39 ms vs 1.26 / 4.61 / 17.6 ms, Qwen3-235B T = 2048: 2.80 vs 4.12 ms
-// (they lose at 16 slots per expert: Qwen3-235B T = 256, 0.90 vs 0.71 ms).
+// From 24 slots per expert the tcgen05 kernels (weights dequantized once per tile, A operand in TMEM) win:
+// Qwen3-30B T = 384 / 512 / 1024 (load 24 / 32 / 64): 235 / 263 / 429 us vs ring16 275 / 346 / 603 us; below
+// that the tile kernels do (T = 256, load 16: 228 vs 208 us). Each M = 128, K = 16 tensor-core step costs about
+// the same up to N = 128 slots, so small tiles leave the tensor pipe mostly idle.
 int choose_policy(int T, int E, int k, int d, int f) {
     const long TK = (long)T * k;
     if (TK <= 16) return MOEB_POLICY_SLOTS;
-    if (TK >= 64L * E && d % 128 == 0 && f % 128 == 0) return MOEB_POLICY_TC;
+    if (TK >= 24L * E && d % 128 == 0 && f % 128 == 0) return MOEB_POLICY_TC;
     return TK >= 8L * E ? MOEB_POLICY_TILES16_RING : MOEB_POLICY_TILES8_RING;
 }
 
-// tcgen05 tile size: 256 slots (weights dequantized once for up to 256 slots; gate/up has one accumulator set)
-// from 128 slots per expert on, else 128 (two accumulator sets overlap the epilogue). Measured: Mixtral T=256
-// (64 slots/expert) 467 vs 538 us; Mixtral T=4096 3.26 vs 3.75 ms; Qwen3-235B T=2048 2.43 vs 2.65 ms.
-int tc_nt(long TK, int E) { return TK >= 128L * E ? 256 : 128; }
+// tcgen05 tile size: the power of two from 32 to 256 at or above 1.5 x the average expert's slots, so that most
+// experts fit one tile (weights are dequantized once per tile; a second, partial tile reads them again).
+int tc_nt(long TK, int E) {
+    const long load = TK / std::max(E, 1), need = load + load / 2;
+    return need > 128 ? 256 : need > 64 ? 128 : need > 32 ? 64 : 32;
+}
 
 int nt_of(int policy, long TK, int E) {
     if (policy == MOEB_POLICY_TC) return tc_nt(TK, E);
@@ -173,6 +176,7 @@ struct KLaunch {
     bool per_warp;
     int rows, sg;
     bool tc = false;  // tensor-core kernel: reads the activations through the expert-sorted row map
+    bool tmem_a = false;  // tensor-core kernel with A in TMEM: activations in the permuted 64-group k order
 };
 struct ExpLaunch {
     KLaunch gu, dn;
@@ -194,16 +198,9 @@ KLaunch ws_kernel(int fmt, int nt8, bool down) {
     return fmt == FMT_FP4 ? ws_kernel_fmt<FMT_FP4>(nt8, down) : ws_kernel_fmt<FMT_Q4>(nt8, down);
 }
 
-// (tile, stages, accumulator sets): gate/up 128 -> (3, 2), 256 -> (3, 1); down 128 / 256 -> (4, 2)
-template <int FMT>
-void (*tc_fn(int nt, bool down))(ExpArgs) {
-    if (nt == 256) return down ? k_experts_tc<FMT, 256, 4, 2, true> : k_experts_tc<FMT, 256, 3, 1, false>;
-    return down ? k_experts_tc<FMT, 128, 4, 2, true> : k_experts_tc<FMT, 128, 3, 2, false>;
-}
 KLaunch tc_kernel(int fmt, int nt, bool down) {
-    void (*fn)(ExpArgs) = fmt == FMT_FP4 ? tc_fn<FMT_FP4>(nt, down) : tc_fn<FMT_Q4>(nt, down);
-    const int ns = down ? 4 : 3, acc = (down || nt == 128) ? 2 : 1;
-    return {fn, 448, experts_tc_smem(nt, ns, acc, down, fmt), false, 8, 1, true};
+    const TcInfo t = experts_tc_info(fmt, nt, down);
+    return {t.fn, t.threads, t.smem, false, 8, 1, true, t.tmem_a};
 }
 
 // Kernels per policy: TILES8 / TILES16 run the register-pipelined tile kernels, the *_RING policies the
@@ -346,10 +343,11 @@ int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaS
             !encode_weights_map(&a.tmsb[2], a.dn.sb, sw, a.f / 64, (long)a.E * RBd, K.dn.sg, K.dn.rows))
             return fail(MOEB_ELAUNCH, "tensor map encoding failed (down)%s");
     }
+    a.h_kperm = K.dn.tc && K.dn.tmem_a ? 1 : 0;
     if (K.gu.tc) {  // activations in expert-sorted order (in the slot-row region, free until down writes it)
         uint16_t *xs = reinterpret_cast<uint16_t *>(a.yp);
         if (launch(k_gather_rows, dim3((unsigned)((TK + 7) / 8)), dim3(256), 0, st, a.x, (const int *)a.sorted, (int)TK,
-                   a.k, a.d, xs) != cudaSuccess)
+                   a.k, a.d, K.gu.tmem_a ? 1 : 0, xs) != cudaSuccess)
             return check_launch("gather");
         if (!encode_rows_map(&a.tmx, xs, TK, a.d, nt)) return fail(MOEB_ELAUNCH, "tensor map encoding failed (x)%s");
     }
@@ -412,7 +410,10 @@ int launch_router(const void *x, const void *wg, const void *bias, int T, int d,
     r.tiles = tiles ? at<int4>(ws, L.tiles) : nullptr;
     r.ntiles = at<int>(ws, L.ntiles);
     r.sorted = at<int>(ws, L.sorted);
-    const size_t smem = tiles ? 8 * (size_t)(E + ns) : 0;
+    // the tile builder keeps the slot ids in shared memory for its second pass when that stays small (every
+    // router CTA carries this allocation, so it is capped to keep the logits phase at full occupancy)
+    size_t smem = tiles ? 8 * (size_t)(E + ns) : 0;
+    if (tiles && smem + 4 * (size_t)T * (k + ns) <= 16 * 1024) smem += 4 * (size_t)T * (k + ns);
     // tokens per CTA: 1 up to T = 64 (more CTAs in flight, the gate row re-read from L2), 4 above
     const int tpb = T <= 64 ? 1 : 4;
     void (*kern)(RouterArgs) = tpb == 1 ? router_kernel<1, 8>(E) : router_kernel<4, 4>(E);
@@ -653,7 +654,8 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
         p.ntiles = at<int>(ws, L.ntiles);
         p.sorted = at<int>(ws, L.sorted);
         p.err = at<unsigned>(ws, L.err);
-        const size_t smem = tiles ? 8 * (size_t)E : 0;
+        size_t smem = tiles ? 8 * (size_t)E : 0;
+        if (tiles && smem + 4 * (size_t)T * k <= 48 * 1024) smem += 4 * (size_t)T * k;  // ids cached (build_tiles)
         if (launch(k_prep, dim3((T + 7) / 8), dim3(256), smem, st, p) != cudaSuccess) return check_launch("prep");
     }
     if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[1]), st);

@@ -1,25 +1,31 @@
-// Grouped expert kernels on the 5th-generation tensor cores (tcgen05, accumulators in TMEM), for high loads
-// (tiles of up to NT = 256 slots of one expert: the weights are dequantized once per tile).
+// Grouped expert kernels on the 5th-generation tensor cores (tcgen05, accumulators in TMEM), for medium and high
+// loads (tiles of up to NT = 32 .. 256 slots of one expert: the weights are dequantized once per tile).
 //
 // A work item is (tile, 128 output rows). D[128 rows][NT slots] = W[128][K] . X[NT][K]^T accumulates in TMEM
-// (fp32, lane = row, column = slot). K streams through an NS-deep shared-memory ring, one 64-group per stage:
-//   warp 0 (producer, one lane): per stage, 2-D tensor copies of the packed int4 codes and scale|bias words of
-//     the 8 row blocks (one group; per projection) and of the tile's activation rows (64 k, NT rows, 128-byte
-//     swizzle: the UMMA K-major layout); "full" mbarrier with transaction bytes. No multicast.
-//   warps 2..9 (dequant): int4 -> bf16 w = s*q + b (q|0x4300 = 128+q exactly; one HSUB2 and one HFMA2, a single
-//     bf16 rounding), written into the stage's A tile in the same swizzled K-major layout; then a proxy fence
-//     (generic writes -> tensor-core reads) and one arrival per warp on the stage's "deq" mbarrier.
-//   warp 1 (MMA, one lane): waits "deq", issues 4 k-steps of tcgen05.mma (M = 128, N = the tile's slot count
-//     rounded up to 16, K = 16, bf16 x bf16 -> fp32) per projection, and tcgen05.commit frees the stage ("empty"); after the last group it commits the
-//     item's accumulator ("accf"). With two accumulator sets (down) the next item's MMAs run while the epilogue
-//     drains the previous one; gate/up's two projections of 256 columns fill TMEM, so it has one set (the
-//     epilogue is a few percent of an item's K loop).
-//   warps 10..13 (epilogue): tcgen05.ld 16 columns at a time (warp w reads TMEM lanes 32*(w%4)..+31 = its rows);
-//     gate/up: bias + activation -> h in slot-sorted order; down: weight * (acc + bias) -> the slot's fp32 row
-//     for the separate combine pass. Then "acce" frees the accumulator set.
+// (fp32, lane = row, column = slot). K advances one 64-group per step through three shared-memory rings, so
+// that each resource is only as deep as its own latency needs:
+//   raw ring (NR stages, 4.5 KB per projection): the packed int4 codes and scale|bias words (or MXFP4 codes and
+//     E8M0 scales) of the item's 8 row blocks for one group. They come from HBM, so this ring is the deep one;
+//   X ring (NX stages, NT x 128 B): the tile's activation rows for the group (64 k, 128-byte swizzle: the UMMA
+//     K-major layout), from L2;
+//   A ring (NA stages, 16 KB per projection): the dequantized bf16 weight tile in the same swizzled layout.
+// Roles (one CTA per SM):
+//   warp 0, one lane: tensor copies of the raw stages ("rfull" mbarrier with transaction bytes; "rempty" frees);
+//   warp 2, one lane: tensor copies of the X stages ("xfull" / "xempty"). No multicast anywhere;
+//   warps 3 .. 3 + DQW - 1 (one per (projection, row block)): wait for a raw stage, read their block into
+//     registers, wait for a free A stage, dequantize (int4: q|0x4300 = 128+q exactly, one HSUB2 and one HFMA2,
+//     a single bf16 rounding of s*q + b; MXFP4: E2M1 * 2^(S-127), exact), write it swizzled, fence the proxy
+//     (generic writes -> tensor-core reads), then arrive on "afull" and release the raw stage;
+//   warp 1, one lane: per step waits "afull" and "xfull", issues 4 k-steps of tcgen05.mma per projection
+//     (M = 128, N = the tile's slots rounded up to 16, K = 16, bf16 x bf16 -> fp32) and commits "aempty" and
+//     "xempty"; after the item's last group it commits the accumulator set ("accf");
+//   EPW epilogue warps: tcgen05.ld 16 columns at a time (warp w reads TMEM lanes 32 * (w % 4) .. + 31, its
+//     rows; with 8 warps two share a lane quarter and split the columns); gate/up: bias + activation -> h in
+//     slot-sorted order; down: weight * (acc + bias) -> the slot's fp32 row for the separate combine pass; then
+//     "acce" frees the set. With ACC = 2 sets the next item's MMAs run while the epilogue drains.
 // The activations arrive in expert-sorted order (x gathered by k_gather_rows; gate/up writes h sorted), so each
-// tile's rows are contiguous for the tensor copy. Weights are dequantized once per tile, so the kernel pays off
-// once tiles hold many slots; the dispatcher uses it from 64 slots per expert on.
+// tile's rows are contiguous for the tensor copy (rows past the tile belong to other tiles or are zero-filled
+// past the end; their columns are never read).
 // Every wait is bounded (timeout -> MOEB_DEVERR_TIMEOUT, the roles stop, in-flight copies and MMAs are drained
 // with bounded waits, TMEM is released).
 #include "experts_common.cuh"
@@ -29,9 +35,6 @@ namespace moeb {
 namespace {
 
 constexpr int TC_M = 128;
-constexpr int TC_DQW = 8;                       // dequant warps
-constexpr int TC_THREADS = 32 * (2 + TC_DQW + 4);  // producer, MMA, dequant, 4 epilogue warps
-
 // K-major operand descriptor, 128-byte swizzle: 8-row groups 1024 B apart (SBO), rows of 128 B.
 MOEB_DEV uint64_t sdesc_sw128(uint32_t saddr) {
     uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
@@ -74,32 +77,104 @@ MOEB_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-template <int FMT, int NT, int ACC, bool DOWN>
+// A from tensor memory: D[tmem] (+)= A[tmem] . B[smem desc]^T (no output lanes disabled)
+MOEB_DEV void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+// 16 TMEM lanes x 32 columns from the warp: thread 4i + j supplies lanes i, i + 8, columns 8m + 2j, 8m + 2j + 1
+// (register 4m + 2h + c = lane i + 8h, column 8m + 2j + c)
+MOEB_DEV void tmem_st_16x256_x4(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.16x256b.x4.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+MOEB_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Dequantize this lane's share of one (16-row block, 64-group): rows gq (out[0]) and gq + 8 (out[1]), k-pairs
+// 8c .. 8c + 7 of the group (k = 16c .. 16c + 15) as bf16x2 words. int4: q|0x4300 = 128+q exactly, one HSUB2 and
+// one HFMA2 (a single bf16 rounding of s*q + b); MXFP4: E2M1 * 2^(S-127), exact in bf16.
+template <int FMT>
+MOEB_DEV void dequant_block(uint4 w, uint32_t sb0, uint32_t sb1, int c, uint32_t (&out)[2][8]) {
+    const uint32_t k128 = 0x43004300u;
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+        const uint32_t wa = hf ? w.z : w.x, wb = hf ? w.w : w.y;
+        if (FMT == FMT_FP4) {
+            const uint32_t S = (sb0 >> (8 * (hf * 2 + (c >> 1)))) & 0xFFu;
+            uint32_t lo[4], hi[4];
+            fp4_word(wa, fp4_scale2(S), lo);
+            fp4_word(wb, fp4_scale2(S), hi);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                out[hf][i] = lo[i];
+                out[hf][4 + i] = hi[i];
+            }
+        } else {
+            const uint32_t sv = hf ? sb1 : sb0;
+            const uint32_t s2 = (sv & 0xFFFFu) | (sv << 16), b2 = (sv >> 16) | (sv & 0xFFFF0000u);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t v = q4pair(i < 4 ? wa : wb, i & 3);  // (128 + q_2p, 128 + q_2p+1)
+                __nv_bfloat162 qv = *reinterpret_cast<const __nv_bfloat162 *>(&v);
+                qv = __hsub2(qv, *reinterpret_cast<const __nv_bfloat162 *>(&k128));
+                const __nv_bfloat162 r2 = __hfma2(qv, *reinterpret_cast<const __nv_bfloat162 *>(&s2),
+                                                  *reinterpret_cast<const __nv_bfloat162 *>(&b2));
+                out[hf][i] = *reinterpret_cast<const uint32_t *>(&r2);
+            }
+        }
+    }
+}
+
+// k order of the tensor-core operands inside a 64-group when A lives in TMEM (see k_experts_tca)
+MOEB_DEV int kperm64(int k) { return (k & ~63) | (((k >> 2) & 3) << 4) | (((k >> 4) & 3) << 2) | (k & 3); }
+
+template <int FMT, int NT, int NR, int NA, int NX, int ACC, bool DOWN>
 struct TCL {
     static constexpr int NP = DOWN ? 1 : 2;
+    static constexpr int DQW = 8 * NP;                   // dequant warps: one (projection, row block) each
+    static constexpr int EPW = DOWN ? 4 : 8;             // epilogue warps
+    static constexpr int THREADS = 32 * (3 + DQW + EPW);
     static constexpr int SBG = FMT == FMT_FP4 ? 32 : 64;  // scale bytes per (row block, group)
-    static constexpr int A_BYTES = TC_M * 128;         // one projection's 128 rows x 64 k, bf16, swizzled
-    static constexpr int X_BYTES = NT * 128;           // NT rows x 64 k
-    static constexpr int Q_BYTES = 8 * 512;            // packed codes, 8 row blocks x one group
-    static constexpr int S_BYTES = 8 * SBG;            // int4 scale|bias words / MXFP4 E8M0 bytes
-    static constexpr int STAGE_RAW = NP * A_BYTES + X_BYTES + NP * (Q_BYTES + S_BYTES);
-    static constexpr int STAGE = (STAGE_RAW + 1023) / 1024 * 1024;
-    static constexpr int TMEM_COLS = ACC * NP * NT;    // ACC accumulator sets
-    static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation");
+    static constexpr int A_BYTES = TC_M * 128;           // one projection's 128 rows x 64 k, bf16, swizzled
+    static constexpr int A_STAGE = NP * A_BYTES;
+    static constexpr int X_STAGE = NT * 128;             // NT rows x 64 k
+    static constexpr int Q_BYTES = 8 * 512;              // packed codes, 8 row blocks x one group
+    static constexpr int S_BYTES = 8 * SBG;              // int4 scale|bias words / MXFP4 E8M0 bytes
+    static constexpr int R_STAGE = NP * (Q_BYTES + S_BYTES);
+    static constexpr int OFF_X = NA * A_STAGE;
+    static constexpr int OFF_R = OFF_X + NX * X_STAGE;
+    static constexpr int OFF_BAR = OFF_R + NR * R_STAGE;
+    static constexpr int NBAR = 2 * (NR + NA + NX + ACC);
+    static constexpr int SMEM = 1024 + OFF_BAR + NBAR * 8;  // + alignment slack
+    static constexpr int TMEM_RAW = ACC * NP * NT;
+    static constexpr int TMEM_COLS = TMEM_RAW < 32 ? 32 : TMEM_RAW;
+    static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0 && TMEM_COLS <= 512, "TMEM allocation");
+    static_assert(SMEM <= 227 * 1024, "shared memory");
+    static_assert(X_STAGE % 1024 == 0 && R_STAGE % 128 == 0, "stage alignment");
 };
 
 }  // namespace
 
-template <int FMT, int NT, int NS, int ACC, bool DOWN>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_constant__ ExpArgs a) {
-    using L = TCL<FMT, NT, ACC, DOWN>;
+template <int FMT, int NT, int NR, int NA, int NX, int ACC, bool DOWN>
+__global__ void __launch_bounds__(TCL<FMT, NT, NR, NA, NX, ACC, DOWN>::THREADS, 1)
+    k_experts_tc(const __grid_constant__ ExpArgs a) {
+    using L = TCL<FMT, NT, NR, NA, NX, ACC, DOWN>;
     pdl_launch();
     pdl_wait();
     extern __shared__ __align__(1024) unsigned char tsm_raw[];
     // 1024-byte aligned base for the swizzled tiles
     unsigned char *tsm = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(tsm_raw) + 1023) & ~(uintptr_t)1023);
-    uint64_t *full = reinterpret_cast<uint64_t *>(tsm + (size_t)NS * L::STAGE);
-    uint64_t *deq = full + NS, *empty = deq + NS, *accf = empty + NS, *acce = accf + ACC;
+    unsigned char *Ab = tsm, *Xb = tsm + L::OFF_X, *Rb = tsm + L::OFF_R;
+    uint64_t *rfull = reinterpret_cast<uint64_t *>(tsm + L::OFF_BAR);
+    uint64_t *rempty = rfull + NR, *afull = rempty + NR, *aempty = afull + NA, *xfull = aempty + NA,
+             *xempty = xfull + NX, *accf = xempty + NX, *acce = accf + ACC;
     __shared__ uint32_t s_tmem;
     __shared__ int s_fail;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -110,19 +185,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_const
     const int n_items = n_tiles * MT;
     const int my_items = (int)blockIdx.x < n_items ? (n_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
     if (threadIdx.x == 0) {
-        for (int i = 0; i < NS; ++i) {
-            mbar_init(full + i, 1);
-            mbar_init(deq + i, TC_DQW);
-            mbar_init(empty + i, 1);
+        for (int i = 0; i < NR; ++i) {
+            mbar_init(rfull + i, 1);
+            mbar_init(rempty + i, L::DQW);
+        }
+        for (int i = 0; i < NA; ++i) {
+            mbar_init(afull + i, L::DQW);
+            mbar_init(aempty + i, 1);
+        }
+        for (int i = 0; i < NX; ++i) {
+            mbar_init(xfull + i, 1);
+            mbar_init(xempty + i, 1);
         }
         for (int b = 0; b < ACC; ++b) {
             mbar_init(accf + b, 1);
-            mbar_init(acce + b, 4);
+            mbar_init(acce + b, L::EPW);
         }
         mbar_fence_init();
         s_fail = 0;
     }
-    if (warp == 1) {  // TMEM: two accumulator sets of NP x NT fp32 columns
+    if (warp == 1) {  // TMEM: ACC accumulator sets of NP x NT fp32 columns
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
                      "r"((uint32_t)L::TMEM_COLS)
                      : "memory");
@@ -136,14 +218,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_const
     const unsigned timeout_err = ERR_TIMEOUT;
 
     if (warp == 0) {
-        // ------------------------------------------------------------ producer
+        // ------------------------------------------------------------ raw producer (codes + scales, from HBM)
         if (lane == 0) {
-            const uint64_t pol = l2_evict_first_policy(), pol_x = l2_evict_last_policy();  // x is re-read per row tile
+            const uint64_t pol = l2_evict_first_policy();
             for (int p = 0; p < L::NP; ++p) {
                 tmap_prefetch(&a.tmq[m0 + p]);
                 tmap_prefetch(&a.tmsb[m0 + p]);
             }
-            tmap_prefetch(&a.tmx);
             int k = 0;
             bool ok = true;
             for (int it = 0; it < my_items && ok; ++it) {
@@ -153,27 +234,50 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_const
                 const int e = (tr.x < 0 || tr.x >= a.E) ? 0 : tr.x;
                 const int row0 = e * RB + mt * 8;
                 for (int g = 0; g < G; ++g, ++k) {
-                    const int s = k % NS;
-                    if (k >= NS && !mbar_wait_bounded(empty + s, (unsigned)(((k / NS) - 1) & 1))) {
+                    const int r = k % NR;
+                    if (k >= NR && !mbar_wait_bounded(rempty + r, (unsigned)(((k / NR) - 1) & 1))) {
                         atomicOr(a.err, timeout_err);
                         s_fail = 1;
                         ok = false;
                         break;
                     }
-                    unsigned char *st = tsm + (size_t)s * L::STAGE;
-                    unsigned char *q = st + L::NP * L::A_BYTES + L::X_BYTES;
-                    mbar_expect_tx(full + s, (unsigned)(L::X_BYTES + L::NP * (L::Q_BYTES + L::S_BYTES)));
-                    tma_load_2d(st + L::NP * L::A_BYTES, &a.tmx, g * 64, tr.y, full + s, pol_x);
+                    unsigned char *q = Rb + (size_t)r * L::R_STAGE;
+                    mbar_expect_tx(rfull + r, (unsigned)L::R_STAGE);
                     for (int p = 0; p < L::NP; ++p) {
-                        tma_load_2d(q + p * L::Q_BYTES, &a.tmq[m0 + p], g * 64, row0, full + s, pol);
+                        tma_load_2d(q + p * L::Q_BYTES, &a.tmq[m0 + p], g * 64, row0, rfull + r, pol);
                         tma_load_2d(q + L::NP * L::Q_BYTES + p * L::S_BYTES, &a.tmsb[m0 + p], g * (L::SBG / 4), row0,
-                                    full + s, pol);
+                                    rfull + r, pol);
                     }
                 }
             }
             // let the copies this CTA issued land before it can exit (bounded)
-            for (int q = k - NS; q < k; ++q)
-                if (q >= 0) mbar_wait_bounded(full + q % NS, (unsigned)((q / NS) & 1), 1u << 16);
+            for (int q = k - NR; q < k; ++q)
+                if (q >= 0) mbar_wait_bounded(rfull + q % NR, (unsigned)((q / NR) & 1), 1u << 16);
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------------------------ X producer (the tile's activation rows, L2)
+        if (lane == 0) {
+            const uint64_t pol_x = l2_evict_last_policy();  // re-read for every 128-row item of the tile
+            tmap_prefetch(&a.tmx);
+            int k = 0;
+            bool ok = true;
+            for (int it = 0; it < my_items && ok; ++it) {
+                const int item = (int)blockIdx.x + it * (int)gridDim.x;
+                const int4 tr = a.tiles[item / MT];
+                for (int g = 0; g < G; ++g, ++k) {
+                    const int x = k % NX;
+                    if (k >= NX && !mbar_wait_bounded(xempty + x, (unsigned)(((k / NX) - 1) & 1))) {
+                        atomicOr(a.err, timeout_err);
+                        s_fail = 1;
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(xfull + x, (unsigned)L::X_STAGE);
+                    tma_load_2d(Xb + (size_t)x * L::X_STAGE, &a.tmx, g * 64, tr.y, xfull + x, pol_x);
+                }
+            }
+            for (int q = k - NX; q < k; ++q)
+                if (q >= 0) mbar_wait_bounded(xfull + q % NX, (unsigned)((q / NX) & 1), 1u << 16);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
@@ -193,99 +297,92 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_const
                 }
                 tc_fence_after();
                 for (int g = 0; g < G; ++g, ++k) {
-                    const int s = k % NS;
-                    if (!mbar_wait_bounded(deq + s, (unsigned)((k / NS) & 1))) {
+                    const int sa = k % NA, sx = k % NX;
+                    if (!mbar_wait_bounded(afull + sa, (unsigned)((k / NA) & 1)) ||
+                        !mbar_wait_bounded(xfull + sx, (unsigned)((k / NX) & 1))) {
                         atomicOr(a.err, timeout_err);
                         s_fail = 1;
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const unsigned char *st = tsm + (size_t)s * L::STAGE;
-                    const uint64_t bdesc = sdesc_sw128(smem_u32(st + L::NP * L::A_BYTES));
+                    const uint64_t bdesc = sdesc_sw128(smem_u32(Xb + (size_t)sx * L::X_STAGE));
 #pragma unroll
                     for (int p = 0; p < L::NP; ++p) {
-                        const uint64_t adesc = sdesc_sw128(smem_u32(st + p * L::A_BYTES));
+                        const uint64_t adesc = sdesc_sw128(smem_u32(Ab + (size_t)sa * L::A_STAGE + p * L::A_BYTES));
                         const uint32_t d_tmem = tmem + (uint32_t)((b * L::NP + p) * NT);
 #pragma unroll
                         for (int ks = 0; ks < 4; ++ks)  // 16 k = 32 bytes along the swizzled row: +2 in 16-byte units
                             umma_bf16(d_tmem, adesc + 2 * ks, bdesc + 2 * ks, idesc, (g > 0 || ks > 0) ? 1u : 0u);
                     }
-                    umma_commit(empty + s);  // the stage is free once these MMAs have read it
+                    umma_commit(aempty + sa);  // both stages are free once these MMAs have read them
+                    umma_commit(xempty + sx);
                 }
                 if (ok) umma_commit(accf + b);
             }
             // MMAs still in flight finish before TMEM is released (bounded)
-            if (k > 0) mbar_wait_bounded(empty + (k - 1) % NS, (unsigned)(((k - 1) / NS) & 1), 1u << 16);
+            if (k > 0) mbar_wait_bounded(aempty + (k - 1) % NA, (unsigned)(((k - 1) / NA) & 1), 1u << 16);
         }
-    } else if (warp < 2 + TC_DQW) {
-        // ------------------------------------------------------------ dequant (8 warps, NP of the 8 * NP blocks each)
-        const int dw = warp - 2;
+    } else if (warp < 3 + L::DQW) {
+        // ------------------------------------------------------------ dequant (one (projection, row block) each)
+        const int dw = warp - 3;
+        const int p = dw >> 3, rb = dw & 7;
         const int gq = lane >> 2, c = lane & 3;
-        const uint32_t k128 = 0x43004300u;
         int k = 0;
         for (int it = 0; it < my_items && !*reinterpret_cast<volatile int *>(&s_fail); ++it) {
             bool ok = true;
             for (int g = 0; g < G; ++g, ++k) {
-                const int s = k % NS;
-                if (!mbar_wait_bounded(full + s, (unsigned)((k / NS) & 1))) {
+                const int r = k % NR, sa = k % NA;
+                if (!mbar_wait_bounded(rfull + r, (unsigned)((k / NR) & 1))) {
                     if (lane == 0) atomicOr(a.err, timeout_err);
                     ok = false;
                     break;
                 }
-                unsigned char *st = tsm + (size_t)s * L::STAGE;
-                const unsigned char *q = st + L::NP * L::A_BYTES + L::X_BYTES;
+                const unsigned char *q = Rb + (size_t)r * L::R_STAGE;
+                const uint4 w = reinterpret_cast<const uint4 *>(q + p * L::Q_BYTES + rb * 512)[lane];
+                const uint32_t *sbw = reinterpret_cast<const uint32_t *>(q + L::NP * L::Q_BYTES + p * L::S_BYTES + rb * L::SBG);
+                uint32_t sbv[2];
+                if (FMT == FMT_FP4) {
+                    sbv[0] = sbw[gq];
+                    sbv[1] = 0;
+                } else {
+                    sbv[0] = sbw[gq * 2];
+                    sbv[1] = sbw[gq * 2 + 1];
+                }
+                if (k >= NA && !mbar_wait_bounded(aempty + sa, (unsigned)(((k / NA) - 1) & 1))) {
+                    if (lane == 0) atomicOr(a.err, timeout_err);
+                    ok = false;
+                    break;
+                }
+                unsigned char *A = Ab + (size_t)sa * L::A_STAGE + p * L::A_BYTES;
+                uint32_t out[2][8];
+                dequant_block<FMT>(w, sbv[0], sbv[1], c, out);
 #pragma unroll
-                for (int j = 0; j < L::NP; ++j) {
-                    const int blk = dw + TC_DQW * j;  // (projection, row block)
-                    const int p = blk >> 3, rb = blk & 7;
-                    const uint4 w = reinterpret_cast<const uint4 *>(q + p * L::Q_BYTES + rb * 512)[lane];
-                    const uint32_t *sbw = reinterpret_cast<const uint32_t *>(q + L::NP * L::Q_BYTES + p * L::S_BYTES + rb * L::SBG);
-                    unsigned char *A = st + p * L::A_BYTES;
-#pragma unroll
-                    for (int hf = 0; hf < 2; ++hf) {  // rows gq (words .x .y) and gq + 8 (words .z .w)
-                        const int r = rb * 16 + gq + 8 * hf;
-                        const uint32_t wa = hf ? w.z : w.x, wb = hf ? w.w : w.y;
-                        uint32_t out[8];
-                        if (FMT == FMT_FP4) {
-                            // E2M1 * 2^(S-127) is exact in bf16; elements 16c .. 16c+15 share the scale of half c / 2
-                            const uint32_t S = (sbw[gq] >> (8 * (hf * 2 + (c >> 1)))) & 0xFFu;
-                            uint32_t lo[4], hi[4];
-                            fp4_word(wa, fp4_scale2(S), lo);
-                            fp4_word(wb, fp4_scale2(S), hi);
-#pragma unroll
-                            for (int i = 0; i < 4; ++i) {
-                                out[i] = lo[i];
-                                out[4 + i] = hi[i];
-                            }
-                        } else {
-                            const uint32_t sbv = sbw[gq * 2 + hf];
-                            const uint32_t s2 = (sbv & 0xFFFFu) | (sbv << 16), b2 = (sbv >> 16) | (sbv & 0xFFFF0000u);
-#pragma unroll
-                            for (int i = 0; i < 8; ++i) {
-                                const uint32_t v = q4pair(i < 4 ? wa : wb, i & 3);  // (128 + q_2p, 128 + q_2p+1)
-                                __nv_bfloat162 qv = *reinterpret_cast<const __nv_bfloat162 *>(&v);
-                                qv = __hsub2(qv, *reinterpret_cast<const __nv_bfloat162 *>(&k128));
-                                const __nv_bfloat162 r2 = __hfma2(qv, *reinterpret_cast<const __nv_bfloat162 *>(&s2),
-                                                                  *reinterpret_cast<const __nv_bfloat162 *>(&b2));
-                                out[i] = *reinterpret_cast<const uint32_t *>(&r2);
-                            }
-                        }
-                        // elements 16c .. 16c+15 of row r = chunks 2c, 2c+1 (16 B each), swizzled by r % 8
-                        uint4 *row = reinterpret_cast<uint4 *>(A + r * 128);
-                        row[(2 * c) ^ (r & 7)] = make_uint4(out[0], out[1], out[2], out[3]);
-                        row[(2 * c + 1) ^ (r & 7)] = make_uint4(out[4], out[5], out[6], out[7]);
-                    }
+                for (int hf = 0; hf < 2; ++hf) {  // rows gq and gq + 8
+                    const int rr = rb * 16 + gq + 8 * hf;
+                    // elements 16c .. 16c+15 of row rr = chunks 2c, 2c+1 (16 B each), swizzled by rr % 8
+                    uint4 *row = reinterpret_cast<uint4 *>(A + rr * 128);
+                    row[(2 * c) ^ (rr & 7)] = make_uint4(out[hf][0], out[hf][1], out[hf][2], out[hf][3]);
+                    row[(2 * c + 1) ^ (rr & 7)] = make_uint4(out[hf][4], out[hf][5], out[hf][6], out[hf][7]);
                 }
                 fence_async_smem();  // generic-proxy writes of A -> the tensor core's reads
                 __syncwarp();
-                if (lane == 0) mbar_arrive1(deq + s);
+                if (lane == 0) {
+                    mbar_arrive1(afull + sa);
+                    mbar_arrive1(rempty + r);  // the raw stage was consumed (its values are in A)
+                }
             }
-            if (!ok) break;
+            if (!ok) {
+                s_fail = 1;
+                break;
+            }
         }
     } else {
-        // ------------------------------------------------------------ epilogue (warps 10..13: rows 32 * (warp % 4) + lane)
+        // ------------------------------------------------------------ epilogue (TMEM lane quarter warp % 4)
+        const int ew = warp - 3 - L::DQW;
         const int quarter = warp & 3;
+        constexpr int HALVES = L::EPW / 4;  // warps sharing a quarter split the columns
+        const int half = ew >> 2;
         for (int it = 0; it < my_items && !*reinterpret_cast<volatile int *>(&s_fail); ++it) {
             const int item = (int)blockIdx.x + it * (int)gridDim.x;
             const int tile = item / MT, mt = item - tile * MT;
@@ -299,21 +396,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_const
             tc_fence_after();
             const int row = mt * TC_M + quarter * 32 + lane;  // output row (f for gate/up, d for down)
             const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16);
+            // this warp's columns: 16-column chunks half, half + HALVES, ... below the tile's slot count
             if (!DOWN) {
                 const float bgr = a.bg ? a.bg[(size_t)e * a.f + row] : 0.f, bur = a.bu ? a.bu[(size_t)e * a.f + row] : 0.f;
-                for (int c0 = 0; c0 < tr.z; c0 += 16) {
+                const int hrow = a.h_kperm ? kperm64(row) : row;  // the down kernel's k order
+                for (int c0 = 16 * half; c0 < tr.z; c0 += 16 * HALVES) {
                     float gv[16], uv[16];
                     tmem_ld16(tl + (uint32_t)((b * 2 + 0) * NT + c0), gv);
                     tmem_ld16(tl + (uint32_t)((b * 2 + 1) * NT + c0), uv);
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const int n = c0 + j;
-                        if (n < tr.z) a.h[(size_t)(tr.y + n) * a.f + row] = f2bf(act_glu(a.act, gv[j] + bgr, uv[j] + bur));
+                        if (n < tr.z) a.h[(size_t)(tr.y + n) * a.f + hrow] = f2bf(act_glu(a.act, gv[j] + bgr, uv[j] + bur));
                     }
                 }
             } else {
                 const float bdr = a.bd ? a.bd[(size_t)e * a.d + row] : 0.f;
-                for (int c0 = 0; c0 < tr.z; c0 += 16) {
+                for (int c0 = 16 * half; c0 < tr.z; c0 += 16 * HALVES) {
                     float dv[16];
                     tmem_ld16(tl + (uint32_t)(b * NT + c0), dv);
 #pragma unroll
@@ -342,34 +441,363 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_experts_tc(const __grid_const
     }
 }
 
-size_t experts_tc_smem(int nt, int ns, int acc, bool down, int fmt) {
-    (void)acc;
-    const int np = down ? 1 : 2, sbg = fmt == FMT_FP4 ? 32 : 64;
-    const size_t raw = (size_t)np * TC_M * 128 + (size_t)nt * 128 + (size_t)np * (8 * 512 + 8 * sbg);
-    const size_t stage = (raw + 1023) / 1024 * 1024;
-    return 1024 /* alignment slack */ + ns * stage + (3 * ns + 2 * acc) * 8;
+
+// ==================================================================== A operand in tensor memory
+// The same work decomposition with the dequantized weights written straight into TMEM (tcgen05.st) instead of
+// shared memory: no shared-memory stores or reads of A, no proxy fence. Rings:
+//   raw ring (NR stages): packed codes + scales from HBM (as above);
+//   operand ring (NS stages): the A tile in TMEM columns and the X tile in shared memory share one "ofull"
+//     barrier (DQW dequant arrivals + the X copy's transaction bytes) and one "oempty" (MMA commit).
+// The 16x256b TMEM store gives lane 4i + j of a warp columns 8m + 2j, 8m + 2j + 1 of rows i, i + 8, while the
+// int4 fragment gives it k = 16j .. 16j + 15. So inside every 64-group the operands use the k order
+// "position 16a + 4b + r holds k = 16b + 4a + r" (a digit swap, its own inverse): A by where the lanes store,
+// X by the gather that builds the expert-sorted rows, h by the gate/up epilogue that writes it (h_kperm). The
+// MMA sums over k, so the order does not change the products, only which bf16 pairs meet in the tensor core.
+
+namespace {
+template <int FMT, int NT, int NR, int NS, int ACC, bool DOWN>
+struct TAL {
+    static constexpr int NP = DOWN ? 1 : 2;
+    static constexpr int DQW = 8 * NP;                   // dequant warps: one (projection, row block) each
+    static constexpr int EPW = 8;                        // epilogue warps (two per TMEM lane quarter)
+    static constexpr int THREADS = 32 * (3 + DQW + EPW);
+    static constexpr int SBG = FMT == FMT_FP4 ? 32 : 64;
+    static constexpr int X_STAGE = NT * 128;
+    static constexpr int Q_BYTES = 8 * 512;
+    static constexpr int S_BYTES = 8 * SBG;
+    static constexpr int R_STAGE = NP * (Q_BYTES + S_BYTES);
+    static constexpr int OFF_R = NS * X_STAGE;
+    static constexpr int OFF_BAR = OFF_R + NR * R_STAGE;
+    static constexpr int NBAR = 2 * (NR + NS + ACC);
+    static constexpr int SMEM = 1024 + OFF_BAR + NBAR * 8;
+    static constexpr int A_COL0 = ACC * NP * NT;         // accumulators first, then the A stages (32 columns each)
+    static constexpr int TMEM_RAW = A_COL0 + NS * NP * 32;
+    static constexpr int TMEM_COLS = TMEM_RAW <= 32 ? 32 : TMEM_RAW <= 64 ? 64 : TMEM_RAW <= 128 ? 128
+                                   : TMEM_RAW <= 256 ? 256 : 512;
+    static_assert(TMEM_RAW <= 512, "TMEM allocation");
+    static_assert(SMEM <= 227 * 1024, "shared memory");
+    static_assert(X_STAGE % 1024 == 0 && R_STAGE % 128 == 0, "stage alignment");
+};
+}  // namespace
+
+template <int FMT, int NT, int NR, int NS, int ACC, bool DOWN>
+__global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN>::THREADS, 1)
+    k_experts_tca(const __grid_constant__ ExpArgs a) {
+    using L = TAL<FMT, NT, NR, NS, ACC, DOWN>;
+    pdl_launch();
+    pdl_wait();
+    extern __shared__ __align__(1024) unsigned char tsm_raw[];
+    unsigned char *tsm = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(tsm_raw) + 1023) & ~(uintptr_t)1023);
+    unsigned char *Xb = tsm, *Rb = tsm + L::OFF_R;
+    uint64_t *rfull = reinterpret_cast<uint64_t *>(tsm + L::OFF_BAR);
+    uint64_t *rempty = rfull + NR, *ofull = rempty + NR, *oempty = ofull + NS, *accf = oempty + NS, *acce = accf + ACC;
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_fail;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int RB = DOWN ? (a.d >> 4) : (a.f >> 4);
+    const int G = DOWN ? (a.f >> 6) : (a.d >> 6);
+    const int MT = RB / 8;
+    const int n_tiles = *a.ntiles;
+    const int n_items = n_tiles * MT;
+    const int my_items = (int)blockIdx.x < n_items ? (n_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NR; ++i) {
+            mbar_init(rfull + i, 1);
+            mbar_init(rempty + i, L::DQW);
+        }
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(ofull + i, L::DQW + 1);
+            mbar_init(oempty + i, 1);
+        }
+        for (int b = 0; b < ACC; ++b) {
+            mbar_init(accf + b, 1);
+            mbar_init(acce + b, L::EPW);
+        }
+        mbar_fence_init();
+        s_fail = 0;
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                     "r"((uint32_t)L::TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+    const int m0 = DOWN ? 2 : 0;
+    const unsigned timeout_err = ERR_TIMEOUT;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ raw producer (codes + scales, from HBM)
+        if (lane == 0) {
+            const uint64_t pol = l2_evict_first_policy();
+            for (int p = 0; p < L::NP; ++p) {
+                tmap_prefetch(&a.tmq[m0 + p]);
+                tmap_prefetch(&a.tmsb[m0 + p]);
+            }
+            int k = 0;
+            bool ok = true;
+            for (int it = 0; it < my_items && ok; ++it) {
+                const int item = (int)blockIdx.x + it * (int)gridDim.x;
+                const int tile = item / MT, mt = item - tile * MT;
+                const int4 tr = a.tiles[tile];
+                const int e = (tr.x < 0 || tr.x >= a.E) ? 0 : tr.x;
+                const int row0 = e * RB + mt * 8;
+                for (int g = 0; g < G; ++g, ++k) {
+                    const int r = k % NR;
+                    if (k >= NR && !mbar_wait_bounded(rempty + r, (unsigned)(((k / NR) - 1) & 1))) {
+                        atomicOr(a.err, timeout_err);
+                        s_fail = 1;
+                        ok = false;
+                        break;
+                    }
+                    unsigned char *q = Rb + (size_t)r * L::R_STAGE;
+                    mbar_expect_tx(rfull + r, (unsigned)L::R_STAGE);
+                    for (int p = 0; p < L::NP; ++p) {
+                        tma_load_2d(q + p * L::Q_BYTES, &a.tmq[m0 + p], g * 64, row0, rfull + r, pol);
+                        tma_load_2d(q + L::NP * L::Q_BYTES + p * L::S_BYTES, &a.tmsb[m0 + p], g * (L::SBG / 4), row0,
+                                    rfull + r, pol);
+                    }
+                }
+            }
+            for (int q = k - NR; q < k; ++q)
+                if (q >= 0) mbar_wait_bounded(rfull + q % NR, (unsigned)((q / NR) & 1), 1u << 16);
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------------------------ X producer (operand stage's B half, from L2)
+        if (lane == 0) {
+            const uint64_t pol_x = l2_evict_last_policy();
+            tmap_prefetch(&a.tmx);
+            int k = 0;
+            bool ok = true;
+            for (int it = 0; it < my_items && ok; ++it) {
+                const int item = (int)blockIdx.x + it * (int)gridDim.x;
+                const int4 tr = a.tiles[item / MT];
+                for (int g = 0; g < G; ++g, ++k) {
+                    const int s = k % NS;
+                    if (k >= NS && !mbar_wait_bounded(oempty + s, (unsigned)(((k / NS) - 1) & 1))) {
+                        atomicOr(a.err, timeout_err);
+                        s_fail = 1;
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(ofull + s, (unsigned)L::X_STAGE);
+                    tma_load_2d(Xb + (size_t)s * L::X_STAGE, &a.tmx, g * 64, tr.y, ofull + s, pol_x);
+                }
+            }
+            for (int q = k - NS; q < k; ++q)
+                if (q >= 0) mbar_wait_bounded(ofull + q % NS, (unsigned)((q / NS) & 1), 1u << 16);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            int k = 0;
+            bool ok = true;
+            for (int it = 0; it < my_items && ok; ++it) {
+                const int b = it % ACC, use = it / ACC;
+                const int item = (int)blockIdx.x + it * (int)gridDim.x;
+                const int nslot = a.tiles[item / MT].z;
+                const uint32_t idesc = idesc_bf16(TC_M, min(NT, max(16, (nslot + 15) & ~15)));
+                if (use >= 1 && !mbar_wait_bounded(acce + b, (unsigned)((use - 1) & 1))) {
+                    atomicOr(a.err, timeout_err);
+                    s_fail = 1;
+                    break;
+                }
+                tc_fence_after();
+                for (int g = 0; g < G; ++g, ++k) {
+                    const int s = k % NS;
+                    if (!mbar_wait_bounded(ofull + s, (unsigned)((k / NS) & 1))) {
+                        atomicOr(a.err, timeout_err);
+                        s_fail = 1;
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t bdesc = sdesc_sw128(smem_u32(Xb + (size_t)s * L::X_STAGE));
+#pragma unroll
+                    for (int p = 0; p < L::NP; ++p) {
+                        const uint32_t d_tmem = tmem + (uint32_t)((b * L::NP + p) * NT);
+                        const uint32_t a_tmem = tmem + (uint32_t)(L::A_COL0 + (s * L::NP + p) * 32);
+#pragma unroll
+                        for (int ks = 0; ks < 4; ++ks)  // 16 k = 8 TMEM columns of A, 32 bytes of the swizzled X row
+                            umma_bf16_ts(d_tmem, a_tmem + 8 * ks, bdesc + 2 * ks, idesc, (g > 0 || ks > 0) ? 1u : 0u);
+                    }
+                    umma_commit(oempty + s);
+                }
+                if (ok) umma_commit(accf + b);
+            }
+            if (k > 0) mbar_wait_bounded(oempty + (k - 1) % NS, (unsigned)(((k - 1) / NS) & 1), 1u << 16);
+        }
+    } else if (warp < 3 + L::DQW) {
+        // ------------------------------------------------------------ dequant: warp -> (projection, row block)
+        // whose 16 rows lie in its TMEM lane quarter (warp % 4)
+        const int i = warp - 3, quarter = warp & 3, j = i >> 2;
+        const int p = L::NP == 2 ? (j >> 1) : 0, rb = 2 * quarter + (j & 1);
+        const int gq = lane >> 2, c = lane & 3;
+        const uint32_t lane_addr = (uint32_t)(rb * 16) << 16;
+        int k = 0;
+        for (int it = 0; it < my_items && !*reinterpret_cast<volatile int *>(&s_fail); ++it) {
+            bool ok = true;
+            for (int g = 0; g < G; ++g, ++k) {
+                const int r = k % NR, s = k % NS;
+                if (!mbar_wait_bounded(rfull + r, (unsigned)((k / NR) & 1))) {
+                    if (lane == 0) atomicOr(a.err, timeout_err);
+                    ok = false;
+                    break;
+                }
+                const unsigned char *q = Rb + (size_t)r * L::R_STAGE;
+                const uint4 w = reinterpret_cast<const uint4 *>(q + p * L::Q_BYTES + rb * 512)[lane];
+                const uint32_t *sbw = reinterpret_cast<const uint32_t *>(q + L::NP * L::Q_BYTES + p * L::S_BYTES + rb * L::SBG);
+                const uint32_t sb0 = FMT == FMT_FP4 ? sbw[gq] : sbw[gq * 2], sb1 = FMT == FMT_FP4 ? 0u : sbw[gq * 2 + 1];
+                uint32_t out[2][8];
+                dequant_block<FMT>(w, sb0, sb1, c, out);
+                __syncwarp();  // every lane's reads of the raw stage are complete (their values are in out)
+                if (lane == 0) mbar_arrive1(rempty + r);
+                if (k >= NS && !mbar_wait_bounded(oempty + s, (unsigned)(((k / NS) - 1) & 1))) {
+                    if (lane == 0) atomicOr(a.err, timeout_err);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                uint32_t v[16];
+#pragma unroll
+                for (int m = 0; m < 4; ++m) {
+                    v[4 * m + 0] = out[0][2 * m];
+                    v[4 * m + 1] = out[0][2 * m + 1];
+                    v[4 * m + 2] = out[1][2 * m];
+                    v[4 * m + 3] = out[1][2 * m + 1];
+                }
+                tmem_st_16x256_x4(tmem + lane_addr + (uint32_t)(L::A_COL0 + (s * L::NP + p) * 32), v);
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive1(ofull + s);
+            }
+            if (!ok) {
+                s_fail = 1;
+                break;
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue (TMEM lane quarter warp % 4)
+        const int ew = warp - 3 - L::DQW;
+        const int quarter = warp & 3;
+        constexpr int HALVES = L::EPW / 4;
+        const int half = ew >> 2;
+        for (int it = 0; it < my_items && !*reinterpret_cast<volatile int *>(&s_fail); ++it) {
+            const int item = (int)blockIdx.x + it * (int)gridDim.x;
+            const int tile = item / MT, mt = item - tile * MT;
+            const int4 tr = a.tiles[tile];
+            const int e = (tr.x < 0 || tr.x >= a.E) ? 0 : tr.x;
+            const int b = it % ACC;
+            if (!mbar_wait_bounded(accf + b, (unsigned)((it / ACC) & 1))) {
+                if (lane == 0) atomicOr(a.err, timeout_err);
+                break;
+            }
+            tc_fence_after();
+            const int row = mt * TC_M + quarter * 32 + lane;
+            const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16);
+            if (!DOWN) {
+                const float bgr = a.bg ? a.bg[(size_t)e * a.f + row] : 0.f, bur = a.bu ? a.bu[(size_t)e * a.f + row] : 0.f;
+                const int hrow = a.h_kperm ? kperm64(row) : row;
+                for (int c0 = 16 * half; c0 < tr.z; c0 += 16 * HALVES) {
+                    float gv[16], uv[16];
+                    tmem_ld16(tl + (uint32_t)((b * 2 + 0) * NT + c0), gv);
+                    tmem_ld16(tl + (uint32_t)((b * 2 + 1) * NT + c0), uv);
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) {
+                        const int n = c0 + jj;
+                        if (n < tr.z) a.h[(size_t)(tr.y + n) * a.f + hrow] = f2bf(act_glu(a.act, gv[jj] + bgr, uv[jj] + bur));
+                    }
+                }
+            } else {
+                const float bdr = a.bd ? a.bd[(size_t)e * a.d + row] : 0.f;
+                for (int c0 = 16 * half; c0 < tr.z; c0 += 16 * HALVES) {
+                    float dv[16];
+                    tmem_ld16(tl + (uint32_t)(b * NT + c0), dv);
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) {
+                        const int n = c0 + jj;
+                        if (n < tr.z) {
+                            const int slot = a.sorted[tr.y + n];
+                            const int e_raw = a.idx[slot];
+                            const float wsl = (e_raw >= 0 && e_raw < a.E) ? a.wts[slot] : 0.f;
+                            a.yp[(size_t)slot * a.d + row] = wsl * (dv[jj] + bdr);
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive1(acce + b);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)L::TMEM_COLS)
+                     : "memory");
+    }
 }
 
-// x rows of the slots in expert-sorted order (the activation operand of the tensor-core gate/up)
+// Configurations. TMEM-operand kernels (k_experts_tca) wherever their accumulators and A stages fit the 512
+// TMEM columns: gate/up tiles of 32 / 64 / 128 slots, down tiles of 32 .. 256. Gate/up tiles of 256 need all 512
+// columns for the two accumulators and keep A in shared memory (k_experts_tc). Raw and operand rings are as deep
+// as the 227 KB of shared memory allow.
+//   tca: (NT, NR, NS, ACC, DOWN)       tc: (NT, NR, NA, NX, ACC, DOWN)
+#define MOEB_TCA_CFGS(X) \
+    X(32, 16, 6, 2, false) X(64, 16, 4, 2, false) X(128, 16, 4, 1, false) \
+    X(32, 24, 8, 2, true) X(64, 24, 8, 2, true) X(128, 24, 6, 2, true) X(256, 16, 4, 1, true)
+
+TcInfo experts_tc_info(int fmt, int nt, bool down) {
+    TcInfo r = {nullptr, 0, 0, false};
+#define MOEB_TCA_PICK(NT_, NR_, NS_, ACC_, DOWN_)                                                     \
+    if (nt == NT_ && down == DOWN_) {                                                                 \
+        if (fmt == FMT_FP4) {                                                                         \
+            using L = TAL<FMT_FP4, NT_, NR_, NS_, ACC_, DOWN_>;                                        \
+            r = {k_experts_tca<FMT_FP4, NT_, NR_, NS_, ACC_, DOWN_>, L::THREADS, (size_t)L::SMEM, true}; \
+        } else {                                                                                      \
+            using L = TAL<FMT_Q4, NT_, NR_, NS_, ACC_, DOWN_>;                                         \
+            r = {k_experts_tca<FMT_Q4, NT_, NR_, NS_, ACC_, DOWN_>, L::THREADS, (size_t)L::SMEM, true};   \
+        }                                                                                             \
+    }
+    MOEB_TCA_CFGS(MOEB_TCA_PICK)
+#undef MOEB_TCA_PICK
+    if (nt == 256 && !down) {
+        if (fmt == FMT_FP4) {
+            using L = TCL<FMT_FP4, 256, 6, 2, 3, 1, false>;
+            r = {k_experts_tc<FMT_FP4, 256, 6, 2, 3, 1, false>, L::THREADS, (size_t)L::SMEM, false};
+        } else {
+            using L = TCL<FMT_Q4, 256, 6, 2, 3, 1, false>;
+            r = {k_experts_tc<FMT_Q4, 256, 6, 2, 3, 1, false>, L::THREADS, (size_t)L::SMEM, false};
+        }
+    }
+    return r;
+}
+
+// x rows of the slots in expert-sorted order (the activation operand of the tensor-core gate/up); perm: in the
+// 64-group k order of the TMEM-operand kernels (8-byte chunks of 4 k: chunk 4b + a goes to 4a + b)
 __global__ void __launch_bounds__(256) k_gather_rows(const uint16_t *__restrict__ x, const int *__restrict__ sorted,
-                                                     int TK, int k, int d, uint16_t *__restrict__ xs) {
+                                                     int TK, int k, int d, int perm, uint16_t *__restrict__ xs) {
     pdl_launch();
     pdl_wait();
     const int i = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (i >= TK) return;
-    const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)(sorted[i] / k) * d);
-    uint4 *dst = reinterpret_cast<uint4 *>(xs + (size_t)i * d);
-    for (int c = lane; c < d / 8; c += 32) dst[c] = src[c];
+    if (!perm) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)(sorted[i] / k) * d);
+        uint4 *dst = reinterpret_cast<uint4 *>(xs + (size_t)i * d);
+        for (int c = lane; c < d / 8; c += 32) dst[c] = src[c];
+    } else {
+        const uint2 *src = reinterpret_cast<const uint2 *>(x + (size_t)(sorted[i] / k) * d);
+        uint2 *dst = reinterpret_cast<uint2 *>(xs + (size_t)i * d);
+        for (int c = lane; c < d / 4; c += 32) {
+            const int u = c & 15;
+            dst[(c & ~15) | ((u & 3) << 2) | (u >> 2)] = src[c];
+        }
+    }
 }
-
-// gate/up: tiles of 256 slots with one accumulator set (2 x 256 TMEM columns) or of 128 with two; down: 4 stages,
-// two sets
-#define MOEB_TC(FMT)                                                                         \
-    template __global__ void k_experts_tc<FMT, 256, 3, 1, false>(const __grid_constant__ ExpArgs); \
-    template __global__ void k_experts_tc<FMT, 256, 4, 2, true>(const __grid_constant__ ExpArgs);  \
-    template __global__ void k_experts_tc<FMT, 128, 3, 2, false>(const __grid_constant__ ExpArgs); \
-    template __global__ void k_experts_tc<FMT, 128, 4, 2, true>(const __grid_constant__ ExpArgs);
-MOEB_TC(FMT_Q4)
-MOEB_TC(FMT_FP4)
 
 }  // namespace moeb

@@ -79,6 +79,7 @@ struct ExpArgs {
     int T, d, f, E, k, act, tile_mode;
     int dn_prefetch;  // gate/up pulls the down weights of its expert into L2
     int fmt;          // FMT_Q4 or FMT_FP4
+    int h_kperm;      // gate/up writes h with the 64-group k order permuted for a TMEM-operand tensor-core down
     int slot_out;     // 1: down stops after writing the weighted per-slot outputs yp (caller's buffer), no combine
     // peer-memory exchange: slot s's weighted row goes to (float *)(ypeers[s / C] + yoff) + (me * C + s % C) * d
     // (C = this call's block size), this rank's return block in the owner's buffer, instead of yp; the writing
@@ -170,10 +171,20 @@ template <int FMT, int NT8, int GPW>
 __global__ void k_down_tiles_reg(ExpArgs a);
 template <int FMT, int NT8, int RBC, int SG, int NS, bool DOWN, int MB>
 __global__ void k_experts_ws(const __grid_constant__ ExpArgs a);
-template <int FMT, int NT, int NS, int ACC, bool DOWN>
+template <int FMT, int NT, int NR, int NA, int NX, int ACC, bool DOWN>
 __global__ void k_experts_tc(const __grid_constant__ ExpArgs a);
-size_t experts_tc_smem(int nt, int ns, int acc, bool down, int fmt);
-__global__ void k_gather_rows(const uint16_t *x, const int *sorted, int TK, int k, int d, uint16_t *xs);
+template <int FMT, int NT, int NR, int NS, int ACC, bool DOWN>
+__global__ void k_experts_tca(const __grid_constant__ ExpArgs a);
+// The tcgen05 expert kernel for (format, tile size 32 / 64 / 128 / 256, projection): entry, block size and
+// dynamic shared memory (fn == nullptr for an unsupported tile size).
+struct TcInfo {
+    void (*fn)(ExpArgs);
+    int threads;
+    size_t smem;
+    bool tmem_a;  // A operand in TMEM: activations in the permuted 64-group k order
+};
+TcInfo experts_tc_info(int fmt, int nt, bool down);
+__global__ void k_gather_rows(const uint16_t *x, const int *sorted, int TK, int k, int d, int perm, uint16_t *xs);
 size_t experts_ws_smem(int nt8, int rbc, int sg, int ns, bool down, int fmt);
 
 

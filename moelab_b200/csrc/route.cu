@@ -50,20 +50,37 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int *total) {
 
 // Counting sort of the TK slots by expert. Slot order inside an expert follows atomic arrival; this does not
 // change any result (every slot is its own MMA column and the combine sums slots in fixed j order).
+// The ids are read in batches of BT independent loads per thread (one L2 round trip per batch, not per slot);
+// when the launch gave enough dynamic shared memory (8 E + 4 TK bytes) they are kept there for the second pass.
 __device__ void build_tiles(const int *__restrict__ idx, int TK, int E, int NT, int4 *__restrict__ tiles,
                             int *__restrict__ ntiles, int *__restrict__ sorted, unsigned *__restrict__ err) {
+    constexpr int BT = 16;
     extern __shared__ int smem[];
     int *cnt = smem;      // [E]
     int *off = smem + E;  // [E]
+    int *ids = smem + 2 * E;  // [TK] when it fits
+    unsigned dsm;
+    asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dsm));
+    const bool cache = (size_t)(2 * E + TK) * 4 <= dsm;
     const int tid = threadIdx.x, nth = blockDim.x;
     for (int e = tid; e < E; e += nth) cnt[e] = 0;
     __syncthreads();
     bool bad = false;
-    for (int s = tid; s < TK; s += nth) {
-        int e = __ldcg(idx + s);
-        if (e == SLOT_SKIP) continue;  // capacity padding: no work, not an error
-        if (e < 0 || e >= E) { bad = true; e = 0; }
-        atomicAdd(&cnt[e], 1);
+    for (int s0 = tid; s0 < TK; s0 += nth * BT) {
+        int ev[BT];
+#pragma unroll
+        for (int i = 0; i < BT; ++i) {
+            const int s = s0 + i * nth;
+            ev[i] = s < TK ? __ldcg(idx + s) : SLOT_SKIP;
+        }
+#pragma unroll
+        for (int i = 0; i < BT; ++i) {
+            int e = ev[i];
+            if (cache && s0 + i * nth < TK) ids[s0 + i * nth] = e;
+            if (e == SLOT_SKIP) continue;  // capacity padding (or past TK): no work, not an error
+            if (e < 0 || e >= E) { bad = true; e = 0; }
+            atomicAdd(&cnt[e], 1);
+        }
     }
     if (bad) atomicOr(err, ERR_EXPERT_ID);
     __syncthreads();
@@ -90,12 +107,21 @@ __device__ void build_tiles(const int *__restrict__ idx, int TK, int E, int NT, 
     __syncthreads();
     for (int e = tid; e < E; e += nth) cnt[e] = 0;
     __syncthreads();
-    for (int s = tid; s < TK; s += nth) {
-        int e = __ldcg(idx + s);
-        if (e == SLOT_SKIP) continue;
-        if (e < 0 || e >= E) e = 0;
-        const int pos = atomicAdd(&cnt[e], 1);
-        sorted[off[e] + pos] = s;
+    for (int s0 = tid; s0 < TK; s0 += nth * BT) {
+        int ev[BT];
+#pragma unroll
+        for (int i = 0; i < BT; ++i) {
+            const int s = s0 + i * nth;
+            ev[i] = s >= TK ? SLOT_SKIP : cache ? ids[s] : __ldcg(idx + s);
+        }
+#pragma unroll
+        for (int i = 0; i < BT; ++i) {
+            int e = ev[i];
+            if (e == SLOT_SKIP) continue;
+            if (e < 0 || e >= E) e = 0;
+            const int pos = atomicAdd(&cnt[e], 1);
+            sorted[off[e] + pos] = s0 + i * nth;
+        }
     }
 }
 

@@ -62,6 +62,10 @@ class Workspace:
                 self.buf, self.T = buf, Tn
             return self.buf
 
+    def for_k(self, k):
+        """This workspace if it was sized for k slots per token, else a new one for k (the layout depends on k)."""
+        return self if self.k == k else Workspace(self.d, self.f, self.E, k, self.device, self.ep)
+
     def read_error(self):
         """Sticky device error bits (MOEB_DEVERR_*); synchronises the current stream and clears them."""
         if self.buf is None:
@@ -184,7 +188,7 @@ def experts_q4(state, x, idx, wts, act=0, policy=POLICY_AUTO, residual=None):
     T, d = x.shape
     k = idx.shape[1]
     E, f = state["E"], state["f"]
-    ws = state["ws"]
+    ws = state["ws"] = state["ws"].for_k(k)
     buf = ws.get(max(T, 1))
     y = torch.empty_like(x)
     fn = "moeb_experts_mxfp4" if _fmt(state) == "mxfp4" else "moeb_experts_q4"
@@ -208,9 +212,10 @@ def layer_q4(state, x, gate_w, k, gate_b=None, norm=True, rscale=1.0, act=0, pol
     _need(residual, torch.bfloat16, "residual")
     T, d = x.shape
     E, f = state["E"], state["f"]
+    ks = k + n_shared
+    state["ws"] = state["ws"].for_k(ks)
     buf = state["ws"].get(max(T, 1))
     y = torch.empty_like(x)
-    ks = k + n_shared
     idx = torch.empty(T, ks, dtype=torch.int32, device=x.device) if return_routing else None
     wts = torch.empty(T, ks, dtype=torch.float32, device=x.device) if return_routing else None
     evp = None

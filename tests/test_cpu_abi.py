@@ -60,6 +60,7 @@ def test_host_only_calls():
     assert lib.moeb_policy(2, 128, 8) == _lib.POLICY_SLOTS
     assert lib.moeb_policy(4, 128, 8) == _lib.POLICY_TILES8_RING
     assert lib.moeb_policy(256, 128, 8) in (_lib.POLICY_TILES8_RING, _lib.POLICY_TILES16_RING)
+    assert lib.moeb_policy(384, 128, 8) == _lib.POLICY_TC  # 24 slots per expert: tcgen05 tiles
 
 
 def test_bad_shape_is_rejected_before_any_device_work():

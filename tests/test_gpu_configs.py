@@ -132,11 +132,13 @@ def test_mixtral(mixtral, fmt, routing, T):
     assert_close(y, ref, what=(fmt, routing, T))
 
 
-# ------------------------------------------------------------------ tensor-core policy (tcgen05, tiles of 128)
-@pytest.mark.parametrize("T,routing", [(1, "uniform"), (3, "uniform"), (64, "uniform"), (300, "uniform"),
-                                       (300, "one_hot"), (513, "zipf")])
+# ------------------------------------------------------------------ tensor-core policy (tcgen05, tiles of 32..256)
+# E = 8, k = 2: T = 1, 3, 64 -> tiles of 32 slots, 200 -> 64, 300 / 513 -> 128, 600 -> 256
+@pytest.mark.parametrize("T,routing", [(1, "uniform"), (3, "uniform"), (64, "uniform"), (200, "uniform"),
+                                       (200, "one_hot"), (300, "uniform"), (300, "one_hot"), (513, "zipf"),
+                                       (600, "uniform"), (600, "one_hot")])
 def test_tc_small_vs_oracle(T, routing):
-    """Tiles of up to 128 slots on the tensor cores: partial tiles, several tiles per expert, empty experts."""
+    """tcgen05 tiles of every size: partial tiles, several tiles per expert, empty experts."""
     from helpers import problem_tensors
     from moelab_b200.shapes import MoEShape
     sh = MoEShape("tc", d=256, f=384, E=8, k=2)
@@ -191,6 +193,20 @@ def test_tc_mixtral_mxfp4(mixtral, T):
     b200_mxfp4_moe._ws(st, 2)
     y = ops.experts(st, x, it, wt, policy=ops.POLICY_TC)
     assert_close(y, torch_ref(b200_mxfp4_moe, st, x, it, wt, deq), what=T)
+
+
+@pytest.mark.parametrize("T", [3, 200, 300, 600])
+def test_tc_small_mxfp4(T):
+    """MXFP4 on the tensor cores (E2M1 x 2^(S-127) dequantized exactly to bf16) for each tile size."""
+    from helpers import problem_tensors
+    from moelab_b200.shapes import MoEShape
+    sh = MoEShape("tc", d=256, f=384, E=8, k=2)
+    p, w, x, idx, wts = problem_tensors(sh, T, "uniform", seed=T)
+    st = b200_mxfp4_moe.prepare(*w)
+    b200_mxfp4_moe._ws(st, sh.k)
+    y = ops.experts(st, x, idx, wts, policy=ops.POLICY_TC)
+    assert_close(y, ref_from_state(b200_mxfp4_moe, st, x, idx, wts), what=T)
+    assert st["ws"].read_error() == 0
 
 
 def test_tc_rejects_unsupported_shapes():
