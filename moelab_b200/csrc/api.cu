@@ -388,6 +388,31 @@ void (*router_kernel(int E))(RouterArgs) {
     return k_router<TPB, 32, U>;
 }
 
+// The register-tiled router needs enough (token block, expert block) CTAs to fill the GPU. Measured (CUDA graph,
+// router alone): E = 128, d = 2048, T = 256 / 1024 / 4096: 11.4 / 34.5 / 127 us vs 21.9 / 68.7 / 277 us for the
+// one-expert-per-warp kernel, which stays ahead below T * E = 16384 (E = 128, T = 32: 8.5 vs 9.1 us; E = 32,
+// T = 256: 9.6 vs 11.5 us) and for few experts up to T = 4096 (E = 8, T = 1024: 11.2 vs 15.2 us).
+// MOEB_ROUTER_TILED_T, if set, replaces the rule with "T >= value" (for measurements).
+bool router_tiled(int T, int E) {
+    static const int v = [] {
+        const char *s = getenv("MOEB_ROUTER_TILED_T");
+        return s ? atoi(s) : -1;
+    }();
+    if (v >= 0) return T >= v;
+    return E >= 32 ? (long)T * E >= 16384 : T >= 4096;
+}
+
+template <int EW>
+void (*router_t_kernel(int E))(RouterArgs) {
+    const int J = (E + 31) / 32;
+    if (J <= 1) return k_router_t<4, EW, 1>;
+    if (J <= 2) return k_router_t<4, EW, 2>;
+    if (J <= 4) return k_router_t<4, EW, 4>;
+    if (J <= 8) return k_router_t<4, EW, 8>;
+    if (J <= 16) return k_router_t<4, EW, 16>;
+    return k_router_t<4, EW, 32>;
+}
+
 // E, k: routed experts / slots; ns shared experts follow as ids E .. E + ns - 1 (slots per token k + ns).
 int launch_router(const void *x, const void *wg, const void *bias, int T, int d, int E, int k, int norm,
                   float scale, int *idx, float *wts, float *logits, bool want_xsum, int policy, const Layout &L,
@@ -414,10 +439,19 @@ int launch_router(const void *x, const void *wg, const void *bias, int T, int d,
     // router CTA carries this allocation, so it is capped to keep the logits phase at full occupancy)
     size_t smem = tiles ? 8 * (size_t)(E + ns) : 0;
     if (tiles && smem + 4 * (size_t)T * (k + ns) <= 16 * 1024) smem += 4 * (size_t)T * (k + ns);
-    // tokens per CTA: 1 up to T = 64 (more CTAs in flight, the gate row re-read from L2), 4 above
-    const int tpb = T <= 64 ? 1 : 4;
-    void (*kern)(RouterArgs) = tpb == 1 ? router_kernel<1, 8>(E) : router_kernel<4, 4>(E);
-    if (launch(kern, dim3((E + 3) / 4, (T + tpb - 1) / tpb), dim3(128), smem, st, r) != cudaSuccess)
+    // one expert per warp and 1 (T <= 64) or 4 tokens, or the register-tiled kernel (4 tokens x EW experts per
+    // warp, EW = 4 from 32 experts on)
+    cudaError_t e;
+    if (router_tiled(T, E)) {
+        const int ew = E >= 32 ? 4 : E >= 16 ? 2 : 1;
+        void (*kern)(RouterArgs) = ew == 4 ? router_t_kernel<4>(E) : ew == 2 ? router_t_kernel<2>(E) : router_t_kernel<1>(E);
+        e = launch(kern, dim3((E + 8 * ew - 1) / (8 * ew), (T + 3) / 4), dim3(256), smem, st, r);
+    } else {
+        const int tpb = T <= 64 ? 1 : 4;
+        void (*kern)(RouterArgs) = tpb == 1 ? router_kernel<1, 8>(E) : router_kernel<4, 4>(E);
+        e = launch(kern, dim3((E + 3) / 4, (T + tpb - 1) / tpb), dim3(128), smem, st, r);
+    }
+    if (e != cudaSuccess)
         return check_launch("router");
     return MOEB_OK;
 }

@@ -150,6 +150,8 @@ __global__ void k_ep_combine(const float *back, const int *slot_pos, int T, int 
 
 template <int TPB, int JMAX, int U>
 __global__ void k_router(RouterArgs a);
+template <int TW, int EW, int JMAX>
+__global__ void k_router_t(RouterArgs a);
 __global__ void k_prep(PrepArgs a);
 
 __global__ void k_q4_quantize(const uint16_t *w, long rows, long K, uint32_t *qw, uint32_t *sb);

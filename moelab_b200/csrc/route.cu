@@ -125,6 +125,40 @@ __device__ void build_tiles(const int *__restrict__ idx, int TK, int E, int NT, 
     }
 }
 
+// After a router CTA has written its logits: the last CTA of each token block (last-arriver counter, no spin)
+// runs top-k for the block's tokens; in tile mode the last token block to finish builds the tiles.
+template <int JMAX>
+__device__ __forceinline__ void router_tail(const RouterArgs &a, int t0, int nt, int warp, int lane) {
+    // the barrier orders the CTA's logits before thread 0's fence (cumulative), the counter picks the last CTA
+    // of the token block, whose thread 0 fences again before the reads
+    __shared__ int s_last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned prev = atomicAdd(a.cnt + blockIdx.y, 1u);
+        s_last = prev == gridDim.x - 1;
+        if (s_last) __threadfence();
+    }
+    __syncthreads();
+    if (!s_last) return;
+    const int nw = blockDim.x >> 5;
+    for (int i = warp; i < nt; i += nw) topk_token<JMAX>(a, t0 + i, lane);
+    if (threadIdx.x == 0) a.cnt[blockIdx.y] = 0;
+    if (a.tiles == nullptr) return;
+    // routing step in the last token block to finish
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned prev = atomicAdd(a.cnt_all, 1u);
+        s_last = prev == gridDim.y - 1;
+        if (s_last) __threadfence();
+    }
+    __syncthreads();
+    if (!s_last) return;
+    build_tiles(a.idx, a.T * (a.k + a.ns), a.E + a.ns, a.NT, a.tiles, a.ntiles, a.sorted, a.err);
+    if (threadIdx.x == 0) *a.cnt_all = 0;
+}
+
 // grid (ceil(E / 4), ceil(T / TPB)), block 128: warp w computes expert blockIdx.x * 4 + w for TPB tokens.
 // Each lane loads U chunks of the gate row and of every token row at once, then runs the fmaf chains; warp 0 of
 // the first expert block also turns its x registers into the per-64-group sums.
@@ -197,33 +231,104 @@ __global__ void __launch_bounds__(128) k_router(RouterArgs a) {
             if (lane == 0 && i < nt) a.logits[(size_t)(t0 + i) * a.E + e] = v;
         }
     }
-    // last-arriver hand-off: the barrier orders the CTA's logits before thread 0's fence (cumulative), the
-    // counter picks the last CTA of the token block, whose thread 0 fences again before the reads
-    __shared__ int s_last;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        const unsigned prev = atomicAdd(a.cnt + blockIdx.y, 1u);
-        s_last = prev == gridDim.x - 1;
-        if (s_last) __threadfence();
+    router_tail<JMAX>(a, t0, nt, warp, lane);
+}
+
+// Register-tiled logits for larger T. grid (ceil(E / (8 EW)), ceil(T / TW)), block 256: warp w computes
+// experts (blockIdx.x * 8 + w) * EW .. + EW - 1 for the block's TW tokens. Every (token, expert) dot product is
+// summed exactly as in k_router (lane l: chunks l, l + 32, ... in order, fmaf over each chunk's 8 elements, then
+// the xor butterfly), so the logits and ids are bit-identical; the tile only reuses each loaded x / gate chunk
+// and its bf16 -> fp32 conversion across EW experts / TW tokens.
+template <int TW, int EW, int JMAX>
+__global__ void __launch_bounds__(256) k_router_t(RouterArgs a) {
+    pdl_launch();
+    pdl_wait();
+    constexpr int U = 2;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int e0 = (blockIdx.x * 8 + warp) * EW;
+    const int t0 = blockIdx.y * TW;
+    const int nt = min(TW, a.T - t0);
+    const int nch = a.d / 8;
+    const bool do_xsum = a.xsum != nullptr && blockIdx.x == 0 && warp == 0;
+    if (e0 < a.E) {
+        float acc[TW][EW];
+#pragma unroll
+        for (int i = 0; i < TW; ++i)
+#pragma unroll
+            for (int j = 0; j < EW; ++j) acc[i][j] = 0.f;
+        const uint16_t *wr[EW];
+        const uint16_t *xr[TW];
+#pragma unroll
+        for (int j = 0; j < EW; ++j) wr[j] = a.wg + (size_t)min(e0 + j, a.E - 1) * a.d;  // clamped rows: never stored
+#pragma unroll
+        for (int i = 0; i < TW; ++i) xr[i] = a.x + (size_t)(t0 + min(i, nt - 1)) * a.d;
+        for (int c0 = lane; c0 - lane < nch; c0 += 32 * U) {  // same trip count on every lane (shuffles below)
+            uint4 w[U][EW], xv[U][TW];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int c = min(c0 + 32 * u, nch - 1);  // clamped: a repeated load, never used
+#pragma unroll
+                for (int j = 0; j < EW; ++j) w[u][j] = *reinterpret_cast<const uint4 *>(wr[j] + 8 * c);
+#pragma unroll
+                for (int i = 0; i < TW; ++i) xv[u][i] = *reinterpret_cast<const uint4 *>(xr[i] + 8 * c);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                if (c0 + 32 * u < nch) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        float wl[EW], wh[EW];
+#pragma unroll
+                        for (int j = 0; j < EW; ++j) {
+                            const uint32_t ww = q == 0 ? w[u][j].x : q == 1 ? w[u][j].y : q == 2 ? w[u][j].z : w[u][j].w;
+                            wl[j] = bf16lo(ww);
+                            wh[j] = bf16hi(ww);
+                        }
+#pragma unroll
+                        for (int i = 0; i < TW; ++i) {
+                            const uint32_t xx = q == 0 ? xv[u][i].x : q == 1 ? xv[u][i].y : q == 2 ? xv[u][i].z : xv[u][i].w;
+                            const float xl = bf16lo(xx), xh = bf16hi(xx);
+#pragma unroll
+                            for (int j = 0; j < EW; ++j) {
+                                acc[i][j] = __fmaf_rn(xl, wl[j], acc[i][j]);
+                                acc[i][j] = __fmaf_rn(xh, wh[j], acc[i][j]);
+                            }
+                        }
+                    }
+                }
+            }
+            if (do_xsum) {  // chunk c of lane l covers group c / 8: 8 consecutive lanes share a group
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int c = c0 + 32 * u;
+#pragma unroll
+                    for (int i = 0; i < TW; ++i) {
+                        const uint4 v = xv[u][i];
+                        float p = bf16lo(v.x) + bf16hi(v.x) + bf16lo(v.y) + bf16hi(v.y) + bf16lo(v.z) +
+                                  bf16hi(v.z) + bf16lo(v.w) + bf16hi(v.w);
+                        p += __shfl_xor_sync(0xffffffffu, p, 1);
+                        p += __shfl_xor_sync(0xffffffffu, p, 2);
+                        p += __shfl_xor_sync(0xffffffffu, p, 4);
+                        if (i < nt && c < nch && (lane & 7) == 0) a.xsum[(size_t)(t0 + i) * xsum_stride(a.d) + c / 8] = p;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < EW; ++j) {
+            const int e = e0 + j;
+            const float bias = (a.bias && e < a.E) ? bf2f(a.bias[e]) : 0.f;
+#pragma unroll
+            for (int i = 0; i < TW; ++i) {
+                float v = acc[i][j];
+#pragma unroll
+                for (int o = 16; o >= 1; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+                if (a.bias) v = __fadd_rn(v, bias);
+                if (lane == 0 && i < nt && e < a.E) a.logits[(size_t)(t0 + i) * a.E + e] = v;
+            }
+        }
     }
-    __syncthreads();
-    if (!s_last) return;
-    for (int i = warp; i < nt; i += 4) topk_token<JMAX>(a, t0 + i, lane);
-    if (threadIdx.x == 0) a.cnt[blockIdx.y] = 0;
-    if (a.tiles == nullptr) return;
-    // routing step in the last token block to finish
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        const unsigned prev = atomicAdd(a.cnt_all, 1u);
-        s_last = prev == gridDim.y - 1;
-        if (s_last) __threadfence();
-    }
-    __syncthreads();
-    if (!s_last) return;
-    build_tiles(a.idx, a.T * (a.k + a.ns), a.E + a.ns, a.NT, a.tiles, a.ntiles, a.sorted, a.err);
-    if (threadIdx.x == 0) *a.cnt_all = 0;
+    router_tail<JMAX>(a, t0, nt, warp, lane);
 }
 
 // Harness path (ids given): grid ceil(T / 8), block 256. Per-token x group sums; tile mode: the last CTA
@@ -289,5 +394,16 @@ __global__ void __launch_bounds__(256) k_prep(PrepArgs a) {
 MOEB_ROUTER_INST(1, 8)
 MOEB_ROUTER_INST(4, 4)
 #undef MOEB_ROUTER_INST
+#define MOEB_ROUTER_T_INST(EW)                               \
+    template __global__ void k_router_t<4, EW, 1>(RouterArgs);  \
+    template __global__ void k_router_t<4, EW, 2>(RouterArgs);  \
+    template __global__ void k_router_t<4, EW, 4>(RouterArgs);  \
+    template __global__ void k_router_t<4, EW, 8>(RouterArgs);  \
+    template __global__ void k_router_t<4, EW, 16>(RouterArgs); \
+    template __global__ void k_router_t<4, EW, 32>(RouterArgs);
+MOEB_ROUTER_T_INST(1)
+MOEB_ROUTER_T_INST(2)
+MOEB_ROUTER_T_INST(4)
+#undef MOEB_ROUTER_T_INST
 
 }  // namespace moeb

@@ -79,7 +79,7 @@ def test_quantize_mxfp4_bit_exact(rows, K, mult):
 # ------------------------------------------------------------------ router
 @pytest.mark.parametrize("E,k", [(8, 2), (16, 6), (32, 4), (60, 4), (64, 6), (128, 8), (256, 8), (128, 1), (512, 32),
                                  (1000, 8)])
-@pytest.mark.parametrize("T", [1, 7, 64])
+@pytest.mark.parametrize("T", [1, 7, 18, 64, 300])
 def test_router_bit_exact(E, k, T):
     g = torch.Generator(device="cuda").manual_seed(E * 131 + T + k)
     d = 256 if E >= 512 else 2048
@@ -99,6 +99,38 @@ def test_router_bit_exact(E, k, T):
         if a != b:
             gap = np.sort(lg64[t])[::-1]
             assert abs(gap[k - 1] - gap[k]) < 1e-4, (t, a ^ b)
+
+
+_TILED_ROUTER_CHECK = """
+import sys, numpy as np, torch
+sys.path.insert(0, {root!r})
+import oracle
+from moelab_b200 import ops
+for E, k, d in [(8, 2, 4096), (16, 6, 2048), (32, 4, 2880), (128, 8, 2048)]:
+    for T in [1, 5, 18, 64]:
+        g = torch.Generator(device="cuda").manual_seed(E + T)
+        x = torch.randn(T, d, generator=g, device="cuda").to(torch.bfloat16)
+        wg = (torch.randn(E, d, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        b = torch.randn(E, generator=g, device="cuda").to(torch.bfloat16)
+        idx, wts, lg = ops.router(x, wg, k, gate_b=b, return_logits=True)
+        ref_lg = oracle.router_logits(x, wg, b)
+        assert np.array_equal(lg.cpu().numpy(), ref_lg), (E, T)
+        assert np.array_equal(idx.cpu().numpy(), oracle.topk(ref_lg, k)[0]), (E, T)
+print("ok")
+"""
+
+
+def test_router_tiled_kernel_every_variant():
+    """The register-tiled router (normally from T * E >= 16384) forced on for every T: 1, 2 and 4 experts per
+    warp, partial token blocks, bias; bit-exact logits and ids."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, MOEB_ROUTER_TILED_T="1")
+    r = subprocess.run([sys.executable, "-c", _TILED_ROUTER_CHECK.format(root=root)], env=env, capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-2000:]
 
 
 @pytest.mark.parametrize("E,k", [(16, 6), (60, 4), (64, 6), (128, 8)])
