@@ -363,6 +363,18 @@ int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaS
     // over the weighted slot rows when down is the warp-specialized kernel (no fences / counters in its epilogue)
     const bool sep = !a.slot_out && separate_combine(K.dn);
     if (sep) a.slot_out = 1;
+    // decode: one CTA per (token, 16-row block) with the token's k slots combined in shared memory
+    if (policy == MOEB_POLICY_SLOTS && !a.slot_out && a.k <= 8) {
+        const KLaunch tk = {fmt == FMT_FP4 ? k_down_tok<FMT_FP4, 4, 4> : k_down_tok<FMT_Q4, 4, 4>, 128 * a.k,
+                            down_tok_smem(a.k, a.f, 4), false, 1, 0};
+        if (tk.smem <= 200 * 1024) {
+            if (!allow_smem((const void *)tk.fn, tk.smem)) return check_launch("cudaFuncSetAttribute");
+            if (launch(tk.fn, dim3(grid_for(tk, (long)a.T * RBd)), dim3(tk.threads), tk.smem, st, a) != cudaSuccess)
+                return check_launch("down");
+            if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[3]), st);
+            return MOEB_OK;
+        }
+    }
     {
         const long units = max_tiles * ((RBd + K.dn.rows - 1) / K.dn.rows);
         if (launch(K.dn.fn, dim3(grid_for(K.dn, units)), dim3(K.dn.threads), K.dn.smem, st, a) != cudaSuccess)

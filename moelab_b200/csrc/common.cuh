@@ -87,6 +87,13 @@ template <int N>
 MOEB_DEV void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // ---- TMA bulk copies (cp.async.bulk, no multicast) completing on an mbarrier
+// Device-scope acquire-release add: the last-arriver hand-offs use it in place of fence + atomic + fence (the
+// release covers the CTA's earlier writes through the preceding __syncthreads, the acquire the other CTAs' ones).
+MOEB_DEV unsigned atom_add_acq_rel_gpu(unsigned *p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
 MOEB_DEV unsigned smem_u32(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
 MOEB_DEV void mbar_init(uint64_t *bar, unsigned count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");

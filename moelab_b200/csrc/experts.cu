@@ -50,6 +50,59 @@ __global__ void __launch_bounds__(32 * KS, FMT == FMT_FP4 ? 4 : 8) k_down_slots(
         down_slot_unit<FMT, KS, GPW>(a, unit, hs4, red);
 }
 
+// Decode down with the combine in shared memory: one CTA per (token, 16-row block of d), the token's k slots as k
+// groups of KS warps. Each slot's value is computed exactly as in k_down_slots (same K split over the KS warps,
+// same reduction order, weight * (acc + bias)); the k values are then summed in slot order plus the residual, as
+// down_store_combine's last arrival does - without the global slot rows, fences and counters. k <= 32 / KS.
+template <int FMT, int KS, int GPW>
+__global__ void __launch_bounds__(1024, 1) k_down_tok(ExpArgs a) {
+    pdl_launch();
+    pdl_wait();
+    extern __shared__ uint4 tsm4[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int grp = warp / KS, lw = warp - grp * KS;  // slot j = grp of the token; local warp
+    const int k = a.k, d = a.d, f = a.f, RB = d >> 4;
+    const int hs_u4 = (f * 2 + f / 16 * 4) / 16;     // h row + block sums, in uint4
+    uint4 *hs4 = tsm4 + (size_t)grp * hs_u4;
+    float *red = reinterpret_cast<float *>(tsm4 + (size_t)k * hs_u4);  // [k][KS][4][32]
+    float *vals = red + k * KS * 4 * 32;                                // [k][16]
+    for (int unit = blockIdx.x; unit < a.T * RB; unit += gridDim.x) {
+        const int t = unit / RB, rb = unit - t * RB;
+        const int slot = t * k + grp;
+        const TileInfo ti = tile_info(a, slot);
+        float C[1][4];
+        down_slot_partial<FMT, KS, GPW>(a, slot, (size_t)ti.e * RB + rb, lw, threadIdx.x - grp * KS * 32, hs4, C);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) red[((grp * KS + lw) * 4 + i) * 32 + lane] = C[0][i];
+        __syncthreads();
+        if (lw == 0 && (lane & 3) == 0) {  // column 0 (the slot) of rows gq, gq + 8
+            float cs[1][4];
+            down_slot_reduce<KS>(red + grp * KS * 4 * 32, lane, cs);
+            const int gq = lane >> 2, r0 = rb * 16 + gq, r1 = r0 + 8;
+            const int e_raw = a.idx[slot];
+            const float wsl = (e_raw >= 0 && e_raw < a.E) ? a.wts[slot] : 0.f;
+            float v0 = cs[0][0], v1 = cs[0][2];
+            if (a.bd) {
+                v0 += a.bd[(size_t)ti.e * d + r0];
+                v1 += a.bd[(size_t)ti.e * d + r1];
+            }
+            vals[grp * 16 + gq] = wsl * v0;
+            vals[grp * 16 + gq + 8] = wsl * v1;
+        }
+        __syncthreads();
+        if (threadIdx.x < 16) {
+            const int r = rb * 16 + threadIdx.x;
+            float acc = 0.f;
+            for (int j = 0; j < k; ++j) acc += vals[j * 16 + threadIdx.x];
+            if (a.residual) acc += bf2f(a.residual[(size_t)t * d + r]);
+            a.y[(size_t)t * d + r] = f2bf(acc);
+        }
+        __syncthreads();  // the shared buffers are reused by the next unit
+    }
+}
+
+size_t down_tok_smem(int k, int f, int ks) { return (size_t)k * ((f * 2 + f / 16 * 4) + ks * 4 * 32 * 4 + 16 * 4); }
+
 // ================================================================== tile mode, register pipeline
 // One warp per (tile, 16-row block) over the whole K; loads run one GPW-group batch ahead of the MMAs in
 // registers (no shared memory), so more warps fit per SM than with the cp.async ring below.
@@ -237,6 +290,8 @@ template __global__ void k_gate_up_slots<FMT_Q4, 8, 4>(ExpArgs);
 template __global__ void k_down_slots<FMT_Q4, 4, 4>(ExpArgs);
 template __global__ void k_gate_up_slots<FMT_FP4, 8, 4>(ExpArgs);
 template __global__ void k_down_slots<FMT_FP4, 4, 4>(ExpArgs);
+template __global__ void k_down_tok<FMT_Q4, 4, 4>(ExpArgs);
+template __global__ void k_down_tok<FMT_FP4, 4, 4>(ExpArgs);
 template __global__ void k_gate_up_tiles_reg<FMT_FP4, 1, 2>(ExpArgs);
 template __global__ void k_down_tiles_reg<FMT_FP4, 1, 2>(ExpArgs);
 template __global__ void k_gate_up_tiles_reg<FMT_FP4, 2, 1>(ExpArgs);

@@ -167,6 +167,9 @@ template <int FMT, int KS, int GPW>
 __global__ void k_gate_up_slots(ExpArgs a);
 template <int FMT, int KS, int GPW>
 __global__ void k_down_slots(ExpArgs a);
+template <int FMT, int KS, int GPW>
+__global__ void k_down_tok(ExpArgs a);
+size_t down_tok_smem(int k, int f, int ks);
 template <int FMT, int NT8, int GPW>
 __global__ void k_gate_up_tiles_reg(ExpArgs a);
 template <int FMT, int NT8, int GPW>

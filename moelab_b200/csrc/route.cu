@@ -133,12 +133,7 @@ __device__ __forceinline__ void router_tail(const RouterArgs &a, int t0, int nt,
     // of the token block, whose thread 0 fences again before the reads
     __shared__ int s_last;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        const unsigned prev = atomicAdd(a.cnt + blockIdx.y, 1u);
-        s_last = prev == gridDim.x - 1;
-        if (s_last) __threadfence();
-    }
+    if (threadIdx.x == 0) s_last = atom_add_acq_rel_gpu(a.cnt + blockIdx.y, 1u) == gridDim.x - 1;
     __syncthreads();
     if (!s_last) return;
     const int nw = blockDim.x >> 5;
@@ -147,12 +142,7 @@ __device__ __forceinline__ void router_tail(const RouterArgs &a, int t0, int nt,
     if (a.tiles == nullptr) return;
     // routing step in the last token block to finish
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        const unsigned prev = atomicAdd(a.cnt_all, 1u);
-        s_last = prev == gridDim.y - 1;
-        if (s_last) __threadfence();
-    }
+    if (threadIdx.x == 0) s_last = atom_add_acq_rel_gpu(a.cnt_all, 1u) == gridDim.y - 1;
     __syncthreads();
     if (!s_last) return;
     build_tiles(a.idx, a.T * (a.k + a.ns), a.E + a.ns, a.NT, a.tiles, a.ntiles, a.sorted, a.err);

@@ -21,7 +21,6 @@ __device__ __forceinline__ void gate_up_slot_unit(const ExpArgs &a, int unit, ui
     const size_t blk = (size_t)ti.e * RB + rb;
     if (warp == KS - 1 && a.dn_prefetch) prefetch_down(a, ti.e, rb, RB, lane);
     const uint4 *xsrc = reinterpret_cast<const uint4 *>(a.x + (size_t)(slot / a.k) * a.xs);
-    for (int i = threadIdx.x; i < d / 8; i += 32 * KS) xs4[i] = xsrc[i];
     const float *sxr = a.xsum + (size_t)(slot / a.k) * xsum_stride(d);
     float Cg[1][4] = {{0.f, 0.f, 0.f, 0.f}}, Cu[1][4] = {{0.f, 0.f, 0.f, 0.f}};
     bool synced = false;
@@ -36,8 +35,9 @@ __device__ __forceinline__ void gate_up_slot_unit(const ExpArgs &a, int unit, ui
             bg[i] = ld_scales<FMT>(a.g, blk, G, g, gq);
             bu[i] = ld_scales<FMT>(a.u, blk, G, g, gq);
         }
-        if (!synced) {
-            __syncthreads();  // x row staged (weights already in flight)
+        if (!synced) {  // stage the x row while the first weight batch is in flight
+            for (int i = threadIdx.x; i < d / 8; i += 32 * KS) xs4[i] = xsrc[i];
+            __syncthreads();
             synced = true;
         }
 #pragma unroll
@@ -52,7 +52,10 @@ __device__ __forceinline__ void gate_up_slot_unit(const ExpArgs &a, int unit, ui
             }
         }
     }
-    if (!synced) __syncthreads();
+    if (!synced) {  // a warp without groups (G < KS) still stages its share
+        for (int i = threadIdx.x; i < d / 8; i += 32 * KS) xs4[i] = xsrc[i];
+        __syncthreads();
+    }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         red[((warp * 2 + 0) * 4 + i) * 32 + lane] = Cg[0][i];
@@ -76,25 +79,21 @@ __device__ __forceinline__ void gate_up_slot_unit(const ExpArgs &a, int unit, ui
     __syncthreads();
 }
 
-// hs4: f bf16 + f/16 floats of shared memory; red: KS * 4 * 32 floats of shared memory.
+// One slot's down dot products for this warp's share of K (warp lw of the KS splitting the f/64 groups), with
+// the slot's h row and block sums staged into hs4 by the KS * 32 threads ltid = 0 .. (the first weight batch is
+// issued before the staging). Contains exactly one __syncthreads; every thread of the CTA must call it.
 template <int FMT, int KS, int GPW>
-__device__ __forceinline__ void down_slot_unit(const ExpArgs &a, int unit, uint4 *hs4, float *red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int gq = lane >> 2, c = lane & 3;
-    const int d = a.d, f = a.f;
-    const int RB = d >> 4, G = f >> 6;
-    const int g_beg = warp * G / KS, g_end = (warp + 1) * G / KS;
+__device__ __forceinline__ void down_slot_partial(const ExpArgs &a, int slot, size_t blk, int lw, int ltid,
+                                                  uint4 *hs4, float (&C)[1][4]) {
+    const int lane = threadIdx.x & 31, gq = lane >> 2, c = lane & 3;
+    const int f = a.f, G = f >> 6;
+    const int g_beg = lw * G / KS, g_end = (lw + 1) * G / KS;
     const uint16_t *hs = reinterpret_cast<const uint16_t *>(hs4);
     const float *hsum_s = reinterpret_cast<const float *>(hs4 + f / 8);
-    const int slot = unit / RB, rb = unit - slot * RB;
-    if (a.idx[slot] == SLOT_SKIP) return;
-    const TileInfo ti = tile_info(a, slot);
-    const size_t blk = (size_t)ti.e * RB + rb;
     const uint4 *hsrc = reinterpret_cast<const uint4 *>(a.h + (size_t)slot * f);
-    for (int i = threadIdx.x; i < f / 8; i += 32 * KS) hs4[i] = __ldcg(hsrc + i);
     const uint4 *ssrc = reinterpret_cast<const uint4 *>(a.hsum + (size_t)slot * (f / 16));
-    for (int i = threadIdx.x; i < f / 64; i += 32 * KS) hs4[f / 8 + i] = __ldcg(ssrc + i);
-    float C[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) C[0][i] = 0.f;
     bool synced = false;
     for (int g0 = g_beg; g0 < g_end; g0 += GPW) {
         uint4 w[GPW];
@@ -105,7 +104,9 @@ __device__ __forceinline__ void down_slot_unit(const ExpArgs &a, int unit, uint4
             w[i] = ld_w(a.dn, blk, G, g, lane);
             b[i] = ld_scales<FMT>(a.dn, blk, G, g, gq);
         }
-        if (!synced) {
+        if (!synced) {  // stage the h row and its block sums while the first weight batch is in flight
+            for (int i = ltid; i < f / 8; i += 32 * KS) hs4[i] = __ldcg(hsrc + i);
+            for (int i = ltid; i < f / 64; i += 32 * KS) hs4[f / 8 + i] = __ldcg(ssrc + i);
             __syncthreads();
             synced = true;
         }
@@ -121,18 +122,41 @@ __device__ __forceinline__ void down_slot_unit(const ExpArgs &a, int unit, uint4
             }
         }
     }
-    if (!synced) __syncthreads();
+    if (!synced) {
+        for (int i = ltid; i < f / 8; i += 32 * KS) hs4[i] = __ldcg(hsrc + i);
+        for (int i = ltid; i < f / 64; i += 32 * KS) hs4[f / 8 + i] = __ldcg(ssrc + i);
+        __syncthreads();
+    }
+}
+
+// The KS partial accumulators of one slot (red[w][4][32], warp w's lanes) summed in warp order.
+template <int KS>
+__device__ __forceinline__ void down_slot_reduce(const float *red, int lane, float (&cs)[1][4]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        cs[0][i] = red[i * 32 + lane];
+#pragma unroll
+        for (int w = 1; w < KS; ++w) cs[0][i] += red[(w * 4 + i) * 32 + lane];
+    }
+}
+
+// hs4: f bf16 + f/16 floats of shared memory; red: KS * 4 * 32 floats of shared memory.
+template <int FMT, int KS, int GPW>
+__device__ __forceinline__ void down_slot_unit(const ExpArgs &a, int unit, uint4 *hs4, float *red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int RB = a.d >> 4;
+    const int slot = unit / RB, rb = unit - slot * RB;
+    if (a.idx[slot] == SLOT_SKIP) return;
+    const TileInfo ti = tile_info(a, slot);
+    const size_t blk = (size_t)ti.e * RB + rb;
+    float C[1][4];
+    down_slot_partial<FMT, KS, GPW>(a, slot, blk, warp, threadIdx.x, hs4, C);
 #pragma unroll
     for (int i = 0; i < 4; ++i) red[(warp * 4 + i) * 32 + lane] = C[0][i];
     __syncthreads();
     if (warp == 0) {
         float cs[1][4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            cs[0][i] = red[i * 32 + lane];
-#pragma unroll
-            for (int w = 1; w < KS; ++w) cs[0][i] += red[(w * 4 + i) * 32 + lane];
-        }
+        down_slot_reduce<KS>(red, lane, cs);
         down_store_combine<1>(a, ti, rb, cs, lane);
     }
     __syncthreads();
