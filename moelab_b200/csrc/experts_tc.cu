@@ -167,7 +167,6 @@ __global__ void __launch_bounds__(TCL<FMT, NT, NR, NA, NX, ACC, DOWN>::THREADS, 
     k_experts_tc(const __grid_constant__ ExpArgs a) {
     using L = TCL<FMT, NT, NR, NA, NX, ACC, DOWN>;
     pdl_launch();
-    pdl_wait();
     extern __shared__ __align__(1024) unsigned char tsm_raw[];
     // 1024-byte aligned base for the swizzled tiles
     unsigned char *tsm = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(tsm_raw) + 1023) & ~(uintptr_t)1023);
@@ -181,9 +180,6 @@ __global__ void __launch_bounds__(TCL<FMT, NT, NR, NA, NX, ACC, DOWN>::THREADS, 
     const int RB = DOWN ? (a.d >> 4) : (a.f >> 4);     // 16-row blocks of the output rows
     const int G = DOWN ? (a.f >> 6) : (a.d >> 6);      // 64-groups of K
     const int MT = RB / 8;                             // 128-row work items per tile
-    const int n_tiles = *a.ntiles;
-    const int n_items = n_tiles * MT;
-    const int my_items = (int)blockIdx.x < n_items ? (n_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
     if (threadIdx.x == 0) {
         for (int i = 0; i < NR; ++i) {
             mbar_init(rfull + i, 1);
@@ -210,10 +206,14 @@ __global__ void __launch_bounds__(TCL<FMT, NT, NR, NA, NX, ACC, DOWN>::THREADS, 
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
+    pdl_wait();  // barrier setup and the TMEM allocation above overlap the upstream kernel's tail
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
+    const int n_tiles = *a.ntiles;
+    const int n_items = n_tiles * MT;
+    const int my_items = (int)blockIdx.x < n_items ? (n_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
     const int m0 = DOWN ? 2 : 0;  // tensor maps of this kernel's projections
     const unsigned timeout_err = ERR_TIMEOUT;
 
@@ -485,7 +485,6 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN>::THREADS, 1)
     k_experts_tca(const __grid_constant__ ExpArgs a) {
     using L = TAL<FMT, NT, NR, NS, ACC, DOWN>;
     pdl_launch();
-    pdl_wait();
     extern __shared__ __align__(1024) unsigned char tsm_raw[];
     unsigned char *tsm = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(tsm_raw) + 1023) & ~(uintptr_t)1023);
     unsigned char *Xb = tsm, *Rb = tsm + L::OFF_R;
@@ -497,9 +496,6 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN>::THREADS, 1)
     const int RB = DOWN ? (a.d >> 4) : (a.f >> 4);
     const int G = DOWN ? (a.f >> 6) : (a.d >> 6);
     const int MT = RB / 8;
-    const int n_tiles = *a.ntiles;
-    const int n_items = n_tiles * MT;
-    const int my_items = (int)blockIdx.x < n_items ? (n_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
     if (threadIdx.x == 0) {
         for (int i = 0; i < NR; ++i) {
             mbar_init(rfull + i, 1);
@@ -522,10 +518,14 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN>::THREADS, 1)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
+    pdl_wait();  // barrier setup and the TMEM allocation above overlap the upstream kernel's tail
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
+    const int n_tiles = *a.ntiles;
+    const int n_items = n_tiles * MT;
+    const int my_items = (int)blockIdx.x < n_items ? (n_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
     const int m0 = DOWN ? 2 : 0;
     const unsigned timeout_err = ERR_TIMEOUT;
 

@@ -53,11 +53,20 @@ template <int FMT, int NT8, int RBC, int SG, int NS, bool DOWN, int MB>
 __global__ void __launch_bounds__(32 * (RBC + 1), MB) k_experts_ws(const __grid_constant__ ExpArgs a) {
     using L = WSL<FMT, NT8, RBC, SG, DOWN>;
     pdl_launch();
-    pdl_wait();
     extern __shared__ __align__(128) unsigned char smem_raw[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem_raw + NS * L::STAGE);
     uint64_t *empty = full + NS;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // barrier setup overlaps the upstream kernel's tail (it touches no upstream data)
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(full + i, 1);
+            mbar_init(empty + i, RBC);
+        }
+        mbar_fence_init();
+    }
+    pdl_wait();
+    __syncthreads();
     const int RB = DOWN ? (a.d >> 4) : (a.f >> 4);
     const int G = DOWN ? (a.f >> 6) : (a.d >> 6);
     const int RBS = (RB + RBC - 1) / RBC;  // super-units per tile
@@ -66,14 +75,6 @@ __global__ void __launch_bounds__(32 * (RBC + 1), MB) k_experts_ws(const __grid_
     const int n_su = n_tiles * RBS;
     const int my_su = (int)blockIdx.x < n_su ? (n_su - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
     const int total = my_su * SPU;
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < NS; ++i) {
-            mbar_init(full + i, 1);
-            mbar_init(empty + i, RBC);
-        }
-        mbar_fence_init();
-    }
-    __syncthreads();
 
     if (warp == RBC) {
         // ------------------------------------------------------------ producer warp
