@@ -20,6 +20,15 @@ __device__ __forceinline__ void row_group_sums(const uint16_t *__restrict__ xr, 
     }
 }
 
+// fp32 -> unsigned with the same order (for the warp max reductions); -0 is folded into +0 by the caller
+__device__ __forceinline__ unsigned fkey(float f) {
+    const unsigned u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float fkey_inv(unsigned k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
 template <int JMAX>
 __device__ void topk_token(const RouterArgs &a, int t, int lane) {
     const int E = a.E, k = a.k;
@@ -29,11 +38,10 @@ __device__ void topk_token(const RouterArgs &a, int t, int lane) {
     for (int j = 0; j < JMAX; ++j) {
         const int e = j * 32 + lane;
         float l = e < E ? __ldcg(a.logits + (size_t)t * E + e) : -INFINITY;
-        v[j] = isnan(l) ? -INFINITY : l;
+        v[j] = isnan(l) ? -INFINITY : l + 0.f;  // NaN = -inf; -0 -> +0 (equal values compare as keys too)
         m0 = fmaxf(m0, v[j]);
     }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+    m0 = fkey_inv(__reduce_max_sync(0xffffffffu, fkey(m0)));
     float den = 0.f;
     if (!a.norm) {
 #pragma unroll
@@ -43,15 +51,15 @@ __device__ void topk_token(const RouterArgs &a, int t, int lane) {
     float myv = -INFINITY, top0 = -INFINITY;
     int myi = 0;
     for (int r = 0; r < k; ++r) {
+        // the largest remaining value (one warp max on order-preserving keys), lowest id among equal ones
         float b = -INFINITY;
         unsigned bi = 0xffffffffu;
 #pragma unroll
         for (int j = 0; j < JMAX; ++j)
             if (v[j] > b) { b = v[j]; bi = (unsigned)(j * 32 + lane); }
-        float m = b;
-#pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        unsigned sel = __reduce_min_sync(0xffffffffu, b == m ? bi : 0xffffffffu);
+        const unsigned kb = fkey(b), km = __reduce_max_sync(0xffffffffu, kb);
+        float m = fkey_inv(km);
+        unsigned sel = __reduce_min_sync(0xffffffffu, kb == km ? bi : 0xffffffffu);
         if (sel == 0xffffffffu) {  // fewer than k values above -inf: lowest unused id, weight 0
             unsigned cand = 0;
             while (__any_sync(0xffffffffu, lane < r && (unsigned)myi == cand)) ++cand;
