@@ -200,7 +200,7 @@ KLaunch ws_kernel(int fmt, int nt8, bool down) {
 
 KLaunch tc_kernel(int fmt, int nt, bool down) {
     const TcInfo t = experts_tc_info(fmt, nt, down);
-    return {t.fn, t.threads, t.smem, false, 8, 1, true, t.tmem_a};
+    return {t.fn, t.threads, t.smem, false, 8, t.sg, true, t.tmem_a};
 }
 
 // Kernels per policy: TILES8 / TILES16 run the register-pipelined tile kernels, the *_RING policies the

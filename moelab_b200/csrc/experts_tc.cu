@@ -455,23 +455,24 @@ __global__ void __launch_bounds__(TCL<FMT, NT, NR, NA, NX, ACC, DOWN>::THREADS, 
 // MMA sums over k, so the order does not change the products, only which bf16 pairs meet in the tensor core.
 
 namespace {
-template <int FMT, int NT, int NR, int NS, int ACC, bool DOWN>
+template <int FMT, int NT, int NR, int NS, int ACC, bool DOWN, int SGK>
 struct TAL {
     static constexpr int NP = DOWN ? 1 : 2;
     static constexpr int DQW = 8 * NP;                   // dequant warps: one (projection, row block) each
     static constexpr int EPW = 8;                        // epilogue warps (two per TMEM lane quarter)
     static constexpr int THREADS = 32 * (3 + DQW + EPW);
     static constexpr int SBG = FMT == FMT_FP4 ? 32 : 64;
-    static constexpr int X_STAGE = NT * 128;
-    static constexpr int Q_BYTES = 8 * 512;
+    static constexpr int X_SUB = NT * 128;               // one 64-group of the tile's activation rows
+    static constexpr int X_STAGE = SGK * X_SUB;
+    static constexpr int Q_BYTES = 8 * 512;              // per group: 8 row blocks of packed codes
     static constexpr int S_BYTES = 8 * SBG;
-    static constexpr int R_STAGE = NP * (Q_BYTES + S_BYTES);
+    static constexpr int R_STAGE = NP * SGK * (Q_BYTES + S_BYTES);
     static constexpr int OFF_R = NS * X_STAGE;
     static constexpr int OFF_BAR = OFF_R + NR * R_STAGE;
     static constexpr int NBAR = 2 * (NR + NS + ACC);
     static constexpr int SMEM = 1024 + OFF_BAR + NBAR * 8;
     static constexpr int A_COL0 = ACC * NP * NT;         // accumulators first, then the A stages (32 columns each)
-    static constexpr int TMEM_RAW = A_COL0 + NS * NP * 32;
+    static constexpr int TMEM_RAW = A_COL0 + NS * NP * SGK * 32;
     static constexpr int TMEM_COLS = TMEM_RAW <= 32 ? 32 : TMEM_RAW <= 64 ? 64 : TMEM_RAW <= 128 ? 128
                                    : TMEM_RAW <= 256 ? 256 : 512;
     static_assert(TMEM_RAW <= 512, "TMEM allocation");
@@ -480,10 +481,10 @@ struct TAL {
 };
 }  // namespace
 
-template <int FMT, int NT, int NR, int NS, int ACC, bool DOWN>
-__global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN>::THREADS, 1)
+template <int FMT, int NT, int NR, int NS, int ACC, bool DOWN, int SGK>
+__global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN, SGK>::THREADS, 1)
     k_experts_tca(const __grid_constant__ ExpArgs a) {
-    using L = TAL<FMT, NT, NR, NS, ACC, DOWN>;
+    using L = TAL<FMT, NT, NR, NS, ACC, DOWN, SGK>;
     pdl_launch();
     extern __shared__ __align__(1024) unsigned char tsm_raw[];
     unsigned char *tsm = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(tsm_raw) + 1023) & ~(uintptr_t)1023);
@@ -494,7 +495,7 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN>::THREADS, 1)
     __shared__ int s_fail;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int RB = DOWN ? (a.d >> 4) : (a.f >> 4);
-    const int G = DOWN ? (a.f >> 6) : (a.d >> 6);
+    const int GS = (DOWN ? (a.f >> 6) : (a.d >> 6)) / SGK;  // stages per item (SGK groups each; G % SGK == 0)
     const int MT = RB / 8;
     if (threadIdx.x == 0) {
         for (int i = 0; i < NR; ++i) {
@@ -545,8 +546,8 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN>::THREADS, 1)
                 const int4 tr = a.tiles[tile];
                 const int e = (tr.x < 0 || tr.x >= a.E) ? 0 : tr.x;
                 const int row0 = e * RB + mt * 8;
-                for (int g = 0; g < G; ++g, ++k) {
-                    const int r = k % NR;
+                for (int gs = 0; gs < GS; ++gs, ++k) {
+                    const int r = k % NR, g = gs * SGK;
                     if (k >= NR && !mbar_wait_bounded(rempty + r, (unsigned)(((k / NR) - 1) & 1))) {
                         atomicOr(a.err, timeout_err);
                         s_fail = 1;
@@ -555,10 +556,10 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN>::THREADS, 1)
                     }
                     unsigned char *q = Rb + (size_t)r * L::R_STAGE;
                     mbar_expect_tx(rfull + r, (unsigned)L::R_STAGE);
-                    for (int p = 0; p < L::NP; ++p) {
-                        tma_load_2d(q + p * L::Q_BYTES, &a.tmq[m0 + p], g * 64, row0, rfull + r, pol);
-                        tma_load_2d(q + L::NP * L::Q_BYTES + p * L::S_BYTES, &a.tmsb[m0 + p], g * (L::SBG / 4), row0,
-                                    rfull + r, pol);
+                    for (int p = 0; p < L::NP; ++p) {  // boxes of 8 row blocks x SGK groups
+                        tma_load_2d(q + p * SGK * L::Q_BYTES, &a.tmq[m0 + p], g * 64, row0, rfull + r, pol);
+                        tma_load_2d(q + L::NP * SGK * L::Q_BYTES + p * SGK * L::S_BYTES, &a.tmsb[m0 + p],
+                                    g * (L::SBG / 4), row0, rfull + r, pol);
                     }
                 }
             }
@@ -575,7 +576,7 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN>::THREADS, 1)
             for (int it = 0; it < my_items && ok; ++it) {
                 const int item = (int)blockIdx.x + it * (int)gridDim.x;
                 const int4 tr = a.tiles[item / MT];
-                for (int g = 0; g < G; ++g, ++k) {
+                for (int gs = 0; gs < GS; ++gs, ++k) {
                     const int s = k % NS;
                     if (k >= NS && !mbar_wait_bounded(oempty + s, (unsigned)(((k / NS) - 1) & 1))) {
                         atomicOr(a.err, timeout_err);
@@ -584,7 +585,9 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN>::THREADS, 1)
                         break;
                     }
                     mbar_expect_tx(ofull + s, (unsigned)L::X_STAGE);
-                    tma_load_2d(Xb + (size_t)s * L::X_STAGE, &a.tmx, g * 64, tr.y, ofull + s, pol_x);
+                    for (int gi = 0; gi < SGK; ++gi)
+                        tma_load_2d(Xb + (size_t)s * L::X_STAGE + gi * L::X_SUB, &a.tmx, (gs * SGK + gi) * 64, tr.y,
+                                    ofull + s, pol_x);
                 }
             }
             for (int q = k - NS; q < k; ++q)
@@ -606,7 +609,7 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN>::THREADS, 1)
                     break;
                 }
                 tc_fence_after();
-                for (int g = 0; g < G; ++g, ++k) {
+                for (int gs = 0; gs < GS; ++gs, ++k) {
                     const int s = k % NS;
                     if (!mbar_wait_bounded(ofull + s, (unsigned)((k / NS) & 1))) {
                         atomicOr(a.err, timeout_err);
@@ -615,14 +618,18 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN>::THREADS, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t bdesc = sdesc_sw128(smem_u32(Xb + (size_t)s * L::X_STAGE));
 #pragma unroll
-                    for (int p = 0; p < L::NP; ++p) {
-                        const uint32_t d_tmem = tmem + (uint32_t)((b * L::NP + p) * NT);
-                        const uint32_t a_tmem = tmem + (uint32_t)(L::A_COL0 + (s * L::NP + p) * 32);
+                    for (int gi = 0; gi < SGK; ++gi) {
+                        const uint64_t bdesc = sdesc_sw128(smem_u32(Xb + (size_t)s * L::X_STAGE + gi * L::X_SUB));
 #pragma unroll
-                        for (int ks = 0; ks < 4; ++ks)  // 16 k = 8 TMEM columns of A, 32 bytes of the swizzled X row
-                            umma_bf16_ts(d_tmem, a_tmem + 8 * ks, bdesc + 2 * ks, idesc, (g > 0 || ks > 0) ? 1u : 0u);
+                        for (int p = 0; p < L::NP; ++p) {
+                            const uint32_t d_tmem = tmem + (uint32_t)((b * L::NP + p) * NT);
+                            const uint32_t a_tmem = tmem + (uint32_t)(L::A_COL0 + ((s * L::NP + p) * SGK + gi) * 32);
+#pragma unroll
+                            for (int ks = 0; ks < 4; ++ks)  // 16 k = 8 TMEM columns of A, 32 bytes of the X row
+                                umma_bf16_ts(d_tmem, a_tmem + 8 * ks, bdesc + 2 * ks, idesc,
+                                             (gs > 0 || gi > 0 || ks > 0) ? 1u : 0u);
+                        }
                     }
                     umma_commit(oempty + s);
                 }
@@ -640,7 +647,7 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN>::THREADS, 1)
         int k = 0;
         for (int it = 0; it < my_items && !*reinterpret_cast<volatile int *>(&s_fail); ++it) {
             bool ok = true;
-            for (int g = 0; g < G; ++g, ++k) {
+            for (int gs = 0; gs < GS; ++gs, ++k) {
                 const int r = k % NR, s = k % NS;
                 if (!mbar_wait_bounded(rfull + r, (unsigned)((k / NR) & 1))) {
                     if (lane == 0) atomicOr(a.err, timeout_err);
@@ -648,11 +655,15 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN>::THREADS, 1)
                     break;
                 }
                 const unsigned char *q = Rb + (size_t)r * L::R_STAGE;
-                const uint4 w = reinterpret_cast<const uint4 *>(q + p * L::Q_BYTES + rb * 512)[lane];
-                const uint32_t *sbw = reinterpret_cast<const uint32_t *>(q + L::NP * L::Q_BYTES + p * L::S_BYTES + rb * L::SBG);
-                const uint32_t sb0 = FMT == FMT_FP4 ? sbw[gq] : sbw[gq * 2], sb1 = FMT == FMT_FP4 ? 0u : sbw[gq * 2 + 1];
-                uint32_t out[2][8];
-                dequant_block<FMT>(w, sb0, sb1, c, out);
+                uint32_t out[SGK][2][8];
+#pragma unroll
+                for (int gi = 0; gi < SGK; ++gi) {  // this warp's block of each of the stage's groups
+                    const uint4 w = reinterpret_cast<const uint4 *>(q + p * SGK * L::Q_BYTES + rb * (SGK * 512) + gi * 512)[lane];
+                    const uint32_t *sbw = reinterpret_cast<const uint32_t *>(q + L::NP * SGK * L::Q_BYTES + p * SGK * L::S_BYTES +
+                                                                             rb * (SGK * L::SBG) + gi * L::SBG);
+                    const uint32_t sb0 = FMT == FMT_FP4 ? sbw[gq] : sbw[gq * 2], sb1 = FMT == FMT_FP4 ? 0u : sbw[gq * 2 + 1];
+                    dequant_block<FMT>(w, sb0, sb1, c, out[gi]);
+                }
                 __syncwarp();  // every lane's reads of the raw stage are complete (their values are in out)
                 if (lane == 0) mbar_arrive1(rempty + r);
                 if (k >= NS && !mbar_wait_bounded(oempty + s, (unsigned)(((k / NS) - 1) & 1))) {
@@ -661,15 +672,18 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN>::THREADS, 1)
                     break;
                 }
                 tc_fence_after();
-                uint32_t v[16];
 #pragma unroll
-                for (int m = 0; m < 4; ++m) {
-                    v[4 * m + 0] = out[0][2 * m];
-                    v[4 * m + 1] = out[0][2 * m + 1];
-                    v[4 * m + 2] = out[1][2 * m];
-                    v[4 * m + 3] = out[1][2 * m + 1];
+                for (int gi = 0; gi < SGK; ++gi) {
+                    uint32_t v[16];
+#pragma unroll
+                    for (int m = 0; m < 4; ++m) {
+                        v[4 * m + 0] = out[gi][0][2 * m];
+                        v[4 * m + 1] = out[gi][0][2 * m + 1];
+                        v[4 * m + 2] = out[gi][1][2 * m];
+                        v[4 * m + 3] = out[gi][1][2 * m + 1];
+                    }
+                    tmem_st_16x256_x4(tmem + lane_addr + (uint32_t)(L::A_COL0 + ((s * L::NP + p) * SGK + gi) * 32), v);
                 }
-                tmem_st_16x256_x4(tmem + lane_addr + (uint32_t)(L::A_COL0 + (s * L::NP + p) * 32), v);
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
@@ -747,32 +761,34 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN>::THREADS, 1)
 // TMEM columns: gate/up tiles of 32 / 64 / 128 slots, down tiles of 32 .. 256. Gate/up tiles of 256 need all 512
 // columns for the two accumulators and keep A in shared memory (k_experts_tc). Raw and operand rings are as deep
 // as the 227 KB of shared memory allow.
-//   tca: (NT, NR, NS, ACC, DOWN)       tc: (NT, NR, NA, NX, ACC, DOWN)
+//   tca: (NT, NR, NS, ACC, DOWN, SGK): SGK 64-groups per stage (two halve the per-stage barrier, TMEM-store and
+//   MMA-issue latencies per group and fetch 1 KB code rows per copy); down tiles of 256 keep one, as their
+//   64 KB activation stages leave no room for a deep raw ring
 #define MOEB_TCA_CFGS(X) \
-    X(32, 16, 6, 2, false) X(64, 16, 4, 2, false) X(128, 16, 4, 1, false) \
-    X(32, 24, 8, 2, true) X(64, 24, 8, 2, true) X(128, 24, 6, 2, true) X(256, 16, 4, 1, true)
+    X(32, 10, 3, 2, false, 2) X(64, 10, 2, 2, false, 2) X(128, 8, 2, 1, false, 2) \
+    X(32, 16, 6, 2, true, 2) X(64, 12, 6, 2, true, 2) X(128, 10, 4, 2, true, 2) X(256, 16, 4, 1, true, 1)
 
 TcInfo experts_tc_info(int fmt, int nt, bool down) {
-    TcInfo r = {nullptr, 0, 0, false};
-#define MOEB_TCA_PICK(NT_, NR_, NS_, ACC_, DOWN_)                                                     \
-    if (nt == NT_ && down == DOWN_) {                                                                 \
-        if (fmt == FMT_FP4) {                                                                         \
-            using L = TAL<FMT_FP4, NT_, NR_, NS_, ACC_, DOWN_>;                                        \
-            r = {k_experts_tca<FMT_FP4, NT_, NR_, NS_, ACC_, DOWN_>, L::THREADS, (size_t)L::SMEM, true}; \
-        } else {                                                                                      \
-            using L = TAL<FMT_Q4, NT_, NR_, NS_, ACC_, DOWN_>;                                         \
-            r = {k_experts_tca<FMT_Q4, NT_, NR_, NS_, ACC_, DOWN_>, L::THREADS, (size_t)L::SMEM, true};   \
-        }                                                                                             \
+    TcInfo r = {nullptr, 0, 0, false, 1};
+#define MOEB_TCA_PICK(NT_, NR_, NS_, ACC_, DOWN_, SGK_)                                                         \
+    if (nt == NT_ && down == DOWN_) {                                                                           \
+        if (fmt == FMT_FP4) {                                                                                   \
+            using L = TAL<FMT_FP4, NT_, NR_, NS_, ACC_, DOWN_, SGK_>;                                            \
+            r = {k_experts_tca<FMT_FP4, NT_, NR_, NS_, ACC_, DOWN_, SGK_>, L::THREADS, (size_t)L::SMEM, true, SGK_}; \
+        } else {                                                                                                \
+            using L = TAL<FMT_Q4, NT_, NR_, NS_, ACC_, DOWN_, SGK_>;                                             \
+            r = {k_experts_tca<FMT_Q4, NT_, NR_, NS_, ACC_, DOWN_, SGK_>, L::THREADS, (size_t)L::SMEM, true, SGK_};  \
+        }                                                                                                       \
     }
     MOEB_TCA_CFGS(MOEB_TCA_PICK)
 #undef MOEB_TCA_PICK
     if (nt == 256 && !down) {
         if (fmt == FMT_FP4) {
             using L = TCL<FMT_FP4, 256, 6, 2, 3, 1, false>;
-            r = {k_experts_tc<FMT_FP4, 256, 6, 2, 3, 1, false>, L::THREADS, (size_t)L::SMEM, false};
+            r = {k_experts_tc<FMT_FP4, 256, 6, 2, 3, 1, false>, L::THREADS, (size_t)L::SMEM, false, 1};
         } else {
             using L = TCL<FMT_Q4, 256, 6, 2, 3, 1, false>;
-            r = {k_experts_tc<FMT_Q4, 256, 6, 2, 3, 1, false>, L::THREADS, (size_t)L::SMEM, false};
+            r = {k_experts_tc<FMT_Q4, 256, 6, 2, 3, 1, false>, L::THREADS, (size_t)L::SMEM, false, 1};
         }
     }
     return r;

@@ -178,7 +178,7 @@ template <int FMT, int NT8, int RBC, int SG, int NS, bool DOWN, int MB>
 __global__ void k_experts_ws(const __grid_constant__ ExpArgs a);
 template <int FMT, int NT, int NR, int NA, int NX, int ACC, bool DOWN>
 __global__ void k_experts_tc(const __grid_constant__ ExpArgs a);
-template <int FMT, int NT, int NR, int NS, int ACC, bool DOWN>
+template <int FMT, int NT, int NR, int NS, int ACC, bool DOWN, int SGK>
 __global__ void k_experts_tca(const __grid_constant__ ExpArgs a);
 // The tcgen05 expert kernel for (format, tile size 32 / 64 / 128 / 256, projection): entry, block size and
 // dynamic shared memory (fn == nullptr for an unsupported tile size).
@@ -187,6 +187,7 @@ struct TcInfo {
     int threads;
     size_t smem;
     bool tmem_a;  // A operand in TMEM: activations in the permuted 64-group k order
+    int sg;       // 64-groups per pipeline stage (the weight tensor maps' box width)
 };
 TcInfo experts_tc_info(int fmt, int nt, bool down);
 __global__ void k_gather_rows(const uint16_t *x, const int *sorted, int TK, int k, int d, int perm, uint16_t *xs);
