@@ -38,6 +38,58 @@ def test_finds_blocks_and_refuses_cpu_weights():
         integrate.patch_hf_moe(m, fmt="int8")
 
 
+class _TorchVariant:
+    """Stand-in for a variant module (CPU, plain torch): prepare keeps the weights, layer runs the block's math
+    (softmax, top-k, renormalise or not, SiLU-gated experts) and counts its calls."""
+    calls = 0
+
+    @staticmethod
+    def prepare(wg, wu, wd):
+        return {"g": wg.float(), "u": wu.float(), "d": wd.float(), "E": wg.shape[0]}
+
+    @staticmethod
+    def dequant(st):
+        return st["g"], st["u"], st["d"]
+
+    @classmethod
+    def layer(cls, st, x, gate_w, k, norm=True):
+        cls.calls += 1
+        p = torch.softmax(x.float() @ gate_w.float().T, dim=-1)
+        w, i = torch.topk(p, k, dim=-1)
+        if norm:
+            w = w / w.sum(-1, keepdim=True)
+        y = torch.zeros(x.shape, dtype=torch.float32)
+        for t in range(x.shape[0]):
+            for j in range(k):
+                e = int(i[t, j])
+                h = torch.nn.functional.silu(st["g"][e] @ x[t].float()) * (st["u"][e] @ x[t].float())
+                y[t] += w[t, j] * (st["d"][e] @ h)
+        return y.to(x.dtype)
+
+
+def test_patch_routes_decode_calls_and_unpatches(monkeypatch):
+    """Host logic of the patch with a CPU stand-in for the variant: calls of up to max_tokens tokens go through
+    `layer` (same result as the stock block on the same weights), larger ones through the stock forward, and
+    unpatching restores the stock forward."""
+    m = _qwen3(dtype=torch.float32).eval()
+    monkeypatch.setattr(integrate, "_variant", lambda fmt: _TorchVariant)
+    monkeypatch.setattr(torch.Tensor, "is_cuda", property(lambda self: True))  # the CUDA-only guard
+    ids = torch.arange(6).view(1, 6)
+    ref = _logits(m, ids)
+    assert integrate.patch_hf_moe(m, max_tokens=6) == 2
+    monkeypatch.undo()
+    monkeypatch.setattr(integrate, "_variant", lambda fmt: _TorchVariant)
+    _TorchVariant.calls = 0
+    out = _logits(m, ids)
+    assert _TorchVariant.calls == 2  # one call per block
+    assert torch.allclose(out, ref, rtol=1e-2, atol=5e-3)  # the layer call takes bf16 activations and gate
+    _TorchVariant.calls = 0
+    _logits(m, torch.arange(7).view(1, 7))  # 7 > 6 tokens: stock blocks
+    assert _TorchVariant.calls == 0
+    assert integrate.unpatch_hf_moe(m) == 2
+    assert "_moeb" not in integrate.moe_blocks(m)[0].__dict__
+
+
 def _logits(model, ids):
     with torch.no_grad():
         return model(ids).logits.float()
