@@ -1,7 +1,9 @@
 // Grouped expert kernels on the 5th-generation tensor cores (tcgen05, accumulators in TMEM), for medium and high
-// loads (tiles of up to NT = 32 .. 256 slots of one expert: the weights are dequantized once per tile).
+// loads (tiles of up to NT = 32 .. 256 slots of one expert: the weights are dequantized once per tile). Two
+// kernels: k_experts_tc below keeps the dequantized A operand in shared memory (gate/up tiles of 256, whose two
+// accumulators fill TMEM); k_experts_tca further down writes A into TMEM (every other tile size).
 //
-// A work item is (tile, 128 output rows). D[128 rows][NT slots] = W[128][K] . X[NT][K]^T accumulates in TMEM
+// k_experts_tc. A work item is (tile, 128 output rows). D[128 rows][NT slots] = W[128][K] . X[NT][K]^T accumulates in TMEM
 // (fp32, lane = row, column = slot). K advances one 64-group per step through three shared-memory rings, so
 // that each resource is only as deep as its own latency needs:
 //   raw ring (NR stages, 4.5 KB per projection): the packed int4 codes and scale|bias words (or MXFP4 codes and
