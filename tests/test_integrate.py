@@ -28,10 +28,40 @@ def _mixtral(dtype=torch.bfloat16):
     return transformers.AutoModelForCausalLM.from_config(cfg, dtype=dtype)
 
 
+def _gptoss(dtype=torch.bfloat16):
+    cfg = transformers.GptOssConfig(vocab_size=512, hidden_size=256, intermediate_size=256, num_hidden_layers=2,
+                                    num_attention_heads=4, num_key_value_heads=2, head_dim=64, num_local_experts=8,
+                                    num_experts_per_tok=2, max_position_embeddings=128, sliding_window=64)
+    torch.manual_seed(2)
+    m = transformers.AutoModelForCausalLM.from_config(cfg, dtype=dtype)
+    g = torch.Generator().manual_seed(7)
+    with torch.no_grad():  # the stock init leaves the expert biases at zero; give them N(0, 0.01)
+        for b in integrate.moe_blocks(m):
+            for t in (b.experts.gate_up_proj_bias, b.experts.down_proj_bias):
+                t.copy_((torch.randn(t.shape, generator=g) * 0.01).to(t.dtype))
+    return m
+
+
+def _deepseek(dtype=torch.bfloat16):
+    cfg = transformers.DeepseekV2Config(vocab_size=512, hidden_size=256, intermediate_size=512, moe_intermediate_size=128,
+                                        num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=4,
+                                        n_routed_experts=16, num_experts_per_tok=4, n_shared_experts=2,
+                                        topk_method="greedy", routed_scaling_factor=1.5, first_k_dense_replace=0,
+                                        kv_lora_rank=64, q_lora_rank=None, qk_rope_head_dim=32, qk_nope_head_dim=32,
+                                        v_head_dim=32, max_position_embeddings=128, rope_scaling=None)
+    torch.manual_seed(3)
+    return transformers.AutoModelForCausalLM.from_config(cfg, dtype=dtype)
+
+
 def test_finds_blocks_and_refuses_cpu_weights():
     m = _qwen3()
     assert len(integrate.moe_blocks(m)) == 2
     assert len(integrate.moe_blocks(_mixtral())) == 2
+    assert len(integrate.moe_blocks(_gptoss())) == 2
+    ds = _deepseek()
+    assert len(integrate.moe_blocks(ds)) == 2
+    with pytest.raises(ValueError, match="int4"):
+        integrate.patch_hf_moe(ds, fmt="mxfp4")
     with pytest.raises(AssertionError, match="CUDA"):
         integrate.patch_hf_moe(m)
     with pytest.raises(ValueError):
@@ -52,12 +82,13 @@ class _TorchVariant:
         return st["g"], st["u"], st["d"]
 
     @classmethod
-    def layer(cls, st, x, gate_w, k, norm=True):
+    def layer(cls, st, x, gate_w, k, norm=True, rscale=1.0):
         cls.calls += 1
         p = torch.softmax(x.float() @ gate_w.float().T, dim=-1)
         w, i = torch.topk(p, k, dim=-1)
         if norm:
             w = w / w.sum(-1, keepdim=True)
+        w = w * rscale
         y = torch.zeros(x.shape, dtype=torch.float32)
         for t in range(x.shape[0]):
             for j in range(k):
@@ -97,11 +128,13 @@ def _logits(model, ids):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("family,fmt", [("qwen3", "q4"), ("qwen3_nonorm", "q4"), ("mixtral", "q4"),
-                                        ("mixtral", "mxfp4")])
+                                        ("mixtral", "mxfp4"), ("gptoss", "mxfp4"), ("deepseek", "q4")])
 def test_patched_matches_stock_on_the_same_weights(family, fmt):
     """Patched model vs the stock model on the dequantized weights: the same network, so logits agree to the
-    kernels' bf16 / fp32 arithmetic (and the top-1 tokens almost everywhere)."""
-    make = {"qwen3": _qwen3, "qwen3_nonorm": lambda: _qwen3(norm=False), "mixtral": _mixtral}[family]
+    kernels' bf16 / fp32 arithmetic (and the top-1 tokens almost everywhere). gpt-oss: biases and the clamped
+    SwiGLU; DeepSeek: greedy routing with a scaling factor and two shared experts."""
+    make = {"qwen3": _qwen3, "qwen3_nonorm": lambda: _qwen3(norm=False), "mixtral": _mixtral, "gptoss": _gptoss,
+            "deepseek": _deepseek}[family]
     patched, stock = make().cuda().eval(), make().cuda().eval()
     assert integrate.patch_hf_moe(patched, fmt=fmt) == 2
     integrate.dequantize_into_stock(patched)  # the stock parameters of `patched` now hold the dequantized weights
