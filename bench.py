@@ -45,6 +45,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bound on the CPU baseline sample")
     ap.add_argument("--soak-seconds", type=float, default=1.5, help="replays before the timed region (clocks)")
     ap.add_argument("--configs", type=int, default=1, help="1: also time the other BASELINE configurations (1 GPU)")
+    ap.add_argument("--ep-stack", default="", help="N > 1: also time BASELINE's expert-parallel stack (8 Qwen3-235B-"
+                    "shaped layers, experts split over the GPUs) at these tokens per GPU, e.g. 32,256,2048")
     ap.add_argument("--profile-config", default="", help="run 3 eager layer calls of the CONFIGS entry whose name "
                     "starts with this (for ncu captures of one kernel) and exit")
     ap.add_argument("--profile-tokens", type=int, default=1024)
@@ -453,6 +455,41 @@ def ep_layer_bytes(layers, xs, n, xch, ws, d=D, f=F, k=K_TOP):
     return total / n
 
 
+def ep_stack(a, ws, rank):
+    """BASELINE's expert-parallel configuration: a stack of 8 Qwen3-235B-shaped int4 layers (d 4096, f 1536, 128
+    experts, top-8; independent seeded weights per layer) with the experts split over the ws GPUs. One step is one
+    pass of T tokens per GPU through the 8 layers, in a CUDA graph, timed on the device (max over ranks)."""
+    from moelab_b200 import ep
+    d, f, e, k, L = 4096, 1536, 128, 8, 8
+    Ts = [int(s_) for s_ in a.ep_stack.split(",") if s_.strip()]
+    layers = make_ep_layers(L, rank, ws, d=d, f=f, e=e)
+    xch = ep.PeerExchange.create(max(Ts) * k, d)
+    rows = []
+    try:
+        for T in Ts:
+            g = torch.Generator(device="cuda").manual_seed(31 + T + rank)
+            xs = [torch.randn(T, d, generator=g, device="cuda").to(torch.bfloat16) for _ in range(L)]
+            ep_steps(layers, xs, L, xch, k=k)  # eager pass (sizes the workspaces)
+            torch.cuda.synchronize()
+            gr = ep_graph(layers, xs, L, xch, ws)
+            t = max_over_ranks(ws, time_graph(gr, ws))  # one replay = one pass through the stack
+            del gr
+            rows.append({"T": T, "us_per_layer": round(t / L * 1e6, 3), "stack_us": round(t * 1e6, 3),
+                         "tokens_per_s": round(ws * T / t, 1)})
+        errs = xch.read_error()
+        torch.cuda.synchronize()
+        barrier(ws)
+    finally:
+        torch.cuda.synchronize()
+        barrier(ws)
+        xch.close()
+    del layers
+    torch.cuda.empty_cache()
+    return {"config": "qwen3-235b-a22b int4-g64, 8 layers, experts split over the GPUs (peer-memory exchange)",
+            "d": d, "f": f, "E": e, "k": k, "layers": L, "experts_per_gpu": e // ws, "rows": rows,
+            "device_errors": errs}
+
+
 def run_ep(a, ws, rank, local, peaks):
     from moelab_b200 import ep
     T = a.tokens
@@ -512,6 +549,7 @@ def run_ep(a, ws, rank, local, peaks):
         torch.cuda.synchronize()
         barrier(ws)
         xch.close()
+    stack = ep_stack(a, ws, rank) if a.ep_stack else None  # every rank takes part
     if rank != 0:
         return
     line = {
@@ -544,6 +582,8 @@ def run_ep(a, ws, rank, local, peaks):
         "clocks": ck,
         "gpu_launches": 8 * a.steps,  # router, plan, send, prep, gate/up, down, signal, combine
     }
+    if stack is not None:
+        line["ep_stack"] = stack
     print(json.dumps(line), flush=True)
 
 
