@@ -87,7 +87,7 @@ size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 // call (moeb_workspace_init); every kernel leaves them zero again.
 struct Layout {
     size_t err, cnt_all, rcnt, ycnt, zero_end;
-    size_t logits, idx, wts, xsum, ntiles, tiles, sorted, h, hsum, yp, total;
+    size_t logits, idx, wts, xsum, ntiles, tiles, sorted, h, hsum, yp, xg, total;
 };
 
 // with_yp = false: no per-slot output region (expert-parallel calls write the slot outputs to the caller's buffer).
@@ -110,6 +110,9 @@ Layout layout(long Tc, int d, int f, int E, int k, bool with_yp = true) {
     L.h = o; o = align256(o + 2 * (size_t)TK * f);
     L.hsum = o; o = align256(o + 4 * (size_t)TK * (f / 16));
     L.yp = o; o = align256(o + (with_yp ? 4 * (size_t)TK * d : 0));
+    // expert-parallel rows gathered in expert order for the tensor-core kernels (a layer call uses the slot-row
+    // region for that)
+    L.xg = o; o = align256(o + (with_yp ? 0 : 2 * (size_t)TK * d));
     L.total = o;
     return L;
 }
@@ -344,10 +347,11 @@ int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaS
             return fail(MOEB_ELAUNCH, "tensor map encoding failed (down)%s");
     }
     a.h_kperm = K.dn.tc && K.dn.tmem_a ? 1 : 0;
-    if (K.gu.tc) {  // activations in expert-sorted order (in the slot-row region, free until down writes it)
-        uint16_t *xs = reinterpret_cast<uint16_t *>(a.yp);
+    if (K.gu.tc) {  // activations in expert-sorted order: in the slot-row region (free until down writes it) of a
+                    // layer call, in their own region for expert-parallel rows (whose slot outputs go elsewhere)
+        uint16_t *xs = a.slot_out ? at<uint16_t>(ws, L.xg) : reinterpret_cast<uint16_t *>(a.yp);
         if (launch(k_gather_rows, dim3((unsigned)((TK + 7) / 8)), dim3(256), 0, st, a.x, (const int *)a.sorted, (int)TK,
-                   a.k, a.d, K.gu.tmem_a ? 1 : 0, xs) != cudaSuccess)
+                   a.k, a.d, a.xs, K.gu.tmem_a ? 1 : 0, xs) != cudaSuccess)
             return check_launch("gather");
         if (!encode_rows_map(&a.tmx, xs, TK, a.d, nt)) return fail(MOEB_ELAUNCH, "tensor map encoding failed (x)%s");
     }
@@ -660,7 +664,7 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
     if (policy == MOEB_POLICY_DECODE && (ep || (long)T * k > 16)) policy = MOEB_POLICY_SLOTS;  // decode only
     if (policy != MOEB_POLICY_SLOTS && policy != MOEB_POLICY_DECODE && !is_tiles(policy))
         return fail(MOEB_EINVAL, "unknown policy%s");
-    if (policy == MOEB_POLICY_TC && (d % 128 || f % 128 || ep))
+    if (policy == MOEB_POLICY_TC && (d % 128 || f % 128))
         return fail(MOEB_EINVAL, "the tensor-core policy needs d, f multiples of 128%s");
     const bool fused = policy == MOEB_POLICY_DECODE;
     const bool tiles = policy != MOEB_POLICY_SLOTS && !fused;
@@ -955,8 +959,9 @@ static int p2p_experts(int fmt, void *const *peers, void *self, int P, int me, i
     if (policy == MOEB_POLICY_AUTO)
         policy = (Cs <= 16 && (long)P * Cs <= 128) ? MOEB_POLICY_SLOTS
                  : ((long)Cs >= 8L * E_local ? MOEB_POLICY_TILES16_RING : MOEB_POLICY_TILES8_RING);
-    else if (policy != MOEB_POLICY_SLOTS && policy != MOEB_POLICY_TILES8_RING && policy != MOEB_POLICY_TILES16_RING)
-        policy = MOEB_POLICY_TILES8_RING;
+    else if (policy != MOEB_POLICY_SLOTS && policy != MOEB_POLICY_TILES8_RING && policy != MOEB_POLICY_TILES16_RING &&
+             policy != MOEB_POLICY_TC)
+        policy = MOEB_POLICY_TILES8_RING;  // (TC on request: its down epilogue stores into the owners' blocks)
     int rc = experts_common(fmt, b + L.rows, qg, sg, qu, su, qd, sd, bg, bu, bd, nullptr, nullptr, P * Cs, d, f,
                             E_local, 1, act, policy, nullptr, nullptr, ws, ws_bytes, st, nullptr, nullptr, 0, 1.f,
                             nullptr, nullptr, nullptr, nullptr, 0, &pp);

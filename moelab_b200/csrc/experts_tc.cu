@@ -134,6 +134,13 @@ MOEB_DEV void dequant_block(uint4 w, uint32_t sb0, uint32_t sb1, int c, uint32_t
     }
 }
 
+// The fp32 output row of a slot: the workspace's slot rows, or - expert-parallel over peer memory - the slot's row
+// in its owner's return block (as the decode and tile epilogues store it)
+MOEB_DEV float *slot_row(const ExpArgs &a, int slot) {
+    return a.ypeers ? reinterpret_cast<float *>(a.ypeers[slot / a.C] + a.yoff) + ((size_t)a.me * a.C + slot % a.C) * a.d
+                    : a.yp + (size_t)slot * a.d;
+}
+
 // k order of the tensor-core operands inside a 64-group when A lives in TMEM (see k_experts_tca)
 MOEB_DEV int kperm64(int k) { return (k & ~63) | (((k >> 2) & 3) << 4) | (((k >> 4) & 3) << 2) | (k & 3); }
 
@@ -424,7 +431,7 @@ __global__ void __launch_bounds__(TCL<FMT, NT, NR, NA, NX, ACC, DOWN>::THREADS, 
                             const int slot = a.sorted[tr.y + n];
                             const int e_raw = a.idx[slot];
                             const float wsl = (e_raw >= 0 && e_raw < a.E) ? a.wts[slot] : 0.f;
-                            a.yp[(size_t)slot * a.d + row] = wsl * (dv[j] + bdr);
+                            slot_row(a, slot)[row] = wsl * (dv[j] + bdr);
                         }
                     }
                 }
@@ -433,6 +440,7 @@ __global__ void __launch_bounds__(TCL<FMT, NT, NR, NA, NX, ACC, DOWN>::THREADS, 
             __syncwarp();
             if (lane == 0) mbar_arrive1(acce + b);
         }
+        if (DOWN && a.ypeers) __threadfence_system();  // peer stores visible before the signal kernel runs
     }
     tc_fence_before();
     __syncthreads();
@@ -740,7 +748,7 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN, SGK>::THREADS,
                             const int slot = a.sorted[tr.y + n];
                             const int e_raw = a.idx[slot];
                             const float wsl = (e_raw >= 0 && e_raw < a.E) ? a.wts[slot] : 0.f;
-                            a.yp[(size_t)slot * a.d + row] = wsl * (dv[jj] + bdr);
+                            slot_row(a, slot)[row] = wsl * (dv[jj] + bdr);
                         }
                     }
                 }
@@ -749,6 +757,7 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN, SGK>::THREADS,
             __syncwarp();
             if (lane == 0) mbar_arrive1(acce + b);
         }
+        if (DOWN && a.ypeers) __threadfence_system();  // peer stores visible before the signal kernel runs
     }
     tc_fence_before();
     __syncthreads();
@@ -799,17 +808,18 @@ TcInfo experts_tc_info(int fmt, int nt, bool down) {
 // x rows of the slots in expert-sorted order (the activation operand of the tensor-core gate/up); perm: in the
 // 64-group k order of the TMEM-operand kernels (8-byte chunks of 4 k: chunk 4b + a goes to 4a + b)
 __global__ void __launch_bounds__(256) k_gather_rows(const uint16_t *__restrict__ x, const int *__restrict__ sorted,
-                                                     int TK, int k, int d, int perm, uint16_t *__restrict__ xs) {
+                                                     int TK, int k, int d, int xstride, int perm,
+                                                     uint16_t *__restrict__ xs) {
     pdl_launch();
     pdl_wait();
     const int i = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (i >= TK) return;
     if (!perm) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)(sorted[i] / k) * d);
+        const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)(sorted[i] / k) * xstride);
         uint4 *dst = reinterpret_cast<uint4 *>(xs + (size_t)i * d);
         for (int c = lane; c < d / 8; c += 32) dst[c] = src[c];
     } else {
-        const uint2 *src = reinterpret_cast<const uint2 *>(x + (size_t)(sorted[i] / k) * d);
+        const uint2 *src = reinterpret_cast<const uint2 *>(x + (size_t)(sorted[i] / k) * xstride);
         uint2 *dst = reinterpret_cast<uint2 *>(xs + (size_t)i * d);
         for (int c = lane; c < d / 4; c += 32) {
             const int u = c & 15;

@@ -190,7 +190,8 @@ struct TcInfo {
     int sg;       // 64-groups per pipeline stage (the weight tensor maps' box width)
 };
 TcInfo experts_tc_info(int fmt, int nt, bool down);
-__global__ void k_gather_rows(const uint16_t *x, const int *sorted, int TK, int k, int d, int perm, uint16_t *xs);
+__global__ void k_gather_rows(const uint16_t *x, const int *sorted, int TK, int k, int d, int xstride, int perm,
+                              uint16_t *xs);
 size_t experts_ws_smem(int nt8, int rbc, int sg, int ns, bool down, int fmt);
 
 

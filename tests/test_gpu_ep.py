@@ -8,7 +8,7 @@ import torch
 
 import oracle
 from ep_workers import ThreadGroup
-from helpers import assert_close, load_variant
+from helpers import assert_close, load_variant, ref_from_state
 from moelab_b200 import ep, ops
 from moelab_b200.variants.cuda import b200_mxfp4_moe, b200_q4_moe
 from oracle import ep as oep
@@ -155,6 +155,49 @@ def test_emulated_ep_gptoss_mxfp4_bit_exact(pol):
             continue
         ys = ops.experts(full, x, idx, wts, act=2, policy=POL[pol], residual=x)
         assert torch.equal(y, ys)
+
+
+# ------------------------------------------------------------------ tensor-core expert kernels, explicitly requested
+@pytest.mark.parametrize("P,tokens", [(2, [40, 33]), (4, [17, 0, 64, 9])])
+def test_ep_tc_policy_vs_oracle(P, tokens):
+    """The tcgen05 kernels serving expert-parallel rows (explicit policy; the dispatcher does not pick them for
+    expert parallelism yet): rows with their 16-byte tails gathered in expert order, slot outputs stored into the
+    owners' return blocks (peer memory, emulated phase by phase) or the caller's rows (NCCL path, emulated by
+    threads). Against the fp64 oracle on the dequantized weights."""
+    E, d, f, k = 32, 256, 384, 4
+    w, gate = _layer(E, d, f, seed=300 + P)
+    full = b200_q4_moe.prepare(*w)
+    b200_q4_moe._ws(full, k)
+    # NCCL path
+    for y, idx, wts, x in _emulated(P, b200_q4_moe, w, gate, tokens, k, ops.POLICY_TC, seed=40 * P):
+        if x.shape[0]:
+            assert_close(y, ref_from_state(b200_q4_moe, full, x, idx, wts) + x.float().cpu().numpy(), what=("nccl", P))
+    # peer-memory path
+    C = max(tokens) * k + 4
+    xchs = ep.PeerExchange.local_group(P, C, d, "cuda")
+    states = [ep.shard(b200_q4_moe, *w, r, P) for r in range(P)]
+    try:
+        for call in range(2):
+            xs = [torch.randn(T, d, generator=torch.Generator(device="cuda").manual_seed(call * 50 + r),
+                              device="cuda").to(torch.bfloat16) for r, T in enumerate(tokens)]
+            routing = []
+            for r in range(P):
+                idx, wts = ops.router(xs[r], gate, k)
+                routing.append((idx, wts, ops.ep_p2p_dispatch(xs[r], idx, wts, E, xchs[r])))
+            for r in range(P):
+                ops.ep_p2p_experts(states[r], xchs[r], policy=ops.POLICY_TC)
+            for r in range(P):
+                idx, wts, sp = routing[r]
+                y = ops.ep_p2p_combine(xchs[r], sp, tokens[r], k, d, residual=xs[r], device="cuda")
+                if tokens[r]:
+                    ref = ref_from_state(b200_q4_moe, full, xs[r], idx, wts) + xs[r].float().cpu().numpy()
+                    assert_close(y, ref, what=("p2p", call, r))
+        torch.cuda.synchronize()
+        assert all(x.read_error() == 0 for x in xchs)
+        assert all(s["ep_ws"].read_error() == 0 for s in states)
+    finally:
+        for x in xchs:
+            x.close()
 
 
 # ------------------------------------------------------------------ exchange over peer memory, emulated
