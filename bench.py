@@ -19,6 +19,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -96,11 +97,10 @@ class ClockSampler:
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_bench_gpu{gpu_index}.csv")
+        self.path = os.path.join(tempfile.gettempdir(), f"moelab_b200_clocks_gpu{gpu_index}_{os.getpid()}.csv")
 
     def start(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={CLOCK_Q}",
                                           "--format=csv,noheader,nounits", "-lms", "100"],

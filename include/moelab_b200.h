@@ -91,6 +91,17 @@ int moeb_mxfp4_from_mlx(const void *wq, const void *scales, long rows, long K, v
 int moeb_router(const void *x, const void *gate_w, const void *gate_b, int T, int d, int E, int k, int norm,
                 float scale, int *idx, float *wts, float *logits, void *ws, size_t ws_bytes, cudaStream_t stream);
 
+/* --- the routing step alone (the tile builder every tiled call runs), for bit-exact checks of its integer work:
+ * stable counting sort of the T*k slots (idx int32 [T*k]) by expert. Writes counts[E] (slots per expert; may be
+ * NULL), offsets[E] (their exclusive prefix sums; may be NULL), sorted[T*k] (slot ids grouped by expert, each
+ * expert's slots in increasing order), tiles[ntiles][4] int32 {expert, start in sorted, n <= nt, 0} (each
+ * expert's run cut every nt slots, experts in increasing order; room for T*k + E entries) and *ntiles. Ids
+ * outside [0, E) set MOEB_DEVERR_EXPERT_ID and are grouped under expert 0. Replaces the map kernel of
+ * moelab/variants/mlx/metal_q4_tiles_v2.py:362-373 (tiles of <= VT consecutive same-expert slots). ws: a workspace
+ * of moeb_workspace_bytes(T, 64, 64, E, k) bytes (its counters and error word). */
+int moeb_route_tables(const int *idx, int T, int k, int E, int nt, int *counts, int *offsets, int *sorted, int *tiles,
+                      int *ntiles, void *ws, size_t ws_bytes, cudaStream_t stream);
+
 /* --- expert forward with given routing: y = sum_j wts[t,j] * (Wd act(Wg x + bg, Wu x + bu) + bd) (+ residual).
  * Replaces the variant run(state, x, idx, wts, act) (metal_q4_moe.py:54-64 dispatcher; contract
  * problem.py:3-10). act: 0 SwiGLU, 1 tanh-GELU GLU, 2 gpt-oss clamped SwiGLU (alpha 1.702, limit 7, up+1).
@@ -199,6 +210,10 @@ int moeb_ep_p2p_experts_q4(void *const *peers, void *self, int P, int me, int C,
                            void *ws, size_t ws_bytes, cudaStream_t stream);
 int moeb_ep_p2p_combine(void *self, const int *slot_pos, int P, int C, int T, int d, int k, const void *residual,
                         void *y, cudaStream_t stream);
+/* Limit of every bounded wait on this rank's exchange buffer (for a peer's dispatch flag or return flag), in
+ * seconds; 0 restores the default of 2 s. After the limit a wait records MOEB_DEVERR_TIMEOUT and the call goes on
+ * without that peer's rows. Synchronises the stream. */
+int moeb_ep_p2p_set_wait_limit(void *self, int P, int C, int d, double seconds, cudaStream_t stream);
 /* Sticky error bits of the exchange buffer (a wait that gave up); synchronises the stream, clears them. */
 int moeb_ep_p2p_read_error(void *self, int P, int C, int d, unsigned *out, cudaStream_t stream);
 
@@ -206,7 +221,8 @@ int moeb_ep_p2p_read_error(void *self, int P, int C, int d, unsigned *out, cudaS
  * always lets the variant allocate its scratch). The scratch lives in a static 16 MiB device array inside the
  * library (held by every GPU that loads it until exit), so the caller passes only inputs and the output. T is
  * limited to what fits: moeb_workspace_bytes(T, d, f, E, k) <= MOEB_STATIC_SCRATCH_BYTES, else MOEB_EINVAL.
- * The first call on a device looks up the array's device address; make it before any stream capture. All
+ * The first call on a device looks up the array's device address; make it before any stream capture. `stream`
+ * must belong to the current device (the address is looked up for the current device). All
  * calls share the array: calls that overlap on the GPU (two streams, two threads) race. Device error bits are
  * cleared on entry and not readable afterwards. Nothing is allocated. */
 #define MOEB_STATIC_SCRATCH_BYTES (16u << 20)

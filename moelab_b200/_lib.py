@@ -36,6 +36,7 @@ SIGNATURES = {
     "moeb_q4_from_mlx": (_I, [_P, _P, _P, _L, _L, _P, _P, _P]),
     "moeb_mxfp4_from_mlx": (_I, [_P, _P, _L, _L, _P, _P, _P]),
     "moeb_router": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _S, _P]),
+    "moeb_route_tables": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _S, _P]),
     "moeb_experts_q4": (_I, [_P] * 12 + [_I] * 7 + [_P, _P, _P, _S, _P]),
     "moeb_experts_q4_static": (_I, [_P] * 12 + [_I] * 7 + [_P, _P, _P]),
     "moeb_layer_q4": (_I, [_P, _P, _P, _I, _F] + [_P] * 9 + [_I] * 7 + [_P, _P, _P, _P, _P, _P, _S, _P]),
@@ -56,6 +57,7 @@ SIGNATURES = {
     "moeb_ep_p2p_dispatch": (_I, [_P, _P, _P] + [_I] * 8 + [_P, _P, _P, _P, _P]),
     "moeb_ep_p2p_experts_q4": (_I, [_P, _P] + [_I] * 7 + [_P] * 9 + [_I, _I, _P, _S, _P]),
     "moeb_ep_p2p_combine": (_I, [_P, _P] + [_I] * 5 + [_P, _P, _P]),
+    "moeb_ep_p2p_set_wait_limit": (_I, [_P, _I, _I, _I, ctypes.c_double, _P]),
     "moeb_ep_p2p_read_error": (_I, [_P, _I, _I, _I, ctypes.POINTER(ctypes.c_uint), _P]),
 }
 

@@ -455,12 +455,12 @@ int launch_router(const void *x, const void *wg, const void *bias, int T, int d,
     r.sorted = at<int>(ws, L.sorted);
     // the tile builder keeps the slot ids in shared memory for its second pass when that stays small (every
     // router CTA carries this allocation, so it is capped to keep the logits phase at full occupancy)
-    size_t smem = tiles ? 8 * (size_t)(E + ns) : 0;
-    if (tiles && smem + 4 * (size_t)T * (k + ns) <= 16 * 1024) smem += 4 * (size_t)T * (k + ns);
+    const bool tiled = router_tiled(T, E);
+    const size_t smem = tiles ? tiles_smem(tiled ? 256 : 128, E + ns, (long)T * (k + ns), 16 * 1024) : 0;
     // one expert per warp and 1 (T <= 64) or 4 tokens, or the register-tiled kernel (4 tokens x EW experts per
     // warp, EW = 4 from 32 experts on)
     cudaError_t e;
-    if (router_tiled(T, E)) {
+    if (tiled) {
         const int ew = E >= 32 ? 4 : E >= 16 ? 2 : 1;
         void (*kern)(RouterArgs) = ew == 4 ? router_t_kernel<4>(E) : ew == 2 ? router_t_kernel<2>(E) : router_t_kernel<1>(E);
         e = launch(kern, dim3((E + 8 * ew - 1) / (8 * ew), (T + 3) / 4), dim3(256), smem, st, r);
@@ -628,11 +628,37 @@ int moeb_router(const void *x, const void *wg, const void *bias, int T, int d, i
     return launch_router(x, wg, bias, T, d, E, k, norm, scale, idx, wts, logits, false, MOEB_POLICY_SLOTS, L, ws, st);
 }
 
+// ------------------------------------------------------------------ routing tables (the routing step alone)
+int moeb_route_tables(const int *idx, int T, int k, int E, int nt, int *counts, int *offsets, int *sorted, int *tiles,
+                      int *ntiles, void *ws, size_t ws_bytes, cudaStream_t st) {
+    if (T < 0 || k <= 0 || k > 32 || E <= 0 || E > 1024 || nt < 1) return fail(MOEB_EINVAL, "bad T, k, E or nt%s");
+    if (!idx || !sorted || !tiles || !ntiles) return fail(MOEB_EINVAL, "idx, sorted, tiles and ntiles are required%s");
+    const long cap = capacity(ws_bytes, 64, 64, E, k);
+    if (cap < std::max(T, 1)) return fail(MOEB_EINVAL, "workspace too small%s");
+    const Layout L = layout(cap, 64, 64, E, k);
+    PrepArgs p = {};
+    p.idx = idx;
+    p.T = T; p.d = 64; p.E = E; p.k = k; p.xs = 64;
+    p.cnt_all = at<unsigned>(ws, L.cnt_all);
+    p.NT = nt;
+    p.tiles = reinterpret_cast<int4 *>(tiles);
+    p.ntiles = ntiles;
+    p.sorted = sorted;
+    p.err = at<unsigned>(ws, L.err);
+    p.counts = counts;
+    p.offsets = offsets;
+    const size_t smem = tiles_smem(256, E, (long)T * k, 48 * 1024);
+    if (launch(k_prep, dim3((unsigned)std::max(1, (T + 7) / 8)), dim3(256), smem, st, p) != cudaSuccess)
+        return check_launch("route_tables");
+    return MOEB_OK;
+}
+
 // ------------------------------------------------------------------ experts (ids given) and full layer
 struct P2PParams {
     const unsigned *rflag;
     const int *rcnt;
     const unsigned *epoch;
+    const unsigned long long *wait_ns;
     int C, me;  // C: this call's rows per source block
     unsigned char *const *peers;
     size_t yoff;
@@ -697,6 +723,7 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
             p.rflag = pp->rflag;
             p.rcnt = pp->rcnt;
             p.epoch = pp->epoch;
+            p.wait_ns = pp->wait_ns;
             p.C = pp->C;
         }
         p.xsum = at<float>(ws, L.xsum);
@@ -706,8 +733,7 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
         p.ntiles = at<int>(ws, L.ntiles);
         p.sorted = at<int>(ws, L.sorted);
         p.err = at<unsigned>(ws, L.err);
-        size_t smem = tiles ? 8 * (size_t)E : 0;
-        if (tiles && smem + 4 * (size_t)T * k <= 48 * 1024) smem += 4 * (size_t)T * k;  // ids cached (build_tiles)
+        const size_t smem = tiles ? tiles_smem(256, E, (long)T * k, 48 * 1024) : 0;  // ids cached when they fit
         if (launch(k_prep, dim3((T + 7) / 8), dim3(256), smem, st, p) != cudaSuccess) return check_launch("prep");
     }
     if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev[1]), st);
@@ -949,6 +975,7 @@ static int p2p_experts(int fmt, void *const *peers, void *self, int P, int me, i
     pp.rflag = reinterpret_cast<const unsigned *>(b + L.rflag);
     pp.rcnt = reinterpret_cast<const int *>(b + L.rcnt);
     pp.epoch = reinterpret_cast<const unsigned *>(b + L.epoch);
+    pp.wait_ns = reinterpret_cast<const unsigned long long *>(b + L.wait);
     pp.C = Cs;
     pp.me = me;
     pp.peers = reinterpret_cast<unsigned char *const *>(peers);
@@ -989,6 +1016,15 @@ int moeb_ep_p2p_combine(void *self, const int *slot_pos, int P, int C, int T, in
                (const unsigned char *)b, slot_pos, P, C, T, d, k, static_cast<const uint16_t *>(residual),
                static_cast<uint16_t *>(y), reinterpret_cast<unsigned *>(b + p2p_layout(P, C, d).err)) != cudaSuccess)
         return check_launch("ep_combine_p2p");
+    return MOEB_OK;
+}
+
+int moeb_ep_p2p_set_wait_limit(void *self, int P, int C, int d, double seconds, cudaStream_t st) {
+    if (!self || !(seconds >= 0.0) || seconds > 3600.0) return fail(MOEB_EINVAL, "need 0 <= seconds <= 3600%s");
+    const unsigned long long v = (unsigned long long)(seconds * 1e9);
+    unsigned char *b = static_cast<unsigned char *>(self) + p2p_layout(P, C, d).wait;
+    if (cudaMemcpyAsync(b, &v, sizeof v, cudaMemcpyHostToDevice, st) != cudaSuccess) return check_launch("set_wait");
+    if (cudaStreamSynchronize(st) != cudaSuccess) return check_launch("set_wait sync");
     return MOEB_OK;
 }
 

@@ -180,13 +180,15 @@ MOEB_DEV unsigned ld_acquire_sys(const unsigned *p) {
 MOEB_DEV void st_release_sys(unsigned *p, unsigned v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-// Bounded wait until *flag == want (acquire, system scope). Gives up after ~2 s of wall time (a peer that never
-// signals), records ERR_TIMEOUT and returns false; the caller then carries on with whatever data is there.
-MOEB_DEV bool wait_flag_sys(const unsigned *flag, unsigned want, unsigned *err) {
+// Bounded wait until *flag == want (acquire, system scope). Gives up after limit_ns of wall time (0: 2 s) - a
+// peer that never signals -, records ERR_TIMEOUT and returns false; the caller then carries on with whatever data
+// is there.
+MOEB_DEV bool wait_flag_sys(const unsigned *flag, unsigned want, unsigned *err, uint64_t limit_ns = 0) {
     if (ld_acquire_sys(flag) == want) return true;
+    const uint64_t lim = limit_ns ? limit_ns : 2000000000ull;
     const uint64_t t0 = globaltimer_ns();
     while (ld_acquire_sys(flag) != want) {
-        if (globaltimer_ns() - t0 > 2000000000ull) {
+        if (globaltimer_ns() - t0 > lim) {
             atomicOr(err, ERR_TIMEOUT);
             return false;
         }

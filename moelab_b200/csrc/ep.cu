@@ -160,9 +160,10 @@ __global__ void __launch_bounds__(128) k_ep_combine_p2p(const unsigned char *sel
     const P2PLayout L = p2p_layout(P, C, d);
     const unsigned ep = *reinterpret_cast<const unsigned *>(self + L.epoch);
     const unsigned *bflag = reinterpret_cast<const unsigned *>(self + L.bflag);
+    const uint64_t lim = *reinterpret_cast<const unsigned long long *>(self + L.wait);
     __shared__ int ok;
     if (threadIdx.x < 32) {  // one warp waits for all P expert ranks (P <= 32)
-        const bool done = threadIdx.x >= P || wait_flag_sys(bflag + threadIdx.x, ep, err);
+        const bool done = threadIdx.x >= P || wait_flag_sys(bflag + threadIdx.x, ep, err, lim);
         (void)done;
         __syncwarp();
         if (threadIdx.x == 0) ok = 1;

@@ -42,6 +42,7 @@ struct PrepArgs {
     const unsigned *rflag;
     const int *rcnt;
     const unsigned *epoch;
+    const unsigned long long *wait_ns;  // the exchange's wait limit (0 = the 2 s default)
     int C;
     float *xsum;
     unsigned *cnt_all;
@@ -50,6 +51,7 @@ struct PrepArgs {
     int *ntiles;
     int *sorted;
     unsigned *err;
+    int *counts, *offsets;  // optional [E] outputs of the tile builder (per-expert slot counts, prefix offsets)
 };
 
 // Expert weights of one projection in the B200 layout.
@@ -98,10 +100,11 @@ struct ExpArgs {
 };
 
 // Per-rank buffer of the peer-memory exchange (one allocation, mapped by every rank of the group):
-//   epoch counter and a grid counter, rflag[P] / rcnt[P] (written by the sources), bflag[P] (written by the
-//   expert ranks), rows [P][C][d + 8] bf16 (source blocks), back [P][C][d] fp32 (return blocks).
+//   epoch counter, error word, a grid counter and the wait limit (u64 ns, 0 = 2 s), rflag[P] / rcnt[P] (written
+//   by the sources), bflag[P] (written by the expert ranks), rows [P][C][d + 8] bf16 (source blocks), back [P][C][d]
+//   fp32 (return blocks).
 struct P2PLayout {
-    size_t epoch, err, ctr, rflag, rcnt, bflag, rows, back, total;
+    size_t epoch, err, ctr, wait, rflag, rcnt, bflag, rows, back, total;
 };
 __host__ __device__ inline P2PLayout p2p_layout(int P, int C, int d) {
     P2PLayout L;
@@ -109,6 +112,7 @@ __host__ __device__ inline P2PLayout p2p_layout(int P, int C, int d) {
     L.epoch = 0;
     L.err = 64;
     L.ctr = 128;
+    L.wait = 192;
     L.rflag = 256;
     L.rcnt = L.rflag + up(4 * (size_t)P);
     L.bflag = L.rcnt + up(4 * (size_t)P);
@@ -153,6 +157,7 @@ __global__ void k_router(RouterArgs a);
 template <int TW, int EW, int JMAX>
 __global__ void k_router_t(RouterArgs a);
 __global__ void k_prep(PrepArgs a);
+size_t tiles_smem(int threads, int E, long TK, size_t cap);
 
 __global__ void k_q4_quantize(const uint16_t *w, long rows, long K, uint32_t *qw, uint32_t *sb);
 __global__ void k_q4_dequant(const uint32_t *qw, const uint32_t *sb, long rows, long K, float *out);

@@ -48,81 +48,118 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int *total) {
     return r;
 }
 
-// Counting sort of the TK slots by expert. Slot order inside an expert follows atomic arrival; this does not
-// change any result (every slot is its own MMA column and the combine sums slots in fixed j order).
-// The ids are read in batches of BT independent loads per thread (one L2 round trip per batch, not per slot);
-// when the launch gave enough dynamic shared memory (8 E + 4 TK bytes) they are kept there for the second pass.
+// Stable counting sort of the TK slots by expert (the routing step), one CTA. The slots are cut into one
+// contiguous segment per warp; each warp walks its segment in slot order, 32 at a time, grouping equal ids with a
+// warp match. A slot's place inside its expert is (slots of that expert in earlier segments) + (earlier slots of
+// that expert in this segment), so the slots of one expert keep increasing slot order and every array written here
+// is a deterministic function of the ids. Tiles are cut from each expert's run, NT slots at a time: the grouping
+// contract of the reference's map kernel (metal_q4_tiles_v2.py:362-373, a tile holds up to VT consecutive
+// same-expert slots in slot order), listed here in expert order.
+// Dynamic shared memory: hist [warps][E] and tot [E] ints, then (when it fits) the TK ids.
+// Ids equal to SLOT_SKIP (capacity padding) are skipped; other ids outside [0, E) set ERR_EXPERT_ID and are
+// grouped under expert 0 (the expert kernels compute them there with weight 0).
+// counts / offsets (may be null): per-expert slot counts and their exclusive prefix sums (offsets into sorted).
 __device__ void build_tiles(const int *__restrict__ idx, int TK, int E, int NT, int4 *__restrict__ tiles,
-                            int *__restrict__ ntiles, int *__restrict__ sorted, unsigned *__restrict__ err) {
-    constexpr int BT = 16;
+                            int *__restrict__ ntiles, int *__restrict__ sorted, unsigned *__restrict__ err,
+                            int *__restrict__ counts, int *__restrict__ offsets) {
+    constexpr int BT = 8;  // ids loaded per lane per batch (independent loads in flight)
     extern __shared__ int smem[];
-    int *cnt = smem;      // [E]
-    int *off = smem + E;  // [E]
-    int *ids = smem + 2 * E;  // [TK] when it fits
+    const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, warp = tid >> 5, nw = nth >> 5;
+    int *hist = smem;                  // [nw][E]: counts, then each warp's first position per expert
+    int *tot = smem + nw * E;          // [E]
+    int *ids = smem + (nw + 1) * E;    // [TK] when it fits
     unsigned dsm;
     asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dsm));
-    const bool cache = (size_t)(2 * E + TK) * 4 <= dsm;
-    const int tid = threadIdx.x, nth = blockDim.x;
-    for (int e = tid; e < E; e += nth) cnt[e] = 0;
+    const bool cache = (size_t)((nw + 1) * E + TK) * 4 <= dsm;
+    const int seg = (TK + nw - 1) / nw;
+    const int s_beg = min(TK, warp * seg), s_end = min(TK, s_beg + seg);
+    const unsigned lt = (1u << lane) - 1u;
+    for (int i = tid; i < nw * E; i += nth) hist[i] = 0;
     __syncthreads();
+    // pass 1: per-warp histograms of the warp's segment (only warp w writes row w: no atomics)
     bool bad = false;
-    for (int s0 = tid; s0 < TK; s0 += nth * BT) {
+    for (int b0 = s_beg; b0 < s_end; b0 += 32 * BT) {
         int ev[BT];
 #pragma unroll
         for (int i = 0; i < BT; ++i) {
-            const int s = s0 + i * nth;
-            ev[i] = s < TK ? __ldcg(idx + s) : SLOT_SKIP;
+            const int s = b0 + 32 * i + lane;
+            ev[i] = s < s_end ? __ldcg(idx + s) : SLOT_SKIP;
         }
 #pragma unroll
         for (int i = 0; i < BT; ++i) {
+            const int s = b0 + 32 * i + lane;
             int e = ev[i];
-            if (cache && s0 + i * nth < TK) ids[s0 + i * nth] = e;
-            if (e == SLOT_SKIP) continue;  // capacity padding (or past TK): no work, not an error
-            if (e < 0 || e >= E) { bad = true; e = 0; }
-            atomicAdd(&cnt[e], 1);
+            if (cache && s < s_end) ids[s] = e;
+            if (e != SLOT_SKIP && (e < 0 || e >= E)) { bad = true; e = 0; }
+            const unsigned peers = __match_any_sync(0xffffffffu, e);
+            if (e != SLOT_SKIP && (peers & lt) == 0u) hist[warp * E + e] += __popc(peers);
+            __syncwarp();
         }
     }
     if (bad) atomicOr(err, ERR_EXPERT_ID);
     __syncthreads();
-    // each thread owns a contiguous chunk of experts; two CTA-wide scans give slot and tile offsets
+    // per expert: total and per-warp exclusive prefix; each thread owns a contiguous chunk of experts, two CTA-wide
+    // scans give the slot and tile offsets
     const int per = (E + nth - 1) / nth;
     const int e0 = min(E, tid * per), e1 = min(E, e0 + per);
     int sc = 0, st = 0;
     for (int e = e0; e < e1; ++e) {
-        sc += cnt[e];
-        st += (cnt[e] + NT - 1) / NT;
+        int c = 0;
+        for (int w = 0; w < nw; ++w) {
+            const int h = hist[w * E + e];
+            hist[w * E + e] = c;
+            c += h;
+        }
+        tot[e] = c;
+        sc += c;
+        st += (c + NT - 1) / NT;
     }
     int tot_s, tot_t;
     int base_s = block_exclusive_scan(sc, &tot_s);
     int base_t = block_exclusive_scan(st, &tot_t);
     if (tid == 0) *ntiles = tot_t;
     for (int e = e0; e < e1; ++e) {
-        const int c = cnt[e];
-        off[e] = base_s;
+        const int c = tot[e];
+        for (int w = 0; w < nw; ++w) hist[w * E + e] += base_s;
+        if (counts) counts[e] = c;
+        if (offsets) offsets[e] = base_s;
         const int nt = (c + NT - 1) / NT;
         for (int i = 0; i < nt; ++i) tiles[base_t + i] = make_int4(e, base_s + i * NT, min(NT, c - i * NT), 0);
         base_s += c;
         base_t += nt;
     }
     __syncthreads();
-    for (int e = tid; e < E; e += nth) cnt[e] = 0;
-    __syncthreads();
-    for (int s0 = tid; s0 < TK; s0 += nth * BT) {
+    // pass 2: scatter, the same walk (a slot's position = its warp's running position + its rank among the
+    // earlier lanes with the same id)
+    for (int b0 = s_beg; b0 < s_end; b0 += 32 * BT) {
         int ev[BT];
 #pragma unroll
         for (int i = 0; i < BT; ++i) {
-            const int s = s0 + i * nth;
-            ev[i] = s >= TK ? SLOT_SKIP : cache ? ids[s] : __ldcg(idx + s);
+            const int s = b0 + 32 * i + lane;
+            ev[i] = s >= s_end ? SLOT_SKIP : cache ? ids[s] : __ldcg(idx + s);
         }
 #pragma unroll
         for (int i = 0; i < BT; ++i) {
+            const int s = b0 + 32 * i + lane;
             int e = ev[i];
-            if (e == SLOT_SKIP) continue;
-            if (e < 0 || e >= E) e = 0;
-            const int pos = atomicAdd(&cnt[e], 1);
-            sorted[off[e] + pos] = s0 + i * nth;
+            if (e != SLOT_SKIP && (e < 0 || e >= E)) e = 0;
+            const unsigned peers = __match_any_sync(0xffffffffu, e);
+            if (e != SLOT_SKIP) {
+                const int pos = hist[warp * E + e] + __popc(peers & lt);
+                sorted[pos] = s;
+            }
+            __syncwarp();
+            if (e != SLOT_SKIP && (peers & lt) == 0u) hist[warp * E + e] += __popc(peers);
+            __syncwarp();
         }
     }
+}
+
+// Dynamic shared memory the tile builder uses in a CTA of `threads` threads: per-warp histograms and totals,
+// plus the ids when that stays under `cap` bytes.
+size_t tiles_smem(int threads, int E, long TK, size_t cap) {
+    const size_t base = 4 * (size_t)(threads / 32 + 1) * E;
+    return base + 4 * (size_t)TK <= cap ? base + 4 * (size_t)TK : base;
 }
 
 // After a router CTA has written its logits: the last CTA of each token block (last-arriver counter, no spin)
@@ -145,7 +182,7 @@ __device__ __forceinline__ void router_tail(const RouterArgs &a, int t0, int nt,
     if (threadIdx.x == 0) s_last = atom_add_acq_rel_gpu(a.cnt_all, 1u) == gridDim.y - 1;
     __syncthreads();
     if (!s_last) return;
-    build_tiles(a.idx, a.T * (a.k + a.ns), a.E + a.ns, a.NT, a.tiles, a.ntiles, a.sorted, a.err);
+    build_tiles(a.idx, a.T * (a.k + a.ns), a.E + a.ns, a.NT, a.tiles, a.ntiles, a.sorted, a.err, nullptr, nullptr);
     if (threadIdx.x == 0) *a.cnt_all = 0;
 }
 
@@ -328,12 +365,12 @@ __global__ void __launch_bounds__(256) k_prep(PrepArgs a) {
     pdl_wait();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int t = blockIdx.x * 8 + warp;
-    if (t < a.T) {
+    if (t < a.T && a.x) {  // (no rows: the routing tables alone, moeb_route_tables)
         const uint16_t *xr = a.x + (size_t)t * a.xs;
         bool valid = true;
         if (a.rflag) {  // peer-memory exchange: row t is slot t % C of source t / C; wait for that source
             const int src = t / a.C;
-            if (lane == 0) wait_flag_sys(a.rflag + src, *a.epoch, a.err);
+            if (lane == 0) wait_flag_sys(a.rflag + src, *a.epoch, a.err, a.wait_ns ? *a.wait_ns : 0ull);
             __syncwarp();
             valid = (t % a.C) < *reinterpret_cast<const volatile int *>(a.rcnt + src);
         }
@@ -370,7 +407,7 @@ __global__ void __launch_bounds__(256) k_prep(PrepArgs a) {
     }
     __syncthreads();
     if (!s_last) return;
-    build_tiles(a.idx, a.T * a.k, a.E, a.NT, a.tiles, a.ntiles, a.sorted, a.err);
+    build_tiles(a.idx, a.T * a.k, a.E, a.NT, a.tiles, a.ntiles, a.sorted, a.err, a.counts, a.offsets);
     if (threadIdx.x == 0) *a.cnt_all = 0;
 }
 

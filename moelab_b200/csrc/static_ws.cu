@@ -23,7 +23,8 @@ __device__ __align__(256) unsigned char g_static_scratch[MOEB_STATIC_SCRATCH_BYT
 // Device address of g_static_scratch for the current device. The host-side symbol is only a stand-in for the
 // array: passing it to a kernel would fault or silently touch the wrong memory. So the first call on a device
 // looks the address up with cudaGetSymbolAddress (with that device current) and caches it; that first call
-// should therefore come before any stream capture.
+// should therefore come before any stream capture. The cache is keyed by the current device, so the caller's
+// stream must belong to the current device (as for every entry point of this library).
 void *scratch_address(int *rc) {
     static std::mutex mu;
     static std::unordered_map<int, void *> addr;
@@ -73,11 +74,13 @@ extern "C" int moeb_experts_q4_static(const void *x, const void *qg, const void 
     void *ws = scratch_address(&rc);
     if (!ws) return rc;
     // The array keeps the previous call's contents: clear the counters and the error word this call relies on.
-    const size_t z = moeb::zero_region_bytes(MOEB_STATIC_SCRATCH_BYTES, d, f, E, k);
+    // The call sees only the first `need` bytes, so its layout (and the cleared region) scales with T; every other
+    // region is written by this call before it is read.
+    const size_t z = moeb::zero_region_bytes(need, d, f, E, k);
     if (z && cudaMemsetAsync(ws, 0, z, stream) != cudaSuccess) {
         moeb::set_error("clearing the static scratch failed");
         return MOEB_ELAUNCH;
     }
     return moeb_experts_q4(x, qg, sbg, qu, sbu, qd, sbd, bg, bu, bd, idx, wts, T, d, f, E, k, act, policy, residual,
-                           y, ws, MOEB_STATIC_SCRATCH_BYTES, stream);
+                           y, ws, need, stream);
 }

@@ -178,6 +178,12 @@ class PeerExchange:
         bases = [cls._alloc(cls.nbytes(P, C, d)) for _ in range(P)]
         return [cls(P, r, C, d, device, bases[r], bases, owns=True) for r in range(P)]
 
+    def set_wait_limit(self, seconds):
+        """Limit of this rank's bounded waits for peers (seconds; 0 = the 2 s default). A wait that runs out
+        records DEVERR_TIMEOUT (see read_error) and the call carries on without that peer."""
+        _lib.call("moeb_ep_p2p_set_wait_limit", ctypes.c_void_p(self.base), self.P, self.C, self.d, float(seconds),
+                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+
     def read_error(self):
         out = ctypes.c_uint(0)
         _lib.call("moeb_ep_p2p_read_error", ctypes.c_void_p(self.base), self.P, self.C, self.d, ctypes.byref(out),

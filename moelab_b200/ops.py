@@ -168,6 +168,25 @@ def router(x, gate_w, k, gate_b=None, norm=True, scale=1.0, return_logits=False)
     return (idx, wts, logits) if return_logits else (idx, wts)
 
 
+def route_tables(idx, E, nt):
+    """The routing step alone (moeb_route_tables): idx int32 [T, k] -> (counts [E], offsets [E], sorted [T*k],
+    tiles [ntiles, 4]) int32, plus the device error bits (MOEB_DEVERR_*). For bit-exact checks of the tile builder."""
+    _need(idx, torch.int32, "idx")
+    T, k = idx.shape
+    dev = idx.device
+    counts = torch.empty(E, dtype=torch.int32, device=dev)
+    offsets = torch.empty(E, dtype=torch.int32, device=dev)
+    sorted_ = torch.empty(max(T * k, 1), dtype=torch.int32, device=dev)
+    tiles = torch.empty(T * k + E, 4, dtype=torch.int32, device=dev)
+    ntiles = torch.empty(1, dtype=torch.int32, device=dev)
+    ws = Workspace(64, 64, E, k, dev)
+    buf = ws.get(max(T, 1))
+    _lib.call("moeb_route_tables", _p(idx), T, k, E, int(nt), _p(counts), _p(offsets), _p(sorted_), _p(tiles),
+              _p(ntiles), _p(buf), buf.numel(), _stream())
+    n = int(ntiles.item())
+    return counts, offsets, sorted_[:T * k], tiles[:n], ws.read_error()
+
+
 # ------------------------------------------------------------------ experts / layer (int4)
 def _expert_ptrs(state):
     (qg, sg), (qu, su), (qd, sd) = state["g"], state["u"], state["d"]

@@ -1,8 +1,8 @@
 """MoE layer shapes (per layer, routed experts): d = hidden, f = expert FFN width, E = experts, k = top-k.
 
-Mirrors moelab/shapes.py:9-39 (MoEShape and the real-model table) and adds the per-family router rules the
-layer call needs (moelab/e2e.py:56-63 Qwen3 renormalised top-k, :136-147 DeepSeek-V2 greedy + shared
-experts, :171-176 gpt-oss biased gate + softmax over the top-k).
+Mirrors moelab/shapes.py:9-39 (MoEShape and the real-model table). The per-family router rules (Qwen3 renormalised
+top-k, DeepSeek-V2 greedy + shared experts, gpt-oss biased gate) are arguments of the layer call (norm, rscale,
+gate_b, shared experts in the state), not part of the shape.
 """
 from dataclasses import asdict, dataclass
 

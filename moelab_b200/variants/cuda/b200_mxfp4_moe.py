@@ -3,7 +3,8 @@
 Drop-in for moelab/variants/mlx/metal_mxfp4_moe.py (:474-512 run, :448-455 prepare/dequant) on NVIDIA B200:
 E2M1 codes with one E8M0 scale per 32 inputs (mx.quantize(w, mode="mxfp4"), W_BITS 4.25). The kernels fold the
 E8M0 scale into exact bf16 MMA operands (e2m1 * 2^(s-127) is representable in bf16), so no accuracy is lost
-to the format conversion. LOAD_MAX / POLICY pin the dispatcher like the reference's LOAD_MAX (:465-471).
+to the format conversion. POLICY pins one kernel path; LOAD_MAX moves the decode -> tile switch like the
+reference's LOAD_MAX / load_max (:465-471).
 """
 import os
 import sys
@@ -20,11 +21,26 @@ META = {"name": "b200_mxfp4_moe", "description": "B200 sm_100a MXFP4: fused rout
                                                  "with exact E2M1/E8M0 decode, deterministic fused combine"}
 MODE, GS, BITS = "mxfp4", 32, 4
 W_BITS = 4 + 8 / 32
-POLICY = None
+POLICY = None  # None = the library's load-based dispatcher; tests pin ops.POLICY_* here
+LOAD_MAX = None  # a number: the decode kernels up to this load (T*k/E), the grouped tile kernels above it
 
 
-def _policy():
-    return ops.POLICY_AUTO if POLICY is None else POLICY
+def load_max(E, k):
+    """Largest load T*k/E the dispatcher serves with the decode kernels (LOAD_MAX when set)."""
+    if LOAD_MAX is not None:
+        return LOAD_MAX
+    T = 1
+    while ops.policy(T + 1, E, k) == ops.POLICY_SLOTS:
+        T += 1
+    return T * k / E
+
+
+def _policy(T=None, E=None, k=None):
+    if POLICY is not None:
+        return POLICY
+    if LOAD_MAX is not None and T is not None:
+        return ops.POLICY_SLOTS if T * k / E <= LOAD_MAX else ops.POLICY_TILES16_RING
+    return ops.POLICY_AUTO
 
 
 def prepare(w_gate, w_up, w_down):
@@ -62,7 +78,7 @@ def run(s, x, idx, wts, act=None):
     _ws(s, k)
     xb = x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
     y = ops.experts(s, xb.contiguous(), idx.to(torch.int32).contiguous(), wts.to(torch.float32).contiguous(),
-                    act=act, policy=_policy())
+                    act=act, policy=_policy(T, s["E"], k))
     return y if x.dtype == torch.bfloat16 else y.to(x.dtype)
 
 
@@ -70,5 +86,6 @@ def layer(s, x, gate_w, k, gate_b=None, norm=True, rscale=1.0, act=None, residua
           stage_events=None):
     act = s.get("act", 0) if act is None else act
     _ws(s, k)
-    return ops.layer(s, x, gate_w, k, gate_b=gate_b, norm=norm, rscale=rscale, act=act, policy=_policy(),
+    return ops.layer(s, x, gate_w, k, gate_b=gate_b, norm=norm, rscale=rscale, act=act,
+                     policy=_policy(x.shape[0], s["E"], k),
                      residual=residual, return_routing=return_routing, stage_events=stage_events)

@@ -259,3 +259,49 @@ def error_metrics(y, y_ref):
         "cos": float((y * r).sum() / (np.linalg.norm(y) * nr + 1e-30)),
         "finite": bool(np.isfinite(y).all()),
     }
+
+
+# ------------------------------------------------------------------ routing step (integer work)
+SLOT_SKIP = -(2 ** 31)
+
+
+def route_tables(idx, E, nt):
+    """Restatement of the routing step (moelab_b200's tile builder) on the CPU: the T*k slots grouped by expert
+    with a stable sort, each expert's run cut every nt slots. Ids outside [0, E) are grouped under expert 0 (and
+    reported as `bad`); SLOT_SKIP entries are left out.
+    Returns counts [E], offsets [E], sorted slot ids, tiles [n, 4] {expert, start, n, 0} (experts in increasing
+    order) and bad (any invalid id) - all int32 / bool.
+    The grouping contract is that of the reference's map kernel (moelab/variants/mlx/metal_q4_tiles_v2.py:362-373):
+    slot p starts a tile iff its rank among the earlier slots of the same expert is a multiple of VT, and the tile
+    holds the next <= VT slots of that expert in slot order."""
+    ids = np.asarray(idx, np.int64).reshape(-1)
+    keep = ids != SLOT_SKIP
+    bad = bool(((ids < 0) | (ids >= E))[keep].any())
+    e = np.where((ids < 0) | (ids >= E), 0, ids)
+    slots = np.nonzero(keep)[0]
+    ek = e[keep]
+    order = np.argsort(ek, kind="stable")
+    sorted_ = slots[order].astype(np.int32)
+    counts = np.bincount(ek, minlength=E).astype(np.int32)
+    offsets = (np.cumsum(counts) - counts).astype(np.int32)
+    tiles = []
+    for x in range(E):
+        for i in range(0, int(counts[x]), nt):
+            tiles.append((x, int(offsets[x]) + i, min(nt, int(counts[x]) - i), 0))
+    return counts, offsets, sorted_, np.asarray(tiles, np.int32).reshape(-1, 4), bad
+
+
+def reference_map_tiles(idx, VT):
+    """The reference's map kernel as a set of tiles (metal_q4_tiles_v2.py:362-373): for every slot p whose rank
+    among the earlier same-expert slots is a multiple of VT, the tuple (expert, next <= VT same-expert slots from p
+    in slot order). Valid ids only (the reference has no invalid-id path)."""
+    ids = np.asarray(idx, np.int64).reshape(-1)
+    seen = {}
+    out = set()
+    for p, e in enumerate(ids):
+        r = seen.get(int(e), 0)
+        seen[int(e)] = r + 1
+        if r % VT == 0:
+            mem = [q for q in range(p, len(ids)) if ids[q] == e][:VT]
+            out.add((int(e), tuple(mem)))
+    return out

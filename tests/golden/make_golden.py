@@ -1,8 +1,8 @@
 """Generate the golden fixtures in tests/golden from the reference's OWN Python code.
 
-Run in a container that has the reference checkout (read-only) at $MOELAB_REF (default /root/reference):
+Run where the reference checkout (read-only) is available, naming its root in MOELAB_REF:
 
-    python tests/golden/make_golden.py
+    MOELAB_REF=<path to the moe-lab checkout> python tests/golden/make_golden.py
 
 It imports moelab.problem (make_routing, make_problem, reference, error_metrics), moelab.torch_backend
 (reference, fp32) and moelab/variants/cuda/torch_loop.py (the CPU torch path) from the reference tree and
@@ -19,7 +19,9 @@ import sys
 import numpy as np
 import torch
 
-REF = os.environ.get("MOELAB_REF", "/root/reference")
+REF = os.environ.get("MOELAB_REF")
+if not REF:
+    sys.exit("set MOELAB_REF to the root of the moe-lab reference checkout")
 OUT = os.path.dirname(os.path.abspath(__file__))
 
 

@@ -99,7 +99,7 @@ def test_qwen3_235b_layer(T):
 
 
 # ------------------------------------------------------------------ Mixtral-8x7B
-MIXTRAL_T = [1, 2, 4, 8, 16, 64, 256, 1024, 4096]
+MIXTRAL_T = [1, 2, 4, 8, 16, 32, 64, 128, 256, 512, 1024, 2048, 4096]  # every power of two (BASELINE)
 
 
 @pytest.fixture(scope="module")

@@ -243,3 +243,36 @@ def test_p2p_emulated_bit_exact_vs_single_gpu(P, tokens, pol, blocks):
     finally:
         for x in xchs:
             x.close()
+
+
+# ------------------------------------------------------------------ failure detection: a peer that never signals
+@pytest.mark.parametrize("pol", ["slots", "tiles8ring"])
+def test_p2p_peer_never_signals_times_out(pol):
+    """Two ranks emulated on one GPU; rank 1 never dispatches nor returns rows (a dead peer, made on the host by
+    not calling it). Rank 0's bounded waits - for rank 1's dispatch flag in the expert call, for its return flag
+    in the combine - run out after the short limit set here, record DEVERR_TIMEOUT, and the calls return; the
+    GPU stays usable (a later call on a healthy pair is checked)."""
+    E, d, f, k, T = 16, 256, 384, 2, 3
+    w, gate = _layer(E, d, f, seed=5)
+    C = T * k
+    xchs = ep.PeerExchange.local_group(2, C, d, "cuda")
+    states = [ep.shard(b200_q4_moe, *w, r, 2) for r in range(2)]
+    try:
+        xchs[0].set_wait_limit(0.05)
+        x = torch.randn(T, d, generator=torch.Generator(device="cuda").manual_seed(1), device="cuda").to(torch.bfloat16)
+        idx, wts = ops.router(x, gate, k)
+        sp = ops.ep_p2p_dispatch(x, idx, wts, E, xchs[0])
+        ops.ep_p2p_experts(states[0], xchs[0], policy=P2P_POL[pol])
+        y = ops.ep_p2p_combine(xchs[0], sp, T, k, d, residual=x, device="cuda")
+        torch.cuda.synchronize()
+        assert states[0]["ep_ws"].read_error() & ops._lib.DEVERR_TIMEOUT
+        assert xchs[0].read_error() & ops._lib.DEVERR_TIMEOUT
+        assert bool(torch.isfinite(y.float()).all())
+    finally:
+        for x_ in xchs:
+            x_.close()
+    # the context is still usable
+    full = b200_q4_moe.prepare(*w)
+    b200_q4_moe._ws(full, k)
+    y2 = ops.experts(full, x, idx, wts)
+    assert_close(y2, ref_from_state(b200_q4_moe, full, x, idx, wts))

@@ -3,58 +3,91 @@ owns the device heap, or a path with a fixed memory plan). Its scratch is a stat
 library, so the call takes only inputs and the output. This file sorts last so a stop-at-first-failure run has
 already run every other test; it must pass both on its own in a fresh process and after the rest.
 
-Checked through the C ABI against moeb_experts_q4 (which uses a caller-provided workspace): two calls in a row
-with different inputs, and a size beyond the static scratch is rejected with a clear error.
+Checked through the C ABI against moeb_experts_q4 (which uses a caller-provided workspace) and against the fp64
+oracle on the layer's own dequantised weights: calls in a row with different inputs, a large call followed by a
+small one (the array keeps the last call's contents), the tcgen05 and decode paths, a residual, and a size beyond
+the static scratch, which is rejected with a clear error.
 """
-import ctypes
-
 import pytest
 import torch
 
-from helpers import Q4_VARIANT, load_variant, problem_tensors
+import oracle
+from helpers import Q4_VARIANT, assert_close, load_variant, problem_tensors
 from moelab_b200 import _lib, ops
 from moelab_b200.shapes import MoEShape
 
 pytestmark = pytest.mark.gpu
 
+SHAPE = MoEShape("qwen3-like", d=2048, f=768, E=128, k=8)
 
-def _call_static(st, x, idx, wts, act=0, policy=0):
+
+def _call_static(st, x, idx, wts, act=0, policy=0, residual=None):
     T, d = x.shape
     k = idx.shape[1]
     y = torch.empty_like(x)
     p = ops._p
     _lib.call("moeb_experts_q4_static", p(x), *ops._expert_ptrs(st), p(idx), p(wts), T, d, st["f"], st["E"], k,
-              act, policy, None, p(y), ops._stream())
+              act, policy, p(residual), p(y), ops._stream())
     return y
 
 
-@pytest.mark.parametrize("policy", [ops.POLICY_AUTO, ops.POLICY_SLOTS, ops.POLICY_TILES8])
-def test_static_scratch_matches_workspace_path(policy):
+@pytest.fixture(scope="module")
+def layer():
     mod = load_variant(Q4_VARIANT)
-    sh = MoEShape("qwen3-like", d=2048, f=768, E=128, k=8)
-    _, w, _, _, _ = problem_tensors(MoEShape("w", d=sh.d, f=sh.f, E=sh.E, k=sh.k), 1, seed=11)
+    _, w, _, _, _ = problem_tensors(SHAPE, 1, seed=11)
     st = mod.prepare(*w)
-    mod._ws(st, sh.k)
-    for call, (T, seed) in enumerate([(4, 1), (32, 2)]):  # two calls in a row share the static array
-        _, _, x, idx, wts = problem_tensors(sh, T, "uniform", seed=seed)
+    mod._ws(st, SHAPE.k)
+    deq = [t.cpu().numpy() for t in mod.dequant(st)]  # the layer's own dequantised weights, once
+    return st, deq
+
+
+def _oracle(deq, x, idx, wts):
+    return oracle.moe_forward(x.float().cpu().numpy(), *deq, idx.cpu().numpy(), wts.cpu().numpy())
+
+
+# (T, seed) sequences: the second call of each pair reuses the array the first one left behind; 32 -> 4 is the
+# large-then-small order (a smaller layout over stale contents of a larger one)
+@pytest.mark.parametrize("policy,calls", [
+    (ops.POLICY_AUTO, [(4, 1), (32, 2), (4, 3)]),
+    (ops.POLICY_AUTO, [(32, 4), (1, 5), (2, 6)]),
+    (ops.POLICY_SLOTS, [(2, 7), (1, 8)]),
+    (ops.POLICY_TILES8, [(32, 9), (4, 10)]),
+    (ops.POLICY_TILES16_RING, [(64, 11), (8, 12)]),
+    (ops.POLICY_TC, [(64, 13), (16, 14)]),
+    (ops.POLICY_DECODE, [(1, 15), (2, 16)]),
+])
+def test_static_scratch_matches_workspace_path_and_oracle(layer, policy, calls):
+    st, deq = layer
+    for call, (T, seed) in enumerate(calls):
+        _, _, x, idx, wts = problem_tensors(SHAPE, T, "uniform", seed=seed)
         ref = ops.experts_q4(st, x, idx, wts, policy=policy)
         y = _call_static(st, x, idx, wts, policy=policy)
         torch.cuda.synchronize()
-        rel = ((y.float() - ref.float()).norm() / ref.float().norm()).item()
-        assert rel < 1e-2, (call, rel)
-        rowmax = ref.float().abs().amax(dim=1, keepdim=True)
-        assert bool(((y.float() - ref.float()).abs() <= 1e-2 * rowmax + 1e-6).all()), call
+        # against the workspace path (same kernels, same inputs): within the tests' bf16 tolerance
+        assert_close(y, ref.float().cpu().numpy(), what=("vs workspace path", policy, call, T))
+        # against the oracle on the layer's dequantised weights
+        assert_close(y, _oracle(deq, x, idx, wts), what=("vs oracle", policy, call, T))
+    assert st["ws"].read_error() == 0
 
 
-def test_static_scratch_rejects_oversize():
-    mod = load_variant(Q4_VARIANT)
-    sh = MoEShape("big", d=2048, f=768, E=128, k=8)
-    _, w, _, _, _ = problem_tensors(MoEShape("w", d=sh.d, f=sh.f, E=sh.E, k=sh.k), 1, seed=12)
-    st = mod.prepare(*w)
+def test_static_scratch_residual(layer):
+    st, deq = layer
+    for T, seed in [(32, 21), (1, 22)]:
+        _, _, x, idx, wts = problem_tensors(SHAPE, T, "uniform", seed=seed)
+        r = torch.randn(T, SHAPE.d, generator=torch.Generator(device="cuda").manual_seed(seed),
+                        device="cuda").to(torch.bfloat16)
+        y = _call_static(st, x, idx, wts, residual=r)
+        torch.cuda.synchronize()
+        ref = _oracle(deq, x, idx, wts) + r.float().cpu().numpy()
+        assert_close(y, ref, what=("residual", T))
+
+
+def test_static_scratch_rejects_oversize(layer):
+    st, _ = layer
     T = 4096
-    assert _lib.load().moeb_workspace_bytes(T, sh.d, sh.f, sh.E, sh.k) > (16 << 20)
-    x = torch.zeros(T, sh.d, dtype=torch.bfloat16, device="cuda")
-    idx = torch.zeros(T, sh.k, dtype=torch.int32, device="cuda")
-    wts = torch.zeros(T, sh.k, dtype=torch.float32, device="cuda")
+    assert _lib.load().moeb_workspace_bytes(T, SHAPE.d, SHAPE.f, SHAPE.E, SHAPE.k) > (16 << 20)
+    x = torch.zeros(T, SHAPE.d, dtype=torch.bfloat16, device="cuda")
+    idx = torch.zeros(T, SHAPE.k, dtype=torch.int32, device="cuda")
+    wts = torch.zeros(T, SHAPE.k, dtype=torch.float32, device="cuda")
     with pytest.raises(_lib.MoebError, match="static scratch holds"):
         _call_static(st, x, idx, wts)
