@@ -8,6 +8,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -87,7 +88,7 @@ size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 // call (moeb_workspace_init); every kernel leaves them zero again.
 struct Layout {
     size_t err, cnt_all, rcnt, ycnt, zero_end;
-    size_t logits, idx, wts, xsum, ntiles, tiles, sorted, h, hsum, yp, xg, total;
+    size_t logits, idx, wts, xsum, ntiles, tiles, sorted, h, hsum, yp, xg, drec, total;
 };
 
 // with_yp = false: no per-slot output region (expert-parallel calls write the slot outputs to the caller's buffer).
@@ -113,6 +114,8 @@ Layout layout(long Tc, int d, int f, int E, int k, bool with_yp = true) {
     // expert-parallel rows gathered in expert order for the tensor-core kernels (a layer call uses the slot-row
     // region for that)
     L.xg = o; o = align256(o + (with_yp ? 0 : 2 * (size_t)TK * d));
+    // single-kernel decode (<= 16 slots): tagged 64-bit records of h [slot][f] and of the slot outputs [slot][d]
+    L.drec = o; o = align256(o + (with_yp ? 8 * (size_t)std::min<long>(TK, 16) * (f + d) : 0));
     L.total = o;
     return L;
 }
@@ -456,6 +459,7 @@ int launch_router(const void *x, const void *wg, const void *bias, int T, int d,
     // the tile builder keeps the slot ids in shared memory for its second pass when that stays small (every
     // router CTA carries this allocation, so it is capped to keep the logits phase at full occupancy)
     const bool tiled = router_tiled(T, E);
+    const int tpb = T <= 64 ? 1 : 4;
     const size_t smem = tiles ? tiles_smem(tiled ? 256 : 128, E + ns, (long)T * (k + ns), 16 * 1024) : 0;
     // one expert per warp and 1 (T <= 64) or 4 tokens, or the register-tiled kernel (4 tokens x EW experts per
     // warp, EW = 4 from 32 experts on)
@@ -465,7 +469,6 @@ int launch_router(const void *x, const void *wg, const void *bias, int T, int d,
         void (*kern)(RouterArgs) = ew == 4 ? router_t_kernel<4>(E) : ew == 2 ? router_t_kernel<2>(E) : router_t_kernel<1>(E);
         e = launch(kern, dim3((E + 8 * ew - 1) / (8 * ew), (T + 3) / 4), dim3(256), smem, st, r);
     } else {
-        const int tpb = T <= 64 ? 1 : 4;
         void (*kern)(RouterArgs) = tpb == 1 ? router_kernel<1, 8>(E) : router_kernel<4, 4>(E);
         e = launch(kern, dim3((E + 3) / 4, (T + tpb - 1) / tpb), dim3(128), smem, st, r);
     }
@@ -474,40 +477,130 @@ int launch_router(const void *x, const void *wg, const void *bias, int T, int d,
     return MOEB_OK;
 }
 
-// ------------------------------------------------------------------ fused decode (one cooperative kernel)
-template <int FMT>
-void (*decode_kernel(int E))(ExpArgs, RouterArgs, unsigned *) {
-    const int J = (E + 31) / 32;
-    if (J <= 1) return k_decode<FMT, 1>;
-    if (J <= 2) return k_decode<FMT, 2>;
-    if (J <= 4) return k_decode<FMT, 4>;
-    if (J <= 8) return k_decode<FMT, 8>;
-    if (J <= 16) return k_decode<FMT, 16>;
-    return k_decode<FMT, 32>;
+// ------------------------------------------------------------------ single-kernel decode (decode.cu)
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Work split and shared-memory layout of one decode launch over G CTAs; false when it does not fit an SM (the
+// caller then uses the three-launch decode path).
+bool decode_plan(int fmt, int T, int d, int f, int ks, int Er, bool routing, int G, size_t static_smem, DecodePlan *P) {
+    const int S = T * ks, RBf = f / 16, RBd = d / 16, Gd = d / 64, Gf = f / 64;
+    if (S < 1 || S > 16 || G < 1) return false;
+    P->NW = DEC_NW;
+    // groups per item: the largest chunk size up to DEC_CG that divides the projection's group count (every item
+    // full, one unrolled item body per projection)
+    auto chunk = [](int G) {
+        for (int c : {8, 6, 5, 4, 3, 2})
+            if (c <= DEC_CG && G % c == 0) return c;
+        return 1;
+    };
+    P->CGd = chunk(Gd);
+    P->CGf = chunk(Gf);
+    P->NCd = Gd / P->CGd;
+    P->NCf = Gf / P->CGf;
+    const long Ugu = (long)S * RBf, Udn = (long)S * RBd;
+    P->max_gu_units = (int)((Ugu + G - 1) / G);
+    P->max_dn_units = (int)((Udn + G - 1) / G);
+    const long max_items = (long)P->max_gu_units * 2 * P->NCd + (long)P->max_dn_units * P->NCf;
+    P->NSL = std::min(S, (std::max(P->max_dn_units, 1) + RBd - 2) / RBd + 1);
+    const int sbw = fmt == FMT_FP4 ? 8 : 16;
+    const int cg = std::max(P->CGd, P->CGf);
+    P->slot_bytes = (int)align_up((size_t)cg * 512 + (size_t)cg * sbw * 4, 128);
+    // the partials array also holds the logits [T][Er] while the CTA selects its experts
+    const size_t part_bytes = std::max((size_t)max_items * 64, routing ? (size_t)T * ((Er + 15) & ~15) * 4 : 0);
+    const size_t fixed = align_up((size_t)T * d * 2, 16) + align_up((size_t)T * Gd * 4, 16) + 2 * align_up((size_t)S * 4, 16) +
+                         align_up(part_bytes, 16) +
+                         align_up((size_t)(P->max_gu_units + P->max_dn_units) * 4, 16) +
+                         align_up((size_t)P->NSL * (f * 2 + f / 16 * 4), 16) + align_up((size_t)P->NSL * 4, 16);
+    const size_t cap = 227 * 1024 - static_smem;
+    if (fixed + 256 >= cap) return false;
+    long nslot = std::min<long>(max_items, (long)((cap - fixed - 256) / (P->slot_bytes + 16)));
+    if (nslot < max_items && nslot < 32) return false;
+    P->NSLOT = (int)std::max<long>(nslot, 1);
+    size_t o = 0;
+    P->o_ring = 0;
+    o = (size_t)P->NSLOT * P->slot_bytes;
+    P->o_bar = (int)o; o = align_up(o + 16 * (size_t)P->NSLOT, 16);
+    P->o_x = (int)o; o = align_up(o + (size_t)T * d * 2, 16);
+    P->o_xsum = (int)o; o = align_up(o + (size_t)T * Gd * 4, 16);
+    P->o_idx = (int)o; o = align_up(o + (size_t)S * 4, 16);
+    P->o_wts = (int)o; o = align_up(o + (size_t)S * 4, 16);
+    P->o_part = (int)o; o = align_up(o + part_bytes, 16);
+    P->o_ucnt = (int)o; o = align_up(o + (size_t)(P->max_gu_units + P->max_dn_units) * 4, 16);
+    P->o_h = (int)o; o = align_up(o + (size_t)P->NSL * (f * 2 + f / 16 * 4), 16);
+    P->o_hstate = (int)o; o = align_up(o + (size_t)P->NSL * 4, 16);
+    P->total = (int)o;
+    if ((size_t)P->total > cap) return false;
+    P->nR = routing ? std::min(G, (Er + DEC_NW - 1) / DEC_NW) : 0;
+    return true;
 }
 
-int launch_decode(int fmt, const ExpArgs &a, const RouterArgs &r, unsigned *ctr, cudaStream_t st) {
-    void (*kern)(ExpArgs, RouterArgs, unsigned *) =
-        fmt == FMT_FP4 ? decode_kernel<FMT_FP4>(r.wg ? r.E : 1) : decode_kernel<FMT_Q4>(r.wg ? r.E : 1);
-    const size_t smem = decode_smem(a.d, a.f);
-    if (!allow_smem((const void *)kern, smem)) return check_launch("decode smem");
+void (*decode_fn(int fmt, int E))(DecodeArgs) {
+    (void)E;
+    return fmt == FMT_FP4 ? k_decode<FMT_FP4> : k_decode<FMT_Q4>;
+}
+
+size_t static_smem_of(const void *fn) {
+    static std::mutex mu;
+    static std::unordered_map<const void *, size_t> cache;
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(fn);
+    if (it != cache.end()) return it->second;
+    cudaFuncAttributes fa;
+    const size_t v = cudaFuncGetAttributes(&fa, fn) == cudaSuccess ? fa.sharedSizeBytes : 1024;
+    cache[fn] = v;
+    return v;
+}
+
+// Whether the single-kernel decode serves this call (routed experts Er for the router's top-k kernel variant).
+bool decode_fits(int fmt, int T, int d, int f, int ks, int Er, bool routing) {
+    DecodePlan P;
+    auto fn = decode_fn(fmt, routing ? Er : 1);
+    return decode_plan(fmt, T, d, f, ks, Er, routing, sm_count(), static_smem_of((const void *)fn), &P);
+}
+
+// Decode words in the workspace: the arrival counter sits in the zeroed counter region, the generation word in
+// the error region (byte 8; never cleared by moeb_read_error), the records in their own region.
+constexpr size_t DEC_ARR_OFF = 16, DEC_GEN_OFF = 8;
+
+int launch_decode(int fmt, const ExpArgs &a, const RouterArgs &r, const Layout &L, void *ws, cudaStream_t st) {
+    const bool routing = r.wg != nullptr;
+    void (*kern)(DecodeArgs) = decode_fn(fmt, routing ? r.E : 1);
+    DecodeArgs A;
+    A.a = a;
+    A.r = r;
+    A.arr = at<unsigned>(ws, L.cnt_all + DEC_ARR_OFF);
+    A.gen = at<unsigned>(ws, L.err + DEC_GEN_OFF);
+    A.hrec = at<unsigned long long>(ws, L.drec);
+    A.yrec = A.hrec + (size_t)a.T * a.k * a.f;
+    const int G = sm_count();
+    if (!decode_plan(fmt, a.T, a.d, a.f, a.k, routing ? r.E : 0, routing, G, static_smem_of((const void *)kern), &A.p))
+        return fail(MOEB_EUNSUP, "decode kernel: this shape does not fit one SM's shared memory%s");
+    if (!allow_smem((const void *)kern, (size_t)A.p.total)) return check_launch("decode smem");
     int occ = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 256, smem) != cudaSuccess || occ < 1)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, DEC_THREADS, A.p.total) != cudaSuccess || occ < 1)
         return fail(MOEB_ELAUNCH, "decode kernel does not fit an SM%s");
-    // every CTA must be resident at once (phases hand over through counters): at most occ per SM
-    const long units = std::max<long>((long)a.T * a.k * std::max(a.f, a.d) / 16, r.wg ? (r.E + 7) / 8 : 1);
-    const int grid = (int)std::max<long>(1, std::min<long>((long)occ * sm_count(), units));
+    // every CTA must be resident at once (they wait on each other's counters): cooperative launch, one per SM
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = smem;
+    cfg.gridDim = dim3(G);
+    cfg.blockDim = dim3(DEC_THREADS);
+    cfg.dynamicSmemBytes = A.p.total;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, kern, a, r, ctr) != cudaSuccess) return check_launch("decode");
+    static std::atomic<int> with_pdl{1};  // cleared if the runtime refuses the pair of attributes
+    cfg.numAttrs = with_pdl.load() ? 2 : 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, A);
+    if (e != cudaSuccess && cfg.numAttrs == 2) {
+        cudaGetLastError();
+        with_pdl.store(0);
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, kern, A);
+    }
+    if (e != cudaSuccess) return check_launch("decode");
     return MOEB_OK;
 }
 
@@ -521,6 +614,19 @@ void set_error(const char *msg) { snprintf(g_err, sizeof g_err, "%s", msg); }
 size_t zero_region_bytes(size_t ws_bytes, int d, int f, int E, int k) {
     const long cap = capacity(ws_bytes, d, f, E, k);
     return cap < 1 ? 0 : layout(cap, d, f, E, k).zero_end;
+}
+
+// The decode records' byte range in a workspace of `ws_bytes` (their tags must not match a later call's tag:
+// a caller that resets the counter region before every call clears these too).
+void decode_record_span(size_t ws_bytes, int d, int f, int E, int k, size_t *off, size_t *len) {
+    const long cap = capacity(ws_bytes, d, f, E, k);
+    if (cap < 1) {
+        *off = *len = 0;
+        return;
+    }
+    const Layout L = layout(cap, d, f, E, k);
+    *off = L.drec;
+    *len = L.total - L.drec;
 }
 }  // namespace moeb
 
@@ -687,7 +793,10 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
         policy = choose_policy(T, E, k, d, f);
         if (policy == MOEB_POLICY_TC && ep) policy = MOEB_POLICY_TILES16_RING;
     }
-    if (policy == MOEB_POLICY_DECODE && (ep || (long)T * k > 16)) policy = MOEB_POLICY_SLOTS;  // decode only
+    // the single-kernel decode: layer and expert calls of <= 16 slots whose plan fits an SM
+    if (policy == MOEB_POLICY_DECODE &&
+        (ep || (long)T * k > 16 || !decode_fits(fmt, T, d, f, k, gate_w ? E - ns : 0, gate_w != nullptr)))
+        policy = MOEB_POLICY_SLOTS;
     if (policy != MOEB_POLICY_SLOTS && policy != MOEB_POLICY_DECODE && !is_tiles(policy))
         return fail(MOEB_EINVAL, "unknown policy%s");
     if (policy == MOEB_POLICY_TC && (d % 128 || f % 128))
@@ -787,7 +896,7 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
             r.xsum = at<float>(ws, L.xsum);
             r.err = at<unsigned>(ws, L.err);
         }
-        rc = launch_decode(fmt, a, r, at<unsigned>(ws, L.cnt_all), st);
+        rc = launch_decode(fmt, a, r, L, ws, st);
         if (ev)
             for (int i = 1; i < 4; ++i) cudaEventRecord(static_cast<cudaEvent_t>(ev[i]), st);
         return rc;

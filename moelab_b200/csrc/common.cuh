@@ -102,6 +102,9 @@ MOEB_DEV void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.clus
 MOEB_DEV void mbar_expect_tx(uint64_t *bar, unsigned bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
+MOEB_DEV void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 MOEB_DEV bool mbar_try_wait(uint64_t *bar, unsigned parity) {
     unsigned ok;
     asm volatile(

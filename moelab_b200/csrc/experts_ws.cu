@@ -45,10 +45,6 @@ MOEB_DEV uint2 stage_scales(const unsigned char *p, int gq) {
     return reinterpret_cast<const uint2 *>(p)[gq];
 }
 
-MOEB_DEV void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
 template <int FMT, int NT8, int RBC, int SG, int NS, bool DOWN, int MB>
 __global__ void __launch_bounds__(32 * (RBC + 1), MB) k_experts_ws(const __grid_constant__ ExpArgs a) {
     using L = WSL<FMT, NT8, RBC, SG, DOWN>;

@@ -142,9 +142,29 @@ struct EPArgs {
 __global__ void k_ep_plan(EPArgs a);
 __global__ void k_ep_pack(EPArgs a);
 __global__ void k_combine(const float *yp, int T, int d, int k, const uint16_t *residual, uint16_t *y);
-template <int FMT, int JMAX>
-__global__ void k_decode(ExpArgs a, RouterArgs r, unsigned *ctr);
-size_t decode_smem(int d, int f);
+// Single-kernel decode layer (decode.cu): DEC_NW consumer warps + 1 producer warp per CTA, one CTA per SM.
+constexpr int DEC_NW = 15, DEC_THREADS = 32 * (DEC_NW + 1), DEC_CG = 8;  // 16 warps: 128 registers each
+struct DecodePlan {
+    int NW, CGd, CGf;      // consumer warps, 64-groups per item (gate/up: a divisor of d/64, down: of f/64)
+    int NCd, NCf;          // items per (gate/up unit, projection) and per down unit
+    int NSLOT, slot_bytes; // ring of bulk-copy slots
+    int NSL;               // h staging rows (distinct down slots of one CTA)
+    int max_gu_units, max_dn_units;
+    int nR;                // CTAs computing logits
+    // dynamic shared memory offsets (bytes)
+    int o_ring, o_bar, o_x, o_xsum, o_idx, o_wts, o_part, o_ucnt, o_h, o_hstate, total;
+};
+struct DecodeArgs {
+    ExpArgs a;
+    RouterArgs r;     // r.wg == null: ids given in a.idx / a.wts
+    DecodePlan p;
+    unsigned *arr;    // arrivals of the call's CTAs (zeroed; the last arrival resets it)
+    unsigned *gen;    // generation word: advanced once per call by the last arrival; the call's record tag
+    unsigned long long *hrec;  // [T*k][f] records {tag, bf16 h}
+    unsigned long long *yrec;  // [T*k][d] records {tag, fp32 weighted slot output}
+};
+template <int FMT>
+__global__ void k_decode(const __grid_constant__ DecodeArgs A);
 __global__ void k_ep_send(EPArgs a);
 __global__ void k_ep_signal(unsigned char *const *peers, unsigned char *self, int P, int C, int d, int me);
 __global__ void k_ep_combine_p2p(const unsigned char *self, const int *slot_pos, int P, int C, int T, int d, int k,
@@ -201,6 +221,7 @@ size_t experts_ws_smem(int nt8, int rbc, int sg, int ns, bool down, int fmt);
 
 
 size_t zero_region_bytes(size_t ws_bytes, int d, int f, int E, int k);
+void decode_record_span(size_t ws_bytes, int d, int f, int E, int k, size_t *off, size_t *len);
 void set_error(const char *msg);  // message returned by moeb_last_error()
 
 }  // namespace moeb

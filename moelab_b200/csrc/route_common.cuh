@@ -29,8 +29,10 @@ __device__ __forceinline__ float fkey_inv(unsigned k) {
     return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
+// Top-k of token t from the fp32 logits in a.logits; writes the token's k + ns slots (routed ids / weights, then
+// the shared experts) to idx_out / wts_out [t * (k + ns) + j].
 template <int JMAX>
-__device__ void topk_token(const RouterArgs &a, int t, int lane) {
+__device__ void topk_token_to(const RouterArgs &a, int t, int lane, int *idx_out, float *wts_out) {
     const int E = a.E, k = a.k;
     float v[JMAX];
     float m0 = -INFINITY;
@@ -82,13 +84,81 @@ __device__ void topk_token(const RouterArgs &a, int t, int lane) {
     const float off = a.norm ? top0 : m0;
     const int ks = k + a.ns;
     if (lane < k) {
-        a.idx[(size_t)t * ks + lane] = myi;
-        a.wts[(size_t)t * ks + lane] = expf(myv - off) / s * a.scale;
+        idx_out[(size_t)t * ks + lane] = myi;
+        wts_out[(size_t)t * ks + lane] = expf(myv - off) / s * a.scale;
     } else if (lane < ks) {  // always-on shared experts after the routed ones (summed last, weight 1)
-        a.idx[(size_t)t * ks + lane] = E + (lane - k);
-        a.wts[(size_t)t * ks + lane] = 1.f;
+        idx_out[(size_t)t * ks + lane] = E + (lane - k);
+        wts_out[(size_t)t * ks + lane] = 1.f;
     }
 }
+
+template <int JMAX>
+__device__ __forceinline__ void topk_token(const RouterArgs &a, int t, int lane) {
+    topk_token_to<JMAX>(a, t, lane, a.idx, a.wts);
+}
+
+// Top-k of every token from the logits in shared memory (lg [T][E], NaN already -inf, -0 already +0), by rank:
+// expert e's rank is the number of experts with a larger value or an equal value and a lower id, so the k experts
+// of rank < k in rank order are exactly router.py's selection (largest first, lowest id on ties, the lowest unused
+// ids when fewer than k are finite). The weights repeat topk_token_to's arithmetic operation for operation.
+// T tokens (rows of lg, each padded to E rounded up to 16 with -inf); sel: [T][k] scratch; idx_out / wts_out:
+// the tokens' [T][k + ns] slots. Every thread of the CTA calls it (blockDim.x a multiple of 32).
+__device__ __forceinline__ void topk_rank(const RouterArgs &r, int T, const float *lg, int *sel, int *idx_out,
+                                          float *wts_out) {
+    const int E = r.E, k = r.k, ks = k + r.ns;
+    // four threads per (token, expert), each comparing a quarter of the row (E4 = E rounded up to 16, the row padded
+    // with -inf entries that never outrank a real one: equal values lose to lower ids, and padding ids are larger)
+    const int E4 = (E + 15) & ~15, q4 = E4 / 4;
+    for (int base = 0; base < T * E; base += blockDim.x / 4) {
+        const int pr = base + (int)threadIdx.x / 4, sub = threadIdx.x & 3;
+        const bool act_ = pr < T * E;
+        const int t = act_ ? pr / E : 0, e = act_ ? pr - t * E : 0;
+        const float *row = lg + (size_t)t * E4;
+        const float v = row[e];
+        int rank = 0;
+        const float4 *r4 = reinterpret_cast<const float4 *>(row + sub * q4);
+        for (int j = 0; j < q4 / 4; ++j) {
+            const float4 o = r4[j];
+            const int e2 = sub * q4 + 4 * j;
+            rank += (o.x > v || (o.x == v && e2 < e)) + (o.y > v || (o.y == v && e2 + 1 < e)) +
+                    (o.z > v || (o.z == v && e2 + 2 < e)) + (o.w > v || (o.w == v && e2 + 3 < e));
+        }
+        rank += __shfl_xor_sync(0xffffffffu, rank, 1);
+        rank += __shfl_xor_sync(0xffffffffu, rank, 2);
+        if (act_ && sub == 0 && rank < k) sel[t * k + rank] = e;
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int t = warp; t < T; t += nw) {
+        const float *row = lg + (size_t)t * E4;
+        float m0 = -INFINITY;
+        for (int e = lane; e < E; e += 32) m0 = fmaxf(m0, row[e]);
+        m0 = fkey_inv(__reduce_max_sync(0xffffffffu, fkey(m0)));
+        float den = 0.f;
+        if (!r.norm) {
+            for (int e = lane; e < E; e += 32) den += row[e] == -INFINITY ? 0.f : expf(row[e] - m0);
+            den = warp_sum(den);
+        }
+        const int myi = lane < k ? sel[t * k + lane] : 0;
+        const float myv = lane < k ? row[myi] : -INFINITY;
+        const float top0 = row[sel[t * k]];
+        float s = 0.f;
+        if (r.norm) {
+            for (int q = 0; q < k; ++q) s += expf(__shfl_sync(0xffffffffu, myv, q) - top0);
+        } else {
+            s = den;
+        }
+        const float off = r.norm ? top0 : m0;
+        if (lane < k) {
+            idx_out[(size_t)t * ks + lane] = myi;
+            wts_out[(size_t)t * ks + lane] = expf(myv - off) / s * r.scale;
+        } else if (lane < ks) {
+            idx_out[(size_t)t * ks + lane] = E + (lane - k);
+            wts_out[(size_t)t * ks + lane] = 1.f;
+        }
+    }
+}
+
 
 
 }  // namespace moeb

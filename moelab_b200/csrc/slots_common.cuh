@@ -1,6 +1,6 @@
 // Decode (slot mode) unit bodies: one (slot, 16-row block) of gate/up or down with KS warps splitting the K
-// groups and GPW groups per warp loaded at once. Used by k_gate_up_slots / k_down_slots (experts.cu) and by the
-// fused single-kernel decode layer (decode.cu). Every thread of the CTA calls them (they use __syncthreads).
+// groups and GPW groups per warp loaded at once. Used by k_gate_up_slots / k_down_slots / k_down_tok (experts.cu).
+// Every thread of the CTA calls them (they use __syncthreads).
 #pragma once
 #include "experts_common.cuh"
 

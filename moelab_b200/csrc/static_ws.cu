@@ -76,8 +76,12 @@ extern "C" int moeb_experts_q4_static(const void *x, const void *qg, const void 
     // The array keeps the previous call's contents: clear the counters and the error word this call relies on.
     // The call sees only the first `need` bytes, so its layout (and the cleared region) scales with T; every other
     // region is written by this call before it is read.
+    // The decode kernel's tagged records are cleared with it: their tags count calls from the cleared counters.
     const size_t z = moeb::zero_region_bytes(need, d, f, E, k);
-    if (z && cudaMemsetAsync(ws, 0, z, stream) != cudaSuccess) {
+    size_t roff = 0, rlen = 0;
+    moeb::decode_record_span(need, d, f, E, k, &roff, &rlen);
+    if ((z && cudaMemsetAsync(ws, 0, z, stream) != cudaSuccess) ||
+        (rlen && cudaMemsetAsync(static_cast<char *>(ws) + roff, 0, rlen, stream) != cudaSuccess)) {
         moeb::set_error("clearing the static scratch failed");
         return MOEB_ELAUNCH;
     }

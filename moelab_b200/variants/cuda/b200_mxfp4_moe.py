@@ -22,7 +22,7 @@ META = {"name": "b200_mxfp4_moe", "description": "B200 sm_100a MXFP4: fused rout
 MODE, GS, BITS = "mxfp4", 32, 4
 W_BITS = 4 + 8 / 32
 POLICY = None  # None = the library's load-based dispatcher; tests pin ops.POLICY_* here
-LOAD_MAX = None  # a number: the decode kernels up to this load (T*k/E), the grouped tile kernels above it
+LOAD_MAX = None  # a number: the decode path up to this load (T*k/E), the grouped tile kernels above it
 
 
 def load_max(E, k):
@@ -30,7 +30,7 @@ def load_max(E, k):
     if LOAD_MAX is not None:
         return LOAD_MAX
     T = 1
-    while ops.policy(T + 1, E, k) == ops.POLICY_SLOTS:
+    while ops.policy(T + 1, E, k) in (ops.POLICY_SLOTS, ops.POLICY_DECODE):
         T += 1
     return T * k / E
 
@@ -39,7 +39,7 @@ def _policy(T=None, E=None, k=None):
     if POLICY is not None:
         return POLICY
     if LOAD_MAX is not None and T is not None:
-        return ops.POLICY_SLOTS if T * k / E <= LOAD_MAX else ops.POLICY_TILES16_RING
+        return ops.POLICY_DECODE if T * k / E <= LOAD_MAX else ops.POLICY_TILES16_RING
     return ops.POLICY_AUTO
 
 

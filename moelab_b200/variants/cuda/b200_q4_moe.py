@@ -112,4 +112,4 @@ def layer(s, x, gate_w, k, gate_b=None, norm=True, rscale=1.0, act=None, residua
 
 def custom_wins(T, k, E, D, F):
     """The dispatcher's choice for these dims (True = grouped expert tiles, False = per-slot tiles)."""
-    return ops.policy(T, E, k) != ops.POLICY_SLOTS
+    return ops.policy(T, E, k) not in (ops.POLICY_SLOTS, ops.POLICY_DECODE)
