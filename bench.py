@@ -46,8 +46,11 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bound on the CPU baseline sample")
     ap.add_argument("--soak-seconds", type=float, default=1.5, help="replays before the timed region (clocks)")
     ap.add_argument("--configs", type=int, default=1, help="1: also time the other BASELINE configurations (1 GPU)")
-    ap.add_argument("--ep-stack", default="", help="N > 1: also time BASELINE's expert-parallel stack (8 Qwen3-235B-"
-                    "shaped layers, experts split over the GPUs) at these tokens per GPU, e.g. 32,256,2048")
+    ap.add_argument("--trace", type=int, default=1, help="1: also time Qwen3-30B on the reference's recorded routing "
+                    "traces (T = 1, 8, 16, 32)")
+    ap.add_argument("--ep-stack", default="1,32,256,2048", help="also time BASELINE's expert-parallel stack (8 "
+                    "Qwen3-235B-shaped layers, experts split over the N GPUs; N = 1 runs the same code on one GPU) at "
+                    "these tokens per GPU ('' = none)")
     ap.add_argument("--profile-config", default="", help="run 3 eager layer calls of the CONFIGS entry whose name "
                     "starts with this (for ncu captures of one kernel) and exit")
     ap.add_argument("--profile-tokens", type=int, default=1024)
@@ -238,7 +241,7 @@ def stage_times(v, layers, xs, n_steps):
     return r, gu, dn, idxs
 
 
-def measure_T(v, layers, T, ws, rank, n_steps, seed):
+def measure_T(v, layers, T, ws, rank, n_steps, seed, peaks):
     xs = make_inputs(T, len(layers), seed)
     gr, _ = capture(v, layers, xs, n_steps)
     gr.replay()
@@ -247,11 +250,52 @@ def measure_T(v, layers, T, ws, rank, n_steps, seed):
     idxs = routing_of_chain(v, layers, xs, n_steps)
     nb = layer_bytes(idxs, T)
     us = t / n_steps * 1e6
-    r_us, gu_us, dn_us, _ = stage_times(v, layers, xs, len(layers))
-    return {"T": T, "us_per_call": round(us, 3), "gbs": round(sum(nb) / t / 1e9, 1),
-            "unique_experts": round(float(np.mean([torch.unique(i).numel() for i in idxs])), 2),
-            "tokens_per_s": round(T * n_steps / t, 1),
-            "stage_us": [round(statistics.mean(x), 2) for x in (r_us, gu_us, dn_us)]}
+    return {"T": T, "us": round(us, 2), "gbs": round(sum(nb) / t / 1e9, 1),
+            "frac": round(layer_frac(sum(nb) / len(nb), 6.0 * D * F * T * K_TOP, us * 1e-6, peaks), 3)}
+
+
+def layer_frac(byts, flops, t, peaks):
+    """Fraction of the layer roofline (north star: the slower of the bytes at the HBM peak and the FLOPs at the bf16
+    tensor peak; moelab/roofline.py:36-41) that a call of t seconds reaches."""
+    return max(byts / (peaks["hbm_gbs"] * 1e9), flops / (peaks["bf16_tflops"] * 1e12)) / t
+
+
+# reference's published M4 Pro numbers for the trace rows (runs/repro/q4_qwen3_trace.txt:2-5, custom kernel B)
+TRACE_M4PRO_US = {1: 110.9, 8: 367.7, 16: 576.1, 32: 923.6}
+
+
+def measure_trace(v, layers, peaks, Ts=(1, 8, 16, 32), n_calls=64):
+    """Qwen3-30B on recorded routing traces: the reference's own trace inputs (moelab/problem.py:38-50 drawn by
+    moelab/torch_backend.py:50-54's make_inputs, tests/golden/trace_qwen3.npz) through the harness contract
+    run(state, x, idx, wts) - the call the reference's trace numbers time. 16 seeds cycled over the 16 layers."""
+    from moelab_b200.problem import make_inputs
+    out = []
+    for T in Ts:
+        ins = []
+        for s in range(16):
+            x, idx, wts = make_inputs(D, E, K_TOP, T, "trace", s)
+            ins.append((torch.from_numpy(x).to("cuda", torch.bfloat16), torch.from_numpy(idx).cuda(),
+                        torch.from_numpy(wts).cuda()))
+        for i in range(16):
+            v.run(layers[i][0], *ins[i])
+        torch.cuda.synchronize()
+        s_ = torch.cuda.Stream()
+        s_.wait_stream(torch.cuda.current_stream())
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s_):
+            with torch.cuda.graph(gr, stream=s_):
+                for i in range(n_calls):
+                    v.run(layers[i % 16][0], *ins[i % 16])
+        torch.cuda.current_stream().wait_stream(s_)
+        gr.replay()
+        torch.cuda.synchronize()
+        t = min(time_graph(gr, 1) for _ in range(3)) / n_calls
+        del gr
+        U = float(np.mean([torch.unique(i[1]).numel() for i in ins]))
+        byts = U * 3 * D * F * W_BITS / 8 + 2 * T * D * 2 + 2 * T * K_TOP * F * 2
+        out.append([T, round(t * 1e6, 2), round(layer_frac(byts, 6.0 * D * F * T * K_TOP, t, peaks), 3),
+                    TRACE_M4PRO_US[T]])
+    return out
 
 
 # ------------------------------------------------------------------ the other BASELINE configurations (1 GPU)
@@ -463,7 +507,8 @@ def ep_stack(a, ws, rank):
     d, f, e, k, L = 4096, 1536, 128, 8, 8
     Ts = [int(s_) for s_ in a.ep_stack.split(",") if s_.strip()]
     layers = make_ep_layers(L, rank, ws, d=d, f=f, e=e)
-    xch = ep.PeerExchange.create(max(Ts) * k, d)
+    xch = ep.PeerExchange.create(max(Ts) * k, d) if ws > 1 else ep.PeerExchange.local_group(1, max(Ts) * k, d,
+                                                                                                "cuda")[0]
     rows = []
     try:
         for T in Ts:
@@ -474,8 +519,22 @@ def ep_stack(a, ws, rank):
             gr = ep_graph(layers, xs, L, xch, ws)
             t = max_over_ranks(ws, time_graph(gr, ws))  # one replay = one pass through the stack
             del gr
-            rows.append({"T": T, "us_per_layer": round(t / L * 1e6, 3), "stack_us": round(t * 1e6, 3),
-                         "tokens_per_s": round(ws * T / t, 1)})
+            row = [T, round(t / L * 1e6, 2), round(ws * T / t, 1)]
+            if ws > 1:  # the NCCL all-to-all-v exchange on the same stack (eager: one host read per layer)
+                from moelab_b200 import ep as ep_
+                for i in range(L):
+                    ep_.layer(layers[i][0], xs[i], layers[i][1], k, residual=xs[i])
+                barrier(ws)
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for i in range(L):
+                    ep_.layer(layers[i][0], xs[i], layers[i][1], k, residual=xs[i])
+                e1.record()
+                e1.synchronize()
+                tn = max_over_ranks(ws, e0.elapsed_time(e1) / 1e3)
+                row += [round(tn / L * 1e6, 2), round(ws * T / tn, 1)]
+            rows.append(row)
         errs = xch.read_error()
         torch.cuda.synchronize()
         barrier(ws)
@@ -485,9 +544,11 @@ def ep_stack(a, ws, rank):
         xch.close()
     del layers
     torch.cuda.empty_cache()
-    return {"config": "qwen3-235b-a22b int4-g64, 8 layers, experts split over the GPUs (peer-memory exchange)",
-            "d": d, "f": f, "E": e, "k": k, "layers": L, "experts_per_gpu": e // ws, "rows": rows,
-            "device_errors": errs}
+    fields = ["T_per_gpu", "us_per_layer", "tokens_per_s"] + (
+        ["nccl_us_per_layer", "nccl_tokens_per_s"] if ws > 1 else [])
+    return {"config": "qwen3-235b-a22b int4-g64, 8 layers, experts split over the GPUs (peer-memory exchange, "
+                      "CUDA graph; NCCL all-to-all-v eager beside it)",
+            "experts_per_gpu": e // ws, "fields": fields, "rows": rows, "device_errors": errs}
 
 
 def run_ep(a, ws, rank, local, peaks):
@@ -680,9 +741,8 @@ def main():
             traffic = None
     sweep = []
     for Ts in [int(s) for s in a.sweep.split(",") if s.strip()]:
-        sweep.append(measure_T(v, layers, Ts, ws, rank, 2 * a.layers if Ts >= 256 else 4 * a.layers, 77 + Ts))
-    for s_ in sweep:
-        s_["frac_of_hbm_peak"] = round(s_["gbs"] / peaks["hbm_gbs"], 3)
+        sweep.append(measure_T(v, layers, Ts, ws, rank, 2 * a.layers if Ts >= 256 else 4 * a.layers, 77 + Ts, peaks))
+    trace = measure_trace(v, layers, peaks) if a.trace else []
     # end to end through the public API with host buffers
     xh = torch.randn(T, D, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16).pin_memory()
     yh = torch.empty_like(xh).pin_memory()
@@ -709,6 +769,9 @@ def main():
     if a.configs:
         for name, shp, kind, Ts in CONFIGS:
             configs += measure_config(name, shp, kind, Ts, peaks)
+    del layers
+    torch.cuda.empty_cache()
+    stack = ep_stack(a, ws, rank) if a.ep_stack else None  # the expert-parallel stack's N = 1 row
     cpu = None
     if rank == 0 and ws == 1:
         val, n, el = cpu_baseline(T, a.cpu_seconds)
@@ -717,6 +780,12 @@ def main():
                          f"dequantised layer, {el:.1f} s"}
     if rank != 0:
         return
+    lay_t = t / a.steps
+    lay_flops = 6.0 * D * F * T * K_TOP
+    cfg = {"fields": ["T", "us_per_call", "layer_roofline_frac"]}
+    for c in configs:
+        cfg.setdefault(c["config"].split(" (")[0], []).append([c["T"], c["us_per_call"], c["roofline_frac"]])
+    # key figures last, so a truncated record still ends with them: sweep, layer fraction, roofline, CPU baseline
     line = {
         "metric": "MoE-layer tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": ws,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(t / a.steps * 1e3, 5),
@@ -727,21 +796,28 @@ def main():
                    "l2": "inputs larger than L2: 16 independent layers cycled (5.4 GB of expert weights)",
                    "parallelism": "single" if ws == 1 else f"replicas{ws}", "graph": "one CUDA graph of K steps"},
         "us_per_call": round(t / a.steps * 1e6, 3),
-        "layer_gbs": round(lay_ach, 1), "layer_frac_of_hbm_peak": round(lay_ach / peaks["hbm_gbs"], 3),
-        "sweep": sweep,
-        "kernels_us": {"router": round(statistics.mean(r_us), 3), "gate_up": round(statistics.mean(gu_us), 3),
-                       "down": round(statistics.mean(dn_us), 3),
-                       "note": "CUDA events between stages (serialised, eager)"},
+        "e2e": e2e, "clocks": ck,
+        "gpu_launches": (3 if T * K_TOP <= 16 else 4) * a.steps,  # router, gate/up, down (+ combine in tile mode)
+        "kernels_us": {"router": round(statistics.mean(r_us), 2), "gate_up": round(statistics.mean(gu_us), 2),
+                       "down": round(statistics.mean(dn_us), 2), "note": "CUDA events between stages (eager)"},
+        "configs": cfg,
+        "trace": {"workload": "qwen3-30b int4 on the reference's recorded routing traces, harness run()",
+                  "fields": ["T", "us_per_call", "layer_roofline_frac", "reference_m4pro_us"], "rows": trace},
+        "ep_stack": stack,
+        "sweep": {"fields": ["T", "us_per_call", "layer_roofline_frac", "layer_gbs"],
+                  "rows": [[s_["T"], s_["us"], s_["frac"], s_["gbs"]] for s_ in sweep]},
+        "layer_frac_of_hbm_peak": round(lay_ach / peaks["hbm_gbs"], 3),
         "roofline": {"bound": "hbm", "kernel": "k_gate_up_slots" if T * K_TOP <= 16 else "k_experts_ws (gate/up)",
                      "achieved": round(gu_ach, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(gu_ach / peaks["hbm_gbs"], 3), "traffic": traffic,
-                     "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)" if peaks["source"] == "measured"
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks["source"] == "measured"
                      else "fallback 6650 GB/s",
                      "algorithmic_bytes_per_launch": round(statistics.mean(gu_b)),
-                     "down_achieved_gbs": round(dn_ach, 1)},
-        "configs": configs,
-        "cpu_baseline": cpu, "e2e": e2e, "clocks": ck,
-        "gpu_launches": (3 if T * K_TOP <= 16 else 4) * a.steps,  # router, gate/up, down (+ combine in tile mode)
+                     "down_achieved_gbs": round(dn_ach, 1),
+                     "layer": {"frac": round(layer_frac(statistics.mean(lay_b), lay_flops, lay_t, peaks), 3),
+                               "us": round(lay_t * 1e6, 2), "bytes": round(statistics.mean(lay_b)),
+                               "flops": lay_flops, "def": "max(bytes / HBM peak, FLOPs / bf16 peak) / measured"}},
+        "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
 

@@ -192,8 +192,9 @@ int moeb_ep_combine(const float *back, const int *slot_pos, int T, int d, int k,
  *   2. moeb_ep_p2p_experts_q4: waits (bounded, ~2 s, then MOEB_DEVERR_TIMEOUT) for each source's flag, runs the
  *      grouped kernels on the valid rows (tile mode; padding rows are skipped) and stores each weighted fp32 row
  *      straight into its owner's return block, then releases the owners' return flags.
- *      Workspace: moeb_ep_workspace_bytes(P * C, d, f, E_local). policy: AUTO picks decode / tile kernels;
- *      MOEB_POLICY_TC (d, f multiples of 128) runs the tcgen05 kernels on request (as does moeb_ep_experts_*).
+ *      Workspace: moeb_ep_workspace_bytes(P * C, d, f, E_local). policy: AUTO picks the decode kernels for small
+ *      calls, the tcgen05 kernels from 24 rows per local expert (Cs >= 24 * E_local; d, f multiples of 128) and
+ *      the warp-specialized tiles in between; moeb_ep_experts_* picks from its R rows as a layer call does.
  *   3. moeb_ep_p2p_combine: waits for the return flags of all P ranks, then y as moeb_ep_combine.
  * The buffers are reused every call without extra synchronisation: a rank sends call n + 1 only after its
  * combine of call n saw every rank's return flag, i.e. after every rank finished reading call n's rows. */

@@ -327,7 +327,8 @@ int grid_for(const KLaunch &k, long units) {
 int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaStream_t st,
                 void *const *ev) {
     const long TK = (long)a.T * a.k;
-    const int nt = nt_of(policy, TK, a.E);
+    // tile size from the rows that carry work: a peer-exchange call's P blocks of Cs rows hold about Cs valid rows
+    const int nt = nt_of(policy, a.ypeers ? (long)a.C : TK, a.E);
     const long max_tiles = a.tile_mode ? std::min<long>(TK, (long)a.E + TK / nt) : TK;
     ExpLaunch K = pick_kernels(fmt, policy, a.d, a.f, nt);
     if (!K.gu.fn) return fail(MOEB_EUNSUP, "format not supported%s");
@@ -789,10 +790,7 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
     if (cap < T) return fail(MOEB_EINVAL, "workspace too small for T tokens%s");
     const Layout L = layout(cap, d, f, E, k, !ep);
     const int xs = ep ? d + 8 : d;
-    if (policy == MOEB_POLICY_AUTO) {
-        policy = choose_policy(T, E, k, d, f);
-        if (policy == MOEB_POLICY_TC && ep) policy = MOEB_POLICY_TILES16_RING;
-    }
+    if (policy == MOEB_POLICY_AUTO) policy = choose_policy(T, E, k, d, f);
     // the single-kernel decode: layer and expert calls of <= 16 slots whose plan fits an SM
     if (policy == MOEB_POLICY_DECODE &&
         (ep || (long)T * k > 16 || !decode_fits(fmt, T, d, f, k, gate_w ? E - ns : 0, gate_w != nullptr)))
@@ -837,7 +835,7 @@ static int experts_common(int fmt, const void *x, const void *qg, const void *sb
         }
         p.xsum = at<float>(ws, L.xsum);
         p.cnt_all = at<unsigned>(ws, L.cnt_all);
-        p.NT = nt_of(policy, (long)T * k, E);
+        p.NT = nt_of(policy, pp ? (long)pp->C : (long)T * k, E);  // as run_experts picks it
         p.tiles = tiles ? at<int4>(ws, L.tiles) : nullptr;
         p.ntiles = at<int>(ws, L.ntiles);
         p.sorted = at<int>(ws, L.sorted);
@@ -1094,7 +1092,9 @@ static int p2p_experts(int fmt, void *const *peers, void *self, int P, int me, i
     // spread over the P owners, an owner receives about Cs rows: the load is Cs / E_local rows per expert.
     if (policy == MOEB_POLICY_AUTO)
         policy = (Cs <= 16 && (long)P * Cs <= 128) ? MOEB_POLICY_SLOTS
-                 : ((long)Cs >= 8L * E_local ? MOEB_POLICY_TILES16_RING : MOEB_POLICY_TILES8_RING);
+                 : ((long)Cs >= 24L * E_local && d % 128 == 0 && f % 128 == 0)
+                     ? MOEB_POLICY_TC  // weights dequantized once per tile (the single-GPU dispatcher's rule)
+                     : ((long)Cs >= 8L * E_local ? MOEB_POLICY_TILES16_RING : MOEB_POLICY_TILES8_RING);
     else if (policy != MOEB_POLICY_SLOTS && policy != MOEB_POLICY_TILES8_RING && policy != MOEB_POLICY_TILES16_RING &&
              policy != MOEB_POLICY_TC)
         policy = MOEB_POLICY_TILES8_RING;  // (TC on request: its down epilogue stores into the owners' blocks)

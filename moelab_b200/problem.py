@@ -5,14 +5,54 @@ x [T, d], w_gate/w_up [E, f, d], w_down [E, d, f] (out, in), idx [T, k] int32, w
 y[t] = sum_j wts[t,j] * down_e(silu(gate_e x_t) * up_e x_t), e = idx[t,j].
 
 make_routing / make_problem restate moelab/problem.py:15-64 call for call (same numpy Generator draws), so a
-seed gives the reference's own inputs; tests/golden pins that. The "trace" mode (recorded Qwen3 routing,
-problem.py:38-50) needs the reference's runs/ data and is not carried here.
+seed gives the reference's own inputs; tests/golden pins that. The "trace" mode (recorded Qwen3-30B-A3B routing,
+moelab/problem.py:38-50) makes the reference's draws - a domain, a layer and a start token of the recorded traces,
+then random combine weights - and takes the window from TraceWindows, the windows the reference drew for a set of
+seeds (tests/golden/trace_qwen3.npz, written by tests/golden/make_trace.py from the reference's own code); a draw
+outside that set raises KeyError.
 """
+import os
+
 import numpy as np
 
+_ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+TRACE_FIXTURE = os.path.join(_ROOT, "tests", "golden", "trace_qwen3.npz")
 
-def make_routing(T, E, k, mode="uniform", rng=None, zipf_a=1.2):
+
+class TraceWindows:
+    """Recorded-routing windows by (domain, layer, start, T), and the domains' (layers, tokens) shapes."""
+
+    def __init__(self, path=TRACE_FIXTURE):
+        z = np.load(path)
+        self.shapes = [tuple(int(v) for v in s) for s in z["shapes"]]
+        self.win = {tuple(int(v) for v in key): z["windows"][i] for i, key in enumerate(z["keys"])}
+        self.E, self.k = 128, int(z["windows"].shape[2])
+
+    def draw(self, T, E, k, rng):
+        """moelab/problem.py:38-50: domain, layer, start, then weights = rng.random((T, k)) normalised."""
+        assert E == self.E and k == self.k, "trace recorded for E=128, k=8 (Qwen3) only"
+        dom = int(rng.integers(len(self.shapes)))
+        layer, start = int(rng.integers(self.shapes[dom][0])), int(rng.integers(self.shapes[dom][1] - T))
+        key = (dom, layer, start, T)
+        if key not in self.win:
+            raise KeyError(f"trace window {key} is not in the fixture (seeds 0..15, T in 1/8/16/32 are)")
+        idx = self.win[key][:T].astype(np.int32)
+        w = rng.random((T, k)).astype(np.float32)
+        return idx, w / w.sum(1, keepdims=True)
+
+
+_TRACE = None
+
+
+def make_routing(T, E, k, mode="uniform", rng=None, zipf_a=1.2, trace=None):
+    global _TRACE
     rng = rng or np.random.default_rng(0)
+    if mode == "trace":
+        if trace is None:
+            if _TRACE is None:
+                _TRACE = TraceWindows()
+            trace = _TRACE
+        return trace.draw(T, E, k, rng)
     if mode == "uniform":
         logits = rng.standard_normal((T, E))
     elif mode == "zipf":  # skewed popularity over a seeded expert permutation
@@ -74,3 +114,12 @@ def error_metrics(y, y_ref):
 
 TOLERANCE = {"float32": 1e-4, "float16": 3e-3, "bfloat16": 2e-2, "q8": 2e-2, "q4": 2e-2}
 ROWREL_TOL = 1e-2  # north star: max |err| <= 1e-2 * row max |ref| for bf16 activations
+
+
+def make_inputs(d, E, k, T, routing, seed):
+    """The reference's benchmark inputs (moelab/torch_backend.py:50-54): rng = default_rng(seed),
+    x = rng.standard_normal((T, d)) then make_routing(T, E, k, routing, rng). -> (x fp32, idx, wts)."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((T, d)).astype(np.float32)
+    idx, wts = make_routing(T, E, k, routing, rng)
+    return x, idx, wts

@@ -218,3 +218,34 @@ def test_tc_rejects_unsupported_shapes():
     b200_q4_moe._ws(st, 2)
     with pytest.raises(ops._lib.MoebError, match="multiples of 128"):
         ops.experts(st, x, idx, wts, policy=ops.POLICY_TC)
+
+
+# ------------------------------------------------------------------ Qwen3-30B-A3B on recorded routing traces
+@pytest.fixture(scope="module")
+def qwen3_trace_layer():
+    from moelab_b200.shapes import MoEShape
+    sh = MoEShape("qwen3-30b-a3b", d=2048, f=768, E=128, k=8)
+    w, _ = _w(sh.E, sh.f, sh.d, seed=301)
+    st = b200_q4_moe.prepare(*w)
+    del w
+    deq = b200_q4_moe.dequant(st)
+    return sh, st, deq
+
+
+@pytest.mark.parametrize("T", [1, 8, 16, 32])
+@pytest.mark.parametrize("seed", [0, 5, 11])
+@pytest.mark.parametrize("policy", [None, ops.POLICY_DECODE, ops.POLICY_TILES8_RING])
+def test_qwen3_trace_routing(qwen3_trace_layer, T, seed, policy, monkeypatch):
+    """The reference's trace inputs (moelab/problem.py:38-50 via moelab/torch_backend.py:50-54: recorded
+    Qwen3-30B-A3B routing windows, skewed and repeated experts) through the harness contract run(); the ids are
+    the reference's own draws (tests/golden/trace_qwen3.npz)."""
+    from moelab_b200.problem import make_inputs
+    sh, st, deq = qwen3_trace_layer
+    monkeypatch.setattr(b200_q4_moe, "POLICY", policy)
+    x, idx, wts = make_inputs(sh.d, sh.E, sh.k, T, "trace", seed)
+    xt = torch.from_numpy(x).to("cuda", torch.bfloat16)
+    it, wt = torch.from_numpy(idx).cuda(), torch.from_numpy(wts).cuda()
+    b200_q4_moe._ws(st, sh.k)
+    y = b200_q4_moe.run(st, xt, it, wt)
+    assert_close(y, torch_ref(b200_q4_moe, st, xt, it, wt, deq), what=(T, seed, policy))
+    assert st["ws"].read_error() == 0

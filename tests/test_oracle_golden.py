@@ -63,3 +63,21 @@ def test_torch_loop_port_matches_reference_torch_loop(case):
     y = oracle.torch_loop_run(s, torch.from_numpy(p["x"]).to(torch.bfloat16), torch.from_numpy(p["idx"]),
                               torch.from_numpy(p["wts"]))
     np.testing.assert_array_equal(y.float().numpy(), VEC[f"prob{case['id']}_yloop"])
+
+
+def test_trace_windows_reproduce_reference_draws():
+    """Trace routing (moelab/problem.py:38-50): the windows and weights the reference's own make_inputs drew for
+    every stored (seed, T) are reproduced bit for bit from the committed fixture."""
+    import os
+    from moelab_b200.problem import TRACE_FIXTURE, make_inputs
+    z = np.load(TRACE_FIXTURE)
+    n = 0
+    for name in z.files:
+        if not name.startswith("idx_"):
+            continue
+        _, seed, T = name.split("_")
+        x, idx, wts = make_inputs(2048, 128, 8, int(T), "trace", int(seed))
+        np.testing.assert_array_equal(idx, z[name])
+        np.testing.assert_array_equal(wts, z[f"wts_{seed}_{T}"])
+        n += 1
+    assert n == 64 and os.path.getsize(TRACE_FIXTURE) < 200_000
