@@ -8,12 +8,20 @@
  * it replaces. All pointers are device pointers unless stated; every call is asynchronous on `stream`,
  * allocates nothing and returns MOEB_OK (0) or an error code with a message from moeb_last_error().
  *
- * Weight layout (B200 layout, produced by moeb_quantize_* or moeb_*_from_mlx from the mlx layout):
- *   int4 affine g64: q  uint32 [E][N][K/8]  (word j = elements 8j..8j+7; nibble p = element 8j+2p and
- *                                             nibble p+4 = element 8j+2p+1, p = 0..3)
- *                    sb uint32 [E][N][K/64] (bf16 scale in bits 0-15, bf16 bias in bits 16-31)
- *   MXFP4:           q  uint32 [E][N][K/8]  (same nibble order, E2M1 codes), sc uint8 [E][N][K/32] (E8M0)
- *   gate/up: N = f, K = d; down: N = d, K = f. Activations x, y, residual: bf16 [T][d].
+ * Weight layout (the B200 layout, produced by moeb_quantize_* or by moeb_*_from_mlx from mlx's layout; the same
+ * byte counts as mlx's [E][N][K/8] codes): each projection is a sequence of 16-row blocks (the E*N rows of all
+ * experts, expert-major, N a multiple of 16), each block a sequence of its K/64 groups of 64 inputs, so one
+ * (row block, group) is a contiguous unit. For weight row r (0 <= r < E*N) and input k (0 <= k < K), with
+ * rb = r / 16, rr = r % 16, g = k / 64, j = (k % 64) / 8 (the 8-input word inside the group), e = k % 8:
+ *   int4 codes q (uint32): word ((rb*(K/64) + g)*32 + lane)*4 + (rr/8)*2 + j%2, lane = (rr%8)*4 + j/2 (the lane of a
+ *       warp whose m16n8k16 A fragment holds it); inside the word, input e sits at nibble e/2 if e is even and at
+ *       nibble 4 + e/2 if odd (low nibble first);
+ *   int4 scale|bias sb (uint32: bf16 scale in bits 0-15, bf16 bias in bits 16-31; w = scale * q + bias):
+ *       word ((rb*(K/64) + g)*8 + rr%8)*2 + rr/8;
+ *   MXFP4 codes q: as int4 (E2M1 codes: sign bit 3, magnitude {0, .5, 1, 1.5, 2, 3, 4, 6} in bits 0-2);
+ *   MXFP4 scales sc (uint8 E8M0, one per 32 inputs, h = k / 32): byte (((rb*(K/64) + h/2)*8 + rr%8)*2 + rr/8)*2 + h%2.
+ *   gate/up: N = f, K = d; down: N = d, K = f. Row counts (E*N) and K are multiples of 16 and 64 (MOEB_EINVAL
+ *   otherwise). Activations x, y, residual: bf16 [T][d], row-major.
  */
 #ifndef MOELAB_B200_H
 #define MOELAB_B200_H
@@ -121,7 +129,9 @@ int moeb_experts_mxfp4(const void *x, const void *qg, const void *scg, const voi
                        const void *residual, void *y, void *ws, size_t ws_bytes, cudaStream_t stream);
 
 /* --- full layer call (x, gate weights, packed expert weights + scales + biases, k) -> y: router, routing
- * step, grouped experts and the weighted combine in one stream-ordered sequence (3 launches).
+ * step, grouped experts and the weighted combine in one stream-ordered sequence: 3 launches for decode calls
+ * (router, gate/up, down with the combine), 4 for tiled calls (router with the routing step, gate/up, down, combine),
+ * 5 on the tensor-core path (+ the expert-sorted activation gather), 1 with MOEB_POLICY_DECODE.
  * Replaces the patched MoE block call of moelab/e2e.py:51-69 (router + mod.run). idx_out / wts_out may be
  * NULL (then they live in the workspace). stage_events: NULL, or 4 cudaEvent_t recorded before the router,
  * after the router, after gate/up and after down (per-kernel timing; recording them serialises the stages). */

@@ -303,7 +303,18 @@ bool allow_smem(const void *fn, size_t bytes) {
     return true;
 }
 
-bool separate_combine(const KLaunch &dn) { return dn.sg > 0; }
+// The warp-specialized down kernel can combine in its epilogue (the last of a token's k slots to finish a 16-row
+// block sums them, as the decode kernels do) or leave the weighted slot rows to a separate combine pass; the
+// tensor-core down kernel always leaves them. MOEB_WS_COMBINE=fused|separate overrides the default (measurements).
+bool separate_combine(const KLaunch &dn) {
+    static const int mode = [] {
+        const char *s = getenv("MOEB_WS_COMBINE");
+        return s ? (strcmp(s, "fused") == 0 ? 1 : strcmp(s, "separate") == 0 ? 2 : 0) : 0;
+    }();
+    if (dn.tc) return true;
+    if (dn.sg == 0) return false;
+    return mode != 1;
+}
 
 // 2-D map over rows x d bf16 activations (row stride d * 2 bytes), box 64 x brows, 128-byte swizzle.
 bool encode_rows_map(CUtensorMap *out, const void *base, long rows, int d, int brows) {

@@ -84,3 +84,41 @@ def test_fragment_major_layout_is_a_permutation():
     s = rng.integers(0, 2**16, (32, 8), dtype=np.uint16)
     q, sb = to_b200_q4(qw, s, s)
     assert q.shape == (32 * 64,) and sb.shape == (32 * 8,)
+
+
+def test_header_layout_formulas_match_the_packing():
+    """The weight layout spelled out in include/moelab_b200.h, implemented element by element, gives the same words
+    as the packing the GPU tests check bit-exact against the kernels (helpers.to_b200_q4 / to_b200_fp4)."""
+    import numpy as np
+    from helpers import to_b200_fp4, to_b200_q4
+    rng = np.random.default_rng(0)
+    rows, K = 32, 128
+    codes = rng.integers(0, 16, size=(rows, K), dtype=np.uint32)
+    nat = np.zeros((rows, K // 8), np.uint32)
+    for i in range(8):
+        nat |= codes[:, i::8] << (4 * i)
+    s = rng.integers(0, 1 << 16, size=(rows, K // 64), dtype=np.uint32)
+    b = rng.integers(0, 1 << 16, size=(rows, K // 64), dtype=np.uint32)
+    q_ref, sb_ref = to_b200_q4(nat, s, b)
+    q = np.zeros(rows * K // 8, np.uint32)
+    sb = np.zeros(rows * K // 64, np.uint32)
+    for r in range(rows):
+        rb, rr = r // 16, r % 16
+        for k in range(K):
+            g, j, e = k // 64, (k % 64) // 8, k % 8
+            lane = (rr % 8) * 4 + j // 2
+            w = ((rb * (K // 64) + g) * 32 + lane) * 4 + (rr // 8) * 2 + j % 2
+            nib = e // 2 if e % 2 == 0 else 4 + e // 2
+            q[w] |= codes[r, k] << (4 * nib)
+        for g in range(K // 64):
+            sb[((rb * (K // 64) + g) * 8 + rr % 8) * 2 + rr // 8] = s[r, g] | (b[r, g] << 16)
+    np.testing.assert_array_equal(q, q_ref)
+    np.testing.assert_array_equal(sb, sb_ref)
+    sc = rng.integers(0, 256, size=(rows, K // 32), dtype=np.uint8)
+    _, sc_ref = to_b200_fp4(nat, sc)
+    sc_h = np.zeros(rows * K // 32, np.uint8)
+    for r in range(rows):
+        rb, rr = r // 16, r % 16
+        for h in range(K // 32):
+            sc_h[(((rb * (K // 64) + h // 2) * 8 + rr % 8) * 2 + rr // 8) * 2 + h % 2] = sc[r, h]
+    np.testing.assert_array_equal(sc_h, sc_ref)
