@@ -201,6 +201,52 @@ def capture(v, layers, xs, n_steps, k0=0):
     return gr, out
 
 
+def e2e_loop(call, xh_list, yh_list, steps, ws):
+    """End-to-end timing through the public API with host buffers: every step copies its input from pinned host
+    memory to the device and its result back to pinned host memory. The copies run on a side stream, double
+    buffered, so step i + 1's input and step i's result move while step i computes (stream-ordered: compute i + 1
+    waits for its input copy, the copy of result i waits for compute i). call(i, x_device) -> y_device.
+    Returns seconds for `steps` steps (CUDA events on the compute stream around the whole loop, both streams
+    drained inside it)."""
+    comp, cp = torch.cuda.current_stream(), torch.cuda.Stream()
+    nb = len(xh_list)
+    xd = [torch.empty_like(xh_list[0], device="cuda") for _ in range(2)]
+    ready = [torch.cuda.Event() for _ in range(2)]
+    done = [torch.cuda.Event() for _ in range(2)]
+
+    def run(n):
+        with torch.cuda.stream(cp):
+            xd[0].copy_(xh_list[0], non_blocking=True)
+            ready[0].record(cp)
+        for i in range(n):
+            b = i & 1
+            if i + 1 < n:  # next input into the other buffer once the step that used it has finished
+                with torch.cuda.stream(cp):
+                    if i >= 1:
+                        cp.wait_event(done[1 - b])
+                    xd[1 - b].copy_(xh_list[(i + 1) % nb], non_blocking=True)
+                    ready[1 - b].record(cp)
+            comp.wait_event(ready[b])
+            y = call(i, xd[b])
+            done[b].record(comp)
+            y.record_stream(cp)  # the allocator keeps y until the copy stream has read it
+            with torch.cuda.stream(cp):
+                cp.wait_event(done[b])
+                yh_list[i % nb].copy_(y, non_blocking=True)
+        comp.wait_stream(cp)
+
+    run(4)
+    torch.cuda.synchronize()
+    barrier(ws)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(comp)
+    run(steps)
+    e1.record(comp)
+    e1.synchronize()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / 1e3
+
+
 def time_graph(gr, ws, reps=1):
     barrier(ws)
     torch.cuda.synchronize()
@@ -584,25 +630,16 @@ def run_ep(a, ws, rank, local, peaks):
             ts = max_over_ranks(ws, time_graph(gs, ws))
             del gs
             sweep.append({"T": Ts, "us_per_call": round(ts / n_s * 1e6, 3), "tokens_per_s": round(ws * Ts * n_s / ts, 1)})
-        # end to end through the public API with host buffers (eager)
-        xh = torch.randn(T, D, generator=torch.Generator().manual_seed(9 + rank)).to(torch.bfloat16).pin_memory()
-        yh = torch.empty_like(xh).pin_memory()
-        for i in range(4):
-            xd = xh.to("cuda", non_blocking=True)
+        # end to end through the public API with host buffers (eager, copies double-buffered on a side stream)
+        gh = torch.Generator().manual_seed(9 + rank)
+        xh = [torch.randn(T, D, generator=gh).to(torch.bfloat16).pin_memory() for _ in range(8)]
+        yh = [torch.empty_like(xh[0]).pin_memory() for _ in range(8)]
+
+        def call(i, xd):
             st, gate = layers[i % len(layers)]
-            yh.copy_(ep.layer_p2p(st, xd, gate, K_TOP, xch, residual=xd, max_tokens=T), non_blocking=True)
-        torch.cuda.synchronize()
-        barrier(ws)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for i in range(a.e2e_steps):
-            xd = xh.to("cuda", non_blocking=True)
-            st, gate = layers[i % len(layers)]
-            yh.copy_(ep.layer_p2p(st, xd, gate, K_TOP, xch, residual=xd, max_tokens=T), non_blocking=True)
-        e1.record()
-        e1.synchronize()
-        torch.cuda.synchronize()
-        te = max_over_ranks(ws, e0.elapsed_time(e1) / 1e3)
+            return ep.layer_p2p(st, xd, gate, K_TOP, xch, residual=xd, max_tokens=T)
+
+        te = max_over_ranks(ws, e2e_loop(call, xh, yh, a.e2e_steps, ws))
         errs = xch.read_error()
         torch.cuda.synchronize()
         barrier(ws)
@@ -638,7 +675,8 @@ def run_ep(a, ws, rank, local, peaks):
         "cpu_baseline": None,
         "e2e": {"value": round(ws * T * a.e2e_steps / te, 1), "unit": "tokens/s", "h2d_bytes_per_step": T * D * 2,
                 "d2h_bytes_per_step": T * D * 2, "us_per_call": round(te / a.e2e_steps * 1e6, 3),
-                "note": "public API ep.layer_p2p(); pinned host x in and y out every step, eager"},
+                "note": "public API ep.layer_p2p() eager; every step's x in from / y out to pinned host memory, on a "
+                        "side stream double-buffered against the compute"},
         "device_errors": errs,
         "clocks": ck,
         "gpu_launches": 8 * a.steps,  # router, plan, send, prep, gate/up, down, signal, combine
@@ -743,28 +781,20 @@ def main():
     for Ts in [int(s) for s in a.sweep.split(",") if s.strip()]:
         sweep.append(measure_T(v, layers, Ts, ws, rank, 2 * a.layers if Ts >= 256 else 4 * a.layers, 77 + Ts, peaks))
     trace = measure_trace(v, layers, peaks) if a.trace else []
-    # end to end through the public API with host buffers
-    xh = torch.randn(T, D, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16).pin_memory()
-    yh = torch.empty_like(xh).pin_memory()
-    for i in range(8):
-        xd = xh.to("cuda", non_blocking=True)
+    # end to end through the public API with host buffers (8 distinct pinned inputs cycled)
+    gh = torch.Generator().manual_seed(9)
+    xh = [torch.randn(T, D, generator=gh).to(torch.bfloat16).pin_memory() for _ in range(8)]
+    yh = [torch.empty_like(xh[0]).pin_memory() for _ in range(8)]
+
+    def call(i, xd):
         st, gate = layers[i % len(layers)]
-        yh.copy_(v.layer(st, xd, gate, K_TOP, residual=xd), non_blocking=True)
-    torch.cuda.synchronize()
-    barrier(ws)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(a.e2e_steps):
-        xd = xh.to("cuda", non_blocking=True)
-        st, gate = layers[i % len(layers)]
-        yh.copy_(v.layer(st, xd, gate, K_TOP, residual=xd), non_blocking=True)
-    e1.record()
-    e1.synchronize()
-    torch.cuda.synchronize()
-    te = max_over_ranks(ws, e0.elapsed_time(e1) / 1e3)
+        return v.layer(st, xd, gate, K_TOP, residual=xd)
+
+    te = max_over_ranks(ws, e2e_loop(call, xh, yh, a.e2e_steps, ws))
     e2e = {"value": round(ws * T * a.e2e_steps / te, 1), "unit": "tokens/s", "h2d_bytes_per_step": T * D * 2,
            "d2h_bytes_per_step": T * D * 2, "us_per_call": round(te / a.e2e_steps * 1e6, 3),
-           "note": "public API v.layer(); pinned host x copied in and y copied out every step, no graph"}
+           "note": "public API v.layer() eager, no graph; every step's x copied in from pinned host memory and y "
+                   "copied out to it, on a side stream double-buffered against the compute"}
     configs = []
     if a.configs:
         for name, shp, kind, Ts in CONFIGS:

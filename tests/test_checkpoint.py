@@ -108,7 +108,7 @@ def test_q4_state_from_checkpoint_equals_quantize_path(tmp_path):
 def _fp4_weights(seed):
     g = torch.Generator().manual_seed(seed)
     ws = [torch.randn(E, F, D, generator=g), torch.randn(E, F, D, generator=g), torch.randn(E, D, F, generator=g)]
-    ws[0][:, :, :32] *= 2.0 ** 6  # E8M0 bytes >= 129 (scales above 1), the real-checkpoint regression
+    ws[0][:, :, :32] *= 2.0 ** 10  # E8M0 bytes >= 129 (scales above 1), the real-checkpoint regression
     return [(w * 0.02).bfloat16() for w in ws]
 
 
@@ -152,10 +152,11 @@ def test_mxfp4_state_from_checkpoint_equals_quantize_path(tmp_path, layout):
     st = ck.mxfp4_layer_state(p, 7)
     ref = vg.state(*(w.cuda() for w in ws), *(b.cuda() for b in bs))
     for n in ("g", "u", "d"):
-        assert torch.equal(st[n][0], ref[n][0]) and torch.equal(st[n][1], ref[n][1]), n
+        assert torch.equal(st[n][0], ref[n][0]), ("codes", n)
+        assert torch.equal(st[n][1], ref[n][1]), ("scales", n)
     for n in ("bg", "bu", "bd"):
         assert torch.equal(st[n], ref[n]), n
-    assert int(st["g"][1].max()) >= 129  # E8M0 >= 129 carried through
+    assert int(st["g"][1].max().item()) >= 129, int(st["g"][1].max().item())  # E8M0 >= 129 carried through
     x = torch.randn(3, D, device="cuda").to(torch.bfloat16)
     idx = torch.tensor([[0, 1], [2, 3], [1, 2]], dtype=torch.int32, device="cuda")
     wts = torch.full((3, 2), 0.5, device="cuda")
