@@ -54,6 +54,7 @@ typedef struct CUstream_st *cudaStream_t;
 #define MOEB_POLICY_TILES8_RING 4  /* tiles of <= 8 slots, weights streamed by TMA into a per-warp ring */
 #define MOEB_POLICY_TILES16_RING 5 /* tiles of <= 16 slots, TMA ring */
 #define MOEB_POLICY_TC 6 /* tiles of <= 256 slots on tcgen05 tensor cores (d and f multiples of 128) */
+#define MOEB_POLICY_TILES24_RING 8 /* tiles of <= 24 slots, TMA ring */
 #define MOEB_POLICY_DECODE 7 /* decode (<= 16 slots) as ONE cooperative kernel, one CTA per SM: router, gate/up,
                                 down and combine, every CTA's expert weights issued by bulk copies right after
                                 routing (opt-in: 24.5 vs 20.7 us for the three decode launches at T=1; SLOTS where

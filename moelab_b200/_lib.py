@@ -13,6 +13,7 @@ MOEB_OK, MOEB_EINVAL, MOEB_ELAUNCH, MOEB_ETIMEOUT, MOEB_EUNSUP = 0, 1, 2, 3, 4
 POLICY_AUTO, POLICY_SLOTS, POLICY_TILES8, POLICY_TILES16, POLICY_TILES8_RING, POLICY_TILES16_RING = 0, 1, 2, 3, 4, 5
 POLICY_TC = 6
 POLICY_DECODE = 7
+POLICY_TILES24_RING = 8
 DEVERR_EXPERT_ID, DEVERR_TIMEOUT = 1, 2
 
 _P = ctypes.c_void_p

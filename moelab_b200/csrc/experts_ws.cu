@@ -74,12 +74,13 @@ __global__ void __launch_bounds__(32 * (RBC + 1), MB) k_experts_ws(const __grid_
 
     if (warp == RBC) {
         // ------------------------------------------------------------ producer warp
-        // Lane 0 issues the weight tensor copies; lanes [16, 16 + COLS) copy one activation column each. Per work
-        // item every lane computes its source bases once; the item's tile record and slot ids are fetched one
-        // item ahead so no global load sits on the issue path.
-        static_assert(L::COLS <= 16, "producer lane roles");
+        // Lane 0 issues the weight tensor copies; lanes [CL0, CL0 + COLS) copy one activation column each (CL0 = 16,
+        // or 32 - COLS for tiles of more than 16 slots). Per work item every lane computes its source bases once;
+        // the item's tile record and slot ids are fetched one item ahead so no global load sits on the issue path.
+        constexpr int CL0 = L::COLS <= 16 ? 16 : 32 - L::COLS;
+        static_assert(L::COLS <= 31, "producer lane roles: lane 0 issues the tensor copies");
         const uint64_t pol = l2_evict_first_policy();
-        const int col = lane - 16;  // column lane: column index
+        const int col = lane - CL0;  // column lane: column index
         const bool clane = col >= 0 && col < L::COLS;
         const int m0 = DOWN ? 2 : 0;  // tensor maps of this kernel's projections
         if (lane == 0)
@@ -259,7 +260,9 @@ size_t experts_ws_smem(int nt8, int rbc, int sg, int ns, bool down, int fmt) {
     template __global__ void k_experts_ws<FMT, 1, 8, 4, 2, false, 2>(const __grid_constant__ ExpArgs); \
     template __global__ void k_experts_ws<FMT, 2, 8, 4, 2, false, 2>(const __grid_constant__ ExpArgs); \
     template __global__ void k_experts_ws<FMT, 1, 8, 4, 4, true, 2>(const __grid_constant__ ExpArgs);  \
-    template __global__ void k_experts_ws<FMT, 2, 8, 4, 4, true, 2>(const __grid_constant__ ExpArgs);
+    template __global__ void k_experts_ws<FMT, 2, 8, 4, 4, true, 2>(const __grid_constant__ ExpArgs);  \
+    template __global__ void k_experts_ws<FMT, 3, 8, 4, 2, false, 2>(const __grid_constant__ ExpArgs); \
+    template __global__ void k_experts_ws<FMT, 3, 8, 4, 3, true, 2>(const __grid_constant__ ExpArgs);
 MOEB_WS(FMT_Q4)
 MOEB_WS(FMT_FP4)
 

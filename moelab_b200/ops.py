@@ -16,6 +16,7 @@ POLICY_AUTO, POLICY_SLOTS, POLICY_TILES8, POLICY_TILES16 = (_lib.POLICY_AUTO, _l
 POLICY_TILES8_RING, POLICY_TILES16_RING = _lib.POLICY_TILES8_RING, _lib.POLICY_TILES16_RING
 POLICY_TC = _lib.POLICY_TC
 POLICY_DECODE = _lib.POLICY_DECODE
+POLICY_TILES24_RING = _lib.POLICY_TILES24_RING
 
 
 def _p(t):

@@ -59,7 +59,8 @@ def test_host_only_calls():
     assert lib.moeb_policy(1, 128, 8) == _lib.POLICY_SLOTS
     assert lib.moeb_policy(2, 128, 8) == _lib.POLICY_SLOTS
     assert lib.moeb_policy(4, 128, 8) == _lib.POLICY_TILES8_RING
-    assert lib.moeb_policy(256, 128, 8) in (_lib.POLICY_TILES8_RING, _lib.POLICY_TILES16_RING)
+    assert lib.moeb_policy(128, 128, 8) == _lib.POLICY_TILES16_RING  # 8 slots per expert
+    assert lib.moeb_policy(256, 128, 8) == _lib.POLICY_TILES24_RING  # 16 slots per expert
     assert lib.moeb_policy(384, 128, 8) == _lib.POLICY_TC  # 24 slots per expert: tcgen05 tiles
 
 

@@ -15,7 +15,8 @@ pytestmark = pytest.mark.gpu
 FP4 = ROOT + "/moelab_b200/variants/cuda/b200_mxfp4_moe.py"
 GPTOSS = ROOT + "/moelab_b200/variants/cuda/b200_mxfp4_gptoss.py"
 POLICIES = {"auto": None, "slots": ops.POLICY_SLOTS, "tiles8": ops.POLICY_TILES8, "tiles16": ops.POLICY_TILES16,
-            "tiles8ring": ops.POLICY_TILES8_RING, "tiles16ring": ops.POLICY_TILES16_RING, "decode": ops.POLICY_DECODE,
+            "tiles8ring": ops.POLICY_TILES8_RING, "tiles16ring": ops.POLICY_TILES16_RING,
+            "tiles24ring": ops.POLICY_TILES24_RING, "decode": ops.POLICY_DECODE,
             "tc": ops.POLICY_TC}
 
 
