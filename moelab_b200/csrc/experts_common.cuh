@@ -30,6 +30,44 @@ __device__ __forceinline__ int tile_slot(const ExpArgs &a, const TileInfo &ti, i
     return a.tile_mode ? a.sorted[ti.start + col] : ti.start;
 }
 
+// A work tile's record {expert, first sorted position, slots}: from the tile list, or slot `tile` alone
+__device__ __forceinline__ int4 tile_rec(const ExpArgs &a, int tile) {
+    return a.tile_mode ? a.tiles[tile] : make_int4(a.idx[tile], tile, 1, 0);
+}
+__device__ __forceinline__ TileInfo tile_info_of(const ExpArgs &a, const int4 t) {
+    TileInfo ti;
+    ti.e = (t.x < 0 || t.x >= a.E) ? 0 : t.x;  // invalid id: computed on expert 0, weighted 0 in the down epilogue
+    ti.start = t.y;
+    ti.n = t.z;
+    return ti;
+}
+
+// The epilogue's per-lane metadata (lane 4gq + c owns columns 8j + 2c + hf): slot ids, and the down combine
+// weights (0 for an invalid expert id). Loaded early by kernels that can hide the global-load latency.
+template <int NT8>
+__device__ __forceinline__ void epi_slots(const ExpArgs &a, const TileInfo &ti, int lane, int (&sl)[NT8][2]) {
+#pragma unroll
+    for (int j = 0; j < NT8; ++j)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) sl[j][hf] = tile_slot(a, ti, j * 8 + 2 * (lane & 3) + hf);
+}
+template <int NT8>
+__device__ __forceinline__ void epi_weights(const ExpArgs &a, const int (&sl)[NT8][2], float (&wv)[NT8][2]) {
+#pragma unroll
+    for (int j = 0; j < NT8; ++j)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+            const int s = sl[j][hf];
+            if (s >= 0) {
+                const int e_raw = a.idx[s];
+                const float w = a.wts[s];
+                wv[j][hf] = (e_raw >= 0 && e_raw < a.E) ? w : 0.f;
+            } else {
+                wv[j][hf] = 0.f;
+            }
+        }
+}
+
 // One 64-group of one projection: 4 k-steps x NT8 column tiles into P, then promotion into C.
 // w: {row gq: word 2c, 2c+1; row gq+8: word 2c, 2c+1}; sb: {row gq, row gq+8} scale|bias.
 template <int NT8>
@@ -167,14 +205,15 @@ __device__ __forceinline__ void wgroup(const uint4 w, const uint2 sc, int c, con
 }
 
 // gate/up epilogue for one column tile j of a unit: bias, activation, bf16 h, block sums.
-template <int NT8>
-__device__ __forceinline__ void gate_up_store(const ExpArgs &a, const TileInfo &ti, int rb, int j,
-                                              const float (&gs)[4], const float (&us)[4], int lane) {
-    const int gq = lane >> 2, c = lane & 3, f = a.f;
+// slot_of(hf): the slot of this lane's column hf, or -1.
+template <class SlotOf>
+__device__ __forceinline__ void gate_up_store_impl(const ExpArgs &a, const TileInfo &ti, int rb, const float (&gs)[4],
+                                                   const float (&us)[4], int lane, SlotOf slot_of) {
+    const int gq = lane >> 2, f = a.f;
     const int r0 = rb * 16 + gq, r1 = r0 + 8;
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
-        const int slot = tile_slot(a, ti, j * 8 + 2 * c + hf);
+        const int slot = slot_of(hf);
         float g0v = gs[hf], g1v = gs[2 + hf], u0v = us[hf], u1v = us[2 + hf];
         if (a.bg) {
             g0v += a.bg[(size_t)ti.e * f + r0];
@@ -194,22 +233,33 @@ __device__ __forceinline__ void gate_up_store(const ExpArgs &a, const TileInfo &
         }
     }
 }
+template <int NT8>
+__device__ __forceinline__ void gate_up_store(const ExpArgs &a, const TileInfo &ti, int rb, int j,
+                                              const float (&gs)[4], const float (&us)[4], int lane) {
+    gate_up_store_impl(a, ti, rb, gs, us, lane, [&](int hf) { return tile_slot(a, ti, j * 8 + 2 * (lane & 3) + hf); });
+}
+// the same with the slot ids loaded ahead (epi_slots)
+__device__ __forceinline__ void gate_up_store_sl(const ExpArgs &a, const TileInfo &ti, int rb, const int (&sl)[2],
+                                                 const float (&gs)[4], const float (&us)[4], int lane) {
+    gate_up_store_impl(a, ti, rb, gs, us, lane, [&](int hf) { return sl[hf]; });
+}
 
 // down epilogue of one warp: write the weighted per-slot rows, arrive on the (token, row block) counters and
 // combine every token this arrival completed. Warp-synchronous; no CTA barrier.
-template <int NT8>
-__device__ __forceinline__ void down_store_combine(const ExpArgs &a, const TileInfo &ti, int rb,
-                                                   const float (&C)[NT8][4], int lane) {
-    const int gq = lane >> 2, c = lane & 3, d = a.d, k = a.k, RB = d >> 4;
+// slot_of(j, hf): the slot of this lane's column 8j + 2c + hf, or -1; weight_of(j, hf, slot): its combine weight.
+template <int NT8, class SlotOf, class WeightOf>
+__device__ __forceinline__ void down_store_combine_impl(const ExpArgs &a, const TileInfo &ti, int rb,
+                                                        const float (&C)[NT8][4], int lane, SlotOf slot_of,
+                                                        WeightOf weight_of) {
+    const int gq = lane >> 2, d = a.d, k = a.k, RB = d >> 4;
     const int r0 = rb * 16 + gq, r1 = r0 + 8;
 #pragma unroll
     for (int j = 0; j < NT8; ++j)
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
-            const int slot = tile_slot(a, ti, j * 8 + 2 * c + hf);
+            const int slot = slot_of(j, hf);
             if (slot >= 0) {
-                const int e_raw = a.idx[slot];
-                const float wsl = (e_raw >= 0 && e_raw < a.E) ? a.wts[slot] : 0.f;
+                const float wsl = weight_of(j, hf, slot);
                 float v0 = C[j][hf], v1 = C[j][2 + hf];
                 if (a.bd) {
                     v0 += a.bd[(size_t)ti.e * d + r0];
@@ -259,6 +309,25 @@ __device__ __forceinline__ void down_store_combine(const ExpArgs &a, const TileI
         }
         if (lane == 0) a.ycnt[(size_t)t * RB + rb] = 0u;
     }
+}
+
+template <int NT8>
+__device__ __forceinline__ void down_store_combine(const ExpArgs &a, const TileInfo &ti, int rb,
+                                                   const float (&C)[NT8][4], int lane) {
+    down_store_combine_impl<NT8>(
+        a, ti, rb, C, lane, [&](int j, int hf) { return tile_slot(a, ti, j * 8 + 2 * (lane & 3) + hf); },
+        [&](int, int, int slot) {
+            const int e_raw = a.idx[slot];
+            return (e_raw >= 0 && e_raw < a.E) ? a.wts[slot] : 0.f;
+        });
+}
+// the same with the slot ids and weights loaded ahead (epi_slots, epi_weights)
+template <int NT8>
+__device__ __forceinline__ void down_store_combine_sl(const ExpArgs &a, const TileInfo &ti, int rb,
+                                                      const float (&C)[NT8][4], int lane, const int (&sl)[NT8][2],
+                                                      const float (&wv)[NT8][2]) {
+    down_store_combine_impl<NT8>(
+        a, ti, rb, C, lane, [&](int j, int hf) { return sl[j][hf]; }, [&](int j, int hf, int) { return wv[j][hf]; });
 }
 
 }  // namespace moeb

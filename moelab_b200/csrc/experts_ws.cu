@@ -160,23 +160,33 @@ __global__ void __launch_bounds__(32 * (RBC + 1), MB) k_experts_ws(const __grid_
     }
 
     // ---------------------------------------------------------------- consumer warps (one row block each)
+    // Global metadata is loaded ahead of its use, so no dependent global load sits between two stages: the next
+    // item's tile record during this item and, for tiles of up to 16 slots (EARLY; 24 would spill), the epilogue's
+    // slot ids at the item's first stage and (down) the combine weights at its second.
+    constexpr bool EARLY = NT8 <= 2;
     const int gq = lane >> 2, c = lane & 3;
     float C0[NT8][4], C1[NT8][4];
+    int sl[NT8][2];
+    float wv[NT8][2];
     TileInfo ti;
     int rb = 0;
+    int4 tr_next = my_su > 0 ? tile_rec(a, (int)blockIdx.x / RBS) : make_int4(0, 0, 0, 0);
     for (int k = 0; k < total; ++k) {
         const int slot = k % NS;
         const int su = (int)blockIdx.x + (k / SPU) * (int)gridDim.x;
         const int tile = su / RBS;
         const int g0 = (k % SPU) * SG, ng = min(SG, G - g0);
         if (g0 == 0) {
-            ti = tile_info(a, tile);
+            ti = tile_info_of(a, tr_next);
+            if (su + (int)gridDim.x < n_su) tr_next = tile_rec(a, (su + (int)gridDim.x) / RBS);
             rb = (su - tile * RBS) * RBC + warp;
+            if (EARLY) epi_slots<NT8>(a, ti, lane, sl);
 #pragma unroll
             for (int j = 0; j < NT8; ++j)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) C0[j][i] = C1[j][i] = 0.f;
         }
+        if (EARLY && DOWN && k % SPU == (SPU > 1 ? 1 : 0)) epi_weights<NT8>(a, sl, wv);
         if (!mbar_wait_bounded(full + slot, (unsigned)((k / NS) & 1))) {
             if (lane == 0) atomicOr(a.err, ERR_TIMEOUT);
             // give the copies that may still be in flight into this CTA's ring a bounded chance to land
@@ -233,11 +243,15 @@ __global__ void __launch_bounds__(32 * (RBC + 1), MB) k_experts_ws(const __grid_
         __syncwarp();
         if (lane == 0) mbar_arrive(empty + slot);
         if (k % SPU == SPU - 1 && rb < RB) {
+            if (!EARLY) {
+                epi_slots<NT8>(a, ti, lane, sl);
+                if (DOWN) epi_weights<NT8>(a, sl, wv);
+            }
             if (DOWN) {
-                down_store_combine<NT8>(a, ti, rb, C0, lane);
+                down_store_combine_sl<NT8>(a, ti, rb, C0, lane, sl, wv);
             } else {
 #pragma unroll
-                for (int j = 0; j < NT8; ++j) gate_up_store<NT8>(a, ti, rb, j, C0[j], C1[j], lane);
+                for (int j = 0; j < NT8; ++j) gate_up_store_sl(a, ti, rb, sl[j], C0[j], C1[j], lane);
             }
         }
     }
