@@ -54,6 +54,9 @@ def parse():
     ap.add_argument("--profile-config", default="", help="run 3 eager layer calls of the CONFIGS entry whose name "
                     "starts with this (for ncu captures of one kernel) and exit")
     ap.add_argument("--profile-tokens", type=int, default=1024)
+    ap.add_argument("--probe-tc", action="store_true", help="print the tcgen05 issue-rate table (MMA shapes of the "
+                    "expert kernels: N, issuing threads, MMAs between barrier waits) and mma.sync for comparison, "
+                    "then exit")
     ap.add_argument("--profile-policy", default="", help="pin the expert kernels for --profile-config (slots, "
                     "tiles8, tiles16, ring8, ring16, tc, decode; default: the load-based dispatcher)")
     return ap.parse_args()
@@ -705,6 +708,27 @@ def run_reference(a, ws, rank):
     print(json.dumps(line), flush=True)
 
 
+def probe_tc():
+    """One JSON line per case of moeb_probe_tc_issue (cycles per M=128, K=16 MMA per SM; TFLOP/s over the GPU),
+    then mma.sync m16n8k16 rates. 200k MMAs per issuer per case."""
+    import ctypes
+    from moelab_b200 import _lib
+    cyc, tf = ctypes.c_double(), ctypes.c_double()
+    for n in (16, 32, 64, 128, 256):
+        for iss in (1, 2, 3, 4):
+            if iss * (64 if n <= 64 else 128 if n <= 128 else 256) > 384:
+                continue
+            for per, wait in ((16, 0), (4, 1), (16, 1)):
+                _lib.call("moeb_probe_tc_issue", n, iss, per, wait, 200000, ctypes.byref(cyc), ctypes.byref(tf))
+                print(json.dumps({"probe": "tcgen05.mma M128 K16", "N": n, "issuers": iss, "mmas_per_wait": per,
+                                  "wait": bool(wait), "cycles_per_mma_per_sm": round(cyc.value, 1),
+                                  "tflops": round(tf.value, 1)}), flush=True)
+    for w in (4, 8, 16):
+        _lib.call("moeb_probe_mma_sync", w, 20000, ctypes.byref(tf))
+        print(json.dumps({"probe": "mma.sync m16n8k16 bf16", "warps_per_sm": w, "tflops": round(tf.value, 1)}),
+              flush=True)
+
+
 def profile_config(a):
     """A few eager layer calls of one configuration: the small, self-ending workload ncu captures are taken on."""
     name, shp, kind, _ = next(c for c in CONFIGS if c[0].startswith(a.profile_config))
@@ -727,6 +751,9 @@ def profile_config(a):
 
 def main():
     a = parse()
+    if a.probe_tc:
+        probe_tc()
+        return
     if a.profile_config:
         profile_config(a)
         return
