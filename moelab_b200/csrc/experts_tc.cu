@@ -141,6 +141,31 @@ MOEB_DEV float *slot_row(const ExpArgs &a, int slot) {
                     : a.yp + (size_t)slot * a.d;
 }
 
+// The down epilogue's per-column metadata for one warp, loaded before its accumulator is ready: lane l holds, for
+// chunk q (columns c0 = c_first + q * c_step .. c0 + 15), the slot and combine weight of column c0 + (l & 15)
+// (slot -1 past the tile). Loading them per column next to the row stores serialises two dependent global-load
+// round trips per column: a load after a store that may alias it stays behind that store.
+template <int NCH>
+MOEB_DEV void down_epi_meta(const ExpArgs &a, const int4 tr, int c_first, int c_step, int lane, int (&msl)[NCH],
+                            float (&mw)[NCH]) {
+#pragma unroll
+    for (int q = 0; q < NCH; ++q) {
+        const int n = c_first + q * c_step + (lane & 15);
+        msl[q] = n < tr.z ? a.sorted[tr.y + n] : -1;
+    }
+#pragma unroll
+    for (int q = 0; q < NCH; ++q) {
+        const int s = msl[q];
+        float w = 0.f;
+        if (s >= 0) {
+            const int e_raw = a.idx[s];
+            const float wt = a.wts[s];
+            w = (e_raw >= 0 && e_raw < a.E) ? wt : 0.f;
+        }
+        mw[q] = w;
+    }
+}
+
 // k order of the tensor-core operands inside a 64-group when A lives in TMEM (see k_experts_tca)
 MOEB_DEV int kperm64(int k) { return (k & ~63) | (((k >> 2) & 3) << 4) | (((k >> 4) & 3) << 2) | (k & 3); }
 
@@ -398,6 +423,10 @@ __global__ void __launch_bounds__(TCL<FMT, NT, NR, NA, NX, ACC, DOWN>::THREADS, 
             const int4 tr = a.tiles[tile];
             const int e = (tr.x < 0 || tr.x >= a.E) ? 0 : tr.x;
             const int b = it % ACC;
+            constexpr int NCH = DOWN ? NT / (16 * HALVES) : 1;
+            int msl[NCH];
+            float mw[NCH];
+            if (DOWN) down_epi_meta<NCH>(a, tr, 16 * half, 16 * HALVES, lane, msl, mw);
             if (!mbar_wait_bounded(accf + b, (unsigned)((it / ACC) & 1))) {
                 if (lane == 0) atomicOr(a.err, timeout_err);
                 break;
@@ -421,18 +450,17 @@ __global__ void __launch_bounds__(TCL<FMT, NT, NR, NA, NX, ACC, DOWN>::THREADS, 
                 }
             } else {
                 const float bdr = a.bd ? a.bd[(size_t)e * a.d + row] : 0.f;
-                for (int c0 = 16 * half; c0 < tr.z; c0 += 16 * HALVES) {
+#pragma unroll
+                for (int q = 0; q < NCH; ++q) {
+                    const int c0 = 16 * half + q * 16 * HALVES;
+                    if (c0 >= tr.z) break;
                     float dv[16];
                     tmem_ld16(tl + (uint32_t)(b * NT + c0), dv);
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        const int n = c0 + j;
-                        if (n < tr.z) {
-                            const int slot = a.sorted[tr.y + n];
-                            const int e_raw = a.idx[slot];
-                            const float wsl = (e_raw >= 0 && e_raw < a.E) ? a.wts[slot] : 0.f;
-                            slot_row(a, slot)[row] = wsl * (dv[j] + bdr);
-                        }
+                        const int slot = __shfl_sync(0xffffffffu, msl[q], j);
+                        const float wsl = __shfl_sync(0xffffffffu, mw[q], j);
+                        if (c0 + j < tr.z) slot_row(a, slot)[row] = wsl * (dv[j] + bdr);
                     }
                 }
             }
@@ -716,6 +744,10 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN, SGK>::THREADS,
             const int4 tr = a.tiles[tile];
             const int e = (tr.x < 0 || tr.x >= a.E) ? 0 : tr.x;
             const int b = it % ACC;
+            constexpr int NCH = DOWN ? NT / (16 * HALVES) : 1;
+            int msl[NCH];
+            float mw[NCH];
+            if (DOWN) down_epi_meta<NCH>(a, tr, 16 * half, 16 * HALVES, lane, msl, mw);
             if (!mbar_wait_bounded(accf + b, (unsigned)((it / ACC) & 1))) {
                 if (lane == 0) atomicOr(a.err, timeout_err);
                 break;
@@ -738,18 +770,17 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN, SGK>::THREADS,
                 }
             } else {
                 const float bdr = a.bd ? a.bd[(size_t)e * a.d + row] : 0.f;
-                for (int c0 = 16 * half; c0 < tr.z; c0 += 16 * HALVES) {
+#pragma unroll
+                for (int q = 0; q < NCH; ++q) {
+                    const int c0 = 16 * half + q * 16 * HALVES;
+                    if (c0 >= tr.z) break;
                     float dv[16];
                     tmem_ld16(tl + (uint32_t)(b * NT + c0), dv);
 #pragma unroll
                     for (int jj = 0; jj < 16; ++jj) {
-                        const int n = c0 + jj;
-                        if (n < tr.z) {
-                            const int slot = a.sorted[tr.y + n];
-                            const int e_raw = a.idx[slot];
-                            const float wsl = (e_raw >= 0 && e_raw < a.E) ? a.wts[slot] : 0.f;
-                            slot_row(a, slot)[row] = wsl * (dv[jj] + bdr);
-                        }
+                        const int slot = __shfl_sync(0xffffffffu, msl[q], jj);
+                        const float wsl = __shfl_sync(0xffffffffu, mw[q], jj);
+                        if (c0 + jj < tr.z) slot_row(a, slot)[row] = wsl * (dv[jj] + bdr);
                     }
                 }
             }
