@@ -52,13 +52,13 @@ def parse():
                     "Qwen3-235B-shaped layers, experts split over the N GPUs; N = 1 runs the same code on one GPU) at "
                     "these tokens per GPU ('' = none)")
     ap.add_argument("--profile-config", default="", help="run 3 eager layer calls of the CONFIGS entry whose name "
-                    "starts with this (for ncu captures of one kernel) and exit")
+                    "starts with this, or of the headline layer ('qwen3-30b'), for ncu captures of one kernel, and exit")
     ap.add_argument("--profile-tokens", type=int, default=1024)
     ap.add_argument("--probe-tc", action="store_true", help="print the tcgen05 issue-rate table (MMA shapes of the "
                     "expert kernels: N, issuing threads, MMAs between barrier waits) and mma.sync for comparison, "
                     "then exit")
     ap.add_argument("--profile-policy", default="", help="pin the expert kernels for --profile-config (slots, "
-                    "tiles8, tiles16, ring8, ring16, tc, decode; default: the load-based dispatcher)")
+                    "tiles8, tiles16, ring8, ring16, ring24, tc, decode; default: the load-based dispatcher)")
     return ap.parse_args()
 
 
@@ -731,12 +731,14 @@ def probe_tc():
 
 def profile_config(a):
     """A few eager layer calls of one configuration: the small, self-ending workload ncu captures are taken on."""
-    name, shp, kind, _ = next(c for c in CONFIGS if c[0].startswith(a.profile_config))
+    headline = ("qwen3-30b-a3b int4 (headline layer)", dict(d=D, f=F, E=E, k=K_TOP), "q4", [])
+    name, shp, kind, _ = next(c for c in [headline] + CONFIGS if c[0].startswith(a.profile_config))
     if a.profile_policy:
         from moelab_b200 import ops
         from moelab_b200.variants.cuda import b200_mxfp4_moe as vm, b200_q4_moe as vq
         pol = {"slots": ops.POLICY_SLOTS, "tiles8": ops.POLICY_TILES8, "tiles16": ops.POLICY_TILES16,
-               "ring8": ops.POLICY_TILES8_RING, "ring16": ops.POLICY_TILES16_RING, "tc": ops.POLICY_TC,
+               "ring8": ops.POLICY_TILES8_RING, "ring16": ops.POLICY_TILES16_RING,
+               "ring24": ops.POLICY_TILES24_RING, "tc": ops.POLICY_TC,
                "decode": ops.POLICY_DECODE}[a.profile_policy]
         vq.POLICY = vm.POLICY = pol  # the gpt-oss variant runs through vm
     layers, _ = config_layers(shp["d"], shp["f"], shp["E"], shp["k"], kind, n_layers=1)

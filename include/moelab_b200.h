@@ -53,7 +53,8 @@ typedef struct CUstream_st *cudaStream_t;
 #define MOEB_POLICY_TILES16 3 /* tiles of <= 16 slots */
 #define MOEB_POLICY_TILES8_RING 4  /* tiles of <= 8 slots, weights streamed by TMA into a per-warp ring */
 #define MOEB_POLICY_TILES16_RING 5 /* tiles of <= 16 slots, TMA ring */
-#define MOEB_POLICY_TC 6 /* tiles of <= 256 slots on tcgen05 tensor cores (d and f multiples of 128) */
+#define MOEB_POLICY_TC 6 /* tiles of 32 / 64 / 128 / 192 / 256 slots on tcgen05 tensor cores (d and f multiples of
+                            128) */
 #define MOEB_POLICY_TILES24_RING 8 /* tiles of <= 24 slots, TMA ring */
 #define MOEB_POLICY_DECODE 7 /* decode (<= 16 slots) as ONE cooperative kernel, one CTA per SM: router, gate/up,
                                 down and combine, every CTA's expert weights issued by bulk copies right after
@@ -75,8 +76,9 @@ size_t moeb_workspace_bytes(int T, int d, int f, int E, int k);
 int moeb_workspace_init(void *ws, size_t ws_bytes, cudaStream_t stream);
 /* Copies the sticky device error word to *out (host) and clears it. Synchronises `stream`. */
 int moeb_read_error(void *ws, unsigned *out, cudaStream_t stream);
-/* Policy the dispatcher picks for AUTO (host-only, no device work) for a layer whose d and f are multiples of 128
- * (other shapes get MOEB_POLICY_TILES16_RING where this returns MOEB_POLICY_TC). */
+/* Policy the dispatcher picks for AUTO (host-only, no device work) for a layer whose d and f are multiples of 128:
+ * SLOTS up to 16 slots, then by load = T*k/E: TILES8_RING below 8, TILES16_RING below 14, TC from 14. Other
+ * shapes get TILES16_RING below 16 and TILES24_RING from 16 where this returns MOEB_POLICY_TC. */
 int moeb_policy(int T, int E, int k);
 
 /* --- quantizers: w bf16 [rows][K] -> B200 layout. Replace mx.quantize(w, group_size=64, bits=4) and

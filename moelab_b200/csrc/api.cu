@@ -155,17 +155,18 @@ int check_shape(int T, int d, int f, int E, int k) {
 int choose_policy(int T, int E, int k, int d, int f) {
     const long TK = (long)T * k;
     if (TK <= 16) return MOEB_POLICY_SLOTS;
-    if (TK >= 24L * E && d % 128 == 0 && f % 128 == 0) return MOEB_POLICY_TC;
-    if (TK >= 16L * E) return MOEB_POLICY_TILES24_RING;  // most experts fit one tile of 24 (T = 256 / 320: 214 / 241 us
-                                                          // vs 218 / 272 with tiles of 16)
+    // tcgen05 from 14 slots per expert (Qwen3-30B T = 192 / 224 / 256: 179.7 / 181.4 / 183.5 us against 172.9 /
+    // 206.5 / 216.6 with tiles of 16 and 207.5 / 211.1 / 215.9 with tiles of 24)
+    if (TK >= 14L * E && d % 128 == 0 && f % 128 == 0) return MOEB_POLICY_TC;
+    if (TK >= 16L * E) return MOEB_POLICY_TILES24_RING;  // shapes the tcgen05 kernels do not take
     return TK >= 8L * E ? MOEB_POLICY_TILES16_RING : MOEB_POLICY_TILES8_RING;
 }
 
-// tcgen05 tile size: the power of two from 32 to 256 at or above 1.5 x the average expert's slots, so that most
-// experts fit one tile (weights are dequantized once per tile; a second, partial tile reads them again).
+// tcgen05 tile size: the smallest of 32, 64, 128, 192, 256 at or above 1.5 x the average expert's slots, so that
+// most experts fit one tile (weights are dequantized once per tile; a second, partial tile reads them again).
 int tc_nt(long TK, int E) {
     const long load = TK / std::max(E, 1), need = load + load / 2;
-    return need > 128 ? 256 : need > 64 ? 128 : need > 32 ? 64 : 32;
+    return need > 192 ? 256 : need > 128 ? 192 : need > 64 ? 128 : need > 32 ? 64 : 32;
 }
 
 int nt_of(int policy, long TK, int E) {
@@ -443,15 +444,25 @@ bool router_tiled(int T, int E) {
     return E >= 32 ? (long)T * E >= 16384 : T >= 4096;
 }
 
-template <int EW>
+template <int TW, int EW>
 void (*router_t_kernel(int E))(RouterArgs) {
     const int J = (E + 31) / 32;
-    if (J <= 1) return k_router_t<4, EW, 1>;
-    if (J <= 2) return k_router_t<4, EW, 2>;
-    if (J <= 4) return k_router_t<4, EW, 4>;
-    if (J <= 8) return k_router_t<4, EW, 8>;
-    if (J <= 16) return k_router_t<4, EW, 16>;
-    return k_router_t<4, EW, 32>;
+    if (J <= 1) return k_router_t<TW, EW, 1>;
+    if (J <= 2) return k_router_t<TW, EW, 2>;
+    if (J <= 4) return k_router_t<TW, EW, 4>;
+    if (J <= 8) return k_router_t<TW, EW, 8>;
+    if (J <= 16) return k_router_t<TW, EW, 16>;
+    return k_router_t<TW, EW, 32>;
+}
+
+// Tokens per warp of the register-tiled router with 4 experts per warp: 8 from T = MOEB_ROUTER_TW8_T (default
+// 512), else 4.
+int router_tw(int T) {
+    static const int v = [] {
+        const char *s = getenv("MOEB_ROUTER_TW8_T");
+        return s ? atoi(s) : 512;
+    }();
+    return T >= v ? 8 : 4;
 }
 
 // E, k: routed experts / slots; ns shared experts follow as ids E .. E + ns - 1 (slots per token k + ns).
@@ -485,9 +496,10 @@ int launch_router(const void *x, const void *wg, const void *bias, int T, int d,
     // warp, EW = 4 from 32 experts on)
     cudaError_t e;
     if (tiled) {
-        const int ew = E >= 32 ? 4 : E >= 16 ? 2 : 1;
-        void (*kern)(RouterArgs) = ew == 4 ? router_t_kernel<4>(E) : ew == 2 ? router_t_kernel<2>(E) : router_t_kernel<1>(E);
-        e = launch(kern, dim3((E + 8 * ew - 1) / (8 * ew), (T + 3) / 4), dim3(256), smem, st, r);
+        const int ew = E >= 32 ? 4 : E >= 16 ? 2 : 1, tw = ew == 4 ? router_tw(T) : 4;
+        void (*kern)(RouterArgs) = ew == 4 ? (tw == 8 ? router_t_kernel<8, 4>(E) : router_t_kernel<4, 4>(E))
+                                 : ew == 2 ? router_t_kernel<4, 2>(E) : router_t_kernel<4, 1>(E);
+        e = launch(kern, dim3((E + 8 * ew - 1) / (8 * ew), (T + tw - 1) / tw), dim3(256), smem, st, r);
     } else {
         void (*kern)(RouterArgs) = tpb == 1 ? router_kernel<1, 8>(E) : router_kernel<4, 4>(E);
         e = launch(kern, dim3((E + 3) / 4, (T + tpb - 1) / tpb), dim3(128), smem, st, r);
@@ -1111,7 +1123,7 @@ static int p2p_experts(int fmt, void *const *peers, void *self, int P, int me, i
     // spread over the P owners, an owner receives about Cs rows: the load is Cs / E_local rows per expert.
     if (policy == MOEB_POLICY_AUTO)
         policy = (Cs <= 16 && (long)P * Cs <= 128) ? MOEB_POLICY_SLOTS
-                 : ((long)Cs >= 24L * E_local && d % 128 == 0 && f % 128 == 0)
+                 : ((long)Cs >= 14L * E_local && d % 128 == 0 && f % 128 == 0)
                      ? MOEB_POLICY_TC  // weights dequantized once per tile (the single-GPU dispatcher's rule)
                      : (long)Cs >= 16L * E_local ? MOEB_POLICY_TILES24_RING
                      : ((long)Cs >= 8L * E_local ? MOEB_POLICY_TILES16_RING : MOEB_POLICY_TILES8_RING);

@@ -141,6 +141,12 @@ MOEB_DEV float *slot_row(const ExpArgs &a, int slot) {
                     : a.yp + (size_t)slot * a.d;
 }
 
+// Tile record of this CTA's work item `it` (items blockIdx.x + it * gridDim.x; MT items per tile). The roles keep the
+// next item's record in flight while they work on the current one.
+MOEB_DEV int4 item_tile(const ExpArgs &a, int it, int MT) {
+    return a.tiles[((int)blockIdx.x + it * (int)gridDim.x) / MT];
+}
+
 // The down epilogue's per-column metadata for one warp, loaded before its accumulator is ready: lane l holds, for
 // chunk q (columns c0 = c_first + q * c_step .. c0 + 15), the slot and combine weight of column c0 + (l & 15)
 // (slot -1 past the tile). Loading them per column next to the row stores serialises two dependent global-load
@@ -261,10 +267,12 @@ __global__ void __launch_bounds__(TCL<FMT, NT, NR, NA, NX, ACC, DOWN>::THREADS, 
             }
             int k = 0;
             bool ok = true;
+            int4 tr_n = my_items > 0 ? item_tile(a, 0, MT) : make_int4(0, 0, 0, 0);
             for (int it = 0; it < my_items && ok; ++it) {
                 const int item = (int)blockIdx.x + it * (int)gridDim.x;
                 const int tile = item / MT, mt = item - tile * MT;
-                const int4 tr = a.tiles[tile];
+                const int4 tr = tr_n;
+                if (it + 1 < my_items) tr_n = item_tile(a, it + 1, MT);
                 const int e = (tr.x < 0 || tr.x >= a.E) ? 0 : tr.x;
                 const int row0 = e * RB + mt * 8;
                 for (int g = 0; g < G; ++g, ++k) {
@@ -295,9 +303,10 @@ __global__ void __launch_bounds__(TCL<FMT, NT, NR, NA, NX, ACC, DOWN>::THREADS, 
             tmap_prefetch(&a.tmx);
             int k = 0;
             bool ok = true;
+            int4 tr_n = my_items > 0 ? item_tile(a, 0, MT) : make_int4(0, 0, 0, 0);
             for (int it = 0; it < my_items && ok; ++it) {
-                const int item = (int)blockIdx.x + it * (int)gridDim.x;
-                const int4 tr = a.tiles[item / MT];
+                const int4 tr = tr_n;
+                if (it + 1 < my_items) tr_n = item_tile(a, it + 1, MT);
                 for (int g = 0; g < G; ++g, ++k) {
                     const int x = k % NX;
                     if (k >= NX && !mbar_wait_bounded(xempty + x, (unsigned)(((k / NX) - 1) & 1))) {
@@ -318,10 +327,11 @@ __global__ void __launch_bounds__(TCL<FMT, NT, NR, NA, NX, ACC, DOWN>::THREADS, 
         if (lane == 0) {
             int k = 0;
             bool ok = true;
+            int4 tr_n = my_items > 0 ? item_tile(a, 0, MT) : make_int4(0, 0, 0, 0);
             for (int it = 0; it < my_items && ok; ++it) {
                 const int b = it % ACC, use = it / ACC;  // accumulator set and how often it was used before
-                const int item = (int)blockIdx.x + it * (int)gridDim.x;
-                const int nslot = a.tiles[item / MT].z;
+                const int nslot = tr_n.z;
+                if (it + 1 < my_items) tr_n = item_tile(a, it + 1, MT);
                 // MMA width: the tile's slots rounded up to 16 (columns past them are never read)
                 const uint32_t idesc = idesc_bf16(TC_M, min(NT, max(16, (nslot + 15) & ~15)));
                 if (use >= 1 && !mbar_wait_bounded(acce + b, (unsigned)((use - 1) & 1))) {
@@ -578,10 +588,12 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN, SGK>::THREADS,
             }
             int k = 0;
             bool ok = true;
+            int4 tr_n = my_items > 0 ? item_tile(a, 0, MT) : make_int4(0, 0, 0, 0);
             for (int it = 0; it < my_items && ok; ++it) {
                 const int item = (int)blockIdx.x + it * (int)gridDim.x;
                 const int tile = item / MT, mt = item - tile * MT;
-                const int4 tr = a.tiles[tile];
+                const int4 tr = tr_n;
+                if (it + 1 < my_items) tr_n = item_tile(a, it + 1, MT);
                 const int e = (tr.x < 0 || tr.x >= a.E) ? 0 : tr.x;
                 const int row0 = e * RB + mt * 8;
                 for (int gs = 0; gs < GS; ++gs, ++k) {
@@ -611,9 +623,10 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN, SGK>::THREADS,
             tmap_prefetch(&a.tmx);
             int k = 0;
             bool ok = true;
+            int4 tr_n = my_items > 0 ? item_tile(a, 0, MT) : make_int4(0, 0, 0, 0);
             for (int it = 0; it < my_items && ok; ++it) {
-                const int item = (int)blockIdx.x + it * (int)gridDim.x;
-                const int4 tr = a.tiles[item / MT];
+                const int4 tr = tr_n;
+                if (it + 1 < my_items) tr_n = item_tile(a, it + 1, MT);
                 for (int gs = 0; gs < GS; ++gs, ++k) {
                     const int s = k % NS;
                     if (k >= NS && !mbar_wait_bounded(oempty + s, (unsigned)(((k / NS) - 1) & 1))) {
@@ -636,10 +649,11 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN, SGK>::THREADS,
         if (lane == 0) {
             int k = 0;
             bool ok = true;
+            int4 tr_n = my_items > 0 ? item_tile(a, 0, MT) : make_int4(0, 0, 0, 0);
             for (int it = 0; it < my_items && ok; ++it) {
                 const int b = it % ACC, use = it / ACC;
-                const int item = (int)blockIdx.x + it * (int)gridDim.x;
-                const int nslot = a.tiles[item / MT].z;
+                const int nslot = tr_n.z;
+                if (it + 1 < my_items) tr_n = item_tile(a, it + 1, MT);
                 const uint32_t idesc = idesc_bf16(TC_M, min(NT, max(16, (nslot + 15) & ~15)));
                 if (use >= 1 && !mbar_wait_bounded(acce + b, (unsigned)((use - 1) & 1))) {
                     atomicOr(a.err, timeout_err);
@@ -800,15 +814,17 @@ __global__ void __launch_bounds__(TAL<FMT, NT, NR, NS, ACC, DOWN, SGK>::THREADS,
 }
 
 // Configurations. TMEM-operand kernels (k_experts_tca) wherever their accumulators and A stages fit the 512
-// TMEM columns: gate/up tiles of 32 / 64 / 128 slots, down tiles of 32 .. 256. Gate/up tiles of 256 need all 512
-// columns for the two accumulators and keep A in shared memory (k_experts_tc). Raw and operand rings are as deep
+// TMEM columns: gate/up tiles of 32 / 64 / 128 / 192 slots (192: one accumulator set of 2 x 192 columns and two
+// single-group A stages fill the 512), down tiles of 32 .. 256. Gate/up tiles of 256 need all 512 columns for the
+// two accumulators and keep A in shared memory (k_experts_tc). Raw and operand rings are as deep
 // as the 227 KB of shared memory allow.
 //   tca: (NT, NR, NS, ACC, DOWN, SGK): SGK 64-groups per stage (two halve the per-stage barrier, TMEM-store and
 //   MMA-issue latencies per group and fetch 1 KB code rows per copy); down tiles of 256 keep one, as their
 //   64 KB activation stages leave no room for a deep raw ring
 #define MOEB_TCA_CFGS(X) \
-    X(32, 10, 3, 2, false, 2) X(64, 10, 2, 2, false, 2) X(128, 8, 2, 1, false, 2) \
-    X(32, 16, 6, 2, true, 2) X(64, 12, 6, 2, true, 2) X(128, 10, 4, 2, true, 2) X(256, 16, 4, 1, true, 1)
+    X(32, 10, 3, 2, false, 2) X(64, 10, 2, 2, false, 2) X(128, 8, 2, 1, false, 2) X(192, 16, 2, 1, false, 1) \
+    X(32, 16, 6, 2, true, 2) X(64, 12, 6, 2, true, 2) X(128, 10, 4, 2, true, 2) X(192, 16, 4, 2, true, 1) \
+    X(256, 16, 4, 1, true, 1)
 
 TcInfo experts_tc_info(int fmt, int nt, bool down) {
     TcInfo r = {nullptr, 0, 0, false, 1};

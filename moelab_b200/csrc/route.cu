@@ -270,7 +270,7 @@ template <int TW, int EW, int JMAX>
 __global__ void __launch_bounds__(256) k_router_t(RouterArgs a) {
     pdl_launch();
     pdl_wait();
-    constexpr int U = 2;
+    constexpr int U = TW * EW >= 32 ? 1 : 2;  // chunks loaded per lane per step (registers: 8 x 4 tiles keep one)
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int e0 = (blockIdx.x * 8 + warp) * EW;
     const int t0 = blockIdx.y * TW;
@@ -432,5 +432,12 @@ MOEB_ROUTER_T_INST(1)
 MOEB_ROUTER_T_INST(2)
 MOEB_ROUTER_T_INST(4)
 #undef MOEB_ROUTER_T_INST
+// 8 tokens x 4 experts per warp (large T: each gate chunk loaded from L2 serves twice the tokens)
+template __global__ void k_router_t<8, 4, 1>(RouterArgs);
+template __global__ void k_router_t<8, 4, 2>(RouterArgs);
+template __global__ void k_router_t<8, 4, 4>(RouterArgs);
+template __global__ void k_router_t<8, 4, 8>(RouterArgs);
+template __global__ void k_router_t<8, 4, 16>(RouterArgs);
+template __global__ void k_router_t<8, 4, 32>(RouterArgs);
 
 }  // namespace moeb

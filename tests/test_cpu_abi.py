@@ -60,8 +60,9 @@ def test_host_only_calls():
     assert lib.moeb_policy(2, 128, 8) == _lib.POLICY_SLOTS
     assert lib.moeb_policy(4, 128, 8) == _lib.POLICY_TILES8_RING
     assert lib.moeb_policy(128, 128, 8) == _lib.POLICY_TILES16_RING  # 8 slots per expert
-    assert lib.moeb_policy(256, 128, 8) == _lib.POLICY_TILES24_RING  # 16 slots per expert
-    assert lib.moeb_policy(384, 128, 8) == _lib.POLICY_TC  # 24 slots per expert: tcgen05 tiles
+    assert lib.moeb_policy(192, 128, 8) == _lib.POLICY_TILES16_RING  # 12 slots per expert
+    assert lib.moeb_policy(224, 128, 8) == _lib.POLICY_TC  # 14 slots per expert: tcgen05 tiles
+    assert lib.moeb_policy(384, 128, 8) == _lib.POLICY_TC
 
 
 def test_bad_shape_is_rejected_before_any_device_work():

@@ -133,10 +133,10 @@ def test_mixtral(mixtral, fmt, routing, T):
 
 
 # ------------------------------------------------------------------ tensor-core policy (tcgen05, tiles of 32..256)
-# E = 8, k = 2: T = 1, 3, 64 -> tiles of 32 slots, 200 -> 64, 300 / 513 -> 128, 600 -> 256
+# E = 8, k = 2: T = 1, 3, 64 -> tiles of 32 slots, 200 -> 64, 300 -> 128, 480 / 513 -> 192, 600 -> 256
 @pytest.mark.parametrize("T,routing", [(1, "uniform"), (3, "uniform"), (64, "uniform"), (200, "uniform"),
-                                       (200, "one_hot"), (300, "uniform"), (300, "one_hot"), (513, "zipf"),
-                                       (600, "uniform"), (600, "one_hot")])
+                                       (200, "one_hot"), (300, "uniform"), (300, "one_hot"), (480, "uniform"),
+                                       (480, "one_hot"), (513, "zipf"), (600, "uniform"), (600, "one_hot")])
 def test_tc_small_vs_oracle(T, routing):
     """tcgen05 tiles of every size: partial tiles, several tiles per expert, empty experts."""
     from helpers import problem_tensors
@@ -195,7 +195,7 @@ def test_tc_mixtral_mxfp4(mixtral, T):
     assert_close(y, torch_ref(b200_mxfp4_moe, st, x, it, wt, deq), what=T)
 
 
-@pytest.mark.parametrize("T", [3, 200, 300, 600])
+@pytest.mark.parametrize("T", [3, 200, 300, 480, 600])
 def test_tc_small_mxfp4(T):
     """MXFP4 on the tensor cores (E2M1 x 2^(S-127) dequantized exactly to bf16) for each tile size."""
     from helpers import problem_tensors

@@ -124,17 +124,35 @@ print("ok")
 """
 
 
-def test_router_tiled_kernel_every_variant():
+@pytest.mark.parametrize("tw8_from", ["1000000", "1"])
+def test_router_tiled_kernel_every_variant(tw8_from):
     """The register-tiled router (normally from T * E >= 16384) forced on for every T: 1, 2 and 4 experts per
-    warp, partial token blocks, bias; bit-exact logits and ids."""
+    warp, 4 or 8 tokens per warp (8 is normally used from T = 512), partial token blocks, bias; bit-exact logits
+    and ids."""
     import os
     import subprocess
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    env = dict(os.environ, MOEB_ROUTER_TILED_T="1")
+    env = dict(os.environ, MOEB_ROUTER_TILED_T="1", MOEB_ROUTER_TW8_T=tw8_from)
     r = subprocess.run([sys.executable, "-c", _TILED_ROUTER_CHECK.format(root=root)], env=env, capture_output=True,
                        text=True, timeout=600)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-2000:]
+
+
+@pytest.mark.parametrize("E,k", [(32, 4), (128, 8), (256, 8)])
+@pytest.mark.parametrize("T", [517, 1029])
+def test_router_bit_exact_large_T(E, k, T):
+    """Large T (the register-tiled router with 8 tokens per warp, partial last token block): bit-exact logits and
+    ids against the oracle."""
+    g = torch.Generator(device="cuda").manual_seed(E * 7 + T)
+    x = torch.randn(T, 2048, generator=g, device="cuda").to(torch.bfloat16)
+    wg = (torch.randn(E, 2048, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    idx, wts, lg = ops.router(x, wg, k, return_logits=True)
+    ref_lg = oracle.router_logits(x, wg)
+    np.testing.assert_array_equal(lg.cpu().numpy(), ref_lg)
+    ref_i, ref_w = oracle.topk(ref_lg, k)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ref_i)
+    np.testing.assert_allclose(wts.cpu().numpy(), ref_w, rtol=2e-6, atol=1e-7)
 
 
 @pytest.mark.parametrize("E,k", [(16, 6), (60, 4), (64, 6), (128, 8)])
