@@ -713,16 +713,29 @@ def probe_tc():
     then mma.sync m16n8k16 rates. 200k MMAs per issuer per case."""
     import ctypes
     from moelab_b200 import _lib
-    cyc, tf = ctypes.c_double(), ctypes.c_double()
-    for n in (16, 32, 64, 128, 256):
-        for iss in (1, 2, 3, 4):
-            if iss * (64 if n <= 64 else 128 if n <= 128 else 256) > 384:
+    cyc, tf, sc = ctypes.c_double(), ctypes.c_double(), ctypes.c_double()
+    for n in (16, 32, 64, 128):  # MMAs beside TMEM stores (dequant warps) / loads (epilogue warps), random operands
+        for iss in (1, 2, 4):
+            if iss * (64 if n <= 64 else 128) > 384:
                 continue
-            for per, wait in ((16, 0), (4, 1), (16, 1)):
-                _lib.call("moeb_probe_tc_issue", n, iss, per, wait, 200000, ctypes.byref(cyc), ctypes.byref(tf))
-                print(json.dumps({"probe": "tcgen05.mma M128 K16", "N": n, "issuers": iss, "mmas_per_wait": per,
-                                  "wait": bool(wait), "cycles_per_mma_per_sm": round(cyc.value, 1),
-                                  "tflops": round(tf.value, 1)}), flush=True)
+            for side in (1, 2, 3):
+                _lib.call("moeb_probe_tc_issue", n, iss, 16, 1, 1, side, 200000, ctypes.byref(cyc), ctypes.byref(tf),
+                          ctypes.byref(sc))
+                print(json.dumps({"probe": "tcgen05.mma M128 K16 beside " + ("TMEM stores", "TMEM loads", "ALU work")[side - 1],
+                                  "N": n, "issuers": iss, "cycles_per_mma_per_sm": round(cyc.value, 1),
+                                  "side_cycles_per_op_per_warp": round(sc.value, 1)}), flush=True)
+    for data in (0, 1):
+        for n in (16, 32, 64, 128, 256):
+            for iss in (1, 2, 3, 4):
+                if iss * (64 if n <= 64 else 128 if n <= 128 else 256) > 384:
+                    continue
+                for per, wait in ((16, 0), (4, 1), (16, 1)):
+                    _lib.call("moeb_probe_tc_issue", n, iss, per, wait, data, 0, 200000, ctypes.byref(cyc),
+                              ctypes.byref(tf), None)
+                    print(json.dumps({"probe": "tcgen05.mma M128 K16", "operands": "random" if data else "zero",
+                                      "N": n, "issuers": iss, "mmas_per_wait": per, "wait": bool(wait),
+                                      "cycles_per_mma_per_sm": round(cyc.value, 1), "tflops": round(tf.value, 1)}),
+                          flush=True)
     for w in (4, 8, 16):
         _lib.call("moeb_probe_mma_sync", w, 20000, ctypes.byref(tf))
         print(json.dumps({"probe": "mma.sync m16n8k16 bf16", "warps_per_sm": w, "tflops": round(tf.value, 1)}),

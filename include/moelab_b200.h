@@ -237,11 +237,13 @@ int moeb_ep_p2p_read_error(void *self, int P, int C, int d, unsigned *out, cudaS
  * moeb_probe_tc_issue: one CTA per SM; `issuers` (1..4) warps each issue back-to-back tcgen05.mma of M = 128,
  * K = 16, N = n (16..256, multiple of 16; 4 issuers need n <= 64, 3 need n <= 128, n > 128 allows one), A in TMEM,
  * into their own accumulators, `per_stage` (4, 8 or 16) MMAs between waits (wait != 0) on an already completed
- * mbarrier phase, `mmas_per_issuer` MMAs each. Out: clock cycles per MMA per SM (all issuers' MMAs together) and
- * TFLOP/s over the GPU from CUDA events. moeb_probe_mma_sync: the same for mma.sync m16n8k16 bf16 over
- * independent chains, warps_per_sm warps per SM. */
-int moeb_probe_tc_issue(int n, int issuers, int per_stage, int wait, int mmas_per_issuer, double *cycles_per_mma,
-                        double *tflops);
+ * mbarrier phase, `mmas_per_issuer` MMAs each; operands zero, or random bf16 (data != 0); side 1 / 2 / 3: four
+ * more warps meanwhile keep storing to / loading from other TMEM columns (tcgen05.st 16x256b.x4 / tcgen05.ld
+ * 32x32b.x16, each followed by its wait) or run integer ALU chains. Out: clock cycles per MMA per SM (all issuers' MMAs together), TFLOP/s
+ * over the GPU from CUDA events, and cycles per side operation per side warp (may be null). moeb_probe_mma_sync:
+ * the same for mma.sync m16n8k16 bf16 over independent chains, warps_per_sm warps per SM. */
+int moeb_probe_tc_issue(int n, int issuers, int per_stage, int wait, int data, int side, int mmas_per_issuer,
+                        double *cycles_per_mma, double *tflops, double *side_cycles_per_op);
 int moeb_probe_mma_sync(int warps_per_sm, int iters, double *tflops);
 
 /* --- moeb_experts_q4 for callers that cannot allocate device memory. No counterpart in the reference (moe-lab

@@ -60,7 +60,7 @@ SIGNATURES = {
     "moeb_ep_p2p_combine": (_I, [_P, _P] + [_I] * 5 + [_P, _P, _P]),
     "moeb_ep_p2p_set_wait_limit": (_I, [_P, _I, _I, _I, ctypes.c_double, _P]),
     "moeb_ep_p2p_read_error": (_I, [_P, _I, _I, _I, ctypes.POINTER(ctypes.c_uint), _P]),
-    "moeb_probe_tc_issue": (_I, [_I] * 5 + [ctypes.POINTER(ctypes.c_double)] * 2),
+    "moeb_probe_tc_issue": (_I, [_I] * 7 + [ctypes.POINTER(ctypes.c_double)] * 3),
     "moeb_probe_mma_sync": (_I, [_I, _I, ctypes.POINTER(ctypes.c_double)]),
 }
 
