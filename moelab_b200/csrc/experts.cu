@@ -286,7 +286,7 @@ __global__ void __launch_bounds__(128) k_down_tiles_reg(ExpArgs a) {
     }
 }
 
-template __global__ void k_gate_up_slots<FMT_Q4, 8, 4>(ExpArgs);
+template __global__ void k_gate_up_slots<FMT_Q4, 4, 8>(ExpArgs);
 template __global__ void k_down_slots<FMT_Q4, 4, 4>(ExpArgs);
 template __global__ void k_gate_up_slots<FMT_FP4, 8, 4>(ExpArgs);
 template __global__ void k_down_slots<FMT_FP4, 4, 4>(ExpArgs);
