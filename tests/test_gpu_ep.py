@@ -157,13 +157,41 @@ def test_emulated_ep_gptoss_mxfp4_bit_exact(pol):
         assert torch.equal(y, ys)
 
 
+def _back_region(xch):
+    """(device address, rows) of an exchange buffer's return rows [P][C][d] fp32 (the layout of
+    moeb_ep_p2p_bytes: 256 bytes of flags and counters, per-source flags / counts / return flags padded to 256,
+    the dispatched rows [P][C][d + 8] bf16, then the return rows)."""
+    up = lambda v: (v + 255) & ~255  # noqa: E731
+    P, C, d = xch.P, xch.C, xch.d
+    rows_off = 256 + 3 * up(4 * P)
+    back_off = rows_off + up(P * C * (d + 8) * 2)
+    return xch.base + back_off, P * C
+
+
+def _fill_back(xch, byte):
+    from cuda.bindings import runtime as rt
+    ptr, n = _back_region(xch)
+    assert rt.cudaMemset(ptr, byte, n * xch.d * 4)[0] == rt.cudaError_t.cudaSuccess
+
+
+def _read_back(xch):
+    from cuda.bindings import runtime as rt
+    ptr, n = _back_region(xch)
+    out = np.empty((n, xch.d), np.float32)
+    err = rt.cudaMemcpy(out.ctypes.data, ptr, out.nbytes, rt.cudaMemcpyKind.cudaMemcpyDeviceToHost)[0]
+    assert err == rt.cudaError_t.cudaSuccess
+    return out
+
+
 # ------------------------------------------------------------------ tensor-core expert kernels, explicitly requested
 @pytest.mark.parametrize("P,tokens", [(2, [40, 33]), (4, [17, 0, 64, 9])])
 def test_ep_tc_policy_vs_oracle(P, tokens):
-    """The tcgen05 kernels serving expert-parallel rows (explicit policy; the dispatcher does not pick them for
-    expert parallelism yet): rows with their 16-byte tails gathered in expert order, slot outputs stored into the
+    """The tcgen05 kernels serving expert-parallel rows (explicit policy here; the dispatcher picks them from 14
+    rows per local expert): rows with their 16-byte tails gathered in expert order, slot outputs stored into the
     owners' return blocks (peer memory, emulated phase by phase) or the caller's rows (NCCL path, emulated by
-    threads). Against the fp64 oracle on the dequantized weights."""
+    threads). Against the fp64 oracle on the dequantized weights. Peer memory: blocks are only partly filled
+    (C above every rank's rows) and one rank sends nothing; every return row that no slot maps to keeps the
+    sentinel written before the experts ran."""
     E, d, f, k = 32, 256, 384, 4
     w, gate = _layer(E, d, f, seed=300 + P)
     full = b200_q4_moe.prepare(*w)
@@ -184,8 +212,19 @@ def test_ep_tc_policy_vs_oracle(P, tokens):
             for r in range(P):
                 idx, wts = ops.router(xs[r], gate, k)
                 routing.append((idx, wts, ops.ep_p2p_dispatch(xs[r], idx, wts, E, xchs[r])))
+            torch.cuda.synchronize()
+            for r in range(P):
+                _fill_back(xchs[r], 0xFF)  # NaN sentinel in every return row
             for r in range(P):
                 ops.ep_p2p_experts(states[r], xchs[r], policy=ops.POLICY_TC)
+            torch.cuda.synchronize()
+            for r in range(P):  # only the rows this rank's slots map to were written
+                back = _read_back(xchs[r])
+                sp = routing[r][2].cpu().numpy().reshape(-1)
+                written = np.zeros(back.shape[0], bool)
+                written[sp[sp >= 0]] = True
+                assert np.isfinite(back[written]).all(), (call, r)
+                assert (back[~written].view(np.uint32) == 0xFFFFFFFF).all(), (call, r)
             for r in range(P):
                 idx, wts, sp = routing[r]
                 y = ops.ep_p2p_combine(xchs[r], sp, tokens[r], k, d, residual=xs[r], device="cuda")
