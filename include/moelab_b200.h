@@ -253,12 +253,15 @@ int moeb_probe_mma_sync(int warps_per_sm, int iters, double *tflops);
  * The first call on a device looks up the array's device address; make it before any stream capture. `stream`
  * must belong to the current device (the address is looked up for the current device). All
  * calls share the array: calls that overlap on the GPU (two streams, two threads) race. Device error bits are
- * cleared on entry and not readable afterwards. Nothing is allocated. */
+ * cleared on entry; moeb_experts_q4_static_read_error returns the last call's. Nothing is allocated. */
 #define MOEB_STATIC_SCRATCH_BYTES (16u << 20)
 int moeb_experts_q4_static(const void *x, const void *qg, const void *sbg, const void *qu, const void *sbu,
                            const void *qd, const void *sbd, const float *bg, const float *bu, const float *bd,
                            const int *idx, const float *wts, int T, int d, int f, int E, int k, int act, int policy,
                            const void *residual, void *y, cudaStream_t stream);
+/* The device error bits (MOEB_DEVERR_*) the last moeb_experts_q4_static call on the current device recorded, read
+ * from the static array and cleared (synchronises `stream`). No counterpart in the reference. Allocates nothing. */
+int moeb_experts_q4_static_read_error(unsigned *out, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -40,6 +40,7 @@ SIGNATURES = {
     "moeb_route_tables": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _S, _P]),
     "moeb_experts_q4": (_I, [_P] * 12 + [_I] * 7 + [_P, _P, _P, _S, _P]),
     "moeb_experts_q4_static": (_I, [_P] * 12 + [_I] * 7 + [_P, _P, _P]),
+    "moeb_experts_q4_static_read_error": (_I, [ctypes.POINTER(ctypes.c_uint), _P]),
     "moeb_layer_q4": (_I, [_P, _P, _P, _I, _F] + [_P] * 9 + [_I] * 7 + [_P, _P, _P, _P, _P, _P, _S, _P]),
     "moeb_experts_mxfp4": (_I, [_P] * 12 + [_I] * 7 + [_P, _P, _P, _S, _P]),
     "moeb_layer_mxfp4": (_I, [_P, _P, _P, _I, _F] + [_P] * 9 + [_I] * 7 + [_P, _P, _P, _P, _P, _P, _S, _P]),

@@ -88,3 +88,16 @@ extern "C" int moeb_experts_q4_static(const void *x, const void *qg, const void 
     return moeb_experts_q4(x, qg, sbg, qu, sbu, qd, sbd, bg, bu, bd, idx, wts, T, d, f, E, k, act, policy, residual,
                            y, ws, need, stream);
 }
+
+// The device error bits (MOEB_DEVERR_*) of the last moeb_experts_q4_static call on the current device: read from the
+// static array's error word and cleared, with the stream synchronised. Allocates nothing.
+extern "C" int moeb_experts_q4_static_read_error(unsigned *out, cudaStream_t stream) {
+    if (!out) {
+        moeb::set_error("out must not be null");
+        return MOEB_EINVAL;
+    }
+    int rc = MOEB_OK;
+    void *ws = scratch_address(&rc);
+    if (!ws) return rc;
+    return moeb_read_error(ws, out, stream);
+}

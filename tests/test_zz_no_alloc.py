@@ -91,3 +91,29 @@ def test_static_scratch_rejects_oversize(layer):
     wts = torch.zeros(T, SHAPE.k, dtype=torch.float32, device="cuda")
     with pytest.raises(_lib.MoebError, match="static scratch holds"):
         _call_static(st, x, idx, wts)
+
+
+def test_static_scratch_error_bits(layer):
+    """An expert id outside [0, E) is computed on expert 0 with weight 0 and recorded as MOEB_DEVERR_EXPERT_ID in the
+    static array's error word; the read returns it once and clears it, and the next clean call reads 0."""
+    import ctypes
+    st, deq = layer
+    _, _, x, idx, wts = problem_tensors(SHAPE, 4, "uniform", seed=31)
+
+    def read():
+        v = ctypes.c_uint(0)
+        _lib.call("moeb_experts_q4_static_read_error", ctypes.byref(v), ops._stream())
+        return v.value
+
+    bad = idx.clone()
+    bad[1, 2] = SHAPE.E
+    y = _call_static(st, x, bad, wts)
+    assert read() == _lib.DEVERR_EXPERT_ID
+    assert read() == 0
+    ok_w = wts.clone()
+    ok_w[1, 2] = 0.0
+    ok_i = idx.clone()
+    ok_i[1, 2] = 0
+    assert_close(y, _oracle(deq, x, ok_i, ok_w), what="invalid id weighted 0")
+    _call_static(st, x, idx, wts)
+    assert read() == 0
