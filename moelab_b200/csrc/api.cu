@@ -346,6 +346,17 @@ int grid_for(const KLaunch &k, long units) {
     return (int)std::max<long>(1, std::min(ctas, cap));
 }
 
+// Warps per slot of the token-major decode down kernel: 2 (Qwen3-30B T=1 / 2: 20.02 / 32.93 us against 20.57 /
+// 33.83 with 4, whose 1024-thread CTAs are capped at 64 registers and spill, and 20.68 / 33.30 with 1).
+// MOEB_DOWN_TOK_KS=4 selects the 4-warp kernel (measurements).
+int down_tok_ks() {
+    static const int v = [] {
+        const char *s = getenv("MOEB_DOWN_TOK_KS");
+        return s && atoi(s) == 4 ? 4 : 2;
+    }();
+    return v;
+}
+
 int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaStream_t st,
                 void *const *ev) {
     const long TK = (long)a.T * a.k;
@@ -397,8 +408,11 @@ int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaS
     // short K: each warp then runs f / 256 groups, and the CTA count is T * d / 16 rather than T * k * d / 16
     // (Mixtral, f = 14336, k = 2: 134 vs 95 us; Qwen3-30B, f = 768: 21.1 vs 23.1 us)
     if (policy == MOEB_POLICY_SLOTS && !a.slot_out && a.k <= 8 && a.f <= 2048) {
-        const KLaunch tk = {fmt == FMT_FP4 ? k_down_tok<FMT_FP4, 4, 4> : k_down_tok<FMT_Q4, 4, 4>, 128 * a.k,
-                            down_tok_smem(a.k, a.f, 4), false, 1, 0};
+        const int ks = down_tok_ks();
+        const KLaunch tk = ks == 2 ? KLaunch{fmt == FMT_FP4 ? k_down_tok<FMT_FP4, 2, 6> : k_down_tok<FMT_Q4, 2, 6>,
+                                             64 * a.k, down_tok_smem(a.k, a.f, 2), false, 1, 0}
+                                   : KLaunch{fmt == FMT_FP4 ? k_down_tok<FMT_FP4, 4, 4> : k_down_tok<FMT_Q4, 4, 4>,
+                                             128 * a.k, down_tok_smem(a.k, a.f, 4), false, 1, 0};
         if (tk.smem <= 200 * 1024) {
             if (!allow_smem((const void *)tk.fn, tk.smem)) return check_launch("cudaFuncSetAttribute");
             if (launch(tk.fn, dim3(grid_for(tk, (long)a.T * RBd)), dim3(tk.threads), tk.smem, st, a) != cudaSuccess)

@@ -51,11 +51,12 @@ __global__ void __launch_bounds__(32 * KS, FMT == FMT_FP4 ? 4 : 8) k_down_slots(
 }
 
 // Decode down with the combine in shared memory: one CTA per (token, 16-row block of d), the token's k slots as k
-// groups of KS warps. Each slot's value is computed exactly as in k_down_slots (same K split over the KS warps,
-// same reduction order, weight * (acc + bias)); the k values are then summed in slot order plus the residual, as
-// down_store_combine's last arrival does - without the global slot rows, fences and counters. k <= 32 / KS.
+// groups of KS warps. Each slot's value is computed as in k_down_slots (its K split over the KS warps, partials
+// summed in warp order, weight * (acc + bias)); the k values are then summed in slot order plus the residual, as
+// down_store_combine's last arrival does - without the global slot rows, fences and counters. k <= 32 / KS; the
+// CTA has 32 * KS * k threads (at most 256 * KS, the launch bound).
 template <int FMT, int KS, int GPW>
-__global__ void __launch_bounds__(1024, 1) k_down_tok(ExpArgs a) {
+__global__ void __launch_bounds__(256 * KS, 1) k_down_tok(ExpArgs a) {
     pdl_launch();
     pdl_wait();
     extern __shared__ uint4 tsm4[];
@@ -292,6 +293,8 @@ template __global__ void k_gate_up_slots<FMT_FP4, 8, 4>(ExpArgs);
 template __global__ void k_down_slots<FMT_FP4, 4, 4>(ExpArgs);
 template __global__ void k_down_tok<FMT_Q4, 4, 4>(ExpArgs);
 template __global__ void k_down_tok<FMT_FP4, 4, 4>(ExpArgs);
+template __global__ void k_down_tok<FMT_Q4, 2, 6>(ExpArgs);
+template __global__ void k_down_tok<FMT_FP4, 2, 6>(ExpArgs);
 template __global__ void k_gate_up_tiles_reg<FMT_FP4, 1, 2>(ExpArgs);
 template __global__ void k_down_tiles_reg<FMT_FP4, 1, 2>(ExpArgs);
 template __global__ void k_gate_up_tiles_reg<FMT_FP4, 2, 1>(ExpArgs);
