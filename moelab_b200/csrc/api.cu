@@ -357,6 +357,16 @@ int down_tok_ks() {
     return v;
 }
 
+// The decode down kernel reads its ids, weights and first weight batch before waiting for gate/up
+// (MOEB_DOWN_EARLY=0: after, for measurements).
+bool down_early() {
+    static const int v = [] {
+        const char *s = getenv("MOEB_DOWN_EARLY");
+        return s ? atoi(s) : 1;
+    }();
+    return v != 0;
+}
+
 int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaStream_t st,
                 void *const *ev) {
     const long TK = (long)a.T * a.k;
@@ -409,6 +419,7 @@ int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaS
     // (Mixtral, f = 14336, k = 2: 134 vs 95 us; Qwen3-30B, f = 768: 21.1 vs 23.1 us)
     if (policy == MOEB_POLICY_SLOTS && !a.slot_out && a.k <= 8 && a.f <= 2048) {
         const int ks = down_tok_ks();
+        a.early_ids = down_early() ? 1 : 0;
         const KLaunch tk = ks == 2 ? KLaunch{fmt == FMT_FP4 ? k_down_tok<FMT_FP4, 2, 6> : k_down_tok<FMT_Q4, 2, 6>,
                                              64 * a.k, down_tok_smem(a.k, a.f, 2), false, 1, 0}
                                    : KLaunch{fmt == FMT_FP4 ? k_down_tok<FMT_FP4, 4, 4> : k_down_tok<FMT_Q4, 4, 4>,

@@ -30,10 +30,12 @@ namespace moeb {
 // ================================================================== slot mode (decode)
 // One CTA per (slot, 16-row block); KS warps split the K groups; GPW groups per warp are loaded at once. The unit
 // bodies live in slots_common.cuh (shared with the fused decode kernel).
+// The dependents are released only after this grid's own wait: the decode down kernel then reads the ids and
+// weights (written upstream of this kernel) before it waits for h.
 template <int FMT, int KS, int GPW>
 __global__ void __launch_bounds__(32 * KS, FMT == FMT_FP4 ? 2 : 3) k_gate_up_slots(ExpArgs a) {
-    pdl_launch();
     pdl_wait();
+    pdl_launch();
     extern __shared__ uint4 xs4[];  // the slot's x row, d bf16
     __shared__ float red[KS * 2 * 4 * 32];
     for (int unit = blockIdx.x; unit < a.T * a.k * (a.f >> 4); unit += gridDim.x)
@@ -55,10 +57,13 @@ __global__ void __launch_bounds__(32 * KS, FMT == FMT_FP4 ? 4 : 8) k_down_slots(
 // summed in warp order, weight * (acc + bias)); the k values are then summed in slot order plus the residual, as
 // down_store_combine's last arrival does - without the global slot rows, fences and counters. k <= 32 / KS; the
 // CTA has 32 * KS * k threads (at most 256 * KS, the launch bound).
+// The expert ids and combine weights come from upstream of the gate/up kernel, which releases this grid only
+// after its own wait, so they are read through L2 (never a stale L1 line) before this grid waits for gate/up; the
+// first weight batch of every slot is issued before the wait too, and h after it (a.early_ids = 0: wait first).
 template <int FMT, int KS, int GPW>
 __global__ void __launch_bounds__(256 * KS, 1) k_down_tok(ExpArgs a) {
     pdl_launch();
-    pdl_wait();
+    if (!a.early_ids) pdl_wait();
     extern __shared__ uint4 tsm4[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int grp = warp / KS, lw = warp - grp * KS;  // slot j = grp of the token; local warp
@@ -70,9 +75,12 @@ __global__ void __launch_bounds__(256 * KS, 1) k_down_tok(ExpArgs a) {
     for (int unit = blockIdx.x; unit < a.T * RB; unit += gridDim.x) {
         const int t = unit / RB, rb = unit - t * RB;
         const int slot = t * k + grp;
-        const TileInfo ti = tile_info(a, slot);
+        const int e_raw = __ldcg(a.idx + slot);
+        const float w_raw = __ldcg(a.wts + slot);
+        const TileInfo ti = {(e_raw >= 0 && e_raw < a.E) ? e_raw : 0, slot, 1};
         float C[1][4];
-        down_slot_partial<FMT, KS, GPW>(a, slot, (size_t)ti.e * RB + rb, lw, threadIdx.x - grp * KS * 32, hs4, C);
+        down_slot_partial<FMT, KS, GPW>(a, slot, (size_t)ti.e * RB + rb, lw, threadIdx.x - grp * KS * 32, hs4, C,
+                                        a.early_ids != 0);
 #pragma unroll
         for (int i = 0; i < 4; ++i) red[((grp * KS + lw) * 4 + i) * 32 + lane] = C[0][i];
         __syncthreads();
@@ -80,8 +88,7 @@ __global__ void __launch_bounds__(256 * KS, 1) k_down_tok(ExpArgs a) {
             float cs[1][4];
             down_slot_reduce<KS>(red + grp * KS * 4 * 32, lane, cs);
             const int gq = lane >> 2, r0 = rb * 16 + gq, r1 = r0 + 8;
-            const int e_raw = a.idx[slot];
-            const float wsl = (e_raw >= 0 && e_raw < a.E) ? a.wts[slot] : 0.f;
+            const float wsl = (e_raw >= 0 && e_raw < a.E) ? w_raw : 0.f;
             float v0 = cs[0][0], v1 = cs[0][2];
             if (a.bd) {
                 v0 += a.bd[(size_t)ti.e * d + r0];

@@ -80,6 +80,7 @@ struct ExpArgs {
     unsigned *err;
     int T, d, f, E, k, act, tile_mode;
     int dn_prefetch;  // gate/up pulls the down weights of its expert into L2
+    int early_ids;    // decode down reads ids, weights and its first weight batch before waiting for gate/up
     int fmt;          // FMT_Q4 or FMT_FP4
     int h_kperm;      // gate/up writes h with the 64-group k order permuted for a TMEM-operand tensor-core down
     int slot_out;     // 1: down stops after writing the weighted per-slot outputs yp (caller's buffer), no combine

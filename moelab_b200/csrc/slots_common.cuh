@@ -82,9 +82,11 @@ __device__ __forceinline__ void gate_up_slot_unit(const ExpArgs &a, int unit, ui
 // One slot's down dot products for this warp's share of K (warp lw of the KS splitting the f/64 groups), with
 // the slot's h row and block sums staged into hs4 by the KS * 32 threads ltid = 0 .. (the first weight batch is
 // issued before the staging). Contains exactly one __syncthreads; every thread of the CTA must call it.
+// wait_h: the kernel has not yet waited for its upstream grid (the gate/up kernel writing h): the wait is taken
+// after the first weight batch is issued, before h is read.
 template <int FMT, int KS, int GPW>
 __device__ __forceinline__ void down_slot_partial(const ExpArgs &a, int slot, size_t blk, int lw, int ltid,
-                                                  uint4 *hs4, float (&C)[1][4]) {
+                                                  uint4 *hs4, float (&C)[1][4], bool wait_h = false) {
     const int lane = threadIdx.x & 31, gq = lane >> 2, c = lane & 3;
     const int f = a.f, G = f >> 6;
     const int g_beg = lw * G / KS, g_end = (lw + 1) * G / KS;
@@ -105,6 +107,7 @@ __device__ __forceinline__ void down_slot_partial(const ExpArgs &a, int slot, si
             b[i] = ld_scales<FMT>(a.dn, blk, G, g, gq);
         }
         if (!synced) {  // stage the h row and its block sums while the first weight batch is in flight
+            if (wait_h) pdl_wait();
             for (int i = ltid; i < f / 8; i += 32 * KS) hs4[i] = __ldcg(hsrc + i);
             for (int i = ltid; i < f / 64; i += 32 * KS) hs4[f / 8 + i] = __ldcg(ssrc + i);
             __syncthreads();
@@ -123,6 +126,7 @@ __device__ __forceinline__ void down_slot_partial(const ExpArgs &a, int slot, si
         }
     }
     if (!synced) {
+        if (wait_h) pdl_wait();
         for (int i = ltid; i < f / 8; i += 32 * KS) hs4[i] = __ldcg(hsrc + i);
         for (int i = ltid; i < f / 64; i += 32 * KS) hs4[f / 8 + i] = __ldcg(ssrc + i);
         __syncthreads();
