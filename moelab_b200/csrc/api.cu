@@ -446,15 +446,24 @@ int run_experts(int fmt, ExpArgs a, int policy, const Layout &L, void *ws, cudaS
     return MOEB_OK;
 }
 
-template <int TPB, int U>
+template <int TPB, int U, bool PRE = false>
 void (*router_kernel(int E))(RouterArgs) {
     const int J = (E + 31) / 32;
-    if (J <= 1) return k_router<TPB, 1, U>;
-    if (J <= 2) return k_router<TPB, 2, U>;
-    if (J <= 4) return k_router<TPB, 4, U>;
-    if (J <= 8) return k_router<TPB, 8, U>;
-    if (J <= 16) return k_router<TPB, 16, U>;
-    return k_router<TPB, 32, U>;
+    if (J <= 1) return k_router<TPB, 1, U, PRE>;
+    if (J <= 2) return k_router<TPB, 2, U, PRE>;
+    if (J <= 4) return k_router<TPB, 4, U, PRE>;
+    if (J <= 8) return k_router<TPB, 8, U, PRE>;
+    if (J <= 16) return k_router<TPB, 16, U, PRE>;
+    return k_router<TPB, 32, U, PRE>;
+}
+
+// Decode-sized router calls (T <= MOEB_ROUTER_PRE_T, default 16) load their gate rows before the PDL wait.
+int router_pre_t() {
+    static const int v = [] {
+        const char *s = getenv("MOEB_ROUTER_PRE_T");
+        return s ? atoi(s) : 16;
+    }();
+    return v;
 }
 
 // The register-tiled router needs enough (token block, expert block) CTAs to fill the GPU. Measured (CUDA graph,
@@ -528,7 +537,9 @@ int launch_router(const void *x, const void *wg, const void *bias, int T, int d,
                                  : ew == 2 ? router_t_kernel<4, 2>(E) : router_t_kernel<4, 1>(E);
         e = launch(kern, dim3((E + 8 * ew - 1) / (8 * ew), (T + tw - 1) / tw), dim3(256), smem, st, r);
     } else {
-        void (*kern)(RouterArgs) = tpb == 1 ? router_kernel<1, 8>(E) : router_kernel<4, 4>(E);
+        void (*kern)(RouterArgs) = tpb == 4             ? router_kernel<4, 4>(E)
+                                   : T <= router_pre_t() ? router_kernel<1, 8, true>(E)
+                                                         : router_kernel<1, 8>(E);
         e = launch(kern, dim3((E + 3) / 4, (T + tpb - 1) / tpb), dim3(128), smem, st, r);
     }
     if (e != cudaSuccess)

@@ -173,7 +173,7 @@ __global__ void k_ep_combine_p2p(const unsigned char *self, const int *slot_pos,
 __global__ void k_ep_combine(const float *back, const int *slot_pos, int T, int d, int k, const uint16_t *residual,
                              uint16_t *y);
 
-template <int TPB, int JMAX, int U>
+template <int TPB, int JMAX, int U, bool PRE>
 __global__ void k_router(RouterArgs a);
 template <int TW, int EW, int JMAX>
 __global__ void k_router_t(RouterArgs a);

@@ -189,27 +189,34 @@ __device__ __forceinline__ void router_tail(const RouterArgs &a, int t0, int nt,
 // grid (ceil(E / 4), ceil(T / TPB)), block 128: warp w computes expert blockIdx.x * 4 + w for TPB tokens.
 // Each lane loads U chunks of the gate row and of every token row at once, then runs the fmaf chains; warp 0 of
 // the first expert block also turns its x registers into the per-64-group sums.
-template <int TPB, int JMAX, int U>
+template <int TPB, int JMAX, int U, bool PRE>
 __global__ void __launch_bounds__(128) k_router(RouterArgs a) {
     pdl_launch();
-    pdl_wait();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int e = blockIdx.x * 4 + warp;
+    const int nch = a.d / 8;
+    const uint16_t *wr = a.wg + (size_t)min(e, a.E - 1) * a.d;
+    // PRE: the gate is a weight (written before any call), so the first chunks of its row are loaded before waiting
+    // for the kernel that produced x (decode-sized calls, whose router latency is on the critical path; the held
+    // registers cost occupancy, so larger calls do not)
+    uint4 w0[U];
+    if (PRE)
+#pragma unroll
+        for (int u = 0; u < U; ++u) w0[u] = *reinterpret_cast<const uint4 *>(wr + 8 * min(lane + 32 * u, nch - 1));
+    pdl_wait();
     const int t0 = blockIdx.y * TPB;
     const int nt = min(TPB, a.T - t0);
-    const int nch = a.d / 8;
     const bool do_xsum = a.xsum != nullptr && blockIdx.x == 0 && warp == 0;
     if (e < a.E) {
         float acc[TPB];
 #pragma unroll
         for (int i = 0; i < TPB; ++i) acc[i] = 0.f;
-        const uint16_t *wr = a.wg + (size_t)e * a.d;
         for (int c0 = lane; c0 - lane < nch; c0 += 32 * U) {  // same trip count on every lane (shuffles below)
             uint4 w[U], xv[TPB][U];
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int c = min(c0 + 32 * u, nch - 1);  // clamped: a repeated load, never used
-                w[u] = *reinterpret_cast<const uint4 *>(wr + 8 * c);
+                w[u] = PRE && c0 == lane ? w0[u] : *reinterpret_cast<const uint4 *>(wr + 8 * c);
 #pragma unroll
                 for (int i = 0; i < TPB; ++i)
                     xv[i][u] = *reinterpret_cast<const uint4 *>(a.x + (size_t)(t0 + min(i, nt - 1)) * a.d + 8 * c);
@@ -411,15 +418,16 @@ __global__ void __launch_bounds__(256) k_prep(PrepArgs a) {
     if (threadIdx.x == 0) *a.cnt_all = 0;
 }
 
-#define MOEB_ROUTER_INST(TPB, U)                          \
-    template __global__ void k_router<TPB, 1, U>(RouterArgs);  \
-    template __global__ void k_router<TPB, 2, U>(RouterArgs);  \
-    template __global__ void k_router<TPB, 4, U>(RouterArgs);  \
-    template __global__ void k_router<TPB, 8, U>(RouterArgs);  \
-    template __global__ void k_router<TPB, 16, U>(RouterArgs); \
-    template __global__ void k_router<TPB, 32, U>(RouterArgs);
-MOEB_ROUTER_INST(1, 8)
-MOEB_ROUTER_INST(4, 4)
+#define MOEB_ROUTER_INST(TPB, U, PRE)                          \
+    template __global__ void k_router<TPB, 1, U, PRE>(RouterArgs);  \
+    template __global__ void k_router<TPB, 2, U, PRE>(RouterArgs);  \
+    template __global__ void k_router<TPB, 4, U, PRE>(RouterArgs);  \
+    template __global__ void k_router<TPB, 8, U, PRE>(RouterArgs);  \
+    template __global__ void k_router<TPB, 16, U, PRE>(RouterArgs); \
+    template __global__ void k_router<TPB, 32, U, PRE>(RouterArgs);
+MOEB_ROUTER_INST(1, 8, false)
+MOEB_ROUTER_INST(1, 8, true)
+MOEB_ROUTER_INST(4, 4, false)
 #undef MOEB_ROUTER_INST
 #define MOEB_ROUTER_T_INST(EW)                               \
     template __global__ void k_router_t<4, EW, 1>(RouterArgs);  \
