@@ -457,13 +457,16 @@ void (*router_kernel(int E))(RouterArgs) {
     return k_router<TPB, 32, U, PRE>;
 }
 
-// Decode-sized router calls (T <= MOEB_ROUTER_PRE_T, default 16) load their gate rows before the PDL wait.
-int router_pre_t() {
+// One-token router CTAs load their gate rows before the PDL wait when the grid (T * E/4 CTAs) stays within 768 CTAs:
+// the held registers cut residency from 6 to 4 CTAs per SM. Qwen3-30B (E = 128), us per layer, with / without:
+// T = 1 18.6 / 19.1, 16 82.9 / 84.4, 24 95.3 / 98.3, 32 111.1 / 111.1, 48 119.4 / 118.7, 64 123.0 / 121.9.
+// MOEB_ROUTER_PRE_T=n replaces the rule with T <= n (measurements).
+bool router_pre(int T, int E) {
     static const int v = [] {
         const char *s = getenv("MOEB_ROUTER_PRE_T");
-        return s ? atoi(s) : 16;
+        return s ? atoi(s) : -1;
     }();
-    return v;
+    return v >= 0 ? T <= v : (long)T * ((E + 3) / 4) <= 768;
 }
 
 // The register-tiled router needs enough (token block, expert block) CTAs to fill the GPU. Measured (CUDA graph,
@@ -538,7 +541,7 @@ int launch_router(const void *x, const void *wg, const void *bias, int T, int d,
         e = launch(kern, dim3((E + 8 * ew - 1) / (8 * ew), (T + tw - 1) / tw), dim3(256), smem, st, r);
     } else {
         void (*kern)(RouterArgs) = tpb == 4             ? router_kernel<4, 4>(E)
-                                   : T <= router_pre_t() ? router_kernel<1, 8, true>(E)
+                                   : router_pre(T, E)    ? router_kernel<1, 8, true>(E)
                                                          : router_kernel<1, 8>(E);
         e = launch(kern, dim3((E + 3) / 4, (T + tpb - 1) / tpb), dim3(128), smem, st, r);
     }
