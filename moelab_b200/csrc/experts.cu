@@ -53,15 +53,17 @@ __global__ void __launch_bounds__(32 * KS, FMT == FMT_FP4 ? 4 : 8) k_down_slots(
 }
 
 // Decode down with the combine in shared memory: one CTA per (token, 16-row block of d), the token's k slots as k
-// groups of KS warps. Each slot's value is computed as in k_down_slots (its K split over the KS warps, partials
-// summed in warp order, weight * (acc + bias)); the k values are then summed in slot order plus the residual, as
-// down_store_combine's last arrival does - without the global slot rows, fences and counters. k <= 32 / KS; the
-// CTA has 32 * KS * k threads (at most 256 * KS, the launch bound).
+// groups of KS warps, each warp carrying VW shares of a KS * VW split of K. Each slot's value is computed exactly as
+// in k_down_slots with 4 warps when KS * VW = 4 (same shares, partials summed in share order, weight * (acc + bias));
+// the k values are then summed in slot order plus the residual, as down_store_combine's last arrival does - without
+// the global slot rows, fences and counters. k <= 32 / KS; the CTA has 32 * KS * k threads (at most 256 * KS, the
+// launch bound).
 // The expert ids and combine weights come from upstream of the gate/up kernel, which releases this grid only
 // after its own wait, so they are read through L2 (never a stale L1 line) before this grid waits for gate/up; the
 // first weight batch of every slot is issued before the wait too, and h after it (a.early_ids = 0: wait first).
-template <int FMT, int KS, int GPW>
+template <int FMT, int KS, int VW, int GPW>
 __global__ void __launch_bounds__(256 * KS, 1) k_down_tok(ExpArgs a) {
+    constexpr int KV = KS * VW;
     pdl_launch();
     if (!a.early_ids) pdl_wait();
     extern __shared__ uint4 tsm4[];
@@ -70,23 +72,25 @@ __global__ void __launch_bounds__(256 * KS, 1) k_down_tok(ExpArgs a) {
     const int k = a.k, d = a.d, f = a.f, RB = d >> 4;
     const int hs_u4 = (f * 2 + f / 16 * 4) / 16;     // h row + block sums, in uint4
     uint4 *hs4 = tsm4 + (size_t)grp * hs_u4;
-    float *red = reinterpret_cast<float *>(tsm4 + (size_t)k * hs_u4);  // [k][KS][4][32]
-    float *vals = red + k * KS * 4 * 32;                                // [k][16]
+    float *red = reinterpret_cast<float *>(tsm4 + (size_t)k * hs_u4);  // [k][KV][4][32]
+    float *vals = red + k * KV * 4 * 32;                                // [k][16]
     for (int unit = blockIdx.x; unit < a.T * RB; unit += gridDim.x) {
         const int t = unit / RB, rb = unit - t * RB;
         const int slot = t * k + grp;
         const int e_raw = __ldcg(a.idx + slot);
         const float w_raw = __ldcg(a.wts + slot);
         const TileInfo ti = {(e_raw >= 0 && e_raw < a.E) ? e_raw : 0, slot, 1};
-        float C[1][4];
-        down_slot_partial<FMT, KS, GPW>(a, slot, (size_t)ti.e * RB + rb, lw, threadIdx.x - grp * KS * 32, hs4, C,
-                                        a.early_ids != 0);
+        float C[VW][1][4];
+        down_slot_partial_v<FMT, KS, VW, GPW>(a, slot, (size_t)ti.e * RB + rb, lw, threadIdx.x - grp * KS * 32, hs4,
+                                              C, a.early_ids != 0);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) red[((grp * KS + lw) * 4 + i) * 32 + lane] = C[0][i];
+        for (int v = 0; v < VW; ++v)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) red[((grp * KV + lw * VW + v) * 4 + i) * 32 + lane] = C[v][0][i];
         __syncthreads();
         if (lw == 0 && (lane & 3) == 0) {  // column 0 (the slot) of rows gq, gq + 8
             float cs[1][4];
-            down_slot_reduce<KS>(red + grp * KS * 4 * 32, lane, cs);
+            down_slot_reduce<KV>(red + grp * KV * 4 * 32, lane, cs);
             const int gq = lane >> 2, r0 = rb * 16 + gq, r1 = r0 + 8;
             const float wsl = (e_raw >= 0 && e_raw < a.E) ? w_raw : 0.f;
             float v0 = cs[0][0], v1 = cs[0][2];
@@ -298,10 +302,10 @@ template __global__ void k_gate_up_slots<FMT_Q4, 4, 8>(ExpArgs);
 template __global__ void k_down_slots<FMT_Q4, 4, 4>(ExpArgs);
 template __global__ void k_gate_up_slots<FMT_FP4, 8, 4>(ExpArgs);
 template __global__ void k_down_slots<FMT_FP4, 4, 4>(ExpArgs);
-template __global__ void k_down_tok<FMT_Q4, 4, 4>(ExpArgs);
-template __global__ void k_down_tok<FMT_FP4, 4, 4>(ExpArgs);
-template __global__ void k_down_tok<FMT_Q4, 2, 6>(ExpArgs);
-template __global__ void k_down_tok<FMT_FP4, 2, 6>(ExpArgs);
+template __global__ void k_down_tok<FMT_Q4, 4, 1, 4>(ExpArgs);
+template __global__ void k_down_tok<FMT_FP4, 4, 1, 4>(ExpArgs);
+template __global__ void k_down_tok<FMT_Q4, 2, 2, 6>(ExpArgs);
+template __global__ void k_down_tok<FMT_FP4, 2, 2, 6>(ExpArgs);
 template __global__ void k_gate_up_tiles_reg<FMT_FP4, 1, 2>(ExpArgs);
 template __global__ void k_down_tiles_reg<FMT_FP4, 1, 2>(ExpArgs);
 template __global__ void k_gate_up_tiles_reg<FMT_FP4, 2, 1>(ExpArgs);

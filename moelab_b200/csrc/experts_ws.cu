@@ -48,7 +48,7 @@ MOEB_DEV uint2 stage_scales(const unsigned char *p, int gq) {
 template <int FMT, int NT8, int RBC, int SG, int NS, bool DOWN, int MB>
 __global__ void __launch_bounds__(32 * (RBC + 1), MB) k_experts_ws(const __grid_constant__ ExpArgs a) {
     using L = WSL<FMT, NT8, RBC, SG, DOWN>;
-    pdl_launch();
+    if (DOWN || !a.early_ids) pdl_launch();
     extern __shared__ __align__(128) unsigned char smem_raw[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem_raw + NS * L::STAGE);
     uint64_t *empty = full + NS;
@@ -61,13 +61,19 @@ __global__ void __launch_bounds__(32 * (RBC + 1), MB) k_experts_ws(const __grid_
         }
         mbar_fence_init();
     }
-    pdl_wait();
     __syncthreads();
+    // Early down (a.early_ids, set for both kernels of the pair): the gate/up kernel releases this grid only after
+    // its own wait (releasing it at the start measured faster when down does not start early), so the routing tables
+    // (written upstream of gate/up) are complete; the producer reads them through L2 and issues the weight copies of
+    // its first NS stages before waiting for h, then the activation copies of those stages.
+    const bool early = DOWN && a.early_ids && warp == RBC;
+    if (!early) pdl_wait();
+    if (!DOWN && a.early_ids) pdl_launch();  // after this grid's own wait: the early down producer relies on it
     const int RB = DOWN ? (a.d >> 4) : (a.f >> 4);
     const int G = DOWN ? (a.f >> 6) : (a.d >> 6);
     const int RBS = (RB + RBC - 1) / RBC;  // super-units per tile
     const int SPU = (G + SG - 1) / SG;     // stages per super-unit
-    const int n_tiles = a.tile_mode ? *a.ntiles : a.T * a.k;
+    const int n_tiles = a.tile_mode ? __ldcg(a.ntiles) : a.T * a.k;
     const int n_su = n_tiles * RBS;
     const int my_su = (int)blockIdx.x < n_su ? (n_su - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
     const int total = my_su * SPU;
@@ -88,12 +94,31 @@ __global__ void __launch_bounds__(32 * (RBC + 1), MB) k_experts_ws(const __grid_
                 tmap_prefetch(&a.tmq[m0 + p]);
                 tmap_prefetch(&a.tmsb[m0 + p]);
             }
-        auto fetch_tile = [&](int su) {  // tile record (expert, start, n)
+        auto fetch_tile = [&](int su) {  // tile record (expert, start, n), through L2
             const int tile = su / RBS;
-            return a.tile_mode ? a.tiles[tile] : make_int4(a.idx[tile], tile, 1, 0);
+            return a.tile_mode ? __ldcg(a.tiles + tile) : make_int4(__ldcg(a.idx + tile), tile, 1, 0);
         };
         auto fetch_slot = [&](const int4 &tr) {  // this lane's slot id, or -1
-            return (clane && col < tr.z) ? (a.tile_mode ? a.sorted[tr.y + col] : tr.y) : -1;
+            return (clane && col < tr.z) ? (a.tile_mode ? __ldcg(a.sorted + tr.y + col) : tr.y) : -1;
+        };
+        // activation copies of the first `nearly` stages, deferred until the upstream grid is complete
+        const int nearly = early ? min(NS, total) : 0;
+        const unsigned char *ps0[NS], *ps1[NS];
+        auto issue_x = [&](int k, const unsigned char *s0, const unsigned char *s1) {
+            const int g0 = (k % SPU) * SG, ng = min(SG, G - g0);
+            const int ga = DOWN ? g0 : (g0 & ~3);
+            const int sum_bytes = DOWN ? ng * 16 : ((g0 + ng - ga + 3) / 4) * 16;
+            unsigned char *st = smem_raw + (size_t)(k % NS) * L::STAGE;
+            tma_load_1d(st + L::W_BYTES + L::SB_BYTES + col * L::X_ROW, s0 + (size_t)g0 * 128, ng * 128,
+                        full + k % NS);
+            tma_load_1d(st + L::W_BYTES + L::SB_BYTES + L::X_BYTES + col * L::S_ROW, s1 + (size_t)ga * (DOWN ? 16 : 4),
+                        sum_bytes, full + k % NS);
+        };
+        auto flush_early = [&]() {
+            pdl_wait();
+#pragma unroll
+            for (int q = 0; q < NS; ++q)
+                if (q < nearly && lane != 0 && ps0[q] != nullptr) issue_x(q, ps0[q], ps1[q]);
         };
         int4 tr_n = make_int4(0, 0, 0, 0);
         int sl_n = -1;
@@ -132,6 +157,7 @@ __global__ void __launch_bounds__(32 * (RBC + 1), MB) k_experts_ws(const __grid_
                 const int nsu = (int)blockIdx.x + (k / SPU + 1) * (int)gridDim.x;
                 if (nsu < n_su) sl_n = fetch_slot(tr_n);
             }
+            if (k == nearly && nearly > 0) flush_early();  // before any wait on a consumed stage
             if (k >= NS && !mbar_wait_bounded(empty + slot, (unsigned)(((k / NS) - 1) & 1))) {
                 if (lane == 0) atomicOr(a.err, ERR_TIMEOUT);
                 return;
@@ -149,13 +175,18 @@ __global__ void __launch_bounds__(32 * (RBC + 1), MB) k_experts_ws(const __grid_
                     tma_load_2d(st + L::W_BYTES + p * RBC * SG * L::SBG, &a.tmsb[m0 + p], g0 * (L::SBG / 4), row0,
                                 full + slot, pol);
                 }
+            } else if (k < nearly) {
+#pragma unroll
+                for (int q = 0; q < NS; ++q)
+                    if (q == k) {
+                        ps0[q] = src0;
+                        ps1[q] = src1;
+                    }
             } else if (src0 != nullptr) {
-                tma_load_1d(st + L::W_BYTES + L::SB_BYTES + col * L::X_ROW, src0 + (size_t)g0 * 128, ng * 128,
-                            full + slot);
-                tma_load_1d(st + L::W_BYTES + L::SB_BYTES + L::X_BYTES + col * L::S_ROW,
-                            src1 + (size_t)ga * (DOWN ? 16 : 4), sum_bytes, full + slot);
+                issue_x(k, src0, src1);
             }
         }
+        if (nearly > 0 && total == nearly) flush_early();  // every stage fit the first ring
         return;
     }
 

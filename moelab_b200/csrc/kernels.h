@@ -80,7 +80,7 @@ struct ExpArgs {
     unsigned *err;
     int T, d, f, E, k, act, tile_mode;
     int dn_prefetch;  // gate/up pulls the down weights of its expert into L2
-    int early_ids;    // decode down reads ids, weights and its first weight batch before waiting for gate/up
+    int early_ids;    // down reads its routing and issues its first weight loads before waiting for gate/up
     int fmt;          // FMT_Q4 or FMT_FP4
     int h_kperm;      // gate/up writes h with the 64-group k order permuted for a TMEM-operand tensor-core down
     int slot_out;     // 1: down stops after writing the weighted per-slot outputs yp (caller's buffer), no combine
@@ -193,7 +193,7 @@ template <int FMT, int KS, int GPW>
 __global__ void k_gate_up_slots(ExpArgs a);
 template <int FMT, int KS, int GPW>
 __global__ void k_down_slots(ExpArgs a);
-template <int FMT, int KS, int GPW>
+template <int FMT, int KS, int VW, int GPW>
 __global__ void k_down_tok(ExpArgs a);
 size_t down_tok_smem(int k, int f, int ks);
 template <int FMT, int NT8, int GPW>
