@@ -82,6 +82,27 @@ cudaError_t launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, c
     return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// The same with thread-block clusters of cluster_x CTAs along x.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, int cluster_x,
+                           Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)cluster_x;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
 // Workspace layout for up to Tc tokens. The first region holds counters that must be zero before the first
@@ -463,6 +484,16 @@ void (*router_kernel(int E))(RouterArgs) {
     return k_router<TPB, 32, U, PRE>;
 }
 
+// Slot-mode router calls (E <= 128, T <= 64) use k_router_cl, a cluster per token with the top-k in shared memory
+// (MOEB_ROUTER_CL=0: the last-arriver k_router, for measurements).
+bool router_cluster() {
+    static const int v = [] {
+        const char *s = getenv("MOEB_ROUTER_CL");
+        return s ? atoi(s) : 1;
+    }();
+    return v != 0;
+}
+
 // One-token router CTAs load their gate rows before the PDL wait when the grid (T * E/4 CTAs) stays within 768 CTAs:
 // the held registers cut residency from 6 to 4 CTAs per SM. Qwen3-30B (E = 128), us per layer, with / without:
 // T = 1 18.6 / 19.1, 16 82.9 / 84.4, 24 95.3 / 98.3, 32 111.1 / 111.1, 48 119.4 / 118.7, 64 123.0 / 121.9.
@@ -540,7 +571,12 @@ int launch_router(const void *x, const void *wg, const void *bias, int T, int d,
     // one expert per warp and 1 (T <= 64) or 4 tokens, or the register-tiled kernel (4 tokens x EW experts per
     // warp, EW = 4 from 32 experts on)
     cudaError_t e;
-    if (tiled) {
+    if (!tiles && E <= 128 && T <= 64 && router_cluster()) {
+        // slot mode: one cluster per token selects its experts in shared memory
+        const int rc = (E + 15) / 16, J = (E + 31) / 32;
+        void (*kern)(RouterArgs) = J <= 1 ? k_router_cl<1> : J <= 2 ? k_router_cl<2> : k_router_cl<4>;
+        e = launch_cluster(kern, dim3(rc, T), dim3(512), 0, st, rc, r);
+    } else if (tiled) {
         const int ew = E >= 32 ? 4 : E >= 16 ? 2 : 1, tw = ew == 4 ? router_tw(T) : 4;
         void (*kern)(RouterArgs) = ew == 4 ? (tw == 8 ? router_t_kernel<8, 4>(E) : router_t_kernel<4, 4>(E))
                                  : ew == 2 ? router_t_kernel<4, 2>(E) : router_t_kernel<4, 1>(E);

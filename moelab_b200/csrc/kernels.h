@@ -177,6 +177,8 @@ template <int TPB, int JMAX, int U, bool PRE>
 __global__ void k_router(RouterArgs a);
 template <int TW, int EW, int JMAX>
 __global__ void k_router_t(RouterArgs a);
+template <int JMAX>
+__global__ void k_router_cl(RouterArgs a);
 __global__ void k_prep(PrepArgs a);
 size_t tiles_smem(int threads, int E, long TK, size_t cap);
 

@@ -13,6 +13,8 @@
 //      slot permutation grouped by expert, cut into tiles of <= NT slots (replaces the O(TK^2) map kernels
 //      metal_q4_tiles_v2.py:362-373 / metal_mxfp4_moe.py:143-153).
 // k_prep: the same steps 2b-3 for the harness contract run(state, x, idx, wts), where ids come from outside.
+#include <cooperative_groups.h>
+
 #include "route_common.cuh"
 
 namespace moeb {
@@ -268,6 +270,77 @@ __global__ void __launch_bounds__(128) k_router(RouterArgs a) {
     router_tail<JMAX>(a, t0, nt, warp, lane);
 }
 
+// Decode router (slot mode, E <= 128): one cluster of ceil(E / 16) <= 8 CTAs per token (grid (ceil(E / 16), T)),
+// 16 warps per CTA, one expert per warp. Each logit is computed exactly as in k_router (lane l sums chunks l, l + 32,
+// ... with fmaf in order, then the xor butterfly; the gate row is loaded before the PDL wait) and stored into cluster
+// rank 0's shared memory; after one cluster barrier rank 0's warp 0 selects the token's experts there with
+// topk_token_to's rules and arithmetic. No global counter and no reload of the logits through L2.
+template <int JMAX>
+__global__ void __launch_bounds__(512, 1) k_router_cl(RouterArgs a) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    __shared__ float s_lg[128];
+    constexpr int U = 8;
+    pdl_launch();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int e = blockIdx.x * 16 + warp, t = blockIdx.y;
+    const int nch = a.d / 8;
+    const uint16_t *wr = a.wg + (size_t)min(e, a.E - 1) * a.d;
+    uint4 w0[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) w0[u] = *reinterpret_cast<const uint4 *>(wr + 8 * min(lane + 32 * u, nch - 1));
+    pdl_wait();
+    const bool do_xsum = a.xsum != nullptr && blockIdx.x == 0 && warp == 0;
+    const uint16_t *xr = a.x + (size_t)t * a.d;
+    float acc = 0.f;
+    for (int c0 = lane; c0 - lane < nch; c0 += 32 * U) {  // same trip count on every lane (shuffles below)
+        uint4 w[U], xv[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int c = min(c0 + 32 * u, nch - 1);  // clamped: a repeated load, never used
+            w[u] = c0 == lane ? w0[u] : *reinterpret_cast<const uint4 *>(wr + 8 * c);
+            xv[u] = *reinterpret_cast<const uint4 *>(xr + 8 * c);
+        }
+        float s = acc;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            if (c0 + 32 * u < nch) {
+                const uint32_t xx[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
+                const uint32_t ww[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    s = __fmaf_rn(bf16lo(xx[j]), bf16lo(ww[j]), s);
+                    s = __fmaf_rn(bf16hi(xx[j]), bf16hi(ww[j]), s);
+                }
+            }
+        }
+        acc = s;
+        if (do_xsum) {  // chunk c of lane l covers group c / 8: 8 consecutive lanes share a group
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int c = c0 + 32 * u;
+                const uint4 v = xv[u];
+                float p = bf16lo(v.x) + bf16hi(v.x) + bf16lo(v.y) + bf16hi(v.y) + bf16lo(v.z) + bf16hi(v.z) +
+                          bf16lo(v.w) + bf16hi(v.w);
+                p += __shfl_xor_sync(0xffffffffu, p, 1);
+                p += __shfl_xor_sync(0xffffffffu, p, 2);
+                p += __shfl_xor_sync(0xffffffffu, p, 4);
+                if (c < nch && (lane & 7) == 0) a.xsum[(size_t)t * xsum_stride(a.d) + c / 8] = p;
+            }
+        }
+    }
+    float v = acc;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (a.bias) v = __fadd_rn(v, bf2f(a.bias[min(e, a.E - 1)]));
+    if (lane == 0 && e < a.E) {
+        *cl.map_shared_rank(s_lg + e, 0) = v;
+        a.logits[(size_t)t * a.E + e] = v;
+    }
+    cl.sync();  // release / acquire across the cluster: rank 0 sees every logit
+    if (cl.block_rank() == 0 && warp == 0) topk_token_to<JMAX>(a, t, lane, a.idx, a.wts, s_lg);
+}
+
 // Register-tiled logits for larger T. grid (ceil(E / (8 EW)), ceil(T / TW)), block 256: warp w computes
 // experts (blockIdx.x * 8 + w) * EW .. + EW - 1 for the block's TW tokens. Every (token, expert) dot product is
 // summed exactly as in k_router (lane l: chunks l, l + 32, ... in order, fmaf over each chunk's 8 elements, then
@@ -440,6 +513,9 @@ MOEB_ROUTER_T_INST(1)
 MOEB_ROUTER_T_INST(2)
 MOEB_ROUTER_T_INST(4)
 #undef MOEB_ROUTER_T_INST
+template __global__ void k_router_cl<1>(RouterArgs);
+template __global__ void k_router_cl<2>(RouterArgs);
+template __global__ void k_router_cl<4>(RouterArgs);
 // 8 tokens x 4 experts per warp (large T: each gate chunk loaded from L2 serves twice the tokens)
 template __global__ void k_router_t<8, 4, 1>(RouterArgs);
 template __global__ void k_router_t<8, 4, 2>(RouterArgs);

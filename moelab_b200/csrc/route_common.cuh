@@ -31,15 +31,17 @@ __device__ __forceinline__ float fkey_inv(unsigned k) {
 
 // Top-k of token t from the fp32 logits in a.logits; writes the token's k + ns slots (routed ids / weights, then
 // the shared experts) to idx_out / wts_out [t * (k + ns) + j].
+// srow: the token's logits in shared memory (null: a.logits row t, read through L2).
 template <int JMAX>
-__device__ void topk_token_to(const RouterArgs &a, int t, int lane, int *idx_out, float *wts_out) {
+__device__ void topk_token_to(const RouterArgs &a, int t, int lane, int *idx_out, float *wts_out,
+                              const float *srow = nullptr) {
     const int E = a.E, k = a.k;
     float v[JMAX];
     float m0 = -INFINITY;
 #pragma unroll
     for (int j = 0; j < JMAX; ++j) {
         const int e = j * 32 + lane;
-        float l = e < E ? __ldcg(a.logits + (size_t)t * E + e) : -INFINITY;
+        float l = e < E ? (srow ? srow[e] : __ldcg(a.logits + (size_t)t * E + e)) : -INFINITY;
         v[j] = isnan(l) ? -INFINITY : l + 0.f;  // NaN = -inf; -0 -> +0 (equal values compare as keys too)
         m0 = fmaxf(m0, v[j]);
     }
